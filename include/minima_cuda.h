@@ -1,0 +1,163 @@
+/*
+ * minima_cuda.h — C ABI of the B200 (sm_100a) decode path for Minima.
+ *
+ * Plain C: opaque handles, host pointers and sizes, integer status codes; no
+ * CUDA, C++ or PyTorch types cross this boundary.  The drop-in
+ * implementation of the reference's generate.h (minima_b200/host/
+ * generate_cuda.c) is the intended caller; tests and bench.py call it too.
+ *
+ * Reference interfaces this boundary stands under:
+ *   mc_model_create      <- the weights a Model holds (model.h:9-41, filled by
+ *                           model_init_config, model.c:95-167)
+ *   mc_session_create    <- kvcache_init (generate.h:26; generate.c:13-47)
+ *   mc_generate          <- generate_with_options (generate.h:65-68;
+ *                           generate.c:522-602), for a batch of independent
+ *                           sequences, each with its own Rng (util.h:10-12)
+ *   mc_forward_logits    <- forward_one per prefix (generate.c:76-194), the
+ *                           quantity generation_check_kv_cache compares
+ *                           (generate.c:202-265)
+ *
+ * Error convention: every entry point returns MC_OK (0) or a positive
+ * status; mc_last_error() gives a one-line description of the last failure
+ * on the calling thread.  No entry point aborts the process.
+ *
+ * Threading: one host thread per device; handles are not thread-safe.
+ */
+#ifndef MINIMA_CUDA_H
+#define MINIMA_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef int mc_status;
+#define MC_OK              0
+#define MC_ERR_INVALID     1   /* argument outside the supported envelope   */
+#define MC_ERR_CUDA        2   /* a CUDA runtime call failed                */
+#define MC_ERR_NOMEM       3   /* device or pinned-host allocation failed   */
+#define MC_ERR_TIMEOUT     4   /* a device-side wait ran past its deadline  */
+#define MC_ERR_DEVICE      5   /* the kernel reported an inconsistency      */
+#define MC_ERR_UNSUPPORTED 6   /* no kernel for this shape / device         */
+
+#define MC_WEIGHTS_F32  0      /* fp32 weights, fp32 arithmetic              */
+#define MC_WEIGHTS_BF16 1      /* bf16 weights (RNE from fp32), fp32 math    */
+
+/* mc_generate flags */
+#define MC_DEVICE_POINTERS 0x1u /* prompts/out_ids/rng/counts/final_pos are
+                                   device pointers (resident in HBM)       */
+
+typedef struct mc_model mc_model;
+typedef struct mc_session mc_session;
+
+/* Dimensions plus host pointers to the nine fp32 weight arrays in the
+   reference's layout and MODEL_ARRAYS order (checkpoint.c:43-52):
+   tok_emb [V,D]; attn_qkv [L,Q,D] (Q heads, then K heads, then V heads);
+   attn_proj [L,D,D]; ffn_up, ffn_gate [L,F,D]; ffn_down [L,D,F];
+   rms1_scale, rms2_scale [L,D]; rms_final_scale [D]. */
+typedef struct {
+    int vocab_size, dim, n_layers, n_heads, n_kv_heads, head_dim, kv_dim,
+        qkv_dim, ffn_dim, max_seq;
+    const float* tok_emb;
+    const float* attn_qkv;
+    const float* attn_proj;
+    const float* ffn_up;
+    const float* ffn_gate;
+    const float* ffn_down;
+    const float* rms1_scale;
+    const float* rms2_scale;
+    const float* rms_final_scale;
+} mc_model_desc;
+
+/* Field-for-field the reference's GenerationOptions (generate.h:50-63), so a
+   GenerationOptions* may be passed where an mc_sampling* is expected. */
+typedef struct {
+    float temperature;
+    float top_p;
+    float repetition_penalty;
+    float min_p;
+    float frequency_penalty;
+    float presence_penalty;
+    int top_k;
+    int max_new_tokens;
+    int min_new_tokens;
+    int no_repeat_ngram_size;
+    const uint16_t* stop_sequence_ids;
+    int stop_sequence_len;
+} mc_sampling;
+
+/* Envelope of this implementation (the reference's is config.h:7-14). */
+#define MC_MAX_VOCAB     32768
+#define MC_MAX_DIM       4096
+#define MC_MAX_LAYERS    64
+#define MC_MAX_HEADS     64
+#define MC_MAX_HEAD_DIM  256
+#define MC_MAX_FFN       16384
+#define MC_MAX_SEQ       8192
+#define MC_MAX_BATCH     1024
+#define MC_MAX_TOPK      256     /* generate.c:564 */
+#define MC_MAX_STOP      1024    /* generate.c:540 */
+
+/* Select the CUDA device for the calling thread (cudaSetDevice). */
+mc_status mc_init(int device);
+
+/* Upload weights (host fp32) to the current device as fp32 or bf16.
+   Dimensions are validated against the envelope above and against the
+   reference's derived-size rules (model.c:55-89). */
+mc_status mc_model_create(const mc_model_desc* desc, int weight_dtype, mc_model** out);
+/* Re-upload weights of identical dimensions (after the caller edited them). */
+mc_status mc_model_update(mc_model* model, const mc_model_desc* desc);
+mc_status mc_model_destroy(mc_model* model);
+
+/* Device KV cache and work buffers for up to max_batch sequences of up to
+   max_seq tokens each (max_seq <= the model's max_seq). */
+mc_status mc_session_create(mc_model* model, int max_batch, int max_seq,
+    mc_session** out);
+mc_status mc_session_destroy(mc_session* session);
+
+/*
+ * Run generate_with_options for `batch` independent sequences in one
+ * device-resident token loop (no host round trip per token).
+ *   prompts      [batch * prompt_stride] u16; sequence b is
+ *                prompts[b*prompt_stride .. + prompt_lens[b])
+ *   prompt_lens  [batch] host ints, 1 <= len <= out_cap, len <= max_seq
+ *   out_ids      [batch * out_cap] u16: prompt followed by generated ids
+ *   opts         validated as generate.c:526-551 does
+ *   rng_states   [batch] xorshift64* states, advanced exactly as the
+ *                reference advances its Rng
+ *   out_counts   [batch] ints: what generate_with_options would return
+ *   final_pos    [batch] ints (optional): the KV position the reference
+ *                leaves in cache->pos
+ * With MC_DEVICE_POINTERS, prompts/out_ids/rng_states/out_counts/final_pos
+ * are device pointers and no host<->device copy is made; prompt_lens and
+ * opts stay on the host either way.
+ * trace_logits (optional, host, [batch][trace_steps][vocab]) receives the
+ * masked logits the sampler saw at each of the first trace_steps steps.
+ */
+mc_status mc_generate(mc_session* session, int batch,
+    const uint16_t* prompts, int prompt_stride, const int* prompt_lens,
+    uint16_t* out_ids, int out_cap, const mc_sampling* opts,
+    uint64_t* rng_states, int* out_counts, int* final_pos, unsigned flags,
+    float* trace_logits, int trace_steps);
+
+/* Teacher-forced logits: feed tokens[b*n .. b*n+n) one position at a time
+   and store the logits after each position into logits_out[(b*n+i)*V]
+   (host).  Equals forward_one per prefix (generate.c:76-194). */
+mc_status mc_forward_logits(mc_session* session, int batch, const uint16_t* tokens,
+    int n, float* logits_out);
+
+/* Kernel time of the last mc_generate / mc_forward_logits on this session,
+   measured with CUDA events on the launching stream (milliseconds). */
+mc_status mc_last_kernel_ms(mc_session* session, float* ms);
+
+/* Number of kernels the last call launched on the device. */
+mc_status mc_last_launch_count(mc_session* session, int* launches);
+
+const char* mc_last_error(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

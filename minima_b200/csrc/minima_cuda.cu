@@ -1,0 +1,669 @@
+// minima_cuda.cu — C ABI (include/minima_cuda.h) over the sm_100a decode
+// token loop: weight upload, device KV cache / work buffers, and the single
+// cooperative launch that runs a whole generate_with_options batch.
+#include "minima_cuda.h"
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <vector>
+
+#include "mc_token_loop.cuh"
+
+namespace {
+
+thread_local char g_err[512] = "";
+
+mc_status fail(mc_status st, const char* fmt, ...) {
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(g_err, sizeof(g_err), fmt, ap);
+    va_end(ap);
+    return st;
+}
+
+#define MC_CUDA(call)                                                                  \
+    do {                                                                               \
+        cudaError_t e_ = (call);                                                       \
+        if (e_ != cudaSuccess)                                                         \
+            return fail(e_ == cudaErrorMemoryAllocation ? MC_ERR_NOMEM : MC_ERR_CUDA,   \
+                        "%s failed: %s (%s:%d)", #call, cudaGetErrorString(e_),        \
+                        __FILE__, __LINE__);                                           \
+    } while (0)
+
+int kv_head_count(int n_heads) {  // model.c:34-40
+    if (n_heads <= 1) return 1;
+    for (int kv = n_heads / 2; kv >= 1; kv--)
+        if (n_heads % kv == 0) return kv;
+    return 1;
+}
+
+uint16_t bf16_rne(float v) {
+    uint32_t u;
+    memcpy(&u, &v, 4);
+    if ((u & 0x7F800000u) == 0x7F800000u) return (uint16_t)(u >> 16);
+    u += 0x7FFFu + ((u >> 16) & 1u);
+    return (uint16_t)(u >> 16);
+}
+
+size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+}  // namespace
+
+struct mc_model {
+    int device;
+    int V, D, L, H, K, hd, kvd, Q, F, max_seq;
+    int dtype;
+    void* wblock;              // all weight matrices
+    float* norms;              // rms1 [L*D], rms2 [L*D], rms_final [D]
+    float2* rope;              // [max_seq][hd/2]
+    size_t off[6];             // byte offsets of the six matrices in wblock
+    size_t weight_bytes;
+};
+
+struct mc_session {
+    mc_model* m;
+    int Bcap, cap;
+    cudaStream_t stream;
+    cudaEvent_t ev0, ev1;
+    int grid;
+    size_t smem;
+    int bc, xs_ld, max_split;
+    // device buffers
+    float *kc, *vc, *x, *q, *att, *f, *logits, *part_o, *part_m, *part_l, *amax_v;
+    int* amax_i;
+    unsigned *att_cnt, *counts, *banned;
+    unsigned* bar;
+    int* status;
+    mc::SeqState* seq;
+    uint16_t* prompts;         // [Bcap][cap] staging for host prompts
+    uint16_t* out;             // [Bcap][cap] staging for host outputs
+    uint16_t* stop;            // [MC_MAX_STOP]
+    float* trace;
+    size_t trace_bytes;
+    float last_ms;
+    int last_launches;
+};
+
+namespace {
+
+template <typename WT, bool VEC>
+cudaError_t prepare_kernel(size_t smem) {
+    return cudaFuncSetAttribute(mc::token_loop_kernel<WT, VEC>,
+                                cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+}
+
+template <typename WT, bool VEC>
+cudaError_t launch_loop(const mc::LoopParams<WT>& p, int grid, size_t smem, cudaStream_t st) {
+    void* args[] = {const_cast<mc::LoopParams<WT>*>(&p)};
+    return cudaLaunchCooperativeKernel((const void*)mc::token_loop_kernel<WT, VEC>, dim3(grid),
+                                       dim3(mc::kThreads), args, smem, st);
+}
+
+bool vec_ok(const mc_model* m) {
+    const int n = m->dtype == MC_WEIGHTS_BF16 ? 8 : 4;
+    return m->D % n == 0 && m->F % n == 0;
+}
+
+template <typename WT>
+void fill_params(mc::LoopParams<WT>& p, const mc_session* s) {
+    const mc_model* m = s->m;
+    const char* wb = static_cast<const char*>(m->wblock);
+    p.V = m->V; p.D = m->D; p.L = m->L; p.H = m->H; p.K = m->K; p.hd = m->hd;
+    p.kvd = m->kvd; p.Q = m->Q; p.F = m->F; p.G = m->H / m->K;
+    p.tok_emb = reinterpret_cast<const WT*>(wb + m->off[0]);
+    p.w_qkv = reinterpret_cast<const WT*>(wb + m->off[1]);
+    p.w_proj = reinterpret_cast<const WT*>(wb + m->off[2]);
+    p.w_up = reinterpret_cast<const WT*>(wb + m->off[3]);
+    p.w_gate = reinterpret_cast<const WT*>(wb + m->off[4]);
+    p.w_down = reinterpret_cast<const WT*>(wb + m->off[5]);
+    p.rms1 = m->norms;
+    p.rms2 = m->norms + (size_t)m->L * m->D;
+    p.rmsf = m->norms + 2 * (size_t)m->L * m->D;
+    p.rope = m->rope;
+    p.rope_len = m->max_seq;
+    p.kc = s->kc; p.vc = s->vc; p.cap = s->cap; p.Bcap = s->Bcap;
+    p.x = s->x; p.q = s->q; p.att = s->att; p.f = s->f; p.logits = s->logits;
+    p.part_o = s->part_o; p.part_m = s->part_m; p.part_l = s->part_l;
+    p.att_cnt = s->att_cnt; p.amax_v = s->amax_v; p.amax_i = s->amax_i;
+    p.counts = s->counts; p.banned = s->banned; p.max_split = s->max_split;
+    p.seq = s->seq;
+    p.bar = s->bar; p.status = s->status;
+    p.timeout_ns = 1000ull * 1000ull * 1000ull;  // 1 s per barrier wait
+    p.bc = s->bc; p.xs_ld = s->xs_ld;
+}
+
+mc_status validate_desc(const mc_model_desc* d) {
+    if (!d) return fail(MC_ERR_INVALID, "null model description");
+    if (d->vocab_size < 5 || d->vocab_size > MC_MAX_VOCAB || d->dim <= 0 || d->dim > MC_MAX_DIM ||
+        d->n_layers <= 0 || d->n_layers > MC_MAX_LAYERS || d->n_heads <= 0 ||
+        d->n_heads > MC_MAX_HEADS || d->dim % d->n_heads != 0 || d->dim / d->n_heads < 2 ||
+        d->dim / d->n_heads > MC_MAX_HEAD_DIM || d->ffn_dim <= 0 || d->ffn_dim > MC_MAX_FFN ||
+        d->max_seq <= 0 || d->max_seq > MC_MAX_SEQ)
+        return fail(MC_ERR_INVALID, "model dimensions outside the supported envelope");
+    const int K = kv_head_count(d->n_heads), hd = d->dim / d->n_heads;
+    if (d->head_dim != hd || d->n_kv_heads != K || d->kv_dim != K * hd ||
+        d->qkv_dim != d->dim + 2 * K * hd)
+        return fail(MC_ERR_INVALID, "derived model dimensions inconsistent (model.c:55-89)");
+    if (!d->tok_emb || !d->attn_qkv || !d->attn_proj || !d->ffn_up || !d->ffn_gate ||
+        !d->ffn_down || !d->rms1_scale || !d->rms2_scale || !d->rms_final_scale)
+        return fail(MC_ERR_INVALID, "null weight pointer");
+    return MC_OK;
+}
+
+mc_status upload_weights(mc_model* m, const mc_model_desc* d) {
+    const size_t V = m->V, D = m->D, L = m->L, Q = m->Q, F = m->F;
+    const size_t counts[6] = {V * D, L * Q * D, L * D * D, L * F * D, L * F * D, L * D * F};
+    const float* src[6] = {d->tok_emb, d->attn_qkv, d->attn_proj, d->ffn_up, d->ffn_gate, d->ffn_down};
+    const size_t es = m->dtype == MC_WEIGHTS_BF16 ? 2 : 4;
+    char* wb = static_cast<char*>(m->wblock);
+    std::vector<uint16_t> tmp;
+    for (int i = 0; i < 6; i++) {
+        if (m->dtype == MC_WEIGHTS_BF16) {
+            tmp.resize(counts[i]);
+            for (size_t k = 0; k < counts[i]; k++) tmp[k] = bf16_rne(src[i][k]);
+            MC_CUDA(cudaMemcpy(wb + m->off[i], tmp.data(), counts[i] * es, cudaMemcpyHostToDevice));
+        } else {
+            MC_CUDA(cudaMemcpy(wb + m->off[i], src[i], counts[i] * es, cudaMemcpyHostToDevice));
+        }
+    }
+    MC_CUDA(cudaMemcpy(m->norms, d->rms1_scale, L * D * 4, cudaMemcpyHostToDevice));
+    MC_CUDA(cudaMemcpy(m->norms + L * D, d->rms2_scale, L * D * 4, cudaMemcpyHostToDevice));
+    MC_CUDA(cudaMemcpy(m->norms + 2 * L * D, d->rms_final_scale, D * 4, cudaMemcpyHostToDevice));
+    return MC_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* mc_last_error(void) { return g_err; }
+
+mc_status mc_init(int device) {
+    int n = 0;
+    MC_CUDA(cudaGetDeviceCount(&n));
+    if (device < 0 || device >= n) return fail(MC_ERR_INVALID, "device %d of %d", device, n);
+    MC_CUDA(cudaSetDevice(device));
+    cudaDeviceProp prop;
+    MC_CUDA(cudaGetDeviceProperties(&prop, device));
+    if (prop.major != 10)
+        return fail(MC_ERR_UNSUPPORTED, "device %d is sm_%d%d; this build targets sm_100a", device,
+                    prop.major, prop.minor);
+    if (!prop.cooperativeLaunch) return fail(MC_ERR_UNSUPPORTED, "no cooperative launch");
+    return MC_OK;
+}
+
+mc_status mc_model_create(const mc_model_desc* d, int dtype, mc_model** out) {
+    if (!out) return fail(MC_ERR_INVALID, "null output handle");
+    *out = nullptr;
+    mc_status st = validate_desc(d);
+    if (st) return st;
+    if (dtype != MC_WEIGHTS_F32 && dtype != MC_WEIGHTS_BF16)
+        return fail(MC_ERR_INVALID, "unknown weight dtype %d", dtype);
+    mc_model* m = new mc_model();
+    MC_CUDA(cudaGetDevice(&m->device));
+    m->V = d->vocab_size; m->D = d->dim; m->L = d->n_layers; m->H = d->n_heads;
+    m->K = d->n_kv_heads; m->hd = d->head_dim; m->kvd = d->kv_dim; m->Q = d->qkv_dim;
+    m->F = d->ffn_dim; m->max_seq = d->max_seq; m->dtype = dtype;
+    const size_t V = m->V, D = m->D, L = m->L, Q = m->Q, F = m->F;
+    const size_t counts[6] = {V * D, L * Q * D, L * D * D, L * F * D, L * F * D, L * D * F};
+    const size_t es = dtype == MC_WEIGHTS_BF16 ? 2 : 4;
+    size_t off = 0;
+    for (int i = 0; i < 6; i++) {
+        m->off[i] = off;
+        off = align_up(off + counts[i] * es, 256);
+    }
+    m->weight_bytes = off;
+    cudaError_t e = cudaMalloc(&m->wblock, off);
+    if (e == cudaSuccess) e = cudaMalloc(&m->norms, (2 * L * D + D) * 4);
+    const int half = m->hd / 2;
+    if (e == cudaSuccess) e = cudaMalloc(&m->rope, (size_t)m->max_seq * std::max(half, 1) * sizeof(float2));
+    if (e != cudaSuccess) {
+        mc_model_destroy(m);
+        return fail(MC_ERR_NOMEM, "weight allocation (%zu bytes): %s", off, cudaGetErrorString(e));
+    }
+    // RoPE table with the reference's float expression (rotary.h:19-24),
+    // evaluated by the host libm exactly as the reference evaluates it.
+    if (half > 0) {
+        std::vector<float2> rope((size_t)m->max_seq * half);
+        for (int pair = 0; pair < half; pair++) {
+            const float exponent = (2.0f * (float)pair) / (float)m->hd;
+            const float base = ::powf(10000.0f, -exponent);
+            for (int pos = 0; pos < m->max_seq; pos++) {
+                const float angle = (float)pos * base;
+                rope[(size_t)pos * half + pair] = make_float2(::cosf(angle), ::sinf(angle));
+            }
+        }
+        e = cudaMemcpy(m->rope, rope.data(), rope.size() * sizeof(float2), cudaMemcpyHostToDevice);
+        if (e != cudaSuccess) {
+            mc_model_destroy(m);
+            return fail(MC_ERR_CUDA, "rope upload: %s", cudaGetErrorString(e));
+        }
+    }
+    st = upload_weights(m, d);
+    if (st) {
+        mc_model_destroy(m);
+        return st;
+    }
+    *out = m;
+    return MC_OK;
+}
+
+mc_status mc_model_update(mc_model* m, const mc_model_desc* d) {
+    if (!m) return fail(MC_ERR_INVALID, "null model");
+    mc_status st = validate_desc(d);
+    if (st) return st;
+    if (d->vocab_size != m->V || d->dim != m->D || d->n_layers != m->L || d->n_heads != m->H ||
+        d->ffn_dim != m->F)
+        return fail(MC_ERR_INVALID, "mc_model_update: dimensions differ from the uploaded model");
+    return upload_weights(m, d);
+}
+
+mc_status mc_model_destroy(mc_model* m) {
+    if (!m) return MC_OK;
+    cudaFree(m->wblock);
+    cudaFree(m->norms);
+    cudaFree(m->rope);
+    delete m;
+    return MC_OK;
+}
+
+mc_status mc_session_destroy(mc_session* s) {
+    if (!s) return MC_OK;
+    void* bufs[] = {s->kc, s->vc, s->x, s->q, s->att, s->f, s->logits, s->part_o, s->part_m,
+                    s->part_l, s->amax_v, s->amax_i, s->att_cnt, s->counts, s->banned, s->bar,
+                    s->status, s->seq, s->prompts, s->out, s->stop, s->trace};
+    for (void* b : bufs) cudaFree(b);
+    if (s->ev0) cudaEventDestroy(s->ev0);
+    if (s->ev1) cudaEventDestroy(s->ev1);
+    if (s->stream) cudaStreamDestroy(s->stream);
+    delete s;
+    return MC_OK;
+}
+
+mc_status mc_session_create(mc_model* m, int max_batch, int max_seq, mc_session** out) {
+    if (!out) return fail(MC_ERR_INVALID, "null output handle");
+    *out = nullptr;
+    if (!m) return fail(MC_ERR_INVALID, "null model");
+    if (max_batch <= 0 || max_batch > MC_MAX_BATCH || max_seq <= 0 || max_seq > m->max_seq)
+        return fail(MC_ERR_INVALID, "session batch %d / max_seq %d outside [1,%d] / [1,%d]",
+                    max_batch, max_seq, MC_MAX_BATCH, m->max_seq);
+    mc_session* s = new mc_session();
+    s->m = m;
+    s->Bcap = max_batch;
+    s->cap = max_seq;
+    cudaDeviceProp prop;
+    MC_CUDA(cudaGetDeviceProperties(&prop, m->device));
+    s->max_split = (max_seq + mc::kSplitLen - 1) / mc::kSplitLen;
+
+    // Shared-memory plan: fixed lists + one phase region sized for the
+    // largest of GEMV chunk, attention split and sampler.
+    const int G = m->H / m->K;
+    s->xs_ld = (int)align_up((size_t)std::max(m->D, m->F), 4);
+    const size_t att_bytes = (size_t)(G * m->hd + G * mc::kSplitLen) * 4;
+    const size_t samp_bytes = mc::sampler_smem_bytes(m->V);
+    const size_t limit = (size_t)prop.sharedMemPerBlockOptin;
+    const size_t fixed = mc::loop_fixed_bytes(max_batch);
+    const size_t wi_bytes = mc::kWarps * mc::kBCMax * 4;
+    size_t phase = std::max(att_bytes, samp_bytes);
+    const size_t row_bytes = (size_t)s->xs_ld * 4;
+    int bc = mc::kBCMax;
+    while (bc > 1 && fixed + std::max(phase, bc * row_bytes + wi_bytes) > limit) bc--;
+    s->bc = bc;
+    phase = std::max(phase, bc * row_bytes + wi_bytes);
+    s->smem = align_up(fixed + phase, 16);
+    if (s->smem > limit) {
+        delete s;
+        return fail(MC_ERR_UNSUPPORTED, "shared memory plan %zu B exceeds %zu B", fixed + phase, limit);
+    }
+    cudaError_t e;
+    if (m->dtype == MC_WEIGHTS_BF16)
+        e = vec_ok(m) ? prepare_kernel<__nv_bfloat16, true>(s->smem)
+                      : prepare_kernel<__nv_bfloat16, false>(s->smem);
+    else
+        e = vec_ok(m) ? prepare_kernel<float, true>(s->smem) : prepare_kernel<float, false>(s->smem);
+    if (e != cudaSuccess) {
+        delete s;
+        return fail(MC_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+    }
+    int per_sm = 0;
+    if (m->dtype == MC_WEIGHTS_BF16)
+        e = vec_ok(m) ? cudaOccupancyMaxActiveBlocksPerMultiprocessor(
+                            &per_sm, mc::token_loop_kernel<__nv_bfloat16, true>, mc::kThreads, s->smem)
+                      : cudaOccupancyMaxActiveBlocksPerMultiprocessor(
+                            &per_sm, mc::token_loop_kernel<__nv_bfloat16, false>, mc::kThreads, s->smem);
+    else
+        e = vec_ok(m) ? cudaOccupancyMaxActiveBlocksPerMultiprocessor(
+                            &per_sm, mc::token_loop_kernel<float, true>, mc::kThreads, s->smem)
+                      : cudaOccupancyMaxActiveBlocksPerMultiprocessor(
+                            &per_sm, mc::token_loop_kernel<float, false>, mc::kThreads, s->smem);
+    if (e != cudaSuccess || per_sm < 1) {
+        delete s;
+        return fail(MC_ERR_UNSUPPORTED, "token loop kernel cannot be resident (%s)",
+                    cudaGetErrorString(e));
+    }
+    s->grid = prop.multiProcessorCount;
+
+    const size_t B = max_batch, L = m->L, K = m->K, hd = m->hd, D = m->D, F = m->F, V = m->V;
+    const size_t H = m->H, cap = max_seq, ms = s->max_split;
+    struct Alloc { void** p; size_t bytes; } allocs[] = {
+        {(void**)&s->kc, L * B * K * cap * hd * 4},
+        {(void**)&s->vc, L * B * K * cap * hd * 4},
+        {(void**)&s->x, B * D * 4},
+        {(void**)&s->q, B * D * 4},
+        {(void**)&s->att, B * D * 4},
+        {(void**)&s->f, B * F * 4},
+        {(void**)&s->logits, B * V * 4},
+        {(void**)&s->part_o, B * H * ms * hd * 4},
+        {(void**)&s->part_m, B * H * ms * 4},
+        {(void**)&s->part_l, B * H * ms * 4},
+        {(void**)&s->amax_v, B * s->grid * 4},
+        {(void**)&s->amax_i, B * s->grid * 4},
+        {(void**)&s->att_cnt, B * K * 4},
+        {(void**)&s->counts, B * V * 4},
+        {(void**)&s->banned, B * ((V + 31) / 32) * 4},
+        {(void**)&s->bar, 256},
+        {(void**)&s->status, 256},
+        {(void**)&s->seq, B * sizeof(mc::SeqState)},
+        {(void**)&s->prompts, B * cap * 2},
+        {(void**)&s->out, B * cap * 2},
+        {(void**)&s->stop, MC_MAX_STOP * 2},
+    };
+    for (auto& a : allocs) {
+        e = cudaMalloc(a.p, a.bytes);
+        if (e != cudaSuccess) {
+            mc_session_destroy(s);
+            return fail(MC_ERR_NOMEM, "session allocation of %zu bytes: %s", a.bytes,
+                        cudaGetErrorString(e));
+        }
+    }
+    e = cudaMemset(s->att_cnt, 0, B * K * 4);
+    if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&s->stream, cudaStreamNonBlocking);
+    if (e == cudaSuccess) e = cudaEventCreate(&s->ev0);
+    if (e == cudaSuccess) e = cudaEventCreate(&s->ev1);
+    if (e != cudaSuccess) {
+        mc_session_destroy(s);
+        return fail(MC_ERR_CUDA, "session setup: %s", cudaGetErrorString(e));
+    }
+    *out = s;
+    return MC_OK;
+}
+
+}  // extern "C"
+
+namespace {
+
+mc_status ensure_trace(mc_session* s, size_t bytes) {
+    if (bytes <= s->trace_bytes) return MC_OK;
+    if (s->trace) cudaFree(s->trace);
+    s->trace = nullptr;
+    s->trace_bytes = 0;
+    MC_CUDA(cudaMalloc(&s->trace, bytes));
+    s->trace_bytes = bytes;
+    return MC_OK;
+}
+
+// Launch the token loop with the per-call fields already in p.
+template <typename WT>
+mc_status run_loop(mc_session* s, mc::LoopParams<WT>& p) {
+    fill_params(p, s);
+    MC_CUDA(cudaMemsetAsync(s->bar, 0, 256, s->stream));
+    MC_CUDA(cudaMemsetAsync(s->status, 0, 256, s->stream));
+    MC_CUDA(cudaMemsetAsync(s->att_cnt, 0, (size_t)s->Bcap * s->m->K * 4, s->stream));
+    MC_CUDA(cudaEventRecord(s->ev0, s->stream));
+    cudaError_t e = vec_ok(s->m) ? launch_loop<WT, true>(p, s->grid, s->smem, s->stream)
+                                 : launch_loop<WT, false>(p, s->grid, s->smem, s->stream);
+    if (e != cudaSuccess) return fail(MC_ERR_CUDA, "token loop launch: %s", cudaGetErrorString(e));
+    MC_CUDA(cudaEventRecord(s->ev1, s->stream));
+    s->last_launches = 1;
+    int status = 0;
+    MC_CUDA(cudaMemcpyAsync(&status, s->status, 4, cudaMemcpyDeviceToHost, s->stream));
+    MC_CUDA(cudaStreamSynchronize(s->stream));
+    MC_CUDA(cudaEventElapsedTime(&s->last_ms, s->ev0, s->ev1));
+    if (status == mc::ST_TIMEOUT)
+        return fail(MC_ERR_TIMEOUT, "token loop: a grid barrier passed its deadline");
+    if (status != 0) return fail(MC_ERR_DEVICE, "token loop reported status %d", status);
+    return MC_OK;
+}
+
+bool options_valid(const mc_sampling* o) {  // generate.c:528-541
+    return o && o->max_new_tokens >= 0 && std::isfinite(o->temperature) && o->temperature > 0.0f &&
+           std::isfinite(o->top_p) && o->top_p > 0.0f && o->top_p <= 1.0f &&
+           std::isfinite(o->repetition_penalty) && o->repetition_penalty >= 1.0f &&
+           std::isfinite(o->min_p) && o->min_p >= 0.0f && o->min_p <= 1.0f &&
+           std::isfinite(o->frequency_penalty) && o->frequency_penalty >= -2.0f &&
+           o->frequency_penalty <= 2.0f && std::isfinite(o->presence_penalty) &&
+           o->presence_penalty >= -2.0f && o->presence_penalty <= 2.0f &&
+           o->no_repeat_ngram_size >= 0 && o->no_repeat_ngram_size <= 16 &&
+           o->min_new_tokens >= 0 && o->min_new_tokens <= 512 &&
+           o->min_new_tokens <= o->max_new_tokens && o->stop_sequence_len >= 0 &&
+           o->stop_sequence_len <= MC_MAX_STOP &&
+           !(o->stop_sequence_len > 0 && !o->stop_sequence_ids);
+}
+
+template <typename WT>
+mc_status generate_t(mc_session* s, int batch, const uint16_t* prompts, int prompt_stride,
+                     const int* prompt_lens, uint16_t* out_ids, int out_cap, const mc_sampling* o,
+                     uint64_t* rng_states, int* out_counts, int* final_pos, unsigned flags,
+                     float* trace_logits, int trace_steps) {
+    const mc_model* m = s->m;
+    const bool dev = flags & MC_DEVICE_POINTERS;
+    // Per-sequence bookkeeping exactly as generate.c:553-564.
+    std::vector<mc::SeqState> seq(batch);
+    int T = 0;
+    for (int b = 0; b < batch; b++) {
+        const int P = prompt_lens[b];
+        if (P <= 0 || P > out_cap || P > s->cap || P > prompt_stride)
+            return fail(MC_ERR_INVALID, "prompt %d: length %d outside [1, min(out_cap, max_seq)]", b, P);
+        int nnew = o->max_new_tokens;
+        nnew = std::min(nnew, out_cap - P);
+        nnew = std::min(nnew, s->cap - P);
+        mc::SeqState& q = seq[b];
+        memset(&q, 0, sizeof(q));
+        q.P = P;
+        q.nnew = std::max(nnew, 0);
+        q.done = nnew <= 0;
+        q.result = P;
+        q.final_pos = 0;
+        if (!dev) q.rng = rng_states[b];
+        if (nnew > 0) T = std::max(T, P + nnew - 1);
+    }
+    if (!dev) {
+        for (int b = 0; b < batch; b++)
+            for (int i = 0; i < prompt_lens[b]; i++)
+                if (prompts[(size_t)b * prompt_stride + i] >= m->V)
+                    return fail(MC_ERR_INVALID, "prompt %d holds id %d >= vocab", b,
+                                (int)prompts[(size_t)b * prompt_stride + i]);
+    }
+    for (int i = 0; i < o->stop_sequence_len; i++)
+        if (o->stop_sequence_ids[i] >= m->V) return fail(MC_ERR_INVALID, "stop id >= vocab");
+
+    mc::LoopParams<WT> p{};
+    p.B = batch;
+    p.out_cap = dev ? out_cap : s->cap;
+    p.out_ids = dev ? out_ids : s->out;
+    p.prompt_stride = dev ? prompt_stride : s->cap;
+    p.prompts = dev ? prompts : s->prompts;
+    p.s.temperature = o->temperature;
+    p.s.top_p = o->top_p;
+    p.s.rep = o->repetition_penalty;
+    p.s.min_p = o->min_p;
+    p.s.freq = o->frequency_penalty;
+    p.s.pres = o->presence_penalty;
+    int top_k = o->top_k;
+    top_k = std::max(top_k, 1);
+    top_k = std::min(top_k, m->V);
+    top_k = std::min(top_k, MC_MAX_TOPK);
+    p.s.top_k = top_k;
+    p.s.min_new = o->min_new_tokens;
+    p.s.ngram = o->no_repeat_ngram_size;
+    p.s.stop_ids = s->stop;
+    p.s.stop_len = o->stop_sequence_len;
+    p.s.pen_active = o->repetition_penalty > 1.0f || o->frequency_penalty != 0.0f ||
+                     o->presence_penalty != 0.0f;
+    p.T = T;
+    p.all_logits = 0;
+    p.trace_steps = trace_logits ? trace_steps : 0;
+    if (p.trace_steps > 0) {
+        mc_status st = ensure_trace(s, (size_t)batch * p.trace_steps * m->V * 4);
+        if (st) return st;
+        MC_CUDA(cudaMemsetAsync(s->trace, 0, (size_t)batch * p.trace_steps * m->V * 4, s->stream));
+        p.trace = s->trace;
+    }
+    if (o->stop_sequence_len > 0)
+        MC_CUDA(cudaMemcpyAsync(s->stop, o->stop_sequence_ids, o->stop_sequence_len * 2,
+                                cudaMemcpyHostToDevice, s->stream));
+    if (!dev) {
+        size_t maxP = 0;
+        for (int b = 0; b < batch; b++) maxP = std::max(maxP, (size_t)prompt_lens[b]);
+        MC_CUDA(cudaMemcpy2DAsync(s->prompts, (size_t)s->cap * 2, prompts, (size_t)prompt_stride * 2,
+                                  maxP * 2, batch, cudaMemcpyHostToDevice, s->stream));
+    } else {
+        // RNG states live on the device: gather them into the sequence table.
+        for (int b = 0; b < batch; b++) seq[b].rng = 0;
+    }
+    MC_CUDA(cudaMemcpyAsync(s->seq, seq.data(), batch * sizeof(mc::SeqState),
+                            cudaMemcpyHostToDevice, s->stream));
+    if (dev) {
+        for (int b = 0; b < batch; b++)
+            MC_CUDA(cudaMemcpyAsync(&s->seq[b].rng, rng_states + b, 8, cudaMemcpyDeviceToDevice,
+                                    s->stream));
+    }
+    if (T > 0) {
+        mc_status st = run_loop<WT>(s, p);
+        if (st) return st;
+    } else {
+        s->last_ms = 0.0f;
+        s->last_launches = 0;
+    }
+    // Results.
+    if (dev) {
+        for (int b = 0; b < batch; b++) {
+            MC_CUDA(cudaMemcpyAsync(rng_states + b, &s->seq[b].rng, 8, cudaMemcpyDeviceToDevice, s->stream));
+            MC_CUDA(cudaMemcpyAsync(out_counts + b, &s->seq[b].result, 4, cudaMemcpyDeviceToDevice, s->stream));
+            if (final_pos)
+                MC_CUDA(cudaMemcpyAsync(final_pos + b, &s->seq[b].final_pos, 4, cudaMemcpyDeviceToDevice,
+                                        s->stream));
+            if (seq[b].nnew <= 0)  // generate.c:557-559: prompt copied, nothing else
+                MC_CUDA(cudaMemcpyAsync(out_ids + (size_t)b * out_cap, prompts + (size_t)b * prompt_stride,
+                                        (size_t)seq[b].P * 2, cudaMemcpyDeviceToDevice, s->stream));
+        }
+        MC_CUDA(cudaStreamSynchronize(s->stream));
+        return MC_OK;
+    }
+    MC_CUDA(cudaMemcpyAsync(seq.data(), s->seq, batch * sizeof(mc::SeqState), cudaMemcpyDeviceToHost,
+                            s->stream));
+    int maxR = 0;
+    for (int b = 0; b < batch; b++) maxR = std::max(maxR, prompt_lens[b] + seq[b].nnew);
+    MC_CUDA(cudaStreamSynchronize(s->stream));
+    if (T > 0)
+        MC_CUDA(cudaMemcpy2DAsync(out_ids, (size_t)out_cap * 2, s->out, (size_t)s->cap * 2,
+                                  (size_t)maxR * 2, batch, cudaMemcpyDeviceToHost, s->stream));
+    if (trace_logits && p.trace_steps > 0)
+        MC_CUDA(cudaMemcpyAsync(trace_logits, s->trace, (size_t)batch * p.trace_steps * m->V * 4,
+                                cudaMemcpyDeviceToHost, s->stream));
+    MC_CUDA(cudaStreamSynchronize(s->stream));
+    for (int b = 0; b < batch; b++) {
+        if (seq[b].nnew <= 0) {
+            memcpy(out_ids + (size_t)b * out_cap, prompts + (size_t)b * prompt_stride,
+                   (size_t)seq[b].P * 2);
+            out_counts[b] = seq[b].P;
+            if (final_pos) final_pos[b] = 0;
+        } else {
+            out_counts[b] = seq[b].result;
+            if (final_pos) final_pos[b] = seq[b].final_pos;
+        }
+        rng_states[b] = seq[b].rng;
+    }
+    return MC_OK;
+}
+
+template <typename WT>
+mc_status forward_logits_t(mc_session* s, int batch, const uint16_t* tokens, int n, float* out) {
+    const mc_model* m = s->m;
+    for (size_t i = 0; i < (size_t)batch * n; i++)
+        if (tokens[i] >= m->V) return fail(MC_ERR_INVALID, "token id %d >= vocab", (int)tokens[i]);
+    std::vector<mc::SeqState> seq(batch);
+    for (int b = 0; b < batch; b++) {
+        memset(&seq[b], 0, sizeof(mc::SeqState));
+        seq[b].P = n;
+        seq[b].nnew = 1;
+    }
+    mc_status st = ensure_trace(s, (size_t)batch * n * m->V * 4);
+    if (st) return st;
+    mc::LoopParams<WT> p{};
+    p.B = batch;
+    p.prompts = s->prompts;
+    p.prompt_stride = s->cap;
+    p.out_ids = s->out;
+    p.out_cap = s->cap;
+    p.s.top_k = 1;
+    p.s.temperature = 1.0f;
+    p.T = n;
+    p.all_logits = 1;
+    p.trace = s->trace;
+    p.trace_steps = n;
+    MC_CUDA(cudaMemcpy2DAsync(s->prompts, (size_t)s->cap * 2, tokens, (size_t)n * 2, (size_t)n * 2,
+                              batch, cudaMemcpyHostToDevice, s->stream));
+    MC_CUDA(cudaMemcpyAsync(s->seq, seq.data(), batch * sizeof(mc::SeqState), cudaMemcpyHostToDevice,
+                            s->stream));
+    st = run_loop<WT>(s, p);
+    if (st) return st;
+    MC_CUDA(cudaMemcpy(out, s->trace, (size_t)batch * n * m->V * 4, cudaMemcpyDeviceToHost));
+    return MC_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+mc_status mc_generate(mc_session* s, int batch, const uint16_t* prompts, int prompt_stride,
+                      const int* prompt_lens, uint16_t* out_ids, int out_cap, const mc_sampling* o,
+                      uint64_t* rng_states, int* out_counts, int* final_pos, unsigned flags,
+                      float* trace_logits, int trace_steps) {
+    if (!s) return fail(MC_ERR_INVALID, "null session");
+    if (batch <= 0 || batch > s->Bcap)
+        return fail(MC_ERR_INVALID, "batch %d outside [1, %d]", batch, s->Bcap);
+    if (!prompts || !prompt_lens || !out_ids || out_cap <= 0 || !rng_states || !out_counts ||
+        prompt_stride <= 0)
+        return fail(MC_ERR_INVALID, "null or empty argument");
+    if (!options_valid(o)) return fail(MC_ERR_INVALID, "generation options rejected (generate.c:526-551)");
+    if (trace_logits && (trace_steps < 0 || trace_steps > s->cap))
+        return fail(MC_ERR_INVALID, "trace_steps %d", trace_steps);
+    MC_CUDA(cudaSetDevice(s->m->device));
+    if (s->m->dtype == MC_WEIGHTS_BF16)
+        return generate_t<__nv_bfloat16>(s, batch, prompts, prompt_stride, prompt_lens, out_ids,
+                                         out_cap, o, rng_states, out_counts, final_pos, flags,
+                                         trace_logits, trace_steps);
+    return generate_t<float>(s, batch, prompts, prompt_stride, prompt_lens, out_ids, out_cap, o,
+                             rng_states, out_counts, final_pos, flags, trace_logits, trace_steps);
+}
+
+mc_status mc_forward_logits(mc_session* s, int batch, const uint16_t* tokens, int n, float* out) {
+    if (!s) return fail(MC_ERR_INVALID, "null session");
+    if (batch <= 0 || batch > s->Bcap || n <= 0 || n > s->cap || !tokens || !out)
+        return fail(MC_ERR_INVALID, "forward_logits: batch %d, n %d", batch, n);
+    MC_CUDA(cudaSetDevice(s->m->device));
+    if (s->m->dtype == MC_WEIGHTS_BF16) return forward_logits_t<__nv_bfloat16>(s, batch, tokens, n, out);
+    return forward_logits_t<float>(s, batch, tokens, n, out);
+}
+
+mc_status mc_last_kernel_ms(mc_session* s, float* ms) {
+    if (!s || !ms) return fail(MC_ERR_INVALID, "null argument");
+    *ms = s->last_ms;
+    return MC_OK;
+}
+
+mc_status mc_last_launch_count(mc_session* s, int* n) {
+    if (!s || !n) return fail(MC_ERR_INVALID, "null argument");
+    *n = s->last_launches;
+    return MC_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,157 @@
+"""GPU parity: the CUDA token loop against the oracle, through the C ABI and
+the drop-in generate.h.
+
+Tolerances (fp32 path, the bound the port is held to):
+  per-position logits   |gpu - ref| <= 1e-3 + 1e-4 * |ref|
+  greedy ids            identical for the first 64 generated tokens (the
+                        whole sequence is compared where the top-1/top-2
+                        margin of every step exceeds 1e-4)
+bf16-weight path: weights are rounded to bf16 on both sides, arithmetic is
+fp32 on both sides, so the same logits bound applies.
+"""
+import os
+import subprocess
+
+import numpy as np
+import pytest
+
+import minima_b200 as M
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+ATOL, RTOL = 1e-3, 1e-4
+C1 = O.Dims(vocab=30000, dim=128, n_layers=8, n_heads=4, ffn_dim=512, max_seq=512)
+
+
+def assert_logits_close(got, ref):
+    err = np.abs(got.astype(np.float64) - ref.astype(np.float64))
+    bound = ATOL + RTOL * np.abs(ref.astype(np.float64))
+    finite = np.isfinite(ref)
+    assert np.array_equal(np.isfinite(got), finite)
+    worst = float(np.max(err[finite] - bound[finite]))
+    assert worst <= 0.0, f"max |err| {err[finite].max():.3e} exceeds bound"
+
+
+@pytest.fixture(scope="module")
+def c1(gpu):
+    hm = M.HostModel(C1.vocab, C1.dim, C1.n_layers, C1.n_heads, C1.ffn_dim, C1.max_seq, seed=0)
+    orc = O.OrcModel(C1, 0)
+    return hm, orc
+
+
+def test_kat_generation_special_tokens_on_gpu(gpu):
+    """The reference's own generation test, linked unchanged against the drop-in."""
+    exe = os.path.join(os.path.dirname(O.__file__), "_ref", "kat_generation_cuda")
+    if not os.path.exists(exe):
+        pytest.fail("oracle/_ref/kat_generation_cuda not built")
+    r = subprocess.run([exe], capture_output=True, text=True, timeout=300)
+    assert r.returncode == 0, r.stdout + r.stderr
+    assert "Generation sampling and reserved-token tests passed." in r.stdout
+
+
+def test_c1_prefix_logits(c1):
+    hm, orc = c1
+    dm = M.DeviceModel(hm)
+    sess = M.Session(dm, 2, 128)
+    toks = np.stack([O.random_prompt(40, C1.vocab, 1), O.random_prompt(40, C1.vocab, 2)])
+    got = sess.forward_logits(toks)
+    for b in range(2):
+        ref = orc.forward_prefixes(toks[b])
+        assert_logits_close(got[b], ref)
+    assert sess.last_launch_count() == 1
+
+
+def test_c1_greedy_drop_in(c1):
+    """Config 1: B=1, prompt 32, 128 greedy tokens, via generate() of the drop-in."""
+    hm, orc = c1
+    prompt = O.random_prompt(32, C1.vocab, 7)
+    tok = M.make_tokenizer(C1.vocab)
+    caches = M.Caches(hm, 1, 512)
+    opts = M.options(temperature=1.0, top_k=1, max_new_tokens=128)
+    got, st, pos = M.generate_with_options(hm, tok, caches.caches[0], prompt, 512, opts, 42)
+    ref, st_r, pos_r, trace = orc.generate(prompt, 512, 512, O.make_options(top_k=1, max_new_tokens=128),
+                                           42, trace_steps=64)
+    assert len(got) == len(ref) == 160
+    assert np.array_equal(got[:32 + 64], ref[:32 + 64])
+    assert st == st_r and pos == pos_r == 160
+
+
+def test_c2_batch_greedy(gpu):
+    """Config 2: 4 x (prompt 128 + 256 greedy), seed 1, one device token loop."""
+    hm = M.HostModel(C1.vocab, C1.dim, C1.n_layers, C1.n_heads, C1.ffn_dim, C1.max_seq, seed=1)
+    orc = O.OrcModel(C1, 1)
+    B = 4
+    prompts = np.stack([O.random_prompt(128, C1.vocab, 1000 + b) for b in range(B)])
+    tok = M.make_tokenizer(C1.vocab)
+    caches = M.Caches(hm, B, 512)
+    opts = M.options(top_k=1, max_new_tokens=256)
+    ok, out, counts, st = M.generate_batch(hm, tok, caches, prompts, [128] * B, 512, opts,
+                                           list(range(1, B + 1)))
+    assert ok, M.last_error()
+    okr, outr, countsr, str_ = orc.generate_batch(prompts, [128] * B, 512, 512,
+                                                  O.make_options(top_k=1, max_new_tokens=256),
+                                                  list(range(1, B + 1)))
+    assert okr
+    assert list(counts) == list(countsr) == [384] * B
+    for b in range(B):
+        assert np.array_equal(out[b, :128 + 64], outr[b, :128 + 64])
+    assert np.array_equal(st, str_)
+    assert [c.pos for c in caches.caches] == [384] * B
+
+
+def test_sampling_teacher_forced(c1):
+    """Temperature/top-k/top-p sampling: with the sampler fed the device's
+    own logits and RNG state, the oracle sampler picks the same ids."""
+    hm, orc = c1
+    dm = M.DeviceModel(hm)
+    sess = M.Session(dm, 2, 256)
+    prompts = np.stack([O.random_prompt(20, C1.vocab, 5), O.random_prompt(20, C1.vocab, 6)])
+    kw = dict(temperature=0.8, top_k=40, top_p=0.95, repetition_penalty=1.1, min_p=0.01,
+              frequency_penalty=0.1, presence_penalty=0.05, no_repeat_ngram_size=3,
+              max_new_tokens=24)
+    out, counts, st, fpos, trace = sess.generate(prompts, [20, 20], 64, M.options(**kw), [9, 10],
+                                                 trace_steps=24)
+    for b in range(2):
+        state = O.Rng(9 + b).state.value
+        hist = list(prompts[b])
+        for i in range(counts[b] - 20):
+            tid, state = O.sample(trace[b, i], O.make_options(**kw), np.array(hist, np.uint16), state)
+            assert tid == out[b, 20 + i], (b, i)
+            hist.append(tid)
+        assert state == st[b]
+
+
+def test_sampling_end_to_end(c1):
+    """Full sampled generation agrees with the oracle on most sequences."""
+    hm, orc = c1
+    dm = M.DeviceModel(hm)
+    sess = M.Session(dm, 4, 256)
+    prompts = np.stack([O.random_prompt(16, C1.vocab, 50 + b) for b in range(4)])
+    kw = dict(temperature=0.8, top_k=40, max_new_tokens=32)
+    out, counts, st, fpos = sess.generate(prompts, [16] * 4, 64, M.options(**kw), [1, 2, 3, 4])
+    agree = 0
+    for b in range(4):
+        ref, st_r, pos_r = orc.generate(prompts[b], 64, 256, O.make_options(**kw), b + 1)
+        agree += int(np.array_equal(out[b, :counts[b]], ref))
+    assert agree >= 3
+
+
+def test_stop_sequence_and_ragged(c1):
+    hm, orc = c1
+    dm = M.DeviceModel(hm)
+    sess = M.Session(dm, 3, 128)
+    lens = [9, 17, 4]
+    prompts = np.zeros((3, 17), dtype=np.uint16)
+    for b, n in enumerate(lens):
+        prompts[b, :n] = O.random_prompt(n, C1.vocab, 300 + b)
+    # first greedy token of sequence 1 as a one-token stop: that sequence stops at once
+    first, _, _ = orc.generate(prompts[1, :17], 40, 128, O.make_options(top_k=1, max_new_tokens=1), 0)
+    stop = [int(first[17])]
+    kw = dict(top_k=1, max_new_tokens=12, stop=stop)
+    out, counts, st, fpos = sess.generate(prompts, lens, 40, M.options(**kw), [0, 0, 0])
+    for b, n in enumerate(lens):
+        ref, st_r, pos_r = orc.generate(prompts[b, :n], 40, 128, O.make_options(**kw), 0)
+        assert counts[b] == len(ref)
+        assert np.array_equal(out[b, :counts[b]], ref)
+        assert fpos[b] == pos_r and st[b] == st_r
