@@ -1,0 +1,364 @@
+#!/usr/bin/env python
+"""Decode throughput of Minima's token loop on B200 (one process per GPU).
+
+Workload (per GPU; weak scaling across GPUs): the Minima default decoder
+(config.h defaults: V=30000, D=128, 8 layers, 4 heads / 2 KV heads, FFN 512;
+5,808,256 fp32 parameters) with seeded model_init_config weights (seed 1),
+max_seq 512, batch 4 x (prompt of 128 uniform non-special ids, then 256
+greedy tokens) — the reference's training shape as prefill followed by
+decode.  One step = one generate_with_options call for the batch (prefill +
+decode, one device launch).  metric = generated tokens / second.
+
+* value: device-resident inputs (mc_generate with MC_DEVICE_POINTERS), timed
+  with CUDA events on the session's stream, L2 flushed (256 MiB write)
+  before every timed step and excluded from the timing.
+* e2e:   the drop-in generate_batch_with_options with host buffers (prompt
+  upload and id download inside the timed region), host wall clock.
+* roofline: algorithmic bytes of the token-loop launch (weights read once
+  per token step + KV cache reads/appends) / its CUDA-event duration,
+  against the measured HBM copy bandwidth.
+* cpu_baseline: the reference's own generate() (oracle/_ref, built from its
+  unmodified C files), one thread, on a bounded sample.
+--impl reference runs the reference's CPU implementation instead (the
+reference arm), OpenMP-free thread pool over the batch's sequences.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+WL = dict(vocab=30000, dim=128, n_layers=8, n_heads=4, ffn_dim=512, max_seq=512, seed=1,
+          batch=4, prompt=128, new_tokens=256)
+WORKLOAD_NAME = ("minima-default-5.8M fp32: 4 seq x (prefill 128 random ids + 256 greedy), "
+                 "seed 1, max_seq 512")
+METRIC = "decode tokens/s (generated ids per second, prefill included)"
+UNIT = "tokens/s"
+FALLBACK_HBM_GBS = 6650.0
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["native", "reference"], default="native")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args()
+
+
+def dist_env():
+    return (int(os.environ.get("RANK", "0")), int(os.environ.get("WORLD_SIZE", "1")),
+            int(os.environ.get("LOCAL_RANK", "0")))
+
+
+def prompt_ids(n, vocab, seed):
+    """Uniform non-special ids in [4, vocab-1] from the reference's rng_int."""
+    import ctypes as C
+    import numpy as np
+    import minima_b200 as M
+    host = M.libs()[0]
+    r = M.Rng()
+    host.rng_seed(C.byref(r), seed)
+    return np.array([host.rng_int(C.byref(r), 4, vocab - 1) for _ in range(n)], dtype=np.uint16)
+
+
+def workload_prompts(rank):
+    import numpy as np
+    B, P = WL["batch"], WL["prompt"]
+    # global sequence index g = rank * B + b gets prompt seed 1000 + g and RNG state g + 1
+    prompts = np.stack([prompt_ids(P, WL["vocab"], 1000 + rank * B + b) for b in range(B)])
+    rng = [rank * B + b + 1 for b in range(B)]
+    return prompts, rng
+
+
+def algorithmic_bytes(P, nnew, B, weight_bytes_per=4):
+    """Bytes one token-loop launch must move: every token step reads the layer
+    weights, steps that produce logits read the tied lm_head, and every active
+    sequence reads its K/V rows 0..t and appends row t (fp32)."""
+    V, D, L, H, F = WL["vocab"], WL["dim"], WL["n_layers"], WL["n_heads"], WL["ffn_dim"]
+    K = H // 2 if H > 1 else 1
+    while H % K:
+        K -= 1
+    hd = D // H
+    kvd = K * hd
+    Q = D + 2 * kvd
+    w_layers = L * (Q * D + D * D + 3 * F * D) * weight_bytes_per + 2 * L * D * 4
+    w_head = V * D * weight_bytes_per + D * 4
+    total = 0
+    T = P + nnew - 1
+    for t in range(T):
+        total += w_layers
+        if t >= P - 1:
+            total += w_head
+        total += B * (L * 2 * (t + 1) * kvd * 4 + D * weight_bytes_per)
+    return total
+
+
+def measured_hbm():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as fh:
+            return float(json.load(fh)["hbm_gbs"]), "measured"
+    return FALLBACK_HBM_GBS, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled every 200 ms."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index):
+        self.proc = None
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(gpu_index), f"--query-gpu={self.Q}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+
+    def stop(self):
+        if not self.proc:
+            return None
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=10)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        rows = [[c.strip() for c in l.split(",")] for l in out.splitlines() if l.strip()]
+        sm = [float(r[1]) for r in rows if len(r) >= 9 and r[1].replace(".", "").isdigit()]
+        if not sm:
+            return None
+        maxc = float(rows[0][2])
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v == "Active"})
+        loaded = [s for s in sm if s > 0.5 * maxc] or sm
+        return {"sm_mhz": statistics.median(loaded), "sm_max_mhz": maxc, "reasons": reasons,
+                "samples": len(sm)}
+
+
+def cpu_baseline(steps_budget_s=20.0):
+    """The reference's generate() (oracle/_ref) on one host core, on the
+    whole batch of one step (4 sequences back to back)."""
+    from oracle import oracle as O
+    dims = O.Dims(WL["vocab"], WL["dim"], WL["n_layers"], WL["n_heads"], WL["ffn_dim"],
+                  WL["max_seq"])
+    kind = "reference" if O.ref_available() else "port"
+    model = O.RefModel(dims, WL["seed"]) if kind == "reference" else O.OrcModel(dims, WL["seed"])
+    prompts, rng = workload_prompts(0)
+    opts = O.make_options(top_k=1, max_new_tokens=WL["new_tokens"])
+    toks, t0 = 0, time.perf_counter()
+    n_seq = 0
+    for b in range(WL["batch"]):
+        ids = model.generate(prompts[b], WL["max_seq"], WL["max_seq"], opts, rng[b])[0]
+        toks += len(ids) - WL["prompt"]
+        n_seq += 1
+        if time.perf_counter() - t0 > steps_budget_s:
+            break
+    dt = time.perf_counter() - t0
+    return {"value": toks / dt, "unit": UNIT, "cores": 1, "kind": kind,
+            "sample": f"{n_seq} of the step's sequences (prompt {WL['prompt']} + "
+                      f"{WL['new_tokens']} greedy), reference generate(), gcc -O2, 1 thread, "
+                      f"{dt:.1f} s"}
+
+
+def reference_arm(args):
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return
+    from concurrent.futures import ThreadPoolExecutor
+    from oracle import oracle as O
+    dims = O.Dims(WL["vocab"], WL["dim"], WL["n_layers"], WL["n_heads"], WL["ffn_dim"],
+                  WL["max_seq"])
+    kind = "reference" if O.ref_available() else "port"
+    model = O.RefModel(dims, WL["seed"]) if kind == "reference" else O.OrcModel(dims, WL["seed"])
+    threads = min(WL["batch"], os.cpu_count() or 1)
+    prompts, rng = workload_prompts(0)
+    opts = O.make_options(top_k=1, max_new_tokens=WL["new_tokens"])
+
+    def one(b):
+        return len(model.generate(prompts[b], WL["max_seq"], WL["max_seq"], opts, rng[b])[0])
+
+    times, toks = [], 0
+    with ThreadPoolExecutor(threads) as ex:
+        for i in range(args.warmup + args.steps):
+            t0 = time.perf_counter()
+            n = sum(ex.map(one, range(WL["batch"])))
+            dt = time.perf_counter() - t0
+            if i >= args.warmup:
+                times.append(dt)
+                toks += n - WL["batch"] * WL["prompt"]
+    total = sum(times)
+    value = toks / total
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * total / args.steps,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic",
+        "config": {"workload": WORKLOAD_NAME, "global_batch": WL["batch"],
+                   "seq_len": WL["prompt"] + WL["new_tokens"], "parallelism": "cpu threads"},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": kind,
+                         "sample": f"each step: the {WL['batch']} sequences of the workload, one "
+                                   f"per thread ({threads} threads, nproc {os.cpu_count()}), "
+                                   "reference generate() built with gcc -O2"},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def native_arm(args):
+    import numpy as np
+    import torch
+    import minima_b200 as M
+
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    pg = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+        pg = dist
+    B, P, N = WL["batch"], WL["prompt"], WL["new_tokens"]
+    hm = M.HostModel(WL["vocab"], WL["dim"], WL["n_layers"], WL["n_heads"], WL["ffn_dim"],
+                     WL["max_seq"], seed=WL["seed"])
+    dm = M.DeviceModel(hm, device=local)
+    sess = M.Session(dm, B, WL["max_seq"])
+    prompts, rng = workload_prompts(rank)
+    out_cap = WL["max_seq"]
+    dev = torch.device("cuda", local)
+    prompts_d = torch.from_numpy(prompts.view(np.int16).copy()).to(dev)
+    out_d = torch.zeros((B, out_cap), dtype=torch.int16, device=dev)
+    rng0 = torch.tensor(np.array(rng, dtype=np.uint64).view(np.int64), device=dev)
+    rng_d = rng0.clone()
+    counts_d = torch.zeros(B, dtype=torch.int32, device=dev)
+    fpos_d = torch.zeros(B, dtype=torch.int32, device=dev)
+    opts = M.options(top_k=1, max_new_tokens=N)
+    flush = torch.empty(64 * 1024 * 1024, dtype=torch.float32, device=dev)  # 256 MiB > L2
+    stream = torch.cuda.ExternalStream(sess.stream_handle(), device=dev)
+
+    def step():
+        sess.generate_device(prompts_d.data_ptr(), P, [P] * B, out_d.data_ptr(), out_cap, opts,
+                             rng_d.data_ptr(), counts_d.data_ptr(), fpos_d.data_ptr())
+
+    with torch.cuda.stream(stream):
+        for _ in range(args.warmup):
+            rng_d.copy_(rng0)
+            step()
+        torch.cuda.synchronize()
+        if pg:
+            pg.barrier()
+        torch.cuda.synchronize()
+        clocks = ClockSampler(local)
+        starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+        ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+        kernel_ms, launches, tokens = [], 0, 0
+        for i in range(args.steps):
+            flush.zero_()
+            rng_d.copy_(rng0)
+            starts[i].record(stream)
+            step()
+            ends[i].record(stream)
+            kernel_ms.append(sess.last_kernel_ms())
+            launches += sess.last_launch_count()
+            tokens += int((counts_d - P).sum().item())
+        torch.cuda.synchronize()
+        if pg:
+            pg.barrier()
+        torch.cuda.synchronize()
+        clk = clocks.stop()
+    step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+    total_ms = sum(step_ms)
+    stamps = sess.last_step_times_ns().astype(np.int64)
+    tok_us = np.diff(stamps) / 1e3
+    dec_us = tok_us[P - 1:]
+    pre_us = tok_us[:P - 1]
+    got = out_d.cpu().numpy().view(np.uint16)
+
+    # ---- end to end through the drop-in generate.h with host buffers
+    tok = M.make_tokenizer(WL["vocab"])
+    caches = M.Caches(hm, B, WL["max_seq"])
+    e2e_times, e2e_tokens = [], 0
+    for i in range(args.warmup + args.steps):
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        ok, out, counts, _ = M.generate_batch(hm, tok, caches, prompts, [P] * B, out_cap, opts, rng)
+        dt = time.perf_counter() - t0
+        if not ok:
+            raise RuntimeError("generate_batch_with_options failed: " + M.last_error())
+        if i >= args.warmup:
+            e2e_times.append(dt)
+            e2e_tokens += int((counts - P).sum())
+    assert np.array_equal(out[:, :P + N], got[:, :P + N]), "e2e and device-resident runs differ"
+
+    # ---- max over ranks
+    t = torch.tensor([total_ms, sum(e2e_times)], dtype=torch.float64, device=dev)
+    if pg:
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+    total_ms, e2e_s = float(t[0]), float(t[1])
+    value = world * tokens / (total_ms / 1e3)
+    e2e_value = world * e2e_tokens / e2e_s
+
+    if rank == 0:
+        T = P + N - 1
+        algo = algorithmic_bytes(P, N, B)
+        kms = statistics.mean(kernel_ms)
+        peak, peak_src = measured_hbm()
+        achieved = algo / (kms / 1e3) / 1e9
+        traffic = None
+        tf = os.path.join(ROOT, "profiles", "token_loop_c2_traffic.json")
+        if os.path.exists(tf):
+            with open(tf) as fh:
+                traffic = json.load(fh).get("dram_bytes_per_launch")
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": total_ms / args.steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic",
+            "config": {"workload": WORKLOAD_NAME, "global_batch": B * world,
+                       "seq_len": P + N, "parallelism": f"dp{world}",
+                       "l2": "flushed (256 MiB write) before each timed step, outside the timing",
+                       "per_gpu_batch": B},
+            "p50_token_us": float(np.median(dec_us)), "p99_token_us": float(np.percentile(dec_us, 99)),
+            "p50_prefill_token_us": float(np.median(pre_us)) if len(pre_us) else None,
+            "token_steps_per_launch": T,
+            "e2e": {"value": e2e_value, "unit": UNIT,
+                    "h2d_bytes_per_step": B * P * 2 + B * 32,
+                    "d2h_bytes_per_step": B * 32 + B * (P + N) * 2 + 4},
+            "gpu_launches": launches,
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "traffic": traffic,
+                         "kernel": "mc::token_loop_kernel<float,true>",
+                         "algorithmic_bytes_per_launch": algo, "kernel_ms": kms,
+                         "peak_source": f"{peak_src} HBM copy bandwidth"},
+            "clocks": clk,
+        }
+        if not args.no_cpu_baseline and world == 1:
+            line["cpu_baseline"] = cpu_baseline()
+        print(json.dumps(line), flush=True)
+    if pg:
+        pg.barrier()
+        pg.destroy_process_group()
+
+
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        reference_arm(args)
+    else:
+        native_arm(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -155,6 +155,16 @@ mc_status mc_last_kernel_ms(mc_session* session, float* ms);
 /* Number of kernels the last call launched on the device. */
 mc_status mc_last_launch_count(mc_session* session, int* launches);
 
+/* Device timestamps (%globaltimer, ns) taken at the start of every token
+   step of the last call, plus one at loop exit: ns[0..*n).  The difference
+   of consecutive stamps is the per-token latency of that step.  Sequences
+   are in prefill while t < prompt length. */
+mc_status mc_last_step_times(mc_session* session, unsigned long long* ns, int cap, int* n);
+
+/* The CUDA stream (cudaStream_t) every call on this session is issued on,
+   so that callers can time or order their own work against it. */
+mc_status mc_session_stream(mc_session* session, void** stream);
+
 const char* mc_last_error(void);
 
 #ifdef __cplusplus

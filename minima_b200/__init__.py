@@ -29,7 +29,8 @@ LIB_HOST = os.path.join(PKG, "libminima_host.so")
 # include/minima_generate.h.
 CUDA_SYMBOLS = ("mc_init", "mc_model_create", "mc_model_update", "mc_model_destroy",
                 "mc_session_create", "mc_session_destroy", "mc_generate", "mc_forward_logits",
-                "mc_last_kernel_ms", "mc_last_launch_count", "mc_last_error")
+                "mc_last_kernel_ms", "mc_last_launch_count", "mc_last_step_times",
+                "mc_session_stream", "mc_last_error")
 GENERATE_SYMBOLS = ("kvcache_init", "kvcache_reset", "generation_check_kv_cache",
                     "generation_inspect_next_tokens", "generate", "generate_with_options",
                     "generate_ex", "generate_batch_with_options", "minima_cuda_select_device",
@@ -200,6 +201,8 @@ def _declare(host, cuda, gen):
     cuda.mc_forward_logits.argtypes = [vp, C.c_int, u16p, C.c_int, _f32p]
     cuda.mc_last_kernel_ms.argtypes = [vp, _f32p]
     cuda.mc_last_launch_count.argtypes = [vp, i32p]
+    cuda.mc_last_step_times.argtypes = [vp, u64p, C.c_int, i32p]
+    cuda.mc_session_stream.argtypes = [vp, C.POINTER(vp)]
     cuda.mc_last_error.restype = C.c_char_p
 
     gen.kvcache_init.restype = C.c_bool
@@ -465,6 +468,20 @@ class Session:
         n = C.c_int()
         _check(libs()[1].mc_last_launch_count(self.h, C.byref(n)), "mc_last_launch_count")
         return n.value
+
+    def last_step_times_ns(self, cap=1 << 16):
+        """%globaltimer stamps at the start of each token step of the last call."""
+        buf = np.zeros(cap, dtype=np.uint64)
+        n = C.c_int()
+        _check(libs()[1].mc_last_step_times(self.h, buf.ctypes.data_as(C.POINTER(C.c_uint64)),
+                                            cap, C.byref(n)), "mc_last_step_times")
+        return buf[:n.value]
+
+    def stream_handle(self) -> int:
+        """cudaStream_t of this session, as an integer handle."""
+        h = C.c_void_p()
+        _check(libs()[1].mc_session_stream(self.h, C.byref(h)), "mc_session_stream")
+        return h.value or 0
 
     def close(self):
         if self.h:

@@ -92,6 +92,7 @@ struct LoopParams {
     unsigned* bar;
     int* status;
     unsigned long long timeout_ns;
+    unsigned long long* stamps;   // [T+1] %globaltimer at each step start, or null
     int bc;               // GEMV chunk (<= kBCMax)
     int xs_ld;            // row stride of the chunk buffer in smem (floats)
 };
@@ -709,6 +710,7 @@ __global__ void __launch_bounds__(kThreads, 1) token_loop_kernel(const LoopParam
         }
         __syncthreads();
         const int nf = sm.ints[12], nh = sm.ints[13];
+        if (p.stamps && blockIdx.x == 0 && threadIdx.x == 0) p.stamps[t] = globaltimer_ns();
         if (nf == 0) break;
         for (int l = 0; l < p.L; l++) {
             phase_qkv<WT, VEC>(p, l, t, sm, nf);
@@ -731,6 +733,7 @@ __global__ void __launch_bounds__(kThreads, 1) token_loop_kernel(const LoopParam
             }
         }
     }
+    if (p.stamps && blockIdx.x == 0 && threadIdx.x == 0) p.stamps[p.T] = globaltimer_ns();
 }
 
 }  // namespace mc

@@ -87,6 +87,8 @@ struct mc_session {
     uint16_t* stop;            // [MC_MAX_STOP]
     float* trace;
     size_t trace_bytes;
+    unsigned long long* stamps;   // [cap + 1]
+    int last_T;
     float last_ms;
     int last_launches;
 };
@@ -278,7 +280,7 @@ mc_status mc_session_destroy(mc_session* s) {
     if (!s) return MC_OK;
     void* bufs[] = {s->kc, s->vc, s->x, s->q, s->att, s->f, s->logits, s->part_o, s->part_m,
                     s->part_l, s->amax_v, s->amax_i, s->att_cnt, s->counts, s->banned, s->bar,
-                    s->status, s->seq, s->prompts, s->out, s->stop, s->trace};
+                    s->status, s->seq, s->prompts, s->out, s->stop, s->trace, s->stamps};
     for (void* b : bufs) cudaFree(b);
     if (s->ev0) cudaEventDestroy(s->ev0);
     if (s->ev1) cudaEventDestroy(s->ev1);
@@ -374,6 +376,7 @@ mc_status mc_session_create(mc_model* m, int max_batch, int max_seq, mc_session*
         {(void**)&s->prompts, B * cap * 2},
         {(void**)&s->out, B * cap * 2},
         {(void**)&s->stop, MC_MAX_STOP * 2},
+        {(void**)&s->stamps, (cap + 2) * 8},
     };
     for (auto& a : allocs) {
         e = cudaMalloc(a.p, a.bytes);
@@ -413,6 +416,9 @@ mc_status ensure_trace(mc_session* s, size_t bytes) {
 template <typename WT>
 mc_status run_loop(mc_session* s, mc::LoopParams<WT>& p) {
     fill_params(p, s);
+    p.stamps = s->stamps;
+    s->last_T = p.T;
+    MC_CUDA(cudaMemsetAsync(s->stamps, 0, ((size_t)p.T + 1) * 8, s->stream));
     MC_CUDA(cudaMemsetAsync(s->bar, 0, 256, s->stream));
     MC_CUDA(cudaMemsetAsync(s->status, 0, 256, s->stream));
     MC_CUDA(cudaMemsetAsync(s->att_cnt, 0, (size_t)s->Bcap * s->m->K * 4, s->stream));
@@ -663,6 +669,22 @@ mc_status mc_last_kernel_ms(mc_session* s, float* ms) {
 mc_status mc_last_launch_count(mc_session* s, int* n) {
     if (!s || !n) return fail(MC_ERR_INVALID, "null argument");
     *n = s->last_launches;
+    return MC_OK;
+}
+
+mc_status mc_last_step_times(mc_session* s, unsigned long long* ns, int cap, int* n) {
+    if (!s || !ns || !n || cap < 0) return fail(MC_ERR_INVALID, "null argument");
+    *n = 0;
+    if (s->last_launches == 0) return MC_OK;
+    const int count = std::min(cap, s->last_T + 1);
+    MC_CUDA(cudaMemcpy(ns, s->stamps, (size_t)count * 8, cudaMemcpyDeviceToHost));
+    *n = count;
+    return MC_OK;
+}
+
+mc_status mc_session_stream(mc_session* s, void** stream) {
+    if (!s || !stream) return fail(MC_ERR_INVALID, "null argument");
+    *stream = (void*)s->stream;
     return MC_OK;
 }
 
