@@ -324,12 +324,14 @@ mc_status mc_session_create(mc_model* m, int max_batch, int max_seq, mc_session*
         delete s;
         return fail(MC_ERR_UNSUPPORTED, "shared memory plan %zu B exceeds %zu B", fixed + phase, limit);
     }
+    // The attribute is a per-function limit shared by every session on the
+    // device, so it is raised to the device maximum rather than to this plan.
     cudaError_t e;
     if (m->dtype == MC_WEIGHTS_BF16)
-        e = vec_ok(m) ? prepare_kernel<__nv_bfloat16, true>(s->smem)
-                      : prepare_kernel<__nv_bfloat16, false>(s->smem);
+        e = vec_ok(m) ? prepare_kernel<__nv_bfloat16, true>(limit)
+                      : prepare_kernel<__nv_bfloat16, false>(limit);
     else
-        e = vec_ok(m) ? prepare_kernel<float, true>(s->smem) : prepare_kernel<float, false>(s->smem);
+        e = vec_ok(m) ? prepare_kernel<float, true>(limit) : prepare_kernel<float, false>(limit);
     if (e != cudaSuccess) {
         delete s;
         return fail(MC_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
