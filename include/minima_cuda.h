@@ -165,6 +165,43 @@ mc_status mc_last_step_times(mc_session* session, unsigned long long* ns, int ca
    so that callers can time or order their own work against it. */
 mc_status mc_session_stream(mc_session* session, void** stream);
 
+/*
+ * mc_generate_static — mc_generate that allocates nothing.  No counterpart
+ * in the reference (whose decode runs on the host stack).
+ *
+ * For callers that cannot call cudaMalloc: code running while a CUDA graph
+ * is being captured, hosts that carve their device memory up front from
+ * their own pool, plugins that must not grow the device footprint after
+ * start-up.  The caller passes device buffers for everything it owns:
+ *   w            dims plus DEVICE pointers to the nine fp32 weight arrays
+ *                (layout as in mc_model_desc)
+ *   prompts, out_ids, rng_states, out_counts   device pointers, as with
+ *                MC_DEVICE_POINTERS in mc_generate
+ *   prompt_lens, opts   host memory
+ *   max_seq      KV-cache capacity per sequence (<= w->max_seq)
+ *   stream       cudaStream_t to run on (NULL: the legacy default stream);
+ *                the call returns after that stream has finished it
+ * The KV cache and all work buffers come from one static __device__ array
+ * of MC_STATIC_SCRATCH_BYTES that every GPU loading this library holds
+ * until the process exits; a model/batch/max_seq that needs more (the
+ * reference's default 5.8M model fits at batch 4 and max_seq 512) is
+ * rejected with MC_ERR_INVALID, as are batch > MC_STATIC_MAX_BATCH and
+ * max_seq * head_dim/2 > MC_STATIC_MAX_ROPE.  Output equals mc_generate's.
+ *
+ * The first call on a device looks up the array's device address and sets
+ * the kernel's shared-memory limit; make it before any stream capture.
+ * Calls share the array (its contents persist between calls; what must
+ * start at zero is cleared by each call), so calls that overlap on the GPU
+ * race.  Not thread-safe.
+ */
+#define MC_STATIC_SCRATCH_BYTES (16u << 20)
+#define MC_STATIC_MAX_BATCH     64
+#define MC_STATIC_MAX_ROPE      (1 << 17)
+mc_status mc_generate_static(const mc_model_desc* w, int batch,
+    const uint16_t* prompts, int prompt_stride, const int* prompt_lens,
+    uint16_t* out_ids, int out_cap, const mc_sampling* opts,
+    uint64_t* rng_states, int* out_counts, int max_seq, void* stream);
+
 const char* mc_last_error(void);
 
 #ifdef __cplusplus

@@ -691,3 +691,266 @@ mc_status mc_session_stream(mc_session* s, void** stream) {
 }
 
 }  // extern "C"
+
+// ===========================================================================
+// mc_generate_static: the token loop with no device allocation at all.
+//
+// For callers that cannot call cudaMalloc: code running while a CUDA graph is
+// being captured, hosts whose device memory is carved up up front by their
+// own pool, and plugins that must not grow the process's device footprint
+// after start-up.  Weights, prompts and outputs are the caller's device
+// buffers; everything else the loop needs (KV cache, activations, split
+// partials, counters, RoPE table, sequence table) lives in one file-scope
+// __device__ array of MC_STATIC_SCRATCH_BYTES, which every GPU that loads
+// this library holds until the process exits.
+//
+// The first call on a device resolves the array's device address with
+// cudaGetSymbolAddress and sets the kernel's shared-memory limit; make that
+// first call before any stream capture.  All calls share the one array and
+// it keeps the last call's contents, so the barrier counter, status word and
+// attention counters are cleared at the start of each call, and calls that
+// overlap on the GPU (on different streams, or from several host threads)
+// race.  Not thread-safe.
+// ===========================================================================
+
+static __device__ __align__(256) unsigned char g_static_scratch[MC_STATIC_SCRATCH_BYTES];
+
+namespace {
+
+struct StaticDevice {
+    bool ready;
+    unsigned char* scratch;   // device address of g_static_scratch on this device
+    int sms;
+    size_t smem_optin;
+};
+StaticDevice g_static_dev[64];
+
+// Host-side staging kept in static storage so that the call allocates no
+// host memory either.
+mc::SeqState g_static_seq[MC_STATIC_MAX_BATCH];
+float2 g_static_rope[MC_STATIC_MAX_ROPE];
+int g_static_status;
+
+struct StaticPlan {
+    size_t off[22];
+    size_t total;
+    size_t smem;
+    int bc, xs_ld, max_split;
+};
+
+// Carve the scratch array the same way mc_session_create sizes its buffers.
+StaticPlan static_plan(const mc_model_desc* d, int batch, int cap, int grid, size_t smem_limit) {
+    StaticPlan pl{};
+    const size_t B = batch, L = d->n_layers, K = d->n_kv_heads, hd = d->head_dim, D = d->dim;
+    const size_t F = d->ffn_dim, V = d->vocab_size, H = d->n_heads;
+    pl.max_split = (cap + mc::kSplitLen - 1) / mc::kSplitLen;
+    const size_t ms = pl.max_split;
+    const size_t sizes[22] = {
+        L * B * K * cap * hd * 4, L * B * K * cap * hd * 4,   // kc, vc
+        B * D * 4, B * D * 4, B * D * 4, B * F * 4,           // x, q, att, f
+        B * V * 4,                                            // logits
+        B * H * ms * hd * 4, B * H * ms * 4, B * H * ms * 4,  // part_o, part_m, part_l
+        B * (size_t)grid * 4, B * (size_t)grid * 4,           // amax_v, amax_i
+        B * K * 4, B * V * 4, B * ((V + 31) / 32) * 4,        // att_cnt, counts, banned
+        256, 256,                                             // bar, status
+        B * sizeof(mc::SeqState), (size_t)MC_MAX_STOP * 2,    // seq, stop ids
+        (size_t)cap * (hd / 2 > 0 ? hd / 2 : 1) * sizeof(float2),  // rope
+        0, 0};
+    size_t off = 0;
+    for (int i = 0; i < 22; i++) {
+        pl.off[i] = off;
+        off = align_up(off + sizes[i], 256);
+    }
+    pl.total = off;
+    const int G = d->n_heads / d->n_kv_heads;
+    pl.xs_ld = (int)align_up((size_t)std::max(d->dim, d->ffn_dim), 4);
+    const size_t att_bytes = (size_t)(G * d->head_dim + G * mc::kSplitLen) * 4;
+    const size_t samp_bytes = mc::sampler_smem_bytes(d->vocab_size);
+    const size_t fixed = mc::loop_fixed_bytes(batch);
+    const size_t wi_bytes = mc::kWarps * mc::kBCMax * 4;
+    size_t phase = std::max(att_bytes, samp_bytes);
+    const size_t row_bytes = (size_t)pl.xs_ld * 4;
+    int bc = mc::kBCMax;
+    while (bc > 1 && fixed + std::max(phase, bc * row_bytes + wi_bytes) > smem_limit) bc--;
+    pl.bc = bc;
+    phase = std::max(phase, bc * row_bytes + wi_bytes);
+    pl.smem = align_up(fixed + phase, 16);
+    return pl;
+}
+
+mc_status static_setup(int dev) {
+    StaticDevice& sd = g_static_dev[dev];
+    if (sd.ready) return MC_OK;
+    void* ptr = nullptr;
+    cudaError_t e = cudaGetSymbolAddress(&ptr, g_static_scratch);
+    if (e != cudaSuccess || !ptr)
+        return fail(MC_ERR_CUDA, "mc_generate_static: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
+    cudaDeviceProp prop;
+    MC_CUDA(cudaGetDeviceProperties(&prop, dev));
+    if (prop.major != 10)
+        return fail(MC_ERR_UNSUPPORTED, "mc_generate_static: device %d is not sm_100", dev);
+    const int optin = (int)prop.sharedMemPerBlockOptin;
+    MC_CUDA(cudaFuncSetAttribute(mc::token_loop_kernel<float, true>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, optin));
+    MC_CUDA(cudaFuncSetAttribute(mc::token_loop_kernel<float, false>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, optin));
+    sd.scratch = static_cast<unsigned char*>(ptr);
+    sd.sms = prop.multiProcessorCount;
+    sd.smem_optin = prop.sharedMemPerBlockOptin;
+    sd.ready = true;
+    return MC_OK;
+}
+
+bool aligned16(const void* p) { return ((uintptr_t)p & 15u) == 0; }
+
+}  // namespace
+
+extern "C" mc_status mc_generate_static(const mc_model_desc* w, int batch,
+                                        const uint16_t* prompts, int prompt_stride,
+                                        const int* prompt_lens, uint16_t* out_ids, int out_cap,
+                                        const mc_sampling* o, uint64_t* rng_states,
+                                        int* out_counts, int max_seq, void* stream) {
+    mc_status st = validate_desc(w);
+    if (st) return st;
+    if (batch <= 0 || batch > MC_STATIC_MAX_BATCH)
+        return fail(MC_ERR_INVALID, "mc_generate_static: batch %d outside [1, %d]", batch,
+                    MC_STATIC_MAX_BATCH);
+    if (max_seq <= 0 || max_seq > w->max_seq || max_seq > MC_STATIC_MAX_ROPE ||
+        (size_t)max_seq * std::max(w->head_dim / 2, 1) > MC_STATIC_MAX_ROPE)
+        return fail(MC_ERR_INVALID, "mc_generate_static: max_seq %d outside [1, %d]", max_seq,
+                    std::min(w->max_seq, MC_STATIC_MAX_ROPE / std::max(w->head_dim / 2, 1)));
+    if (!prompts || !prompt_lens || !out_ids || out_cap <= 0 || !rng_states || !out_counts ||
+        prompt_stride <= 0)
+        return fail(MC_ERR_INVALID, "mc_generate_static: null or empty argument");
+    if (!options_valid(o))
+        return fail(MC_ERR_INVALID, "mc_generate_static: options rejected (generate.c:526-551)");
+    int dev = 0;
+    MC_CUDA(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= 64) return fail(MC_ERR_UNSUPPORTED, "device index %d", dev);
+    st = static_setup(dev);
+    if (st) return st;
+    const StaticDevice& sd = g_static_dev[dev];
+    const StaticPlan pl = static_plan(w, batch, max_seq, sd.sms, sd.smem_optin);
+    if (pl.total > (size_t)MC_STATIC_SCRATCH_BYTES)
+        return fail(MC_ERR_INVALID,
+                    "mc_generate_static: this model/batch/max_seq needs %zu bytes of scratch; the "
+                    "static array holds %u (use mc_session_create + mc_generate instead)",
+                    pl.total, (unsigned)MC_STATIC_SCRATCH_BYTES);
+    if (pl.smem > sd.smem_optin)
+        return fail(MC_ERR_UNSUPPORTED, "mc_generate_static: shared memory plan %zu B", pl.smem);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    unsigned char* base = sd.scratch;
+
+    // Per-sequence bookkeeping exactly as generate.c:553-564.
+    int T = 0;
+    for (int b = 0; b < batch; b++) {
+        const int P = prompt_lens[b];
+        if (P <= 0 || P > out_cap || P > max_seq || P > prompt_stride)
+            return fail(MC_ERR_INVALID, "mc_generate_static: prompt %d length %d", b, P);
+        int nnew = o->max_new_tokens;
+        nnew = std::min(nnew, out_cap - P);
+        nnew = std::min(nnew, max_seq - P);
+        mc::SeqState& q = g_static_seq[b];
+        memset(&q, 0, sizeof(q));
+        q.P = P;
+        q.nnew = std::max(nnew, 0);
+        q.done = nnew <= 0;
+        q.result = P;
+        if (nnew > 0) T = std::max(T, P + nnew - 1);
+    }
+    for (int i = 0; i < o->stop_sequence_len; i++)
+        if (o->stop_sequence_ids[i] >= w->vocab_size)
+            return fail(MC_ERR_INVALID, "mc_generate_static: stop id >= vocab");
+
+    // RoPE table (rotary.h:19-24) with the host libm, as mc_model_create does.
+    const int half = w->head_dim / 2;
+    for (int pair = 0; pair < half; pair++) {
+        const float exponent = (2.0f * (float)pair) / (float)w->head_dim;
+        const float rbase = ::powf(10000.0f, -exponent);
+        for (int pos = 0; pos < max_seq; pos++) {
+            const float angle = (float)pos * rbase;
+            g_static_rope[(size_t)pos * half + pair] = make_float2(::cosf(angle), ::sinf(angle));
+        }
+    }
+
+    mc::LoopParams<float> p{};
+    p.V = w->vocab_size; p.D = w->dim; p.L = w->n_layers; p.H = w->n_heads; p.K = w->n_kv_heads;
+    p.hd = w->head_dim; p.kvd = w->kv_dim; p.Q = w->qkv_dim; p.F = w->ffn_dim;
+    p.G = w->n_heads / w->n_kv_heads;
+    p.tok_emb = w->tok_emb; p.w_qkv = w->attn_qkv; p.w_proj = w->attn_proj; p.w_up = w->ffn_up;
+    p.w_gate = w->ffn_gate; p.w_down = w->ffn_down;
+    p.rms1 = w->rms1_scale; p.rms2 = w->rms2_scale; p.rmsf = w->rms_final_scale;
+    p.kc = reinterpret_cast<float*>(base + pl.off[0]);
+    p.vc = reinterpret_cast<float*>(base + pl.off[1]);
+    p.x = reinterpret_cast<float*>(base + pl.off[2]);
+    p.q = reinterpret_cast<float*>(base + pl.off[3]);
+    p.att = reinterpret_cast<float*>(base + pl.off[4]);
+    p.f = reinterpret_cast<float*>(base + pl.off[5]);
+    p.logits = reinterpret_cast<float*>(base + pl.off[6]);
+    p.part_o = reinterpret_cast<float*>(base + pl.off[7]);
+    p.part_m = reinterpret_cast<float*>(base + pl.off[8]);
+    p.part_l = reinterpret_cast<float*>(base + pl.off[9]);
+    p.amax_v = reinterpret_cast<float*>(base + pl.off[10]);
+    p.amax_i = reinterpret_cast<int*>(base + pl.off[11]);
+    p.att_cnt = reinterpret_cast<unsigned*>(base + pl.off[12]);
+    p.counts = reinterpret_cast<unsigned*>(base + pl.off[13]);
+    p.banned = reinterpret_cast<unsigned*>(base + pl.off[14]);
+    p.bar = reinterpret_cast<unsigned*>(base + pl.off[15]);
+    p.status = reinterpret_cast<int*>(base + pl.off[16]);
+    mc::SeqState* dseq = reinterpret_cast<mc::SeqState*>(base + pl.off[17]);
+    uint16_t* dstop = reinterpret_cast<uint16_t*>(base + pl.off[18]);
+    float2* drope = reinterpret_cast<float2*>(base + pl.off[19]);
+    p.rope = drope; p.rope_len = max_seq;
+    p.cap = max_seq; p.Bcap = batch; p.max_split = pl.max_split;
+    p.seq = dseq; p.B = batch;
+    p.prompts = prompts; p.prompt_stride = prompt_stride;
+    p.out_ids = out_ids; p.out_cap = out_cap;
+    p.s.temperature = o->temperature; p.s.top_p = o->top_p; p.s.rep = o->repetition_penalty;
+    p.s.min_p = o->min_p; p.s.freq = o->frequency_penalty; p.s.pres = o->presence_penalty;
+    p.s.top_k = std::min(std::min(std::max(o->top_k, 1), w->vocab_size), MC_MAX_TOPK);
+    p.s.min_new = o->min_new_tokens; p.s.ngram = o->no_repeat_ngram_size;
+    p.s.stop_ids = dstop; p.s.stop_len = o->stop_sequence_len;
+    p.s.pen_active = o->repetition_penalty > 1.0f || o->frequency_penalty != 0.0f ||
+                     o->presence_penalty != 0.0f;
+    p.T = T;
+    p.timeout_ns = 1000ull * 1000ull * 1000ull;
+    p.bc = pl.bc; p.xs_ld = pl.xs_ld;
+
+    // Clear what must start at zero; the array keeps the previous call's data.
+    MC_CUDA(cudaMemsetAsync(p.bar, 0, 256, s));
+    MC_CUDA(cudaMemsetAsync(p.status, 0, 256, s));
+    MC_CUDA(cudaMemsetAsync(p.att_cnt, 0, (size_t)batch * w->n_kv_heads * 4, s));
+    if (half > 0)
+        MC_CUDA(cudaMemcpyAsync(drope, g_static_rope, (size_t)max_seq * half * sizeof(float2),
+                                cudaMemcpyHostToDevice, s));
+    if (o->stop_sequence_len > 0)
+        MC_CUDA(cudaMemcpyAsync(dstop, o->stop_sequence_ids, o->stop_sequence_len * 2,
+                                cudaMemcpyHostToDevice, s));
+    MC_CUDA(cudaMemcpyAsync(dseq, g_static_seq, batch * sizeof(mc::SeqState),
+                            cudaMemcpyHostToDevice, s));
+    for (int b = 0; b < batch; b++)
+        MC_CUDA(cudaMemcpyAsync(&dseq[b].rng, rng_states + b, 8, cudaMemcpyDeviceToDevice, s));
+    if (T > 0) {
+        const bool vec = w->dim % 4 == 0 && w->ffn_dim % 4 == 0 && aligned16(w->tok_emb) &&
+                         aligned16(w->attn_qkv) && aligned16(w->attn_proj) &&
+                         aligned16(w->ffn_up) && aligned16(w->ffn_gate) && aligned16(w->ffn_down);
+        const cudaError_t e = vec ? launch_loop<float, true>(p, sd.sms, pl.smem, s)
+                                  : launch_loop<float, false>(p, sd.sms, pl.smem, s);
+        if (e != cudaSuccess)
+            return fail(MC_ERR_CUDA, "mc_generate_static launch: %s", cudaGetErrorString(e));
+    }
+    for (int b = 0; b < batch; b++) {
+        MC_CUDA(cudaMemcpyAsync(rng_states + b, &dseq[b].rng, 8, cudaMemcpyDeviceToDevice, s));
+        MC_CUDA(cudaMemcpyAsync(out_counts + b, &dseq[b].result, 4, cudaMemcpyDeviceToDevice, s));
+        if (g_static_seq[b].nnew <= 0)  // generate.c:557-559
+            MC_CUDA(cudaMemcpyAsync(out_ids + (size_t)b * out_cap, prompts + (size_t)b * prompt_stride,
+                                    (size_t)g_static_seq[b].P * 2, cudaMemcpyDeviceToDevice, s));
+    }
+    MC_CUDA(cudaMemcpyAsync(&g_static_status, p.status, 4, cudaMemcpyDeviceToHost, s));
+    MC_CUDA(cudaStreamSynchronize(s));
+    if (g_static_status == mc::ST_TIMEOUT)
+        return fail(MC_ERR_TIMEOUT, "mc_generate_static: a grid barrier passed its deadline");
+    if (g_static_status != 0)
+        return fail(MC_ERR_DEVICE, "mc_generate_static: kernel status %d", g_static_status);
+    return MC_OK;
+}
