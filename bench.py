@@ -278,6 +278,7 @@ def native_arm(args):
             pg.barrier()
         torch.cuda.synchronize()
         clk = clocks.stop()
+    kernel_name = sess.last_kernel_name()
     step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
     total_ms = sum(step_ms)
     stamps = sess.last_step_times_ns().astype(np.int64)
@@ -339,7 +340,7 @@ def native_arm(args):
             "gpu_launches": launches,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": traffic,
-                         "kernel": "mc::token_loop_kernel<float,true>",
+                         "kernel": kernel_name,
                          "algorithmic_bytes_per_launch": algo, "kernel_ms": kms,
                          "peak_source": f"{peak_src} HBM copy bandwidth"},
             "clocks": clk,

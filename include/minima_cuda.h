@@ -161,6 +161,10 @@ mc_status mc_last_launch_count(mc_session* session, int* launches);
    are in prefill while t < prompt length. */
 mc_status mc_last_step_times(mc_session* session, unsigned long long* ns, int cap, int* n);
 
+/* Name of the kernel the last call ran: "mc::token_loop_kernel" (grid-barrier
+   loop) or "mc::cluster_loop_kernel" (cluster-resident greedy loop). */
+const char* mc_last_kernel_name(mc_session* session);
+
 /* The CUDA stream (cudaStream_t) every call on this session is issued on,
    so that callers can time or order their own work against it. */
 mc_status mc_session_stream(mc_session* session, void** stream);

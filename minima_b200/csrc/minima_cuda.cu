@@ -12,9 +12,11 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <type_traits>
 #include <vector>
 
 #include "mc_token_loop.cuh"
+#include "mc_cluster_loop.cuh"
 
 namespace {
 
@@ -91,6 +93,17 @@ struct mc_session {
     int last_T;
     float last_ms;
     int last_launches;
+    // cluster-resident loop (greedy fp32 decode of small models)
+    bool cl_ok;                   // plan fits this device
+    int cl_cs, cl_nc;             // CTAs per cluster, clusters
+    size_t cl_smem;
+    mc::ClusterParams cl_plan;    // shared-memory offsets and geometry
+    float* xfin;
+    int* hgen;
+    unsigned* hsync;              // [0] go, [32] hdone (separate lines)
+    float* hpv;
+    int* hpi;
+    int last_path;                // 0 grid loop, 1 cluster loop
 };
 
 namespace {
@@ -139,6 +152,122 @@ void fill_params(mc::LoopParams<WT>& p, const mc_session* s) {
     p.bar = s->bar; p.status = s->status;
     p.timeout_ns = 1000ull * 1000ull * 1000ull;  // 1 s per barrier wait
     p.bc = s->bc; p.xs_ld = s->xs_ld;
+}
+
+cudaError_t launch_cluster(const mc::ClusterParams& cp, int cs, int nc, size_t smem,
+                           cudaStream_t st, bool cooperative) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(nc * cs);
+    cfg.blockDim = dim3(mc::kThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = cs;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeCooperative;
+    attr[1].val.cooperative = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = cooperative ? 2 : 1;
+    return cudaLaunchKernelEx(&cfg, mc::cluster_loop_kernel, cp);
+}
+
+// Plan of the cluster-resident loop (mc_cluster_loop.cuh) for this model on
+// this device: shared-memory offsets, cluster size and count such that every
+// cluster is co-resident.  Returns false when the loop does not apply; the
+// grid-barrier loop then serves every call.
+bool plan_cluster(mc_session* s, const cudaDeviceProp& prop) {
+    const mc_model* m = s->m;
+    if (m->dtype != MC_WEIGHTS_F32) return false;
+    const int G = m->H / m->K;
+    if (m->hd % 4 || m->D % 4 || m->F % 4 || m->Q % 2 || G > 16) return false;
+    const char* env = getenv("MINIMA_CUDA_LOOP");
+    if (env && strcmp(env, "grid") == 0) return false;
+    const size_t optin = prop.sharedMemPerBlockOptin;
+    if (cudaFuncSetAttribute(mc::cluster_loop_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)optin) != cudaSuccess ||
+        cudaFuncSetAttribute(mc::cluster_loop_kernel,
+                             cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess) {
+        cudaGetLastError();
+        return false;
+    }
+    const int B8 = mc::kBCMax;
+    for (int cs : {16, 8}) {
+        mc::ClusterParams cp{};
+        cp.cs = cs;
+        const mc::CSlice s0 = mc::cluster_slice(0, cs, m->Q, m->D, m->F);
+        const size_t stage_f = align_up(mc::slice_floats(s0, m->D, m->F), 32);
+        if (stage_f * 4 >= (1u << 20)) continue;           // mbarrier tx-count limit
+        int attp_rows = 0;                                   // max over B of B * splits(B)
+        for (int B = 1; B <= B8; B++) attp_rows = std::max(attp_rows, B * std::max(1, cs / (B * m->K)));
+        size_t off = mc::kLcHeader;
+        auto take = [&](size_t floats, size_t align) {
+            off = align_up(off, align);
+            const size_t o = off;
+            off += floats * 4;
+            return (unsigned)o;
+        };
+        cp.off_x = take((size_t)B8 * m->D, 16);
+        cp.off_xn = take((size_t)B8 * m->D, 16);
+        cp.off_qkv = take((size_t)B8 * m->Q, 16);
+        cp.off_attp = take((size_t)attp_rows * m->H * (m->hd + 2), 16);
+        cp.off_att = take((size_t)B8 * m->D, 16);
+        cp.off_f = take((size_t)B8 * m->F, 16);
+        const size_t fixed = off;
+        int tile = 128;
+        for (; tile >= 16; tile /= 2) {
+            size_t o2 = align_up(fixed, 16) + ((size_t)G * tile + (size_t)G * m->hd) * 4;
+            o2 = align_up(o2, 16) + 2 * (size_t)tile * (m->hd + 4) * 4;
+            o2 = align_up(o2, 128) + mc::kStages * stage_f * 4;
+            if (o2 <= optin) break;
+        }
+        if (tile < 16) continue;
+        cp.kv_tile = tile;
+        cp.off_sc = take((size_t)G * tile + (size_t)G * m->hd, 16);
+        cp.off_kv = take(2 * (size_t)tile * (m->hd + 4), 16);
+        cp.off_stage = take(mc::kStages * stage_f, 128);
+        cp.stage_floats = (unsigned)stage_f;
+        const size_t lc_bytes = off;
+        for (int nc = prop.multiProcessorCount / cs; nc >= 2; nc--) {
+            const int nhc = (nc - 1) * cs;
+            const int rows = (m->V + nhc - 1) / nhc;
+            const size_t ld = (size_t)m->D + 4;
+            if ((size_t)rows * m->D * 4 >= (1u << 20)) break;
+            const size_t hc_x = align_up(mc::kHcEmbOffset + (size_t)rows * ld * 4, 16);
+            const size_t hc_bytes = hc_x + (size_t)B8 * m->D * 4;
+            const size_t smem = align_up(std::max(lc_bytes, hc_bytes), 128);
+            if (smem > optin) break;
+            cudaLaunchConfig_t cfg = {};
+            cfg.gridDim = dim3(nc * cs);
+            cfg.blockDim = dim3(mc::kThreads);
+            cfg.dynamicSmemBytes = smem;
+            cudaLaunchAttribute attr[1];
+            attr[0].id = cudaLaunchAttributeClusterDimension;
+            attr[0].val.clusterDim.x = cs;
+            attr[0].val.clusterDim.y = 1;
+            attr[0].val.clusterDim.z = 1;
+            cfg.attrs = attr;
+            cfg.numAttrs = 1;
+            int maxc = 0;
+            if (cudaOccupancyMaxActiveClusters(&maxc, (void*)mc::cluster_loop_kernel, &cfg) != cudaSuccess) {
+                cudaGetLastError();
+                break;
+            }
+            if (maxc >= nc) {
+                cp.n_clusters = nc;
+                cp.hc_rows = rows;
+                cp.hc_ld = (unsigned)ld;
+                cp.off_hc_x = (unsigned)hc_x;
+                s->cl_cs = cs;
+                s->cl_nc = nc;
+                s->cl_smem = smem;
+                s->cl_plan = cp;
+                return true;
+            }
+        }
+    }
+    return false;
 }
 
 mc_status validate_desc(const mc_model_desc* d) {
@@ -280,7 +409,8 @@ mc_status mc_session_destroy(mc_session* s) {
     if (!s) return MC_OK;
     void* bufs[] = {s->kc, s->vc, s->x, s->q, s->att, s->f, s->logits, s->part_o, s->part_m,
                     s->part_l, s->amax_v, s->amax_i, s->att_cnt, s->counts, s->banned, s->bar,
-                    s->status, s->seq, s->prompts, s->out, s->stop, s->trace, s->stamps};
+                    s->status, s->seq, s->prompts, s->out, s->stop, s->trace, s->stamps,
+                    s->xfin, s->hgen, s->hsync, s->hpv, s->hpi};
     for (void* b : bufs) cudaFree(b);
     if (s->ev0) cudaEventDestroy(s->ev0);
     if (s->ev1) cudaEventDestroy(s->ev1);
@@ -388,6 +518,25 @@ mc_status mc_session_create(mc_model* m, int max_batch, int max_seq, mc_session*
                         cudaGetErrorString(e));
         }
     }
+    s->cl_ok = plan_cluster(s, prop);
+    if (s->cl_ok) {
+        const size_t nhc = (size_t)(s->cl_nc - 1) * s->cl_cs;
+        struct Alloc cl_allocs[] = {
+            {(void**)&s->xfin, B * D * 4},
+            {(void**)&s->hgen, B * 4},
+            {(void**)&s->hsync, 64 * 4},
+            {(void**)&s->hpv, B * nhc * 2 * 4},
+            {(void**)&s->hpi, B * nhc * 2 * 4},
+        };
+        for (auto& a : cl_allocs) {
+            e = cudaMalloc(a.p, a.bytes);
+            if (e != cudaSuccess) {
+                mc_session_destroy(s);
+                return fail(MC_ERR_NOMEM, "session allocation of %zu bytes: %s", a.bytes,
+                            cudaGetErrorString(e));
+            }
+        }
+    }
     e = cudaMemset(s->att_cnt, 0, B * K * 4);
     if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&s->stream, cudaStreamNonBlocking);
     if (e == cudaSuccess) e = cudaEventCreate(&s->ev0);
@@ -430,6 +579,7 @@ mc_status run_loop(mc_session* s, mc::LoopParams<WT>& p) {
     if (e != cudaSuccess) return fail(MC_ERR_CUDA, "token loop launch: %s", cudaGetErrorString(e));
     MC_CUDA(cudaEventRecord(s->ev1, s->stream));
     s->last_launches = 1;
+    s->last_path = 0;
     int status = 0;
     MC_CUDA(cudaMemcpyAsync(&status, s->status, 4, cudaMemcpyDeviceToHost, s->stream));
     MC_CUDA(cudaStreamSynchronize(s->stream));
@@ -437,6 +587,45 @@ mc_status run_loop(mc_session* s, mc::LoopParams<WT>& p) {
     if (status == mc::ST_TIMEOUT)
         return fail(MC_ERR_TIMEOUT, "token loop: a grid barrier passed its deadline");
     if (status != 0) return fail(MC_ERR_DEVICE, "token loop reported status %d", status);
+    return MC_OK;
+}
+
+// Launch the cluster-resident loop (greedy, fp32, batch <= kBCMax).
+mc_status run_cluster(mc_session* s, mc::LoopParams<float>& p) {
+    fill_params(p, s);
+    p.stamps = s->stamps;
+    s->last_T = p.T;
+    mc::ClusterParams cp = s->cl_plan;
+    cp.lp = p;
+    cp.n_split = std::max(1, s->cl_cs / (p.B * s->m->K));
+    cp.xfin = s->xfin;
+    cp.hgen = s->hgen;
+    cp.go = s->hsync;
+    cp.hdone = s->hsync + 32;
+    cp.hpv = s->hpv;
+    cp.hpi = s->hpi;
+    MC_CUDA(cudaMemsetAsync(s->stamps, 0, ((size_t)p.T + 1) * 8, s->stream));
+    MC_CUDA(cudaMemsetAsync(s->status, 0, 256, s->stream));
+    MC_CUDA(cudaMemsetAsync(s->hsync, 0, 64 * 4, s->stream));
+    MC_CUDA(cudaEventRecord(s->ev0, s->stream));
+    cudaError_t e = launch_cluster(cp, s->cl_cs, s->cl_nc, s->cl_smem, s->stream, true);
+    if (e != cudaSuccess) {
+        // cooperative scheduling of clusters unsupported: the plan already
+        // checked that every cluster can be resident, and every wait is bounded
+        cudaGetLastError();
+        e = launch_cluster(cp, s->cl_cs, s->cl_nc, s->cl_smem, s->stream, false);
+    }
+    if (e != cudaSuccess) return fail(MC_ERR_CUDA, "cluster loop launch: %s", cudaGetErrorString(e));
+    MC_CUDA(cudaEventRecord(s->ev1, s->stream));
+    s->last_launches = 1;
+    s->last_path = 1;
+    int status = 0;
+    MC_CUDA(cudaMemcpyAsync(&status, s->status, 4, cudaMemcpyDeviceToHost, s->stream));
+    MC_CUDA(cudaStreamSynchronize(s->stream));
+    MC_CUDA(cudaEventElapsedTime(&s->last_ms, s->ev0, s->ev1));
+    if (status == mc::ST_TIMEOUT)
+        return fail(MC_ERR_TIMEOUT, "cluster loop: a device-side wait passed its deadline");
+    if (status != 0) return fail(MC_ERR_DEVICE, "cluster loop reported status %d", status);
     return MC_OK;
 }
 
@@ -544,7 +733,13 @@ mc_status generate_t(mc_session* s, int batch, const uint16_t* prompts, int prom
                                     s->stream));
     }
     if (T > 0) {
-        mc_status st = run_loop<WT>(s, p);
+        mc_status st;
+        if constexpr (std::is_same<WT, float>::value) {
+            if (s->cl_ok && p.s.top_k == 1 && batch <= mc::kBCMax) st = run_cluster(s, p);
+            else st = run_loop<WT>(s, p);
+        } else {
+            st = run_loop<WT>(s, p);
+        }
         if (st) return st;
     } else {
         s->last_ms = 0.0f;
@@ -682,6 +877,11 @@ mc_status mc_last_step_times(mc_session* s, unsigned long long* ns, int cap, int
     MC_CUDA(cudaMemcpy(ns, s->stamps, (size_t)count * 8, cudaMemcpyDeviceToHost));
     *n = count;
     return MC_OK;
+}
+
+const char* mc_last_kernel_name(mc_session* s) {
+    if (!s || s->last_launches == 0) return "";
+    return s->last_path == 1 ? "mc::cluster_loop_kernel" : "mc::token_loop_kernel";
 }
 
 mc_status mc_session_stream(mc_session* s, void** stream) {

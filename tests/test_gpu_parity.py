@@ -100,6 +100,33 @@ def test_c2_batch_greedy(gpu):
     assert [c.pos for c in caches.caches] == [384] * B
 
 
+@pytest.mark.parametrize("loop", ["cluster", "grid"])
+def test_c2_shape_both_loops(gpu, loop, monkeypatch):
+    """The config-2 shape (4 x prompt 128, greedy) on the cluster-resident loop
+    and on the grid-barrier loop: same ids as the oracle, and each session
+    reports the loop it ran."""
+    if loop == "grid":
+        monkeypatch.setenv("MINIMA_CUDA_LOOP", "grid")
+    else:
+        monkeypatch.delenv("MINIMA_CUDA_LOOP", raising=False)
+    hm = M.HostModel(C1.vocab, C1.dim, C1.n_layers, C1.n_heads, C1.ffn_dim, C1.max_seq, seed=1)
+    orc = O.OrcModel(C1, 1)
+    B = 4
+    prompts = np.stack([O.random_prompt(128, C1.vocab, 2000 + b) for b in range(B)])
+    sess = M.Session(M.DeviceModel(hm), B, 512)
+    opts = M.options(top_k=1, max_new_tokens=96, repetition_penalty=1.05)
+    out, counts, st, fpos = sess.generate(prompts, [128] * B, 512, opts, [5, 6, 7, 8])
+    assert sess.last_kernel_name() == ("mc::cluster_loop_kernel" if loop == "cluster"
+                                       else "mc::token_loop_kernel")
+    ok, outr, countsr, str_ = orc.generate_batch(
+        prompts, [128] * B, 512, 512, O.make_options(top_k=1, max_new_tokens=96,
+                                                      repetition_penalty=1.05), [5, 6, 7, 8])
+    assert list(counts) == list(countsr)
+    for b in range(B):
+        assert np.array_equal(out[b, :counts[b]], outr[b, :countsr[b]])
+    assert np.array_equal(st, str_)
+
+
 def test_sampling_teacher_forced(c1):
     """Temperature/top-k/top-p sampling: with the sampler fed the device's
     own logits and RNG state, the oracle sampler picks the same ids."""
