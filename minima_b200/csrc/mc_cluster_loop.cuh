@@ -47,16 +47,18 @@ struct CSlice {
     int q0, q1, p0, p1, f0, f1;     // rows: qkv [q0,q1), proj/down [p0,p1), up/gate [f0,f1)
 };
 
-// Row slice of CTA `c` in a cluster of `cs`; qkv rows stay in RoPE pairs.
+// Row slice of CTA `c` in a cluster of `cs`.  Slices are whole groups of 4
+// rows (Q, D and F are multiples of 4 here), so each CTA's results can be
+// pushed to the other CTAs as float4 chunks; qkv slices keep RoPE pairs.
 __host__ __device__ inline CSlice cluster_slice(int c, int cs, int Q, int D, int F) {
     CSlice s;
-    const int pairs = Q / 2, ppc = (pairs + cs - 1) / cs;
-    s.q0 = min(2 * c * ppc, Q);
-    s.q1 = min(2 * (c + 1) * ppc, Q);
-    const int rpc = (D + cs - 1) / cs;
+    const int qpc = 4 * ((Q / 4 + cs - 1) / cs);
+    s.q0 = min(c * qpc, Q);
+    s.q1 = min((c + 1) * qpc, Q);
+    const int rpc = 4 * ((D / 4 + cs - 1) / cs);
     s.p0 = min(c * rpc, D);
     s.p1 = min((c + 1) * rpc, D);
-    const int fpc = (F + cs - 1) / cs;
+    const int fpc = 4 * ((F / 4 + cs - 1) / cs);
     s.f0 = min(c * fpc, F);
     s.f1 = min((c + 1) * fpc, F);
     return s;
@@ -73,7 +75,8 @@ struct ClusterParams {
     int n_clusters;
     // layer-cluster shared-memory plan (byte offsets)
     unsigned off_x, off_xn, off_qkv, off_attp, off_att, off_f, off_sc, off_kv, off_stage;
-    unsigned stage_floats;      // floats per weight stage
+    unsigned off_rmsf, off_rope;
+    unsigned stage_floats;      // floats per weight stage (slice + rms1 + rms2)
     int n_split;                // attention splits per (sequence, KV head)
     int kv_tile;                // keys staged per attention tile
     // head clusters
@@ -145,11 +148,29 @@ struct LcState {
     float* sc;     // [G][kv_tile]
     float* kv;     // [2][kv_tile][hd + 4]
     float* stage;  // [kStages][stage_floats]
+    float* rmsf;   // [D] final RMSNorm scale
+    float2* rope;  // [hd/2] (cos, sin) at the current position
     unsigned long long* bar;  // [kStages]
-    int* ints;     // [64]: 0..15 fwd list, 16..31 head list, 32.. scalars, 36/37 error slots
+    int* ints;     // [64]: 0..15 fwd list, 16..31 head list, 32.. scalars,
+                   //       36/37 cluster error slots, 38 this CTA saw an error
     float* red;    // [64]
+    struct SeqMirror* seq;    // [kBCMax] sequence table mirrored in shared memory
     int epoch;     // cluster barriers passed (identical in every CTA of the cluster)
 };
+
+// The sequence table in shared memory: the layer cluster reads it every
+// step, so it is kept here (identical in every layer CTA; rank 0 updates it
+// and broadcasts) and written back to global memory once, at exit.
+struct SeqMirror {
+    int P, nnew, gen, done, tok, result, final_pos, pad;
+    unsigned long long rng;
+};
+
+// Flag a failure seen by this CTA; the next lc_sync makes it cluster-wide.
+__device__ __forceinline__ void lc_fail(LcState& S, int* status, int code) {
+    atomicMax(status, code);
+    S.ints[38] = 1;
+}
 
 // Issue the TMA bulk copies of layer `l`'s weight slice into stage `s`.
 __device__ void lc_issue_layer(const ClusterParams& cp, const CSlice& sl, LcState& S, int l, int s) {
@@ -157,12 +178,12 @@ __device__ void lc_issue_layer(const ClusterParams& cp, const CSlice& sl, LcStat
     const size_t D = p.D, F = p.F;
     float* dst = S.stage + (size_t)s * cp.stage_floats;
     const unsigned nq = sl.q1 - sl.q0, np = sl.p1 - sl.p0, nf = sl.f1 - sl.f0;
-    const unsigned bytes = (unsigned)((nq * D + np * D + 2 * nf * D + np * F) * 4);
-    if (bytes == 0) {   // empty slice: complete the phase without a transfer
-        asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(&S.bar[s])) : "memory");
-        return;
-    }
+    // slice rows, then this layer's rms1 and rms2 scales (D floats each)
+    const unsigned bytes = (unsigned)((nq * D + np * D + 2 * nf * D + np * F + 2 * D) * 4);
     mbar_expect_tx(&S.bar[s], bytes);
+    float* scales = dst + slice_floats(sl, p.D, p.F);
+    bulk_g2s(scales, p.rms1 + (size_t)l * D, D * 4, &S.bar[s]);
+    bulk_g2s(scales + D, p.rms2 + (size_t)l * D, D * 4, &S.bar[s]);
     if (nq) bulk_g2s(dst, p.w_qkv + ((size_t)l * p.Q + sl.q0) * D, nq * D * 4, &S.bar[s]);
     dst += nq * D;
     if (np) bulk_g2s(dst, p.w_proj + ((size_t)l * p.D + sl.p0) * D, np * D * 4, &S.bar[s]);
@@ -188,9 +209,78 @@ __device__ void lc_norm(const float* x, float* xn, const float* scale, const int
     __syncthreads();
     for (int i = 0; i < n; i++) {
         const int b = list[i];
-        for (int k = threadIdx.x; k < D; k += blockDim.x) xn[b * D + k] = x[b * D + k] * red[i] * __ldg(scale + k);
+        for (int k = threadIdx.x; k < D; k += blockDim.x) xn[b * D + k] = x[b * D + k] * red[i] * scale[k];
     }
     __syncthreads();
+}
+
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
+// Start async copies of cached K/V rows [a0, a0+n) of one (sequence, KV
+// head) into the staging tile; row t is produced this step and is filled
+// from shared memory separately.
+__device__ __forceinline__ void att_issue(const float* kg, const float* vg, float* ks, float* vs,
+                                          int a0, int n, int t, int hd, int ldk) {
+    const int q4 = hd / 4;
+    for (int e = threadIdx.x; e < n * q4; e += blockDim.x) {
+        const int j = e / q4, c4 = (e % q4) * 4, pos = a0 + j;
+        if (pos == t) continue;
+        cp_async16(ks + j * ldk + c4, kg + (size_t)pos * hd + c4);
+        cp_async16(vs + j * ldk + c4, vg + (size_t)pos * hd + c4);
+    }
+}
+
+// 32 per-lane partial sums -> lane l ends with the complete sum of value l
+// (a transposed butterfly: 16+8+4+2+1 shuffles instead of 5 per value).
+__device__ __forceinline__ float transpose_reduce32(float (&v)[32]) {
+    const int lane = threadIdx.x & 31;
+#pragma unroll
+    for (int m = 16, n = 32; m >= 1; m >>= 1, n >>= 1) {
+        const bool upper = lane & m;
+#pragma unroll
+        for (int j = 0; j < n / 2; j++) {
+            const float send = upper ? v[j] : v[j + n / 2];
+            const float keep = upper ? v[j + n / 2] : v[j];
+            v[j] = keep + __shfl_xor_sync(0xffffffffu, send, m);
+        }
+    }
+    return v[0];
+}
+
+// Four shared-memory rows of length `len` against the activation rows of the
+// sequences in `list` (n <= kBCMax).  Lanes split each row in float4 chunks;
+// lane l returns the full dot product of row (l >> 3) with sequence
+// list[l & 7] (0 for slots past n).
+__device__ __forceinline__ float lc_gemv4(const float* r0, const float* r1, const float* r2,
+                                          const float* r3, int len, const float* xs, int ld,
+                                          const int* list, int n) {
+    const int lane = threadIdx.x & 31;
+    const float* xb[kBCMax];
+#pragma unroll
+    for (int i = 0; i < kBCMax; i++) xb[i] = xs + (i < n ? list[i] : 0) * ld;
+    float acc[32];
+#pragma unroll
+    for (int i = 0; i < 32; i++) acc[i] = 0.0f;
+    for (int k = lane * 4; k < len; k += 128) {
+        const float4 w0 = *reinterpret_cast<const float4*>(r0 + k);
+        const float4 w1 = *reinterpret_cast<const float4*>(r1 + k);
+        const float4 w2 = *reinterpret_cast<const float4*>(r2 + k);
+        const float4 w3 = *reinterpret_cast<const float4*>(r3 + k);
+#pragma unroll
+        for (int i = 0; i < kBCMax; i++) {
+            if (i < n) {
+                const float4 x = *reinterpret_cast<const float4*>(xb[i] + k);
+                acc[0 * 8 + i] += w0.x * x.x + w0.y * x.y + w0.z * x.z + w0.w * x.w;
+                acc[1 * 8 + i] += w1.x * x.x + w1.y * x.y + w1.z * x.z + w1.w * x.w;
+                acc[2 * 8 + i] += w2.x * x.x + w2.y * x.y + w2.z * x.z + w2.w * x.w;
+                acc[3 * 8 + i] += w3.x * x.x + w3.y * x.y + w3.z * x.z + w3.w * x.w;
+            }
+        }
+    }
+    return transpose_reduce32(acc);
 }
 
 // Dot of `nr` (<= 2) shared-memory rows of length `len` with the activation
@@ -218,13 +308,34 @@ __device__ __forceinline__ void lc_dot2(const float* r0, const float* r1, int le
         if (i < n) { acc[0][i] = warp_sum(acc[0][i]); acc[1][i] = warp_sum(acc[1][i]); }
 }
 
-// Store v at smem offset `off` (floats from base) in every CTA of the cluster;
-// lanes 0..cs-1 of the calling warp each take one destination.
-__device__ __forceinline__ void bcast(cg::cluster_group& cl, float* base, int off, float v, int cs) {
-    const int lane = threadIdx.x & 31;
-    for (int r = lane; r < cs; r += 32) {
-        float* dst = cl.map_shared_rank(base, r);
-        dst[off] = v;
+// Copy rows [r0, r1) of buf[b][ld] for the sequences in `list` from this
+// CTA's shared memory into the same place in every other CTA of the
+// cluster, as float4 stores (remote-store cost is per transaction, so 16-byte
+// chunks move four times the data of scalar stores for the same cost).
+// Caller: all threads, after the rows are written locally and a CTA barrier.
+__device__ __forceinline__ void push_rows(cg::cluster_group& cl, float* buf, int ld, int r0, int r1,
+                                          const int* list, int n, int cs, int crank) {
+    const int n4 = (r1 - r0) >> 2, per_rank = n * n4;
+    for (int e = threadIdx.x; e < per_rank * cs; e += blockDim.x) {
+        const int r = e / per_rank;
+        if (r == crank) continue;
+        const int w = e - r * per_rank, i = w / n4, c = w - i * n4;
+        const int off = list[i] * ld + r0 + 4 * c;
+        const float4 v = *reinterpret_cast<const float4*>(buf + off);
+        *reinterpret_cast<float4*>(cl.map_shared_rank(buf, r) + off) = v;
+    }
+}
+
+// Copy floats [off, off + len) (len % 4 == 0, off % 4 == 0) to every other CTA.
+__device__ __forceinline__ void push_block(cg::cluster_group& cl, float* buf, int off, int len, int cs,
+                                           int crank) {
+    const int n4 = len >> 2;
+    for (int e = threadIdx.x; e < n4 * cs; e += blockDim.x) {
+        const int r = e / n4;
+        if (r == crank) continue;
+        const int o = off + 4 * (e - r * n4);
+        *reinterpret_cast<float4*>(cl.map_shared_rank(buf, r) + o) =
+            *reinterpret_cast<const float4*>(buf + o);
     }
 }
 
@@ -233,9 +344,12 @@ __device__ __forceinline__ void bcast(cg::cluster_group& cl, float* base, int of
 // CTA; after the barrier all CTAs read the same flag, so they all leave at
 // the same barrier.  Flags alternate between two slots so that a flag meant
 // for the next barrier cannot be seen by a CTA still reading this one.
-__device__ bool lc_sync(cg::cluster_group& cl, LcState& S, int cs, const int* status) {
+// Failures are raised by the CTA that sees them (lc_fail), so no global
+// memory is read here.
+__device__ bool lc_sync(cg::cluster_group& cl, LcState& S, int cs) {
     const int slot = 36 + (S.epoch & 1);
-    if (threadIdx.x == 0 && ld_volatile_i32(status) != ST_OK)
+    __syncthreads();
+    if (threadIdx.x == 0 && S.ints[38])
         for (int r = 0; r < cs; r++) cl.map_shared_rank(S.ints, r)[slot] = 1;
     cl.sync();
     const bool ok = S.ints[slot] == 0;
@@ -256,48 +370,57 @@ __device__ bool lc_layer(const ClusterParams& cp, const CSlice& sl, LcState& S,
     const float* wu = wp + (size_t)(sl.p1 - sl.p0) * D;
     const float* wg = wu + (size_t)(sl.f1 - sl.f0) * D;
     const float* wd = wg + (size_t)(sl.f1 - sl.f0) * D;
+    const float* rms1 = w + slice_floats(sl, D, F);
+    const float* rms2 = rms1 + D;
 
-    // ---- QKV + RoPE + K/V append (generate.c:99-119)
-    lc_norm(S.x, S.xn, p.rms1 + (size_t)l * D, fl, nf, D, S.red);
-    for (int r = sl.q0 + 2 * warp; r < sl.q1; r += 2 * kWarps) {
-        float acc[2][kBCMax];
-        lc_dot2(wq + (size_t)(r - sl.q0) * D, wq + (size_t)(r + 1 - sl.q0) * D, D, S.xn, D, fl, nf, acc);
-        const int slot = r / hd, d = r % hd;
-        const bool rotate = slot < H + K;
-        float cs_ = 1.0f, sn = 0.0f;
-        if (rotate) {
-            const float2 rr = p.rope[(size_t)t * (hd / 2) + d / 2];
-            cs_ = rr.x; sn = rr.y;
-        }
-        for (int i = 0; i < nf; i++) {
-            const int b = fl[i];
-            float a = acc[0][i], z = acc[1][i];
-            if (rotate) {
-                const float a2 = a * cs_ - z * sn, z2 = a * sn + z * cs_;
-                a = a2; z = z2;
-            }
-            bcast(cl, S.qkv, b * Q + r, a, cs);
-            bcast(cl, S.qkv, b * Q + r + 1, z, cs);
-            if (slot >= H && lane == 31) {
-                const bool isk = slot < H + K;
-                const int g = isk ? slot - H : slot - H - K;
-                float* dst = (isk ? p.kc : p.vc) +
-                    ((((size_t)l * p.Bcap + b) * K + g) * p.cap + t) * hd + d;
-                dst[0] = a;
-                dst[1] = z;
-            }
-        }
-    }
-    __threadfence();   // K/V rows are read from global by other CTAs in later steps
-    if (!lc_sync(cl, S, cs, p.status)) return false;
-
-    // ---- attention, split over the cluster (generate.c:121-156)
+    // Attention geometry; the first tile of this CTA's first unit is fetched
+    // now so that its L2 latency overlaps the QKV phase.
     const int ns = cp.n_split;
     const int units = nf * K * ns;
-    const float scale = 1.0f / sqrtf((float)hd);
     const int ldk = hd + 4;
     float* ks = S.kv;
     float* vs = S.kv + cp.kv_tile * ldk;
+    if (crank < units) {
+        const int u = crank, s = u % ns, g = (u / ns) % K, b = fl[u / (ns * K)];
+        const int per = (t + 1 + ns - 1) / ns;
+        const int j0 = min(s * per, t + 1), j1 = min(j0 + per, t + 1);
+        const size_t cbase = (((size_t)l * p.Bcap + b) * K + g) * p.cap;
+        att_issue(p.kc + cbase * hd, p.vc + cbase * hd, ks, vs, j0, min(cp.kv_tile, j1 - j0), t, hd, ldk);
+    }
+
+    // ---- QKV + RoPE + K/V append (generate.c:99-119)
+    lc_norm(S.x, S.xn, rms1, fl, nf, D, S.red);
+    for (int r0 = sl.q0 + 4 * warp; r0 < sl.q1; r0 += 4 * kWarps) {
+        const float* w0 = wq + (size_t)(r0 - sl.q0) * D;
+        const float val = lc_gemv4(w0, w0 + D, w0 + 2 * D, w0 + 3 * D, D, S.xn, D, fl, nf);
+        // lane: row r0 + (lane >> 3), sequence slot lane & 7; the RoPE partner
+        // row (2p <-> 2p+1) sits in lane ^ 8
+        const float other = __shfl_xor_sync(0xffffffffu, val, 8);
+        const int r = r0 + (lane >> 3), i = lane & 7;
+        const int slot = r / hd, d = r % hd;
+        float out = val;
+        if (slot < H + K) {
+            const float2 rr = S.rope[d / 2];
+            out = (d & 1) ? other * rr.y + val * rr.x     // z' = a s + z c
+                          : val * rr.x - other * rr.y;    // a' = a c - z s
+        }
+        if (i < nf) {
+            const int b = fl[i];
+            S.qkv[b * Q + r] = out;
+            if (slot >= H) {
+                const bool isk = slot < H + K;
+                const int g = isk ? slot - H : slot - H - K;
+                (isk ? p.kc : p.vc)[((((size_t)l * p.Bcap + b) * K + g) * p.cap + t) * hd + d] = out;
+            }
+        }
+    }
+    __syncthreads();
+    push_rows(cl, S.qkv, Q, sl.q0, sl.q1, fl, nf, cs, crank);
+    __threadfence();   // K/V rows are read from global by other CTAs in later steps
+    if (!lc_sync(cl, S, cs)) return false;
+
+    // ---- attention, split over the cluster (generate.c:121-156)
+    const float scale = 1.0f / sqrtf((float)hd);
     for (int u = crank; u < units; u += cs) {
         const int s = u % ns, g = (u / ns) % K, b = fl[u / (ns * K)];
         const int nkeys = t + 1;
@@ -314,21 +437,17 @@ __device__ bool lc_layer(const ClusterParams& cp, const CSlice& sl, LcState& S,
         for (int a0 = j0; a0 < j1; a0 += cp.kv_tile) {
             const int n = min(cp.kv_tile, j1 - a0);
             __syncthreads();
-            // stage K/V rows [a0, a0+n); the row at t comes from this step's qkv
-            const int q4 = hd / 4;
-            for (int e = threadIdx.x; e < n * q4; e += blockDim.x) {
-                const int j = e / q4, c4 = (e % q4) * 4, pos = a0 + j;
-                float4 kv4, vv4;
-                if (pos == t) {
-                    kv4 = *reinterpret_cast<const float4*>(S.qkv + b * Q + D + g * hd + c4);
-                    vv4 = *reinterpret_cast<const float4*>(S.qkv + b * Q + D + p.kvd + g * hd + c4);
-                } else {
-                    kv4 = ldcg4(kg + (size_t)pos * hd + c4);
-                    vv4 = ldcg4(vg + (size_t)pos * hd + c4);
+            // stage K/V rows [a0, a0+n) (the first tile of the first unit is
+            // already in flight); the row at t comes from this step's qkv
+            if (!(u == crank && a0 == j0)) att_issue(kg, vg, ks, vs, a0, n, t, hd, ldk);
+            if (t >= a0 && t < a0 + n) {
+                const int j = t - a0;
+                for (int c = threadIdx.x; c < hd; c += blockDim.x) {
+                    ks[j * ldk + c] = S.qkv[b * Q + D + g * hd + c];
+                    vs[j * ldk + c] = S.qkv[b * Q + D + p.kvd + g * hd + c];
                 }
-                *reinterpret_cast<float4*>(ks + j * ldk + c4) = kv4;
-                *reinterpret_cast<float4*>(vs + j * ldk + c4) = vv4;
             }
+            cp_async_wait_all();
             __syncthreads();
             for (int e = threadIdx.x; e < G * n; e += blockDim.x) {
                 const int h = e / n, j = e % n;
@@ -371,81 +490,81 @@ __device__ bool lc_layer(const ClusterParams& cp, const CSlice& sl, LcState& S,
             }
         }
         __syncthreads();
-        // partial (o, m, l) of heads g*G.. to every CTA
-        const int pw = hd + 2;
+        // partial (o, m, l) of the unit's G heads: one contiguous block of
+        // G rows of pw = hd + 4 floats, written locally and pushed
+        const int pw = hd + 4;
+        const int blk = (((b * K + g) * ns + s) * G) * pw;
         for (int i = threadIdx.x; i < G * pw; i += blockDim.x) {
             const int h = i / pw, e = i % pw;
-            const float v = e < hd ? o[h * hd + e] : S.red[2 * h + (e - hd)];
-            const int off = ((b * H + g * G + h) * ns + s) * pw + e;
-            for (int r = 0; r < cs; r++) {
-                float* dst = cl.map_shared_rank(S.attp, r);
-                dst[off] = v;
-            }
+            S.attp[blk + i] = e < hd ? o[h * hd + e] : (e < hd + 2 ? S.red[2 * h + (e - hd)] : 0.0f);
         }
+        __syncthreads();
+        push_block(cl, S.attp, blk, G * pw, cs, crank);
         __syncthreads();   // o and red are reused by this CTA's next unit
     }
-    if (!lc_sync(cl, S, cs, p.status)) return false;
+    if (!lc_sync(cl, S, cs)) return false;
 
     // ---- combine splits (every CTA), then PROJ + residual (generate.c:158-163)
     {
-        const int pw = hd + 2;
+        const int pw = hd + 4;
         for (int e = threadIdx.x; e < nf * H * hd; e += blockDim.x) {
             const int i = e / (H * hd), h = (e / hd) % H, d = e % hd, b = fl[i];
-            const float* pp = S.attp + (size_t)(b * H + h) * ns * pw;
+            const int g = h / G, hh = h % G;
+            const float* pp = S.attp + ((size_t)((b * K + g) * ns) * G + hh) * pw;  // split stride G*pw
             float M = -INFINITY;
-            for (int s2 = 0; s2 < ns; s2++) M = fmaxf(M, pp[s2 * pw + hd]);
+            for (int s2 = 0; s2 < ns; s2++) M = fmaxf(M, pp[s2 * G * pw + hd]);
             float num = 0.0f, den = 0.0f;
             for (int s2 = 0; s2 < ns; s2++) {
-                const float ls = pp[s2 * pw + hd + 1];
+                const float* q2 = pp + s2 * G * pw;
+                const float ls = q2[hd + 1];
                 if (ls > 0.0f) {
-                    const float wgt = expf(pp[s2 * pw + hd] - M);
+                    const float wgt = expf(q2[hd] - M);
                     den += wgt * ls;
-                    num += wgt * pp[s2 * pw + d];
+                    num += wgt * q2[d];
                 }
             }
             S.att[b * D + h * hd + d] = num / den;
         }
         __syncthreads();
     }
-    for (int r = sl.p0 + 2 * warp; r < sl.p1; r += 2 * kWarps) {
-        const bool has1 = r + 1 < sl.p1;
-        float acc[2][kBCMax];
-        lc_dot2(wp + (size_t)(r - sl.p0) * D, wp + (size_t)((has1 ? r + 1 : r) - sl.p0) * D, D, S.att,
-                D, fl, nf, acc);
-        for (int i = 0; i < nf; i++) {
-            const int b = fl[i];
-            bcast(cl, S.x, b * D + r, S.x[b * D + r] + acc[0][i], cs);
-            if (has1) bcast(cl, S.x, b * D + r + 1, S.x[b * D + r + 1] + acc[1][i], cs);
-        }
+    for (int r0 = sl.p0 + 4 * warp; r0 < sl.p1; r0 += 4 * kWarps) {
+        const float* w0 = wp + (size_t)(r0 - sl.p0) * D;
+        const float val = lc_gemv4(w0, w0 + D, w0 + 2 * D, w0 + 3 * D, D, S.att, D, fl, nf);
+        const int i = lane & 7;
+        if (i < nf) S.x[fl[i] * D + r0 + (lane >> 3)] += val;
     }
-    if (!lc_sync(cl, S, cs, p.status)) return false;
+    __syncthreads();
+    push_rows(cl, S.x, D, sl.p0, sl.p1, fl, nf, cs, crank);
+    if (!lc_sync(cl, S, cs)) return false;
 
     // ---- FFN up/gate + SwiGLU (generate.c:165-179)
-    lc_norm(S.x, S.xn, p.rms2 + (size_t)l * D, fl, nf, D, S.red);
-    for (int r = sl.f0 + warp; r < sl.f1; r += kWarps) {
-        float acc[2][kBCMax];
-        lc_dot2(wu + (size_t)(r - sl.f0) * D, wg + (size_t)(r - sl.f0) * D, D, S.xn, D, fl, nf, acc);
-        for (int i = 0; i < nf; i++) {
-            const float up = acc[0][i], g = acc[1][i];
-            const float sv = g / (1.0f + expf(-g));
-            bcast(cl, S.f, fl[i] * F + r, sv * up, cs);
+    lc_norm(S.x, S.xn, rms2, fl, nf, D, S.red);
+    for (int j = sl.f0 + 2 * warp; j < sl.f1; j += 2 * kWarps) {
+        // rows: up j, up j+1, gate j, gate j+1 -> the gate of lane's up row is in lane ^ 16
+        const float* u0 = wu + (size_t)(j - sl.f0) * D;
+        const float* g0 = wg + (size_t)(j - sl.f0) * D;
+        const float val = lc_gemv4(u0, u0 + D, g0, g0 + D, D, S.xn, D, fl, nf);
+        const float gate = __shfl_xor_sync(0xffffffffu, val, 16);
+        const int i = lane & 7;
+        if (lane < 16 && i < nf) {
+            const float sv = gate / (1.0f + expf(-gate));
+            S.f[fl[i] * F + j + (lane >> 3)] = sv * val;
         }
     }
-    if (!lc_sync(cl, S, cs, p.status)) return false;
+    __syncthreads();
+    push_rows(cl, S.f, F, sl.f0, sl.f1, fl, nf, cs, crank);
+    if (!lc_sync(cl, S, cs)) return false;
 
     // ---- down + residual (generate.c:181-184)
-    for (int r = sl.p0 + 2 * warp; r < sl.p1; r += 2 * kWarps) {
-        const bool has1 = r + 1 < sl.p1;
-        float acc[2][kBCMax];
-        lc_dot2(wd + (size_t)(r - sl.p0) * F, wd + (size_t)((has1 ? r + 1 : r) - sl.p0) * F, F, S.f, F,
-                fl, nf, acc);
-        for (int i = 0; i < nf; i++) {
-            const int b = fl[i];
-            bcast(cl, S.x, b * D + r, S.x[b * D + r] + acc[0][i], cs);
-            if (has1) bcast(cl, S.x, b * D + r + 1, S.x[b * D + r + 1] + acc[1][i], cs);
-        }
+    for (int r0 = sl.p0 + 4 * warp; r0 < sl.p1; r0 += 4 * kWarps) {
+        const float* w0 = wd + (size_t)(r0 - sl.p0) * F;
+        const float val = lc_gemv4(w0, w0 + F, w0 + 2 * F, w0 + 3 * F, F, S.f, F, fl, nf);
+        const int i = lane & 7;
+        if (i < nf) S.x[fl[i] * D + r0 + (lane >> 3)] += val;
     }
-    return lc_sync(cl, S, cs, p.status);
+    __syncthreads();
+    push_rows(cl, S.x, D, sl.p0, sl.p1, fl, nf, cs, crank);
+    return lc_sync(cl, S, cs);
 }
 
 // Greedy choice from the head partials for sequence b (generate.c:469-478,
@@ -499,15 +618,27 @@ __device__ void lc_main(const ClusterParams& cp, unsigned char* smem, cg::cluste
     S.sc = reinterpret_cast<float*>(smem + cp.off_sc);
     S.kv = reinterpret_cast<float*>(smem + cp.off_kv);
     S.stage = reinterpret_cast<float*>(smem + cp.off_stage);
+    S.rmsf = reinterpret_cast<float*>(smem + cp.off_rmsf);
+    S.rope = reinterpret_cast<float2*>(smem + cp.off_rope);
+    S.seq = reinterpret_cast<SeqMirror*>(smem + 576);
     const CSlice sl = cluster_slice(crank, cp.cs, p.Q, p.D, p.F);
     const int nhc = (cp.n_clusters - 1) * cp.cs;
     int* fl = S.ints;        // [16]
     int* hl = S.ints + 16;   // [16]
+    int* toks = S.ints + 40; // [8] ids fed at this step
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kStages; s++) mbar_init(&S.bar[s], 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        S.ints[38] = 0;
     }
+    for (int b = threadIdx.x; b < p.B; b += blockDim.x) {
+        const SeqState& g = p.seq[b];
+        SeqMirror& m = S.seq[b];
+        m.P = g.P; m.nnew = g.nnew; m.gen = g.gen; m.done = g.done; m.tok = g.tok;
+        m.result = g.result; m.final_pos = g.final_pos; m.rng = g.rng;
+    }
+    for (int k = threadIdx.x; k < p.D; k += blockDim.x) S.rmsf[k] = __ldg(p.rmsf + k);
     __syncthreads();
     // prologue: prompts into the history, penalty counts, first bans (CTA b)
     for (int b = crank; b < p.B; b += cp.cs) {
@@ -537,18 +668,16 @@ __device__ void lc_main(const ClusterParams& cp, unsigned char* smem, cg::cluste
     S.epoch = 0;
     if (threadIdx.x == 0) { S.ints[36] = 0; S.ints[37] = 0; }
     cl.sync();   // error slots are zero everywhere before anyone can set one
-    bool ok = lc_sync(cl, S, cp.cs, p.status);
+    bool ok = lc_sync(cl, S, cp.cs);
 
     for (int t = 0; ok && t < p.T; t++) {
         if (threadIdx.x == 0) {
             int nf = 0, nh = 0;
             for (int b = 0; b < p.B; b++) {
-                const SeqState* st = p.seq + b;
-                if (ld_volatile_i32(&st->done)) continue;
-                const int P = ld_volatile_i32(&st->P), nnew = ld_volatile_i32(&st->nnew);
-                if (t >= P + nnew - 1) continue;
+                const SeqMirror& m = S.seq[b];
+                if (m.done || t >= m.P + m.nnew - 1) continue;
                 fl[nf++] = b;
-                if (t >= P - 1) hl[nh++] = b;
+                if (t >= m.P - 1) hl[nh++] = b;
             }
             S.ints[32] = nf;
             S.ints[33] = nh;
@@ -557,17 +686,24 @@ __device__ void lc_main(const ClusterParams& cp, unsigned char* smem, cg::cluste
         __syncthreads();
         const int nf = S.ints[32], nh = S.ints[33];
         if (nf == 0) break;
-        // embedding of the token at position t (generate.c:86-88)
-        for (int i = 0; i < nf; i++) {
-            const int b = fl[i];
-            const SeqState* st = p.seq + b;
-            const int P = ld_volatile_i32(&st->P);
-            int tok = t < P ? (int)p.prompts[(size_t)b * p.prompt_stride + t] : ld_volatile_i32(&st->tok);
+        // ids fed at position t and this position's RoPE row, in one round trip
+        if (threadIdx.x < nf) {
+            const int b = fl[threadIdx.x];
+            const SeqMirror& m = S.seq[b];
+            int tok = t < m.P ? (int)p.prompts[(size_t)b * p.prompt_stride + t] : m.tok;
             if (tok < 0 || tok >= p.V) {
-                if (threadIdx.x == 0) atomicMax(p.status, (int)ST_DEVICE);
+                lc_fail(S, p.status, ST_DEVICE);
                 tok = 0;
             }
-            for (int k = threadIdx.x; k < p.D; k += blockDim.x) S.x[b * p.D + k] = __ldg(p.tok_emb + (size_t)tok * p.D + k);
+            toks[threadIdx.x] = tok;
+        }
+        for (int j = threadIdx.x; j < p.hd / 2; j += blockDim.x)
+            S.rope[j] = p.rope[(size_t)t * (p.hd / 2) + j];
+        __syncthreads();
+        // embedding of the token at position t (generate.c:86-88)
+        for (int e = threadIdx.x; e < nf * p.D; e += blockDim.x) {
+            const int i = e / p.D, k = e % p.D;
+            S.x[fl[i] * p.D + k] = __ldg(p.tok_emb + (size_t)toks[i] * p.D + k);
         }
         __syncthreads();
         for (int l = 0; ok && l < p.L; l++) {
@@ -577,7 +713,7 @@ __device__ void lc_main(const ClusterParams& cp, unsigned char* smem, cg::cluste
             // shared memory) so that every CTA meets the same cluster
             // barriers, and the next barrier turns the status into a
             // cluster-wide exit.
-            if (!mbar_wait(&S.bar[s], parity, p.timeout_ns)) atomicMax(p.status, (int)ST_TIMEOUT);
+            if (!mbar_wait(&S.bar[s], parity, p.timeout_ns)) lc_fail(S, p.status, ST_TIMEOUT);
             ok = lc_layer(cp, sl, S, cl, crank, l, t, fl, nf, S.stage + (size_t)s * cp.stage_floats);
             layer_count++;
             // every thread of this CTA is past the stage: refill it kStages layers ahead
@@ -590,7 +726,7 @@ __device__ void lc_main(const ClusterParams& cp, unsigned char* smem, cg::cluste
         if (nh == 0) continue;
 
         // ---- hand the final norm to the head CTAs (generate.c:187-191)
-        lc_norm(S.x, S.xn, p.rmsf, hl, nh, p.D, S.red);
+        lc_norm(S.x, S.xn, S.rmsf, hl, nh, p.D, S.red);
         {
             const int cols = (p.D + cp.cs - 1) / cp.cs, c0 = crank * cols, c1 = min(p.D, c0 + cols);
             for (int e = threadIdx.x; e < nh * (c1 - c0); e += blockDim.x) {
@@ -601,12 +737,12 @@ __device__ void lc_main(const ClusterParams& cp, unsigned char* smem, cg::cluste
                 for (int b = threadIdx.x; b < p.B; b += blockDim.x) {
                     int g = -1;
                     for (int i = 0; i < nh; i++)
-                        if (hl[i] == b) g = ld_volatile_i32(&p.seq[b].gen);
+                        if (hl[i] == b) g = S.seq[b].gen;
                     cp.hgen[b] = g;
                 }
         }
         __threadfence();
-        ok = lc_sync(cl, S, cp.cs, p.status);
+        ok = lc_sync(cl, S, cp.cs);
         if (!ok) break;
         heads++;
         if (crank == 0) {
@@ -617,7 +753,7 @@ __device__ void lc_main(const ClusterParams& cp, unsigned char* smem, cg::cluste
                 const unsigned long long t0 = globaltimer_ns();
                 while ((int)(ld_acquire_u32(cp.hdone) - target) < 0) {
                     if (globaltimer_ns() - t0 > p.timeout_ns) {
-                        atomicMax(p.status, (int)ST_TIMEOUT);
+                        lc_fail(S, p.status, ST_TIMEOUT);
                         break;
                     }
                 }
@@ -629,49 +765,62 @@ __device__ void lc_main(const ClusterParams& cp, unsigned char* smem, cg::cluste
                 bool draws;
                 lc_choose(cp, b, nhc, S.red, S.ints, id, draws);
                 if (threadIdx.x == 0) {
-                    SeqState* st = p.seq + b;
-                    unsigned long long rng = st->rng;
-                    if (draws) (void)rng_f32(rng);
-                    const int P = st->P, g = st->gen, nnew = st->nnew;
+                    SeqMirror& m = S.seq[b];
+                    if (draws) (void)rng_f32(m.rng);
+                    const int P = m.P, g = m.gen, nnew = m.nnew;
                     uint16_t* out = p.out_ids + (size_t)b * p.out_cap;
                     out[P + g] = (uint16_t)id;
                     if (p.s.pen_active) p.counts[(size_t)b * p.V + id] += 1u;
                     const int generated = g + 1;
-                    st->gen = generated;
-                    st->rng = rng;
+                    m.gen = generated;
                     bool stop = false;
                     if (p.s.stop_len > 0 && generated >= p.s.min_new && generated >= p.s.stop_len) {
                         stop = true;
                         const int s0 = P + generated - p.s.stop_len;
                         for (int k = 0; k < p.s.stop_len; k++)
-                            if (out[s0 + k] != p.s.stop_ids[k]) { stop = false; break; }
+                            if (ld_u16_cg(out + s0 + k) != (int)p.s.stop_ids[k]) { stop = false; break; }
                     }
                     if (stop) {
-                        st->result = P + generated - p.s.stop_len;
-                        st->final_pos = P + g;
-                        st->done = 1;
+                        m.result = P + generated - p.s.stop_len;
+                        m.final_pos = P + g;
+                        m.done = 1;
                     } else if (generated >= nnew) {
-                        st->result = P + nnew;
-                        st->final_pos = P + nnew;
-                        st->done = 1;
+                        m.result = P + nnew;
+                        m.final_pos = P + nnew;
+                        m.done = 1;
                     } else {
-                        st->tok = id;
+                        m.tok = id;
                     }
-                    S.ints[34] = st->done;
+                    S.ints[34] = m.done;
+                    S.ints[35] = m.gen;
                 }
                 __syncthreads();
-                if (p.s.ngram > 0 && !S.ints[34])
-                    compute_bans(p, b, ld_volatile_i32(&p.seq[b].P) + ld_volatile_i32(&p.seq[b].gen));
+                if (p.s.ngram > 0 && !S.ints[34]) compute_bans(p, b, S.seq[b].P + S.ints[35]);
                 __syncthreads();
+            }
+            // the other layer CTAs get the updated table before the barrier
+            const int words = p.B * (int)(sizeof(SeqMirror) / 4);
+            for (int e = threadIdx.x; e < words * cp.cs; e += blockDim.x) {
+                const int r = e / words, w = e % words;
+                if (r == 0) continue;
+                int* dst = reinterpret_cast<int*>(cl.map_shared_rank(S.seq, r));
+                dst[w] = reinterpret_cast<const int*>(S.seq)[w];
             }
             __threadfence();
         }
-        ok = lc_sync(cl, S, cp.cs, p.status);
+        ok = lc_sync(cl, S, cp.cs);
     }
-    // release the head CTAs and drain this CTA's bulk copies
-    if (crank == 0 && threadIdx.x == 0) {
+    // release the head CTAs, publish the sequence table, drain bulk copies
+    if (crank == 0) {
+        for (int b = threadIdx.x; b < p.B; b += blockDim.x) {
+            const SeqMirror& m = S.seq[b];
+            SeqState& g = p.seq[b];
+            g.gen = m.gen; g.done = m.done; g.tok = m.tok; g.result = m.result;
+            g.final_pos = m.final_pos; g.rng = m.rng;
+        }
         __threadfence();
-        st_release_u32(cp.go, kExit);
+        __syncthreads();
+        if (threadIdx.x == 0) st_release_u32(cp.go, kExit);
     }
     if (threadIdx.x == 0 && crank == 0 && p.stamps) p.stamps[p.T] = globaltimer_ns();
     for (unsigned k = layer_count; k < issued; k++) {
@@ -725,23 +874,25 @@ __device__ void hc_main(const ClusterParams& cp, unsigned char* smem, int hc) {
                 }
             }
             ints[0] = (int)g;
-            int nh = 0;
-            if (g != kExit)
-                for (int b = 0; b < p.B; b++)
-                    if (__ldcg(cp.hgen + b) >= 0) ints[8 + nh++] = b;
-            ints[1] = nh;
         }
         __syncthreads();
         const unsigned g = (unsigned)ints[0];
         if (g == kExit) break;
         seen = g;
-        const int nh = ints[1];
-        const int* hl = ints + 8;
-        for (int e = threadIdx.x; e < nh * D; e += blockDim.x) {
-            const int i = e / D, k = e % D;
-            xs[i * D + k] = ldcg(cp.xfin + (size_t)hl[i] * D + k);
+        // which sequences need logits, and all normalised rows, in one round trip
+        int* hg = ints + 16;   // [kBCMax] sampler step per sequence, -1 = none
+        for (int b = threadIdx.x; b < p.B; b += blockDim.x) hg[b] = __ldcg(cp.hgen + b);
+        for (int e = threadIdx.x; e < p.B * D; e += blockDim.x) xs[e] = ldcg(cp.xfin + e);
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            int nh = 0;
+            for (int b = 0; b < p.B; b++)
+                if (hg[b] >= 0) ints[8 + nh++] = b;
+            ints[1] = nh;
         }
         __syncthreads();
+        const int nh = ints[1];
+        const int* hl = ints + 8;
         // thread per row: full dot products from the resident slice
         float bv[2][kBCMax];
         int bi[2][kBCMax];
@@ -750,26 +901,36 @@ __device__ void hc_main(const ClusterParams& cp, unsigned char* smem, int hc) {
             bv[0][i] = bv[1][i] = -INFINITY;
             bi[0][i] = bi[1][i] = 0x7fffffff;
         }
+        const float* xb[kBCMax];
+#pragma unroll
+        for (int i = 0; i < kBCMax; i++) xb[i] = xs + (i < nh ? hl[i] : 0) * D;
         for (int r = threadIdx.x; r < nr; r += blockDim.x) {
-            const float* er = emb + (size_t)r * cp.hc_ld;
+            const float* __restrict__ er = emb + (size_t)r * cp.hc_ld;
             float acc[kBCMax];
 #pragma unroll
             for (int i = 0; i < kBCMax; i++) acc[i] = 0.0f;
+#pragma unroll 4
             for (int k = 0; k < D; k += 4) {
                 const float4 w = *reinterpret_cast<const float4*>(er + k);
 #pragma unroll
                 for (int i = 0; i < kBCMax; i++)
                     if (i < nh) {
-                        const float4 xv = *reinterpret_cast<const float4*>(xs + i * D + k);
-                        acc[i] += w.x * xv.x + w.y * xv.y + w.z * xv.z + w.w * xv.w;
+                        const float4 xv = *reinterpret_cast<const float4*>(xb[i] + k);
+                        acc[i] = fmaf(w.x, xv.x, acc[i]);
+                        acc[i] = fmaf(w.y, xv.y, acc[i]);
+                        acc[i] = fmaf(w.z, xv.z, acc[i]);
+                        acc[i] = fmaf(w.w, xv.w, acc[i]);
                     }
             }
             const int v = r0 + r;
-            for (int i = 0; i < nh; i++) {
+            // static indices only: the per-sequence state stays in registers
+#pragma unroll
+            for (int i = 0; i < kBCMax; i++) {
+                if (i >= nh) continue;
                 const int b = hl[i];
                 const float lg = v < 4 ? -INFINITY : acc[i];
                 if (p.trace) {
-                    const int gi = __ldcg(cp.hgen + b);
+                    const int gi = hg[b];
                     if (gi < p.trace_steps) p.trace[((size_t)b * p.trace_steps + gi) * p.V + v] = lg;
                 }
                 const unsigned cnt = p.s.pen_active ? __ldcg(p.counts + (size_t)b * p.V + v) : 0u;
@@ -783,7 +944,10 @@ __device__ void hc_main(const ClusterParams& cp, unsigned char* smem, int hc) {
                 }
             }
         }
-        for (int i = 0; i < nh; i++) {
+#pragma unroll
+        for (int i = 0; i < kBCMax; i++) {
+            if (i >= nh) continue;
+#pragma unroll
             for (int k = 0; k < 2; k++) {
                 float v = bv[k][i];
                 int id = bi[k][i];

@@ -197,7 +197,8 @@ bool plan_cluster(mc_session* s, const cudaDeviceProp& prop) {
         mc::ClusterParams cp{};
         cp.cs = cs;
         const mc::CSlice s0 = mc::cluster_slice(0, cs, m->Q, m->D, m->F);
-        const size_t stage_f = align_up(mc::slice_floats(s0, m->D, m->F), 32);
+        // weight slice plus this layer's rms1 / rms2 scales
+        const size_t stage_f = align_up(mc::slice_floats(s0, m->D, m->F) + 2 * (size_t)m->D, 32);
         if (stage_f * 4 >= (1u << 20)) continue;           // mbarrier tx-count limit
         int attp_rows = 0;                                   // max over B of B * splits(B)
         for (int B = 1; B <= B8; B++) attp_rows = std::max(attp_rows, B * std::max(1, cs / (B * m->K)));
@@ -211,9 +212,11 @@ bool plan_cluster(mc_session* s, const cudaDeviceProp& prop) {
         cp.off_x = take((size_t)B8 * m->D, 16);
         cp.off_xn = take((size_t)B8 * m->D, 16);
         cp.off_qkv = take((size_t)B8 * m->Q, 16);
-        cp.off_attp = take((size_t)attp_rows * m->H * (m->hd + 2), 16);
+        cp.off_attp = take((size_t)attp_rows * m->H * (m->hd + 4), 16);
         cp.off_att = take((size_t)B8 * m->D, 16);
         cp.off_f = take((size_t)B8 * m->F, 16);
+        cp.off_rmsf = take((size_t)m->D, 16);
+        cp.off_rope = take((size_t)std::max(m->hd, 2), 16);
         const size_t fixed = off;
         int tile = 128;
         for (; tile >= 16; tile /= 2) {
