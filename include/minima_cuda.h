@@ -152,6 +152,12 @@ mc_status mc_forward_logits(mc_session* session, int batch, const uint16_t* toke
    measured with CUDA events on the launching stream (milliseconds). */
 mc_status mc_last_kernel_ms(mc_session* session, float* ms);
 
+/* Prompt positions the last mc_generate ran as one batched prefill (all
+   sequences' positions [0, shortest prompt - 1), no logits computed for
+   them) and its device time in milliseconds (included in
+   mc_last_kernel_ms).  The token loop starts at that position. */
+mc_status mc_last_prefill(mc_session* session, int* positions, float* ms);
+
 /* Number of kernels the last call launched on the device. */
 mc_status mc_last_launch_count(mc_session* session, int* launches);
 

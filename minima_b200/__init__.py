@@ -30,7 +30,7 @@ LIB_HOST = os.path.join(PKG, "libminima_host.so")
 CUDA_SYMBOLS = ("mc_init", "mc_model_create", "mc_model_update", "mc_model_destroy",
                 "mc_session_create", "mc_session_destroy", "mc_generate", "mc_forward_logits",
                 "mc_last_kernel_ms", "mc_last_launch_count", "mc_last_step_times",
-                "mc_last_kernel_name", "mc_session_stream", "mc_last_error")
+                "mc_last_kernel_name", "mc_last_prefill", "mc_session_stream", "mc_last_error")
 GENERATE_SYMBOLS = ("kvcache_init", "kvcache_reset", "generation_check_kv_cache",
                     "generation_inspect_next_tokens", "generate", "generate_with_options",
                     "generate_ex", "generate_batch_with_options", "minima_cuda_select_device",
@@ -203,6 +203,7 @@ def _declare(host, cuda, gen):
     cuda.mc_last_launch_count.argtypes = [vp, i32p]
     cuda.mc_last_step_times.argtypes = [vp, u64p, C.c_int, i32p]
     cuda.mc_session_stream.argtypes = [vp, C.POINTER(vp)]
+    cuda.mc_last_prefill.argtypes = [vp, i32p, _f32p]
     cuda.mc_last_kernel_name.restype = C.c_char_p
     cuda.mc_last_kernel_name.argtypes = [vp]
     cuda.mc_last_error.restype = C.c_char_p
@@ -478,6 +479,12 @@ class Session:
         _check(libs()[1].mc_last_step_times(self.h, buf.ctypes.data_as(C.POINTER(C.c_uint64)),
                                             cap, C.byref(n)), "mc_last_step_times")
         return buf[:n.value]
+
+    def last_prefill(self):
+        """(positions prefilled in one batch, prefill device ms) of the last call."""
+        n, ms = C.c_int(), C.c_float()
+        _check(libs()[1].mc_last_prefill(self.h, C.byref(n), C.byref(ms)), "mc_last_prefill")
+        return n.value, ms.value
 
     def last_kernel_name(self) -> str:
         return libs()[1].mc_last_kernel_name(self.h).decode()

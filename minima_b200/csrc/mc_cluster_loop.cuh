@@ -670,7 +670,7 @@ __device__ void lc_main(const ClusterParams& cp, unsigned char* smem, cg::cluste
     cl.sync();   // error slots are zero everywhere before anyone can set one
     bool ok = lc_sync(cl, S, cp.cs);
 
-    for (int t = 0; ok && t < p.T; t++) {
+    for (int t = p.t0; ok && t < p.T; t++) {
         if (threadIdx.x == 0) {
             int nf = 0, nh = 0;
             for (int b = 0; b < p.B; b++) {

@@ -1,0 +1,277 @@
+// mc_prefill.cuh — batched prefill of prompt positions for sm_100a.
+//
+// generate_with_options feeds the prompt one position at a time
+// (generate.c:575-578); every position's forward is independent of the
+// sampler, so positions [0, Pf) of all sequences (Pf = shortest prompt - 1)
+// run here as one causal batched forward (the arithmetic of model_forward,
+// forward.c:176-274, restricted to the layers) on M = B * Pf rows:
+//   norm -> QKV GEMM (+RoPE, K/V into the cache) -> causal attention ->
+//   proj GEMM (+residual) -> norm -> up/gate GEMM (+SwiGLU) -> down GEMM
+//   (+residual)
+// The tied lm_head is not applied: no logits of those positions are read.
+// The token loop then continues at position Pf.  GEMMs are fp32 on CUDA
+// cores (64x64 tiles, 4x4 per thread, k-major shared tiles).
+#pragma once
+
+#include "mc_device.cuh"
+
+namespace mc {
+
+struct PrefillArgs {
+    int V, D, L, H, K, hd, kvd, Q, F, G;
+    int B, Bcap, cap;          // sequences, cache batch stride, cache capacity
+    int c0, c1;                // positions of this chunk
+    int chunk;                 // rows per sequence in the work buffers (>= c1 - c0)
+    const uint16_t* prompts;
+    int prompt_stride;
+    const float2* rope;
+    float* kc;
+    float* vc;
+    float* X;                  // [B*chunk][D] residual
+    float* XN;                 // [B*chunk][D]
+    float* QB;                 // [B*chunk][D] rotated queries
+    float* ATT;                // [B*chunk][D]
+    float* FH;                 // [B*chunk][F]
+    int* status;
+};
+
+__device__ __forceinline__ int pf_rows(const PrefillArgs& a) { return a.B * (a.c1 - a.c0); }
+// row m <-> (sequence b, position t)
+__device__ __forceinline__ void pf_row(const PrefillArgs& a, int m, int& b, int& t) {
+    const int n = a.c1 - a.c0;
+    b = m / n;
+    t = a.c0 + m % n;
+}
+
+// X = embedding (layer 0 only), XN = rmsnorm(X, scale) (generate.c:57-63,
+// 86-88); one warp per row.
+template <typename WT>
+__global__ void __launch_bounds__(256) pf_norm_kernel(PrefillArgs a, const WT* tok_emb,
+                                                      const float* scale, int embed) {
+    const int lane = threadIdx.x & 31;
+    const int m = blockIdx.x * 8 + (threadIdx.x >> 5);
+    if (m >= pf_rows(a)) return;
+    int b, t;
+    pf_row(a, m, b, t);
+    float* x = a.X + (size_t)m * a.D;
+    if (embed) {
+        int tok = a.prompts[(size_t)b * a.prompt_stride + t];
+        if (tok >= a.V) {
+            if (lane == 0) atomicMax(a.status, (int)ST_DEVICE);
+            tok = 0;
+        }
+        for (int k = lane; k < a.D; k += 32) x[k] = wload1(tok_emb + (size_t)tok * a.D + k);
+        __syncwarp();
+    }
+    float ss = 0.0f;
+    for (int k = lane; k < a.D; k += 32) ss += x[k] * x[k];
+    ss = warp_sum(ss);
+    const float inv = 1.0f / sqrtf(ss / (float)a.D + 1e-5f);
+    for (int k = lane; k < a.D; k += 32) a.XN[(size_t)m * a.D + k] = x[k] * inv * scale[k];
+}
+
+enum PfEpi { EPI_QKV = 0, EPI_RESID = 1, EPI_SWIGLU = 2 };
+
+constexpr int GBM = 64, GBN = 64, GBK = 32;
+
+// C[M][N] = A[M][K] . W[N][K]^T with a fused epilogue.  For EPI_SWIGLU, W2 is
+// the gate matrix and the output is silu(A.W2) * (A.W).  K % 4 == 0.
+template <typename WT, int EPI>
+__global__ void __launch_bounds__(256, 1) pf_gemm_kernel(PrefillArgs a, const float* A, int M, int N,
+                                                      int Kd, const WT* W, const WT* W2, float* C,
+                                                      int ldc, int layer) {
+    constexpr int DUAL = EPI == EPI_SWIGLU ? 2 : 1;
+    __shared__ __align__(16) float As[GBK][GBM + 4];
+    __shared__ __align__(16) float Ws[DUAL][GBK][GBN + 4];
+    const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
+    const int m0 = blockIdx.y * GBM, n0 = blockIdx.x * GBN;
+    float acc[DUAL][4][4];
+#pragma unroll
+    for (int d = 0; d < DUAL; d++)
+#pragma unroll
+        for (int i = 0; i < 4; i++)
+#pragma unroll
+            for (int j = 0; j < 4; j++) acc[d][i][j] = 0.0f;
+    for (int k0 = 0; k0 < Kd; k0 += GBK) {
+        // tiles: 64 rows x 32 k = 512 float4, two per thread, stored k-major
+        for (int e = threadIdx.x; e < GBM * GBK / 4; e += 256) {
+            const int r = e / (GBK / 4), kq = (e % (GBK / 4)) * 4;
+            const int gm = m0 + r, gk = k0 + kq;
+            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (gm < M && gk < Kd) v = *reinterpret_cast<const float4*>(A + (size_t)gm * Kd + gk);
+            As[kq + 0][r] = v.x; As[kq + 1][r] = v.y; As[kq + 2][r] = v.z; As[kq + 3][r] = v.w;
+        }
+#pragma unroll
+        for (int d = 0; d < DUAL; d++) {
+            const WT* Wd = d == 0 ? W : W2;
+            for (int e = threadIdx.x; e < GBN * GBK / 4; e += 256) {
+                const int r = e / (GBK / 4), kq = (e % (GBK / 4)) * 4;
+                const int gn = n0 + r, gk = k0 + kq;
+                float w4[4] = {0.f, 0.f, 0.f, 0.f};
+                if (gn < N && gk < Kd) {
+                    const WT* src = Wd + (size_t)gn * Kd + gk;
+#pragma unroll
+                    for (int q = 0; q < 4; q++) w4[q] = wload1(src + q);
+                }
+#pragma unroll
+                for (int q = 0; q < 4; q++) Ws[d][kq + q][r] = w4[q];
+            }
+        }
+        __syncthreads();
+#pragma unroll 8
+        for (int kk = 0; kk < GBK; kk++) {
+            const float4 av = *reinterpret_cast<const float4*>(&As[kk][ty * 4]);
+            const float ar[4] = {av.x, av.y, av.z, av.w};
+#pragma unroll
+            for (int d = 0; d < DUAL; d++) {
+                const float4 wv = *reinterpret_cast<const float4*>(&Ws[d][kk][tx * 4]);
+                const float wr[4] = {wv.x, wv.y, wv.z, wv.w};
+#pragma unroll
+                for (int i = 0; i < 4; i++)
+#pragma unroll
+                    for (int j = 0; j < 4; j++) acc[d][i][j] = fmaf(ar[i], wr[j], acc[d][i][j]);
+            }
+        }
+        __syncthreads();
+    }
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+        const int m = m0 + ty * 4 + i;
+        if (m >= M) continue;
+        if constexpr (EPI == EPI_QKV) {
+            int b, t;
+            pf_row(a, m, b, t);
+#pragma unroll
+            for (int j = 0; j < 4; j += 2) {
+                const int n = n0 + tx * 4 + j;      // even; n and n+1 are a RoPE pair
+                if (n >= N) continue;
+                float v0 = acc[0][i][j], v1 = acc[0][i][j + 1];
+                const int slot = n / a.hd, dd = n % a.hd;
+                if (slot < a.H + a.K) {
+                    const float2 r = a.rope[(size_t)t * (a.hd / 2) + dd / 2];
+                    const float x0 = v0 * r.x - v1 * r.y, x1 = v0 * r.y + v1 * r.x;
+                    v0 = x0; v1 = x1;
+                }
+                if (slot < a.H) {
+                    a.QB[(size_t)m * a.D + n] = v0;
+                    a.QB[(size_t)m * a.D + n + 1] = v1;
+                } else {
+                    const bool isk = slot < a.H + a.K;
+                    const int g = isk ? slot - a.H : slot - a.H - a.K;
+                    float* dst = (isk ? a.kc : a.vc) +
+                                 ((((size_t)layer * a.Bcap + b) * a.K + g) * a.cap + t) * a.hd + dd;
+                    dst[0] = v0;
+                    dst[1] = v1;
+                }
+            }
+        } else {
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                const int n = n0 + tx * 4 + j;
+                if (n >= N) continue;
+                if constexpr (EPI == EPI_RESID) {
+                    C[(size_t)m * ldc + n] += acc[0][i][j];
+                } else {
+                    const float up = acc[0][i][j], g = acc[DUAL - 1][i][j];
+                    C[(size_t)m * ldc + n] = (g / (1.0f + expf(-g))) * up;
+                }
+            }
+        }
+    }
+}
+
+// Causal attention for the chunk's queries over cached keys [0, t]
+// (generate.c:121-156 per position).  Block = (query tile, KV head,
+// sequence); rows = G heads x QT positions, 16 rows per warp; keys staged
+// 64 at a time; online softmax.
+constexpr int PF_KT = 64;
+
+__global__ void __launch_bounds__(256) pf_attention_kernel(PrefillArgs a, int layer, int QT) {
+    extern __shared__ __align__(16) float pfs[];
+    const int hd = a.hd, G = a.G, n = a.c1 - a.c0;
+    const int qt0 = a.c0 + blockIdx.x * QT;           // first query position of the tile
+    const int g = blockIdx.y, b = blockIdx.z;
+    if (qt0 >= a.c1) return;
+    const int qt1 = min(a.c1, qt0 + QT);
+    const int rows = G * QT;
+    float* Qs = pfs;                                  // [rows][hd]
+    float* Ks = Qs + rows * hd;                       // [KT][hd+1]
+    float* Vs = Ks + PF_KT * (hd + 1);                // [KT][hd]
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const float scale = 1.0f / sqrtf((float)hd);
+    for (int e = threadIdx.x; e < rows * hd; e += blockDim.x) {
+        const int r = e / hd, d = e % hd, h = r / QT, qi = r % QT;
+        const int t = qt0 + qi;
+        Qs[e] = t < qt1 ? a.QB[((size_t)b * n + (t - a.c0)) * a.D + (g * G + h) * hd + d] : 0.0f;
+    }
+    // per-row state: rows handled by this warp are r = warp + 8 * k
+    constexpr int RPW = 16;
+    float m_run[RPW], l_run[RPW], o_acc[RPW][2];
+#pragma unroll
+    for (int k = 0; k < RPW; k++) { m_run[k] = -INFINITY; l_run[k] = 0.0f; o_acc[k][0] = o_acc[k][1] = 0.0f; }
+    const size_t cbase = (((size_t)layer * a.Bcap + b) * a.K + g) * a.cap;
+    const float* kg = a.kc + cbase * hd;
+    const float* vg = a.vc + cbase * hd;
+    for (int k0 = 0; k0 < qt1; k0 += PF_KT) {
+        const int kn = min(PF_KT, qt1 - k0);
+        __syncthreads();
+        for (int e = threadIdx.x; e < kn * hd; e += blockDim.x) {
+            const int j = e / hd, d = e % hd;
+            Ks[j * (hd + 1) + d] = ldcg(kg + (size_t)(k0 + j) * hd + d);
+            Vs[j * hd + d] = ldcg(vg + (size_t)(k0 + j) * hd + d);
+        }
+        __syncthreads();
+#pragma unroll
+        for (int k = 0; k < RPW; k++) {
+            const int r = warp + 8 * k;
+            if (r >= rows) break;
+            const int t = qt0 + r % QT;
+            if (t >= qt1 || k0 > t) continue;           // padded row / no visible key
+            const float* q = Qs + r * hd;
+            float s0 = -INFINITY, s1 = -INFINITY;
+            const int j0 = lane, j1 = lane + 32;
+            if (j0 < kn && k0 + j0 <= t) {
+                float dot = 0.0f;
+                for (int d = 0; d < hd; d++) dot += q[d] * Ks[j0 * (hd + 1) + d];
+                s0 = dot * scale;
+            }
+            if (j1 < kn && k0 + j1 <= t) {
+                float dot = 0.0f;
+                for (int d = 0; d < hd; d++) dot += q[d] * Ks[j1 * (hd + 1) + d];
+                s1 = dot * scale;
+            }
+            const float mt = warp_max(fmaxf(s0, s1));
+            const float mnew = fmaxf(m_run[k], mt);
+            const float p0 = s0 == -INFINITY ? 0.0f : expf(s0 - mnew);
+            const float p1 = s1 == -INFINITY ? 0.0f : expf(s1 - mnew);
+            const float corr = m_run[k] == -INFINITY ? 0.0f : expf(m_run[k] - mnew);
+            l_run[k] = l_run[k] * corr + warp_sum(p0 + p1);
+            m_run[k] = mnew;
+            float o0 = o_acc[k][0] * corr, o1 = o_acc[k][1] * corr;
+            for (int j = 0; j < kn; j++) {
+                const float pj = __shfl_sync(0xffffffffu, j < 32 ? p0 : p1, j & 31);
+                o0 += pj * Vs[j * hd + lane];
+                if (lane + 32 < hd) o1 += pj * Vs[j * hd + lane + 32];
+            }
+            o_acc[k][0] = o0;
+            o_acc[k][1] = o1;
+        }
+    }
+#pragma unroll
+    for (int k = 0; k < RPW; k++) {
+        const int r = warp + 8 * k;
+        if (r >= rows) break;
+        const int h = r / QT, t = qt0 + r % QT;
+        if (t >= qt1) continue;
+        float* dst = a.ATT + ((size_t)b * n + (t - a.c0)) * a.D + (g * G + h) * hd;
+        const float inv = 1.0f / l_run[k];
+        if (lane < hd) dst[lane] = o_acc[k][0] * inv;
+        if (lane + 32 < hd) dst[lane + 32] = o_acc[k][1] * inv;
+    }
+}
+
+__host__ inline size_t pf_attention_smem(int hd, int G, int QT) {
+    return ((size_t)G * QT * hd + (size_t)PF_KT * (hd + 1) + (size_t)PF_KT * hd) * 4;
+}
+
+}  // namespace mc

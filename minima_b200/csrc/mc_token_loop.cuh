@@ -86,6 +86,7 @@ struct LoopParams {
     int out_cap;
     SamplingArgs s;
     int T;                // forward steps to run
+    int t0;               // first position (earlier ones were prefilled)
     int all_logits;       // teacher-forced logits mode (no sampling)
     float* trace;         // [B][trace_steps][V] or null
     int trace_steps;
@@ -691,7 +692,7 @@ __global__ void __launch_bounds__(kThreads, 1) token_loop_kernel(const LoopParam
     }
     if (!gs.sync()) return;
 
-    for (int t = 0; t < p.T; t++) {
+    for (int t = p.t0; t < p.T; t++) {
         // Sequence lists for this step (identical in every CTA).
         if (threadIdx.x == 0) {
             int nf = 0, nh = 0;

@@ -17,6 +17,7 @@
 
 #include "mc_token_loop.cuh"
 #include "mc_cluster_loop.cuh"
+#include "mc_prefill.cuh"
 
 namespace {
 
@@ -104,6 +105,12 @@ struct mc_session {
     float* hpv;
     int* hpi;
     int last_path;                // 0 grid loop, 1 cluster loop
+    // batched prefill work buffers (allocated on first use)
+    float *pf_x, *pf_xn, *pf_q, *pf_att, *pf_f;
+    size_t pf_rows;               // rows the buffers hold
+    cudaEvent_t ev_mid;           // end of prefill
+    int last_prefill_pos;         // positions prefilled by the last call
+    float last_prefill_ms;
 };
 
 namespace {
@@ -413,8 +420,10 @@ mc_status mc_session_destroy(mc_session* s) {
     void* bufs[] = {s->kc, s->vc, s->x, s->q, s->att, s->f, s->logits, s->part_o, s->part_m,
                     s->part_l, s->amax_v, s->amax_i, s->att_cnt, s->counts, s->banned, s->bar,
                     s->status, s->seq, s->prompts, s->out, s->stop, s->trace, s->stamps,
-                    s->xfin, s->hgen, s->hsync, s->hpv, s->hpi};
+                    s->xfin, s->hgen, s->hsync, s->hpv, s->hpi,
+                    s->pf_x, s->pf_xn, s->pf_q, s->pf_att, s->pf_f};
     for (void* b : bufs) cudaFree(b);
+    if (s->ev_mid) cudaEventDestroy(s->ev_mid);
     if (s->ev0) cudaEventDestroy(s->ev0);
     if (s->ev1) cudaEventDestroy(s->ev1);
     if (s->stream) cudaStreamDestroy(s->stream);
@@ -543,6 +552,7 @@ mc_status mc_session_create(mc_model* m, int max_batch, int max_seq, mc_session*
     e = cudaMemset(s->att_cnt, 0, B * K * 4);
     if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&s->stream, cudaStreamNonBlocking);
     if (e == cudaSuccess) e = cudaEventCreate(&s->ev0);
+    if (e == cudaSuccess) e = cudaEventCreate(&s->ev_mid);
     if (e == cudaSuccess) e = cudaEventCreate(&s->ev1);
     if (e != cudaSuccess) {
         mc_session_destroy(s);
@@ -576,7 +586,6 @@ mc_status run_loop(mc_session* s, mc::LoopParams<WT>& p) {
     MC_CUDA(cudaMemsetAsync(s->bar, 0, 256, s->stream));
     MC_CUDA(cudaMemsetAsync(s->status, 0, 256, s->stream));
     MC_CUDA(cudaMemsetAsync(s->att_cnt, 0, (size_t)s->Bcap * s->m->K * 4, s->stream));
-    MC_CUDA(cudaEventRecord(s->ev0, s->stream));
     cudaError_t e = vec_ok(s->m) ? launch_loop<WT, true>(p, s->grid, s->smem, s->stream)
                                  : launch_loop<WT, false>(p, s->grid, s->smem, s->stream);
     if (e != cudaSuccess) return fail(MC_ERR_CUDA, "token loop launch: %s", cudaGetErrorString(e));
@@ -610,7 +619,6 @@ mc_status run_cluster(mc_session* s, mc::LoopParams<float>& p) {
     MC_CUDA(cudaMemsetAsync(s->stamps, 0, ((size_t)p.T + 1) * 8, s->stream));
     MC_CUDA(cudaMemsetAsync(s->status, 0, 256, s->stream));
     MC_CUDA(cudaMemsetAsync(s->hsync, 0, 64 * 4, s->stream));
-    MC_CUDA(cudaEventRecord(s->ev0, s->stream));
     cudaError_t e = launch_cluster(cp, s->cl_cs, s->cl_nc, s->cl_smem, s->stream, true);
     if (e != cudaSuccess) {
         // cooperative scheduling of clusters unsupported: the plan already
@@ -629,6 +637,83 @@ mc_status run_cluster(mc_session* s, mc::LoopParams<float>& p) {
     if (status == mc::ST_TIMEOUT)
         return fail(MC_ERR_TIMEOUT, "cluster loop: a device-side wait passed its deadline");
     if (status != 0) return fail(MC_ERR_DEVICE, "cluster loop reported status %d", status);
+    return MC_OK;
+}
+
+// Shapes the batched prefill kernels handle (float4 GEMM tiles, RoPE pairs
+// inside a thread's columns, two head dimensions per lane in attention).
+bool prefill_ok(const mc_model* m) {
+    return m->D % 4 == 0 && m->F % 4 == 0 && m->hd % 2 == 0 && m->hd <= 64 && m->H / m->K <= 128;
+}
+
+constexpr int kPrefillChunk = 256;   // positions per prefill pass
+
+// Batched forward of positions [0, Pf) of every sequence (mc_prefill.cuh):
+// fills the KV cache so that the token loop can start at position Pf.
+template <typename WT>
+mc_status run_prefill(mc_session* s, int batch, const uint16_t* prompts, int stride, int Pf,
+                      int& launches) {
+    const mc_model* m = s->m;
+    const size_t rows = (size_t)s->Bcap * std::min(kPrefillChunk, s->cap);
+    if (s->pf_rows < rows) {
+        float** bufs[] = {&s->pf_x, &s->pf_xn, &s->pf_q, &s->pf_att, &s->pf_f};
+        for (float** b : bufs) { cudaFree(*b); *b = nullptr; }
+        s->pf_rows = 0;
+        const size_t D = m->D, F = m->F;
+        MC_CUDA(cudaMalloc(&s->pf_x, rows * D * 4));
+        MC_CUDA(cudaMalloc(&s->pf_xn, rows * D * 4));
+        MC_CUDA(cudaMalloc(&s->pf_q, rows * D * 4));
+        MC_CUDA(cudaMalloc(&s->pf_att, rows * D * 4));
+        MC_CUDA(cudaMalloc(&s->pf_f, rows * F * 4));
+        s->pf_rows = rows;
+    }
+    mc::PrefillArgs a{};
+    a.V = m->V; a.D = m->D; a.L = m->L; a.H = m->H; a.K = m->K; a.hd = m->hd; a.kvd = m->kvd;
+    a.Q = m->Q; a.F = m->F; a.G = m->H / m->K;
+    a.B = batch; a.Bcap = s->Bcap; a.cap = s->cap;
+    a.prompts = prompts; a.prompt_stride = stride;
+    a.rope = m->rope; a.kc = s->kc; a.vc = s->vc;
+    a.X = s->pf_x; a.XN = s->pf_xn; a.QB = s->pf_q; a.ATT = s->pf_att; a.FH = s->pf_f;
+    a.status = s->status;
+    const char* wb = static_cast<const char*>(m->wblock);
+    const WT* emb = reinterpret_cast<const WT*>(wb + m->off[0]);
+    const WT* wqkv = reinterpret_cast<const WT*>(wb + m->off[1]);
+    const WT* wproj = reinterpret_cast<const WT*>(wb + m->off[2]);
+    const WT* wup = reinterpret_cast<const WT*>(wb + m->off[3]);
+    const WT* wgate = reinterpret_cast<const WT*>(wb + m->off[4]);
+    const WT* wdown = reinterpret_cast<const WT*>(wb + m->off[5]);
+    const float* rms1 = m->norms;
+    const float* rms2 = m->norms + (size_t)m->L * m->D;
+    const int QT = std::max(1, 128 / a.G);
+    const size_t att_smem = mc::pf_attention_smem(m->hd, a.G, QT);
+    MC_CUDA(cudaFuncSetAttribute(mc::pf_attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)att_smem));
+    cudaStream_t st = s->stream;
+    const size_t D = m->D, F = m->F, Q = m->Q;
+    auto grid2 = [](int N, int M) { return dim3((N + mc::GBN - 1) / mc::GBN, (M + mc::GBM - 1) / mc::GBM); };
+    for (int c0 = 0; c0 < Pf; c0 += kPrefillChunk) {
+        a.c0 = c0;
+        a.c1 = std::min(Pf, c0 + kPrefillChunk);
+        a.chunk = a.c1 - a.c0;
+        const int M = batch * a.chunk;
+        for (int l = 0; l < m->L; l++) {
+            mc::pf_norm_kernel<WT><<<(M + 7) / 8, 256, 0, st>>>(a, emb, rms1 + l * D, l == 0);
+            mc::pf_gemm_kernel<WT, mc::EPI_QKV><<<grid2(m->Q, M), 256, 0, st>>>(
+                a, a.XN, M, m->Q, m->D, wqkv + l * Q * D, nullptr, nullptr, 0, l);
+            mc::pf_attention_kernel<<<dim3((a.chunk + QT - 1) / QT, m->K, batch), 256, att_smem, st>>>(
+                a, l, QT);
+            mc::pf_gemm_kernel<WT, mc::EPI_RESID><<<grid2(m->D, M), 256, 0, st>>>(
+                a, a.ATT, M, m->D, m->D, wproj + l * D * D, nullptr, a.X, m->D, l);
+            mc::pf_norm_kernel<WT><<<(M + 7) / 8, 256, 0, st>>>(a, emb, rms2 + l * D, 0);
+            mc::pf_gemm_kernel<WT, mc::EPI_SWIGLU><<<grid2(m->F, M), 256, 0, st>>>(
+                a, a.XN, M, m->F, m->D, wup + l * F * D, wgate + l * F * D, a.FH, m->F, l);
+            mc::pf_gemm_kernel<WT, mc::EPI_RESID><<<grid2(m->D, M), 256, 0, st>>>(
+                a, a.FH, M, m->D, m->F, wdown + l * D * F, nullptr, a.X, m->D, l);
+            launches += 7;
+        }
+    }
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return fail(MC_ERR_CUDA, "prefill launch: %s", cudaGetErrorString(e));
     return MC_OK;
 }
 
@@ -736,6 +821,18 @@ mc_status generate_t(mc_session* s, int batch, const uint16_t* prompts, int prom
                                     s->stream));
     }
     if (T > 0) {
+        // positions every sequence feeds before its first sampled id
+        int Pf = s->cap;
+        for (int b = 0; b < batch; b++) Pf = std::min(Pf, seq[b].P - 1);
+        if (!prefill_ok(m)) Pf = 0;
+        MC_CUDA(cudaEventRecord(s->ev0, s->stream));
+        int pf_launches = 0;
+        if (Pf > 0) {
+            mc_status st = run_prefill<WT>(s, batch, p.prompts, p.prompt_stride, Pf, pf_launches);
+            if (st) return st;
+        }
+        MC_CUDA(cudaEventRecord(s->ev_mid, s->stream));
+        p.t0 = Pf;
         mc_status st;
         if constexpr (std::is_same<WT, float>::value) {
             if (s->cl_ok && p.s.top_k == 1 && batch <= mc::kBCMax) st = run_cluster(s, p);
@@ -744,6 +841,9 @@ mc_status generate_t(mc_session* s, int batch, const uint16_t* prompts, int prom
             st = run_loop<WT>(s, p);
         }
         if (st) return st;
+        s->last_launches += pf_launches;
+        s->last_prefill_pos = Pf;
+        MC_CUDA(cudaEventElapsedTime(&s->last_prefill_ms, s->ev0, s->ev_mid));
     } else {
         s->last_ms = 0.0f;
         s->last_launches = 0;
@@ -819,8 +919,12 @@ mc_status forward_logits_t(mc_session* s, int batch, const uint16_t* tokens, int
                               batch, cudaMemcpyHostToDevice, s->stream));
     MC_CUDA(cudaMemcpyAsync(s->seq, seq.data(), batch * sizeof(mc::SeqState), cudaMemcpyHostToDevice,
                             s->stream));
+    MC_CUDA(cudaEventRecord(s->ev0, s->stream));
+    p.t0 = 0;
     st = run_loop<WT>(s, p);
     if (st) return st;
+    s->last_prefill_pos = 0;
+    s->last_prefill_ms = 0.0f;
     MC_CUDA(cudaMemcpy(out, s->trace, (size_t)batch * n * m->V * 4, cudaMemcpyDeviceToHost));
     return MC_OK;
 }
@@ -863,6 +967,13 @@ mc_status mc_forward_logits(mc_session* s, int batch, const uint16_t* tokens, in
 mc_status mc_last_kernel_ms(mc_session* s, float* ms) {
     if (!s || !ms) return fail(MC_ERR_INVALID, "null argument");
     *ms = s->last_ms;
+    return MC_OK;
+}
+
+mc_status mc_last_prefill(mc_session* s, int* positions, float* ms) {
+    if (!s || !positions || !ms) return fail(MC_ERR_INVALID, "null argument");
+    *positions = s->last_prefill_pos;
+    *ms = s->last_prefill_ms;
     return MC_OK;
 }
 
