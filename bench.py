@@ -79,6 +79,21 @@ def workload_prompts(rank):
     return prompts, rng
 
 
+def max_over_ranks(pg, values, device):
+    """Element-wise MAX of per-rank timings (the slowest rank sets the time)."""
+    import torch
+    t = torch.tensor(values, dtype=torch.float64, device=device)
+    if pg is not None:
+        pg.all_reduce(t, op=pg.ReduceOp.MAX)
+    return [float(v) for v in t]
+
+
+def whole_job_rate(world, tokens_per_rank, max_seconds):
+    """Aggregate generated tokens/s over all ranks (weak scaling: every rank
+    decodes its own, disjoint sequences)."""
+    return world * tokens_per_rank / max_seconds
+
+
 def algorithmic_bytes(P, nnew, B, t0=0, weight_bytes_per=4):
     """Bytes the token-loop launch must move for positions t0..T-1: every
     token step reads the layer weights, steps that produce logits read the
@@ -307,12 +322,9 @@ def native_arm(args):
     assert np.array_equal(out[:, :P + N], got[:, :P + N]), "e2e and device-resident runs differ"
 
     # ---- max over ranks
-    t = torch.tensor([total_ms, sum(e2e_times)], dtype=torch.float64, device=dev)
-    if pg:
-        pg.all_reduce(t, op=pg.ReduceOp.MAX)
-    total_ms, e2e_s = float(t[0]), float(t[1])
-    value = world * tokens / (total_ms / 1e3)
-    e2e_value = world * e2e_tokens / e2e_s
+    total_ms, e2e_s = max_over_ranks(pg, [total_ms, sum(e2e_times)], dev)
+    value = whole_job_rate(world, tokens, total_ms / 1e3)
+    e2e_value = whole_job_rate(world, e2e_tokens, e2e_s)
 
     if rank == 0:
         T = P + N - 1
