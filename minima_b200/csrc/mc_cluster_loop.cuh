@@ -9,7 +9,7 @@
 //  * layer cluster (cluster 0): runs every transformer layer of every step
 //    for the whole batch.  Each CTA owns a fixed row slice of every layer
 //    matrix; the slices of upcoming layers stream from L2/HBM into shared
-//    memory with TMA bulk copies (cp.async.bulk, no multicast) tracked by
+//    memory with TMA bulk copies (cp.async.bulk, one destination CTA) tracked by
 //    mbarriers, kStages layers ahead.  Activations are replicated in every
 //    CTA's shared memory and exchanged through distributed shared memory;
 //    the five phases of a layer (forward_one, generate.c:97-185) are
@@ -113,7 +113,7 @@ __device__ __forceinline__ bool mbar_try_wait(unsigned long long* bar, unsigned 
         : "memory");
     return ok != 0;
 }
-// 1-D bulk copy global -> this CTA's shared memory (no multicast).
+// 1-D bulk copy global -> this CTA's own shared memory (single destination).
 __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, unsigned bytes,
                                          unsigned long long* bar) {
     asm volatile(
