@@ -239,6 +239,7 @@ def native_arm(args):
 
     rank, world, local = dist_env()
     torch.cuda.set_device(local)
+    os.environ["MINIMA_CUDA_DEVICE"] = str(local)   # the drop-in's device (e2e leg)
     pg = None
     if world > 1:
         import datetime
