@@ -749,7 +749,7 @@ __device__ void lc_main(const ClusterParams& cp, unsigned char* smem, cg::cluste
             // ---- release the head CTAs, wait for all of them, choose the next ids
             if (threadIdx.x == 0) {
                 st_release_u32(cp.go, heads);
-                const unsigned target = heads * (unsigned)nhc;
+                const unsigned target = heads * ((unsigned)nhc + p.extra_arrivals);
                 const unsigned long long t0 = globaltimer_ns();
                 while ((int)(ld_acquire_u32(cp.hdone) - target) < 0) {
                     if (globaltimer_ns() - t0 > p.timeout_ns) {

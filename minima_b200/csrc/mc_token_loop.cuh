@@ -94,6 +94,7 @@ struct LoopParams {
     int* status;
     unsigned long long timeout_ns;
     unsigned long long* stamps;   // [T+1] %globaltimer at each step start, or null
+    unsigned extra_arrivals;      // test hook: arrivals a wait expects beyond the real ones
     int bc;               // GEMV chunk (<= kBCMax)
     int xs_ld;            // row stride of the chunk buffer in smem (floats)
 };
@@ -665,7 +666,7 @@ __global__ void __launch_bounds__(kThreads, 1) token_loop_kernel(const LoopParam
     sm.head = sm.fwd + p.Bcap;
     sm.ints = sm.head + p.Bcap;
     sm.xs = smem_f + loop_fixed_bytes(p.Bcap) / 4;
-    GridSync gs{p.bar, p.status, gridDim.x, 0u, p.timeout_ns};
+    GridSync gs{p.bar, p.status, gridDim.x + p.extra_arrivals, 0u, p.timeout_ns};
 
     // Prologue: one CTA per sequence copies the prompt into its history,
     // seeds penalty counts and first-draw n-gram bans.

@@ -157,7 +157,14 @@ void fill_params(mc::LoopParams<WT>& p, const mc_session* s) {
     p.counts = s->counts; p.banned = s->banned; p.max_split = s->max_split;
     p.seq = s->seq;
     p.bar = s->bar; p.status = s->status;
-    p.timeout_ns = 1000ull * 1000ull * 1000ull;  // 1 s per barrier wait
+    // Every device-side wait gives up after this deadline (default 1 s) and
+    // reports MC_ERR_TIMEOUT.  MINIMA_CUDA_WAIT_NS shortens it and
+    // MINIMA_CUDA_TEST_STALL=1 makes each wait expect one arrival that never
+    // comes: test hooks for the failure path, off unless set.
+    const char* wait_ns = getenv("MINIMA_CUDA_WAIT_NS");
+    p.timeout_ns = wait_ns ? strtoull(wait_ns, nullptr, 10) : 1000ull * 1000ull * 1000ull;
+    const char* stall = getenv("MINIMA_CUDA_TEST_STALL");
+    p.extra_arrivals = (stall && stall[0] == '1') ? 1u : 0u;
     p.bc = s->bc; p.xs_ld = s->xs_ld;
 }
 
