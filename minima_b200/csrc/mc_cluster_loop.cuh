@@ -42,6 +42,11 @@ constexpr int kStages = 2;          // layers of weights in flight per CTA
 constexpr unsigned kExit = 0x7fffffffu;
 constexpr unsigned kHcEmbOffset = 2048;   // head CTA: byte offset of the lm_head slice
 constexpr unsigned kLcHeader = 1024;      // layer CTA: mbarriers, ints, red scratch
+constexpr int kAttMaxG = 4;               // query heads per KV head (attention unit)
+constexpr int kAttMaxND = 2;              // head_dim / 32, rounded up
+constexpr int kAttMaxO = kAttMaxG * kAttMaxND;
+constexpr int kAttMaxQ4 = 8 * kAttMaxND;      // head_dim / 4
+constexpr int kAttMaxTile = 8 * 32;       // keys per tile: a run of 32 per warp
 
 struct CSlice {
     int q0, q1, p0, p1, f0, f1;     // rows: qkv [q0,q1), proj/down [p0,p1), up/gate [f0,f1)
@@ -74,10 +79,9 @@ struct ClusterParams {
     int cs;                     // CTAs per cluster
     int n_clusters;
     // layer-cluster shared-memory plan (byte offsets)
-    unsigned off_x, off_xn, off_qkv, off_attp, off_att, off_f, off_sc, off_kv, off_stage;
+    unsigned off_x, off_xn, off_qkv, off_att, off_attp, off_f, off_sc, off_kv, off_stage;
     unsigned off_rmsf, off_rope;
     unsigned stage_floats;      // floats per weight stage (slice + rms1 + rms2)
-    int n_split;                // attention splits per (sequence, KV head)
     int kv_tile;                // keys staged per attention tile
     // head clusters
     int hc_rows;                // tok_emb rows per head CTA
@@ -142,20 +146,24 @@ struct LcState {
     float* x;      // [B][D]
     float* xn;     // [B][D]
     float* qkv;    // [B][Q]
-    float* attp;   // [B][H][n_split][hd + 2]
     float* att;    // [B][D]
+    float* attp;   // [units][G * hd + 2 G, padded to 4] merged states of split units
     float* f;      // [B][F]
-    float* sc;     // [G][kv_tile]
-    float* kv;     // [2][kv_tile][hd + 4]
+    float* sc;     // [kWarps][G * hd + 2 G] per-warp attention states, [kWarps][kAttMaxG][32] probabilities
+    float* kv;     // [K, V][kv_tile][hd]
     float* stage;  // [kStages][stage_floats]
     float* rmsf;   // [D] final RMSNorm scale
     float2* rope;  // [hd/2] (cos, sin) at the current position
     unsigned long long* bar;  // [kStages]
+    unsigned long long* kvbar;  // K/V tile copies
     int* ints;     // [64]: 0..15 fwd list, 16..31 head list, 32.. scalars,
-                   //       36/37 cluster error slots, 38 this CTA saw an error
+                   //       36/37 cluster error slots, 38 this CTA saw an error,
+                   //       39 a K/V tile wait failed (thread 0)
     float* red;    // [64]
     struct SeqMirror* seq;    // [kBCMax] sequence table mirrored in shared memory
     int epoch;     // cluster barriers passed (identical in every CTA of the cluster)
+    unsigned kvph;      // thread 0: phase of kvbar awaited next
+    int kvpend;         // thread 0: a copy into the K/V tile is outstanding
 };
 
 // The sequence table in shared memory: the layer cluster reads it every
@@ -214,22 +222,33 @@ __device__ void lc_norm(const float* x, float* xn, const float* scale, const int
     __syncthreads();
 }
 
-__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(dst)), "l"(src) : "memory");
+// Copy cached K/V rows [a0, a0 + n) of one (sequence, KV head) into the
+// K/V tile with two bulk copies that complete on kvbar.  The row at position
+// t is produced in this step and is read from the qkv buffer instead, so the
+// copies stop below it.  Thread 0 only; after a failed wait no further
+// copies are issued (the cluster leaves at its next barrier).
+__device__ __forceinline__ void att_issue_tile(const ClusterParams& cp, LcState& S, const float* kg,
+                                               const float* vg, int a0, int n, int t, int hd) {
+    if (S.ints[39]) return;
+    const int rows = min(n, t - a0);
+    const unsigned bytes = rows > 0 ? (unsigned)(rows * hd * 4) : 0u;
+    mbar_expect_tx(S.kvbar, 2 * bytes);
+    if (bytes) {
+        bulk_g2s(S.kv, kg + (size_t)a0 * hd, bytes, S.kvbar);
+        bulk_g2s(S.kv + (size_t)cp.kv_tile * hd, vg + (size_t)a0 * hd, bytes, S.kvbar);
+    }
+    S.kvpend = 1;
 }
-__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 
-// Start async copies of cached K/V rows [a0, a0+n) of one (sequence, KV
-// head) into the staging tile; row t is produced this step and is filled
-// from shared memory separately.
-__device__ __forceinline__ void att_issue(const float* kg, const float* vg, float* ks, float* vs,
-                                          int a0, int n, int t, int hd, int ldk) {
-    const int q4 = hd / 4;
-    for (int e = threadIdx.x; e < n * q4; e += blockDim.x) {
-        const int j = e / q4, c4 = (e % q4) * 4, pos = a0 + j;
-        if (pos == t) continue;
-        cp_async16(ks + j * ldk + c4, kg + (size_t)pos * hd + c4);
-        cp_async16(vs + j * ldk + c4, vg + (size_t)pos * hd + c4);
+// Thread 0: wait (bounded) for the copies into the K/V tile.
+__device__ __forceinline__ void att_wait_tile(const LoopParams<float>& p, LcState& S) {
+    if (!S.kvpend || S.ints[39]) return;
+    if (mbar_wait(S.kvbar, S.kvph, p.timeout_ns)) {
+        S.kvph ^= 1u;
+        S.kvpend = 0;
+    } else {
+        S.ints[39] = 1;
+        lc_fail(S, p.status, ST_TIMEOUT);
     }
 }
 
@@ -283,31 +302,6 @@ __device__ __forceinline__ float lc_gemv4(const float* r0, const float* r1, cons
     return transpose_reduce32(acc);
 }
 
-// Dot of `nr` (<= 2) shared-memory rows of length `len` with the activation
-// rows xs[b] for every b in list; lanes split the row (float4).  Returns the
-// sums in acc[r][i] on every lane.
-__device__ __forceinline__ void lc_dot2(const float* r0, const float* r1, int len, const float* xs,
-                                        int ld, const int* list, int n, float (&acc)[2][kBCMax]) {
-    const int lane = threadIdx.x & 31;
-#pragma unroll
-    for (int i = 0; i < kBCMax; i++) { acc[0][i] = 0.0f; acc[1][i] = 0.0f; }
-    for (int k = lane * 4; k < len; k += 128) {
-        const float4 w0 = *reinterpret_cast<const float4*>(r0 + k);
-        const float4 w1 = *reinterpret_cast<const float4*>(r1 + k);
-#pragma unroll
-        for (int i = 0; i < kBCMax; i++) {
-            if (i < n) {
-                const float4 xv = *reinterpret_cast<const float4*>(xs + list[i] * ld + k);
-                acc[0][i] += w0.x * xv.x + w0.y * xv.y + w0.z * xv.z + w0.w * xv.w;
-                acc[1][i] += w1.x * xv.x + w1.y * xv.y + w1.z * xv.z + w1.w * xv.w;
-            }
-        }
-    }
-#pragma unroll
-    for (int i = 0; i < kBCMax; i++)
-        if (i < n) { acc[0][i] = warp_sum(acc[0][i]); acc[1][i] = warp_sum(acc[1][i]); }
-}
-
 // Copy rows [r0, r1) of buf[b][ld] for the sequences in `list` from this
 // CTA's shared memory into the same place in every other CTA of the
 // cluster, as float4 stores (remote-store cost is per transaction, so 16-byte
@@ -357,12 +351,249 @@ __device__ bool lc_sync(cg::cluster_group& cl, LcState& S, int cs) {
     return ok;
 }
 
+// Attention unit u: sequence fl[u / (ns K)], KV head (u / ns) mod K, keys
+// [j0, j1) of split u mod ns.
+struct AttUnit {
+    int b, g, j0, j1;
+};
+__device__ __forceinline__ AttUnit att_unit(int u, int K, int ns, int per, int nkeys, const int* fl) {
+    AttUnit a;
+    const int s = u % ns;
+    a.g = (u / ns) % K;
+    a.b = fl[u / (ns * K)];
+    a.j0 = min(s * per, nkeys);
+    a.j1 = min(a.j0 + per, nkeys);
+    return a;
+}
+
+// One run of up to 32 keys (a warp) for all G heads of a KV head: lane j
+// scores key j against every head, then owns output dims lane + 32 i in
+// P.V; (mrun, lrun, o) is the warp's running state per head.  Rows past the
+// run may be read: their scores are masked and the V rows there are zero
+// (the tile loop clears them).  HD > 0 fixes head_dim at compile time; 0 =
+// any multiple of 4 up to 32 kAttMaxND.
+template <int HD>
+__device__ __forceinline__ void att_run(const float* kr0, const float* vr0, const float* q, float* pb,
+                                        int kn, int hd_rt, int G, float scale,
+                                        float (&mrun)[kAttMaxG], float (&lrun)[kAttMaxG],
+                                        float (&o)[kAttMaxG][kAttMaxND]) {
+    const int hd = HD > 0 ? HD : hd_rt;
+    const int q4 = hd / 4;
+    const int lane = threadIdx.x & 31;
+    // scores; lane j starts at chunk (j mod hd/4) so that the rows the lanes
+    // read fall in different banks
+    const float* kr = kr0 + lane * hd;
+    const int r = lane % q4;
+    float dd[kAttMaxG];
+#pragma unroll
+    for (int h = 0; h < kAttMaxG; h++) dd[h] = 0.0f;
+#pragma unroll 8
+    for (int c = 0; c < (HD > 0 ? HD / 4 : kAttMaxQ4); c++)
+        if (HD > 0 || c < q4) {
+            const int cc = r + c < q4 ? r + c : r + c - q4;
+            const float4 kk = *reinterpret_cast<const float4*>(kr + 4 * cc);
+#pragma unroll
+            for (int h = 0; h < kAttMaxG; h++)
+                if (h < G) {
+                    const float4 qq = *reinterpret_cast<const float4*>(q + h * hd + 4 * cc);
+                    dd[h] = fmaf(qq.x, kk.x, dd[h]);
+                    dd[h] = fmaf(qq.y, kk.y, dd[h]);
+                    dd[h] = fmaf(qq.z, kk.z, dd[h]);
+                    dd[h] = fmaf(qq.w, kk.w, dd[h]);
+                }
+        }
+    const bool valid = lane < kn;
+    float corr[kAttMaxG];
+#pragma unroll
+    for (int h = 0; h < kAttMaxG; h++) {
+        corr[h] = 1.0f;
+        if (h < G) {
+            const float sv = valid ? dd[h] * scale : -INFINITY;
+            const float mnew = fmaxf(mrun[h], warp_max(sv));
+            const float e = valid ? expf(sv - mnew) : 0.0f;
+            corr[h] = expf(mrun[h] - mnew);
+            lrun[h] = lrun[h] * corr[h] + warp_sum(e);
+            mrun[h] = mnew;
+            pb[h * 32 + lane] = e;
+        }
+    }
+    __syncwarp();
+    // P.V, four keys at a time; V loads are shared by the heads
+    float acc[kAttMaxG][kAttMaxND][2];
+#pragma unroll
+    for (int h = 0; h < kAttMaxG; h++)
+#pragma unroll
+        for (int i = 0; i < kAttMaxND; i++) acc[h][i][0] = acc[h][i][1] = 0.0f;
+    const float* vr = vr0 + lane;
+#pragma unroll 2
+    for (int kk = 0; kk < 32; kk += 4) {
+#pragma unroll
+        for (int i = 0; i < kAttMaxND; i++)
+            if (32 * i < hd && lane + 32 * i < hd) {
+                const float* v = vr + kk * hd + 32 * i;
+                const float v0 = v[0], v1 = v[hd], v2 = v[2 * hd], v3 = v[3 * hd];
+#pragma unroll
+                for (int h = 0; h < kAttMaxG; h++)
+                    if (h < G) {
+                        const float4 p4 = *reinterpret_cast<const float4*>(pb + h * 32 + kk);
+                        acc[h][i][0] = fmaf(p4.x, v0, acc[h][i][0]);
+                        acc[h][i][1] = fmaf(p4.y, v1, acc[h][i][1]);
+                        acc[h][i][0] = fmaf(p4.z, v2, acc[h][i][0]);
+                        acc[h][i][1] = fmaf(p4.w, v3, acc[h][i][1]);
+                    }
+            }
+    }
+    __syncwarp();   // pb is rewritten by this warp's next run
+#pragma unroll
+    for (int h = 0; h < kAttMaxG; h++)
+#pragma unroll
+        for (int i = 0; i < kAttMaxND; i++) o[h][i] = o[h][i] * corr[h] + (acc[h][i][0] + acc[h][i][1]);
+}
+
+// Attention phase of one layer at position t (generate.c:121-156), ending
+// with the cluster barrier; false when the cluster must leave.  A unit
+// stages its keys in tiles of kv_tile (bulk copies; the first tile of a
+// CTA's first unit was requested before the QKV phase); the warps take the
+// tile's runs of 32 keys.  The warps' states are merged per unit; split
+// units exchange their merged states and every CTA combines them.
+template <int HD>
+__device__ bool lc_attention(const ClusterParams& cp, LcState& S, cg::cluster_group& cl, int crank,
+                             int l, int t, const int* fl, int nf, int ns, int per, int units,
+                             bool wrote_kv) {
+    const LoopParams<float>& p = cp.lp;
+    const int D = p.D, Q = p.Q, hd = HD > 0 ? HD : p.hd, K = p.K, G = p.G, H = p.H;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int cs = cp.cs, nkeys = t + 1;
+    const float scale = 1.0f / sqrtf((float)hd);
+    const int ghd = G * hd, nd = (hd + 31) / 32;
+    const int pw = ghd + 2 * G;                        // outputs, then (max, sum) per head
+    const int pwp = (pw + 3) & ~3;                     // exchanged state stride (float4 pushes)
+    float* part = S.sc;                                // [kWarps][pw]
+    float* pb = S.sc + kWarps * pw + warp * 32 * kAttMaxG;   // this warp's probabilities
+    float* ks = S.kv;
+    float* vs = S.kv + (size_t)cp.kv_tile * hd;
+    for (int u = crank; u < units; u += cs) {
+        const AttUnit a = att_unit(u, K, ns, per, nkeys, fl);
+        const size_t cbase = (((size_t)l * p.Bcap + a.b) * K + a.g) * p.cap;
+        const float* kg = p.kc + cbase * hd;
+        const float* vg = p.vc + cbase * hd;
+        const float* q = S.qkv + a.b * Q + a.g * ghd;
+        const float* kq = S.qkv + a.b * Q + D + a.g * hd;          // row t of K
+        const float* vq = kq + p.kvd;                              // row t of V
+        float mrun[kAttMaxG], lrun[kAttMaxG], o[kAttMaxG][kAttMaxND];
+#pragma unroll
+        for (int h = 0; h < kAttMaxG; h++) {
+            mrun[h] = -INFINITY;
+            lrun[h] = 0.0f;
+#pragma unroll
+            for (int i = 0; i < kAttMaxND; i++) o[h][i] = 0.0f;
+        }
+        for (int a0 = a.j0; a0 < a.j1; a0 += cp.kv_tile) {
+            const int n = min(cp.kv_tile, a.j1 - a0);
+            // every warp is past the previous tile (the barrier closing it,
+            // or the merge of the previous unit): the tile buffer is free
+            if (threadIdx.x == 0 && (u != crank || a0 != a.j0))
+                att_issue_tile(cp, S, kg, vg, a0, n, t, hd);
+            // Row t is produced in this step: the copies stop below it and its
+            // slot is filled from the qkv buffer.  V rows from n up to the next
+            // multiple of 32 are cleared for the unmasked P.V.  The copies
+            // write neither range.
+            if (t >= a0 && t < a0 + n)
+                for (int c = threadIdx.x; c < 2 * hd; c += blockDim.x) {
+                    if (c < hd) ks[(t - a0) * hd + c] = kq[c];
+                    else vs[(t - a0) * hd + c - hd] = vq[c - hd];
+                }
+            const int pad = ((n + 31) & ~31) - n;
+            for (int c = threadIdx.x; c < pad * hd; c += blockDim.x) vs[n * hd + c] = 0.0f;
+            if (threadIdx.x == 0) att_wait_tile(p, S);
+            __syncthreads();
+            for (int rr = warp; rr * 32 < n; rr += kWarps)
+                att_run<HD>(ks + (size_t)rr * 32 * hd, vs + (size_t)rr * 32 * hd, q, pb,
+                            min(32, n - rr * 32), hd, G, scale, mrun, lrun, o);
+            __syncthreads();
+        }
+        // merge the warps' states: (m, l) per head, then the outputs
+#pragma unroll
+        for (int h = 0; h < kAttMaxG; h++)
+            if (h < G) {
+                if (lane == 0) {
+                    part[warp * pw + ghd + 2 * h] = mrun[h];
+                    part[warp * pw + ghd + 2 * h + 1] = lrun[h];
+                }
+#pragma unroll
+                for (int i = 0; i < kAttMaxND; i++) {
+                    const int d = lane + 32 * i;
+                    if (i < nd && d < hd) part[warp * pw + h * hd + d] = o[h][i];
+                }
+            }
+        __syncthreads();
+        float* dst = ns == 1 ? S.att + a.b * D + a.g * ghd : S.attp + (size_t)u * pwp;
+        for (int i = threadIdx.x; i < ghd; i += blockDim.x) {
+            const int h = i / hd;
+            float M = -INFINITY;
+#pragma unroll
+            for (int w = 0; w < kWarps; w++) M = fmaxf(M, part[w * pw + ghd + 2 * h]);
+            float num = 0.0f, den = 0.0f;
+#pragma unroll
+            for (int w = 0; w < kWarps; w++) {
+                const float mw = part[w * pw + ghd + 2 * h];
+                const float c = mw == -INFINITY ? 0.0f : expf(mw - M);   // a warp may see no keys
+                den += c * part[w * pw + ghd + 2 * h + 1];
+                num += c * part[w * pw + i];
+            }
+            if (ns == 1) {
+                dst[i] = num / den;
+            } else {
+                dst[i] = num;
+                if (i % hd == 0) {
+                    dst[ghd + 2 * h] = M;
+                    dst[ghd + 2 * h + 1] = den;
+                }
+            }
+        }
+        __syncthreads();
+        if (ns == 1) push_block(cl, S.att, a.b * D + a.g * ghd, ghd, cs, crank);
+        else push_block(cl, S.attp, u * pwp, pwp, cs, crank);
+        __syncthreads();   // part is rewritten by this CTA's next unit
+    }
+    // K/V rows written in this step are read by later steps' bulk copies
+    // (async proxy) in other CTAs: order them before the cluster barrier
+    if (wrote_kv) asm volatile("fence.proxy.async.global;" ::: "memory");
+    if (!lc_sync(cl, S, cs)) return false;
+    // combine the splits (every CTA): a warp per (sequence, head)
+    if (ns > 1) {
+        for (int pr = warp; pr < nf * H; pr += kWarps) {
+            const int i = pr / H, h = pr - i * H, g = h / G, hh = h - g * G;
+            const float* pp = S.attp + (size_t)((i * K + g) * ns) * pwp;
+            float M = -INFINITY;
+            for (int s2 = 0; s2 < ns; s2++) M = fmaxf(M, pp[s2 * pwp + ghd + 2 * hh]);
+            float den = 0.0f, num[kAttMaxND];
+#pragma unroll
+            for (int j = 0; j < kAttMaxND; j++) num[j] = 0.0f;
+            for (int s2 = 0; s2 < ns; s2++) {
+                const float* ps = pp + s2 * pwp;
+                const float ms = ps[ghd + 2 * hh];
+                const float c = ms == -INFINITY ? 0.0f : expf(ms - M);   // a split may see no keys
+                den += c * ps[ghd + 2 * hh + 1];
+#pragma unroll
+                for (int j = 0; j < kAttMaxND; j++)
+                    if (lane + 32 * j < hd) num[j] += c * ps[hh * hd + lane + 32 * j];
+            }
+#pragma unroll
+            for (int j = 0; j < kAttMaxND; j++)
+                if (lane + 32 * j < hd) S.att[fl[i] * D + h * hd + lane + 32 * j] = num[j] / den;
+        }
+        __syncthreads();
+    }
+    return true;
+}
+
 // One layer for the sequences in the fwd list at position t.
 __device__ bool lc_layer(const ClusterParams& cp, const CSlice& sl, LcState& S,
                          cg::cluster_group& cl, int crank, int l, int t, const int* fl, int nf,
                          const float* w) {
     const LoopParams<float>& p = cp.lp;
-    const int D = p.D, Q = p.Q, F = p.F, hd = p.hd, K = p.K, G = p.G, H = p.H;
+    const int D = p.D, Q = p.Q, F = p.F, hd = p.hd, K = p.K, H = p.H;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int cs = cp.cs;
     const float* wq = w;
@@ -373,23 +604,25 @@ __device__ bool lc_layer(const ClusterParams& cp, const CSlice& sl, LcState& S,
     const float* rms1 = w + slice_floats(sl, D, F);
     const float* rms2 = rms1 + D;
 
-    // Attention geometry; the first tile of this CTA's first unit is fetched
-    // now so that its L2 latency overlaps the QKV phase.
-    const int ns = cp.n_split;
+    // Attention units are (sequence, KV head, key split); keys are split
+    // when there are fewer (sequence, KV head) pairs than CTAs.  The first
+    // K/V tile of this CTA's first unit is requested now so that its
+    // transfer overlaps the QKV phase.
+    const int nkeys = t + 1;
+    const int ns = min(nkeys, max(1, cs / (nf * K)));
+    const int per = (nkeys + ns - 1) / ns;
     const int units = nf * K * ns;
-    const int ldk = hd + 4;
-    float* ks = S.kv;
-    float* vs = S.kv + cp.kv_tile * ldk;
-    if (crank < units) {
-        const int u = crank, s = u % ns, g = (u / ns) % K, b = fl[u / (ns * K)];
-        const int per = (t + 1 + ns - 1) / ns;
-        const int j0 = min(s * per, t + 1), j1 = min(j0 + per, t + 1);
-        const size_t cbase = (((size_t)l * p.Bcap + b) * K + g) * p.cap;
-        att_issue(p.kc + cbase * hd, p.vc + cbase * hd, ks, vs, j0, min(cp.kv_tile, j1 - j0), t, hd, ldk);
+    if (crank < units && threadIdx.x == 0) {
+        const AttUnit a = att_unit(crank, K, ns, per, nkeys, fl);
+        const size_t cbase = (((size_t)l * p.Bcap + a.b) * K + a.g) * p.cap;
+        if (a.j1 > a.j0)
+            att_issue_tile(cp, S, p.kc + cbase * hd, p.vc + cbase * hd, a.j0,
+                           min(cp.kv_tile, a.j1 - a.j0), t, hd);
     }
 
     // ---- QKV + RoPE + K/V append (generate.c:99-119)
     lc_norm(S.x, S.xn, rms1, fl, nf, D, S.red);
+    bool wrote_kv = false;
     for (int r0 = sl.q0 + 4 * warp; r0 < sl.q1; r0 += 4 * kWarps) {
         const float* w0 = wq + (size_t)(r0 - sl.q0) * D;
         const float val = lc_gemv4(w0, w0 + D, w0 + 2 * D, w0 + 3 * D, D, S.xn, D, fl, nf);
@@ -411,122 +644,25 @@ __device__ bool lc_layer(const ClusterParams& cp, const CSlice& sl, LcState& S,
                 const bool isk = slot < H + K;
                 const int g = isk ? slot - H : slot - H - K;
                 (isk ? p.kc : p.vc)[((((size_t)l * p.Bcap + b) * K + g) * p.cap + t) * hd + d] = out;
+                wrote_kv = true;
             }
         }
     }
     __syncthreads();
     push_rows(cl, S.qkv, Q, sl.q0, sl.q1, fl, nf, cs, crank);
-    __threadfence();   // K/V rows are read from global by other CTAs in later steps
     if (!lc_sync(cl, S, cs)) return false;
 
-    // ---- attention, split over the cluster (generate.c:121-156)
-    const float scale = 1.0f / sqrtf((float)hd);
-    for (int u = crank; u < units; u += cs) {
-        const int s = u % ns, g = (u / ns) % K, b = fl[u / (ns * K)];
-        const int nkeys = t + 1;
-        const int per = (nkeys + ns - 1) / ns;
-        const int j0 = min(s * per, nkeys), j1 = min(j0 + per, nkeys);
-        const size_t cbase = (((size_t)l * p.Bcap + b) * K + g) * p.cap;
-        const float* kg = p.kc + cbase * hd;
-        const float* vg = p.vc + cbase * hd;
-        const float* q = S.qkv + b * Q + g * G * hd;
-        // running softmax state per head: m, l in red[2h], red[2h+1]; o accumulates in att scratch
-        float* o = S.sc + G * cp.kv_tile;          // [G][hd]
-        for (int i = threadIdx.x; i < G * hd; i += blockDim.x) o[i] = 0.0f;
-        if (threadIdx.x < G) { S.red[2 * threadIdx.x] = -INFINITY; S.red[2 * threadIdx.x + 1] = 0.0f; }
-        for (int a0 = j0; a0 < j1; a0 += cp.kv_tile) {
-            const int n = min(cp.kv_tile, j1 - a0);
-            __syncthreads();
-            // stage K/V rows [a0, a0+n) (the first tile of the first unit is
-            // already in flight); the row at t comes from this step's qkv
-            if (!(u == crank && a0 == j0)) att_issue(kg, vg, ks, vs, a0, n, t, hd, ldk);
-            if (t >= a0 && t < a0 + n) {
-                const int j = t - a0;
-                for (int c = threadIdx.x; c < hd; c += blockDim.x) {
-                    ks[j * ldk + c] = S.qkv[b * Q + D + g * hd + c];
-                    vs[j * ldk + c] = S.qkv[b * Q + D + p.kvd + g * hd + c];
-                }
-            }
-            cp_async_wait_all();
-            __syncthreads();
-            for (int e = threadIdx.x; e < G * n; e += blockDim.x) {
-                const int h = e / n, j = e % n;
-                const float* qh = q + h * hd;
-                const float* kr = ks + j * ldk;
-                float dot = 0.0f;
-                for (int d = 0; d < hd; d += 4) {
-                    const float4 kk = *reinterpret_cast<const float4*>(kr + d);
-                    dot += qh[d] * kk.x + qh[d + 1] * kk.y + qh[d + 2] * kk.z + qh[d + 3] * kk.w;
-                }
-                S.sc[h * cp.kv_tile + j] = dot * scale;
-            }
-            __syncthreads();
-            for (int h = warp; h < G; h += kWarps) {
-                float m = -INFINITY;
-                for (int j = lane; j < n; j += 32) m = fmaxf(m, S.sc[h * cp.kv_tile + j]);
-                m = warp_max(m);
-                const float mold = S.red[2 * h], mnew = fmaxf(mold, m);
-                float ls = 0.0f;
-                for (int j = lane; j < n; j += 32) {
-                    const float e = expf(S.sc[h * cp.kv_tile + j] - mnew);
-                    S.sc[h * cp.kv_tile + j] = e;
-                    ls += e;
-                }
-                ls = warp_sum(ls);
-                __syncwarp();
-                if (lane == 0) {
-                    const float corr = expf(mold - mnew);
-                    S.red[2 * h] = mnew;
-                    S.red[2 * h + 1] = S.red[2 * h + 1] * corr + ls;
-                    S.red[32 + h] = corr;
-                }
-            }
-            __syncthreads();
-            for (int i = threadIdx.x; i < G * hd; i += blockDim.x) {
-                const int h = i / hd, d = i % hd;
-                float acc = o[i] * S.red[32 + h];
-                for (int j = 0; j < n; j++) acc += S.sc[h * cp.kv_tile + j] * vs[j * ldk + d];
-                o[i] = acc;
-            }
-        }
-        __syncthreads();
-        // partial (o, m, l) of the unit's G heads: one contiguous block of
-        // G rows of pw = hd + 4 floats, written locally and pushed
-        const int pw = hd + 4;
-        const int blk = (((b * K + g) * ns + s) * G) * pw;
-        for (int i = threadIdx.x; i < G * pw; i += blockDim.x) {
-            const int h = i / pw, e = i % pw;
-            S.attp[blk + i] = e < hd ? o[h * hd + e] : (e < hd + 2 ? S.red[2 * h + (e - hd)] : 0.0f);
-        }
-        __syncthreads();
-        push_block(cl, S.attp, blk, G * pw, cs, crank);
-        __syncthreads();   // o and red are reused by this CTA's next unit
+    // ---- attention (generate.c:121-156)
+    bool ok;
+    switch (hd) {
+    case 16: ok = lc_attention<16>(cp, S, cl, crank, l, t, fl, nf, ns, per, units, wrote_kv); break;
+    case 32: ok = lc_attention<32>(cp, S, cl, crank, l, t, fl, nf, ns, per, units, wrote_kv); break;
+    case 64: ok = lc_attention<64>(cp, S, cl, crank, l, t, fl, nf, ns, per, units, wrote_kv); break;
+    default: ok = lc_attention<0>(cp, S, cl, crank, l, t, fl, nf, ns, per, units, wrote_kv); break;
     }
-    if (!lc_sync(cl, S, cs)) return false;
+    if (!ok) return false;
 
-    // ---- combine splits (every CTA), then PROJ + residual (generate.c:158-163)
-    {
-        const int pw = hd + 4;
-        for (int e = threadIdx.x; e < nf * H * hd; e += blockDim.x) {
-            const int i = e / (H * hd), h = (e / hd) % H, d = e % hd, b = fl[i];
-            const int g = h / G, hh = h % G;
-            const float* pp = S.attp + ((size_t)((b * K + g) * ns) * G + hh) * pw;  // split stride G*pw
-            float M = -INFINITY;
-            for (int s2 = 0; s2 < ns; s2++) M = fmaxf(M, pp[s2 * G * pw + hd]);
-            float num = 0.0f, den = 0.0f;
-            for (int s2 = 0; s2 < ns; s2++) {
-                const float* q2 = pp + s2 * G * pw;
-                const float ls = q2[hd + 1];
-                if (ls > 0.0f) {
-                    const float wgt = expf(q2[hd] - M);
-                    den += wgt * ls;
-                    num += wgt * q2[d];
-                }
-            }
-            S.att[b * D + h * hd + d] = num / den;
-        }
-        __syncthreads();
-    }
+    // ---- PROJ + residual (generate.c:158-163)
     for (int r0 = sl.p0 + 4 * warp; r0 < sl.p1; r0 += 4 * kWarps) {
         const float* w0 = wp + (size_t)(r0 - sl.p0) * D;
         const float val = lc_gemv4(w0, w0 + D, w0 + 2 * D, w0 + 3 * D, D, S.att, D, fl, nf);
@@ -607,13 +743,14 @@ __device__ void lc_main(const ClusterParams& cp, unsigned char* smem, cg::cluste
     const LoopParams<float>& p = cp.lp;
     LcState S;
     S.bar = reinterpret_cast<unsigned long long*>(smem);
+    S.kvbar = S.bar + kStages;
     S.ints = reinterpret_cast<int*>(smem + 64);
     S.red = reinterpret_cast<float*>(smem + 64 + 64 * 4);
     S.x = reinterpret_cast<float*>(smem + cp.off_x);
     S.xn = reinterpret_cast<float*>(smem + cp.off_xn);
     S.qkv = reinterpret_cast<float*>(smem + cp.off_qkv);
-    S.attp = reinterpret_cast<float*>(smem + cp.off_attp);
     S.att = reinterpret_cast<float*>(smem + cp.off_att);
+    S.attp = reinterpret_cast<float*>(smem + cp.off_attp);
     S.f = reinterpret_cast<float*>(smem + cp.off_f);
     S.sc = reinterpret_cast<float*>(smem + cp.off_sc);
     S.kv = reinterpret_cast<float*>(smem + cp.off_kv);
@@ -629,9 +766,13 @@ __device__ void lc_main(const ClusterParams& cp, unsigned char* smem, cg::cluste
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kStages; s++) mbar_init(&S.bar[s], 1);
+        mbar_init(S.kvbar, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         S.ints[38] = 0;
+        S.ints[39] = 0;
     }
+    S.kvph = 0u;
+    S.kvpend = 0;
     for (int b = threadIdx.x; b < p.B; b += blockDim.x) {
         const SeqState& g = p.seq[b];
         SeqMirror& m = S.seq[b];
@@ -830,6 +971,9 @@ __device__ void lc_main(const ClusterParams& cp, unsigned char* smem, cg::cluste
             break;
         }
     }
+    // a K/V tile still in flight after a failed wait
+    if (threadIdx.x == 0 && S.kvpend && !mbar_wait(S.kvbar, S.kvph, p.timeout_ns))
+        atomicMax(p.status, (int)ST_TIMEOUT);
     __syncthreads();
     cl.sync();   // no CTA leaves while others may still write its shared memory
 }

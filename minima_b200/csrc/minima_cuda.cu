@@ -195,7 +195,10 @@ bool plan_cluster(mc_session* s, const cudaDeviceProp& prop) {
     const mc_model* m = s->m;
     if (m->dtype != MC_WEIGHTS_F32) return false;
     const int G = m->H / m->K;
-    if (m->hd % 4 || m->D % 4 || m->F % 4 || m->Q % 2 || G > 16) return false;
+    // attention units hold G heads x hd/32 outputs per lane in registers
+    if (m->hd % 4 || m->D % 4 || m->F % 4 || m->Q % 2 || G > mc::kAttMaxG ||
+        m->hd > 32 * mc::kAttMaxND)
+        return false;
     const char* env = getenv("MINIMA_CUDA_LOOP");
     if (env && strcmp(env, "grid") == 0) return false;
     const size_t optin = prop.sharedMemPerBlockOptin;
@@ -206,7 +209,7 @@ bool plan_cluster(mc_session* s, const cudaDeviceProp& prop) {
         cudaGetLastError();
         return false;
     }
-    const int B8 = mc::kBCMax;
+    const int B8 = std::min(s->Bcap, mc::kBCMax);    // activation rows held per CTA
     for (int cs : {16, 8}) {
         mc::ClusterParams cp{};
         cp.cs = cs;
@@ -214,8 +217,6 @@ bool plan_cluster(mc_session* s, const cudaDeviceProp& prop) {
         // weight slice plus this layer's rms1 / rms2 scales
         const size_t stage_f = align_up(mc::slice_floats(s0, m->D, m->F) + 2 * (size_t)m->D, 32);
         if (stage_f * 4 >= (1u << 20)) continue;           // mbarrier tx-count limit
-        int attp_rows = 0;                                   // max over B of B * splits(B)
-        for (int B = 1; B <= B8; B++) attp_rows = std::max(attp_rows, B * std::max(1, cs / (B * m->K)));
         size_t off = mc::kLcHeader;
         auto take = [&](size_t floats, size_t align) {
             off = align_up(off, align);
@@ -226,23 +227,26 @@ bool plan_cluster(mc_session* s, const cudaDeviceProp& prop) {
         cp.off_x = take((size_t)B8 * m->D, 16);
         cp.off_xn = take((size_t)B8 * m->D, 16);
         cp.off_qkv = take((size_t)B8 * m->Q, 16);
-        cp.off_attp = take((size_t)attp_rows * m->H * (m->hd + 4), 16);
         cp.off_att = take((size_t)B8 * m->D, 16);
+        // merged states of split attention units: at most max(cs, B K) units
+        cp.off_attp = take((size_t)std::max(cs, B8 * m->K) * ((G * m->hd + 2 * G + 3) & ~3), 16);
         cp.off_f = take((size_t)B8 * m->F, 16);
         cp.off_rmsf = take((size_t)m->D, 16);
         cp.off_rope = take((size_t)std::max(m->hd, 2), 16);
         const size_t fixed = off;
-        int tile = 128;
-        for (; tile >= 16; tile /= 2) {
-            size_t o2 = align_up(fixed, 16) + ((size_t)G * tile + (size_t)G * m->hd) * 4;
-            o2 = align_up(o2, 16) + 2 * (size_t)tile * (m->hd + 4) * 4;
+        // per-warp attention states and probabilities, then the K/V tile
+        const size_t sc_f = (size_t)mc::kWarps * (G * m->hd + 2 * G + 32 * mc::kAttMaxG);
+        int tile = mc::kAttMaxTile;
+        for (; tile >= 32; tile /= 2) {
+            size_t o2 = align_up(fixed, 16) + sc_f * 4;
+            o2 = align_up(o2, 16) + 2 * (size_t)tile * m->hd * 4;
             o2 = align_up(o2, 128) + mc::kStages * stage_f * 4;
             if (o2 <= optin) break;
         }
-        if (tile < 16) continue;
+        if (tile < 32) continue;
         cp.kv_tile = tile;
-        cp.off_sc = take((size_t)G * tile + (size_t)G * m->hd, 16);
-        cp.off_kv = take(2 * (size_t)tile * (m->hd + 4), 16);
+        cp.off_sc = take(sc_f, 16);
+        cp.off_kv = take(2 * (size_t)tile * m->hd, 16);
         cp.off_stage = take(mc::kStages * stage_f, 128);
         cp.stage_floats = (unsigned)stage_f;
         const size_t lc_bytes = off;
@@ -616,7 +620,6 @@ mc_status run_cluster(mc_session* s, mc::LoopParams<float>& p) {
     s->last_T = p.T;
     mc::ClusterParams cp = s->cl_plan;
     cp.lp = p;
-    cp.n_split = std::max(1, s->cl_cs / (p.B * s->m->K));
     cp.xfin = s->xfin;
     cp.hgen = s->hgen;
     cp.go = s->hsync;
