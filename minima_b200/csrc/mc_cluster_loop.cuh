@@ -703,39 +703,66 @@ __device__ bool lc_layer(const ClusterParams& cp, const CSlice& sl, LcState& S,
     return lc_sync(cl, S, cs);
 }
 
-// Greedy choice from the head partials for sequence b (generate.c:469-478,
-// 510): returns the id and whether the reference draws from the RNG.
-__device__ void lc_choose(const ClusterParams& cp, int b, int nhc, float* red, int* ints,
-                          int& id, bool& draws) {
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    float bv[2] = {-INFINITY, -INFINITY};
-    int bi[2] = {0x7fffffff, 0x7fffffff};
-    for (int c = threadIdx.x; c < nhc; c += blockDim.x)
-        for (int k = 0; k < 2; k++) {
-            const size_t at = ((size_t)b * nhc + c) * 2 + k;
-            const float v = ldcg(cp.hpv + at);
-            const int i = __ldcg(cp.hpi + at);
-            if (better(v, i, bv[k], bi[k])) { bv[k] = v; bi[k] = i; }
+// Greedy choice for head sequence b from the head CTAs' partials
+// (generate.c:447-460 with top_k == 1: NaN never wins, ties go to the lowest
+// id, and with every id banned the unbanned values decide) and its
+// bookkeeping (generate.c:560-595): history, penalty counts, stop sequence,
+// length.  One warp; lane 0 updates the mirrored table entry m and leaves
+// done / generated in ints[40 + slot] / ints[48 + slot].
+__device__ void lc_choose(const ClusterParams& cp, SeqMirror& m, int b, int nhc, int slot, int* ints) {
+    const LoopParams<float>& p = cp.lp;
+    const int lane = threadIdx.x & 31;
+    const bool twok = p.s.ngram > 0;
+    float bv0 = -INFINITY, bv1 = -INFINITY;
+    int bi0 = 0x7fffffff, bi1 = 0x7fffffff;
+    for (int c = lane; c < nhc; c += 32) {
+        const size_t at = ((size_t)b * nhc + c) * 2;
+        const float v = ldcg(cp.hpv + at);
+        const int i = __ldcg(cp.hpi + at);
+        if (better(v, i, bv0, bi0)) { bv0 = v; bi0 = i; }
+        if (twok) {
+            const float v1 = ldcg(cp.hpv + at + 1);
+            const int i1 = __ldcg(cp.hpi + at + 1);
+            if (better(v1, i1, bv1, bi1)) { bv1 = v1; bi1 = i1; }
         }
-    for (int k = 0; k < 2; k++) warp_argmax(bv[k], bi[k]);
-    __syncthreads();
-    if (lane == 0) {
-        red[warp] = bv[0]; ints[40 + warp] = bi[0];
-        red[16 + warp] = bv[1]; ints[48 + warp] = bi[1];
     }
-    __syncthreads();
-    float v0 = red[0], v1 = red[16];
-    int i0 = ints[40], i1 = ints[48];
-    for (int w = 1; w < kWarps; w++) {
-        if (better(red[w], ints[40 + w], v0, i0)) { v0 = red[w]; i0 = ints[40 + w]; }
-        if (better(red[16 + w], ints[48 + w], v1, i1)) { v1 = red[16 + w]; i1 = ints[48 + w]; }
+    warp_argmax(bv0, bi0);
+    if (twok) warp_argmax(bv1, bi1);
+    if (lane != 0) return;
+    if (bi0 == 0x7fffffff) bi0 = 0;
+    if (bi1 == 0x7fffffff) bi1 = 0;
+    int id;
+    bool draws;
+    if (isfinite(bv0)) { id = bi0; draws = true; }
+    else if (twok) { id = bi1; draws = isfinite(bv1); }
+    else { id = bi0; draws = false; }
+    if (draws) (void)rng_f32(m.rng);
+    const int P = m.P, g = m.gen, nnew = m.nnew;
+    uint16_t* out = p.out_ids + (size_t)b * p.out_cap;
+    out[P + g] = (uint16_t)id;
+    if (p.s.pen_active) p.counts[(size_t)b * p.V + id] += 1u;
+    const int generated = g + 1;
+    m.gen = generated;
+    bool stop = false;
+    if (p.s.stop_len > 0 && generated >= p.s.min_new && generated >= p.s.stop_len) {
+        stop = true;
+        const int s0 = P + generated - p.s.stop_len;
+        for (int k = 0; k < p.s.stop_len; k++)
+            if (ld_u16_cg(out + s0 + k) != (int)p.s.stop_ids[k]) { stop = false; break; }
     }
-    if (i0 == 0x7fffffff) i0 = 0;
-    if (i1 == 0x7fffffff) i1 = 0;
-    __syncthreads();
-    if (isfinite(v0)) { id = i0; draws = true; }
-    else if (cp.lp.s.ngram > 0) { id = i1; draws = isfinite(v1); }
-    else { id = i0; draws = false; }
+    if (stop) {
+        m.result = P + generated - p.s.stop_len;
+        m.final_pos = P + g;
+        m.done = 1;
+    } else if (generated >= nnew) {
+        m.result = P + nnew;
+        m.final_pos = P + nnew;
+        m.done = 1;
+    } else {
+        m.tok = id;
+    }
+    ints[40 + slot] = m.done;
+    ints[48 + slot] = m.gen;
 }
 
 __device__ void lc_main(const ClusterParams& cp, unsigned char* smem, cg::cluster_group& cl,
@@ -763,6 +790,7 @@ __device__ void lc_main(const ClusterParams& cp, unsigned char* smem, cg::cluste
     int* fl = S.ints;        // [16]
     int* hl = S.ints + 16;   // [16]
     int* toks = S.ints + 40; // [8] ids fed at this step
+    const int warp = threadIdx.x >> 5;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kStages; s++) mbar_init(&S.bar[s], 1);
@@ -900,45 +928,13 @@ __device__ void lc_main(const ClusterParams& cp, unsigned char* smem, cg::cluste
                 }
             }
             __syncthreads();
-            for (int i = 0; i < nh; i++) {
-                const int b = hl[i];
-                int id;
-                bool draws;
-                lc_choose(cp, b, nhc, S.red, S.ints, id, draws);
-                if (threadIdx.x == 0) {
-                    SeqMirror& m = S.seq[b];
-                    if (draws) (void)rng_f32(m.rng);
-                    const int P = m.P, g = m.gen, nnew = m.nnew;
-                    uint16_t* out = p.out_ids + (size_t)b * p.out_cap;
-                    out[P + g] = (uint16_t)id;
-                    if (p.s.pen_active) p.counts[(size_t)b * p.V + id] += 1u;
-                    const int generated = g + 1;
-                    m.gen = generated;
-                    bool stop = false;
-                    if (p.s.stop_len > 0 && generated >= p.s.min_new && generated >= p.s.stop_len) {
-                        stop = true;
-                        const int s0 = P + generated - p.s.stop_len;
-                        for (int k = 0; k < p.s.stop_len; k++)
-                            if (ld_u16_cg(out + s0 + k) != (int)p.s.stop_ids[k]) { stop = false; break; }
-                    }
-                    if (stop) {
-                        m.result = P + generated - p.s.stop_len;
-                        m.final_pos = P + g;
-                        m.done = 1;
-                    } else if (generated >= nnew) {
-                        m.result = P + nnew;
-                        m.final_pos = P + nnew;
-                        m.done = 1;
-                    } else {
-                        m.tok = id;
-                    }
-                    S.ints[34] = m.done;
-                    S.ints[35] = m.gen;
-                }
-                __syncthreads();
-                if (p.s.ngram > 0 && !S.ints[34]) compute_bans(p, b, S.seq[b].P + S.ints[35]);
-                __syncthreads();
-            }
+            // one warp per head sequence; bans need the whole CTA afterwards
+            if (warp < nh) lc_choose(cp, S.seq[hl[warp]], hl[warp], nhc, warp, S.ints);
+            __syncthreads();
+            if (p.s.ngram > 0)
+                for (int i = 0; i < nh; i++)
+                    if (!S.ints[40 + i]) compute_bans(p, hl[i], S.seq[hl[i]].P + S.ints[48 + i]);
+            __syncthreads();
             // the other layer CTAs get the updated table before the barrier
             const int words = p.B * (int)(sizeof(SeqMirror) / 4);
             for (int e = threadIdx.x; e < words * cp.cs; e += blockDim.x) {
@@ -978,6 +974,98 @@ __device__ void lc_main(const ClusterParams& cp, unsigned char* smem, cg::cluste
     cl.sync();   // no CTA leaves while others may still write its shared memory
 }
 
+// Logits of this head CTA's rows for the head sequences (generate.c:187-191)
+// and the sampler's greedy choice among them.  NHP is nh rounded up to a
+// power of two: a warp takes groups of 32 / NHP rows; lanes split each row
+// in float4 chunks (the sequences' chunks stay in registers) and a
+// transposed reduction leaves lane l with row l / NHP of the group for
+// sequence slot l % NHP.  Each lane keeps the best transformed value of its
+// slot; the warp's best per slot lands in red / ints (k = 0: with bans,
+// k = 1: without, only when bans are active).
+template <int NHP>
+__device__ __forceinline__ void hc_rows(const ClusterParams& cp, const float* emb, const float* xs,
+                                        const int* hl, const int* hg, int nh, int r0, int nr,
+                                        float* red, int* ints) {
+    const LoopParams<float>& p = cp.lp;
+    const int D = p.D;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    constexpr int R = 32 / NHP;
+    const int s = lane % NHP;
+    const int nwords = (p.V + 31) >> 5;
+    const bool twok = p.s.ngram > 0;
+    float bv0 = -INFINITY, bv1 = -INFINITY;
+    int bi0 = 0x7fffffff, bi1 = 0x7fffffff;
+    const int ngroups = (nr + R - 1) / R;
+    for (int gq = warp; gq < ngroups; gq += kWarps) {
+        float v[32];
+#pragma unroll
+        for (int j = 0; j < 32; j++) v[j] = 0.0f;
+        for (int k0 = 0; k0 < D; k0 += 128) {
+            const int k = k0 + 4 * lane;
+            const bool kin = k < D;
+            float4 xv[NHP];
+#pragma unroll
+            for (int ss = 0; ss < NHP; ss++)
+                xv[ss] = kin && ss < nh ? *reinterpret_cast<const float4*>(xs + hl[ss] * D + k)
+                                        : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+#pragma unroll
+            for (int rr = 0; rr < R; rr++) {
+                const int row = gq * R + rr;
+                const float4 w = kin && row < nr
+                                     ? *reinterpret_cast<const float4*>(emb + (size_t)row * cp.hc_ld + k)
+                                     : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+#pragma unroll
+                for (int ss = 0; ss < NHP; ss++) {
+                    float& a = v[rr * NHP + ss];
+                    a = fmaf(w.x, xv[ss].x, a);
+                    a = fmaf(w.y, xv[ss].y, a);
+                    a = fmaf(w.z, xv[ss].z, a);
+                    a = fmaf(w.w, xv[ss].w, a);
+                }
+            }
+        }
+        const float dot = transpose_reduce32(v);
+        const int row = gq * R + lane / NHP, vid = r0 + row;
+        if (row < nr && s < nh) {
+            const int b = hl[s];
+            const float lg = vid < 4 ? -INFINITY : dot;
+            if (p.trace) {
+                const int gi = hg[b];
+                if (gi < p.trace_steps) p.trace[((size_t)b * p.trace_steps + gi) * p.V + vid] = lg;
+            }
+            const unsigned cnt = p.s.pen_active ? __ldcg(p.counts + (size_t)b * p.V + vid) : 0u;
+            const bool ban =
+                twok && ((__ldcg(p.banned + (size_t)b * nwords + (vid >> 5)) >> (vid & 31)) & 1u);
+            const float tv = transform_value(lg, cnt, ban, p.s);
+            if (better(tv, vid, bv0, bi0)) { bv0 = tv; bi0 = vid; }
+            if (twok) {
+                const float tn = transform_value(lg, cnt, false, p.s);
+                if (better(tn, vid, bv1, bi1)) { bv1 = tn; bi1 = vid; }
+            }
+        }
+    }
+    // the warp's best per slot: lanes of one slot are NHP apart
+#pragma unroll
+    for (int o = NHP; o < 32; o <<= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, bv0, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi0, o);
+        if (better(ov, oi, bv0, bi0)) { bv0 = ov; bi0 = oi; }
+        if (twok) {
+            const float ov1 = __shfl_xor_sync(0xffffffffu, bv1, o);
+            const int oi1 = __shfl_xor_sync(0xffffffffu, bi1, o);
+            if (better(ov1, oi1, bv1, bi1)) { bv1 = ov1; bi1 = oi1; }
+        }
+    }
+    if (lane < nh && lane < NHP) {
+        red[lane * kWarps + warp] = bv0;
+        ints[64 + lane * kWarps + warp] = bi0;
+        if (twok) {
+            red[(kBCMax + lane) * kWarps + warp] = bv1;
+            ints[64 + (kBCMax + lane) * kWarps + warp] = bi1;
+        }
+    }
+}
+
 // ------------------------------------------------------------- head CTAs
 __device__ void hc_main(const ClusterParams& cp, unsigned char* smem, int hc) {
     const LoopParams<float>& p = cp.lp;
@@ -990,8 +1078,6 @@ __device__ void hc_main(const ClusterParams& cp, unsigned char* smem, int hc) {
     float* emb = reinterpret_cast<float*>(smem + kHcEmbOffset);
     float* xs = reinterpret_cast<float*>(smem + cp.off_hc_x);
     const int nhc = (cp.n_clusters - 1) * cp.cs;
-    const int nwords = (p.V + 31) >> 5;
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     if (threadIdx.x == 0) {
         mbar_init(bar, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -1037,70 +1123,14 @@ __device__ void hc_main(const ClusterParams& cp, unsigned char* smem, int hc) {
         __syncthreads();
         const int nh = ints[1];
         const int* hl = ints + 8;
-        // thread per row: full dot products from the resident slice
-        float bv[2][kBCMax];
-        int bi[2][kBCMax];
-#pragma unroll
-        for (int i = 0; i < kBCMax; i++) {
-            bv[0][i] = bv[1][i] = -INFINITY;
-            bi[0][i] = bi[1][i] = 0x7fffffff;
-        }
-        const float* xb[kBCMax];
-#pragma unroll
-        for (int i = 0; i < kBCMax; i++) xb[i] = xs + (i < nh ? hl[i] : 0) * D;
-        for (int r = threadIdx.x; r < nr; r += blockDim.x) {
-            const float* __restrict__ er = emb + (size_t)r * cp.hc_ld;
-            float acc[kBCMax];
-#pragma unroll
-            for (int i = 0; i < kBCMax; i++) acc[i] = 0.0f;
-#pragma unroll 4
-            for (int k = 0; k < D; k += 4) {
-                const float4 w = *reinterpret_cast<const float4*>(er + k);
-#pragma unroll
-                for (int i = 0; i < kBCMax; i++)
-                    if (i < nh) {
-                        const float4 xv = *reinterpret_cast<const float4*>(xb[i] + k);
-                        acc[i] = fmaf(w.x, xv.x, acc[i]);
-                        acc[i] = fmaf(w.y, xv.y, acc[i]);
-                        acc[i] = fmaf(w.z, xv.z, acc[i]);
-                        acc[i] = fmaf(w.w, xv.w, acc[i]);
-                    }
-            }
-            const int v = r0 + r;
-            // static indices only: the per-sequence state stays in registers
-#pragma unroll
-            for (int i = 0; i < kBCMax; i++) {
-                if (i >= nh) continue;
-                const int b = hl[i];
-                const float lg = v < 4 ? -INFINITY : acc[i];
-                if (p.trace) {
-                    const int gi = hg[b];
-                    if (gi < p.trace_steps) p.trace[((size_t)b * p.trace_steps + gi) * p.V + v] = lg;
-                }
-                const unsigned cnt = p.s.pen_active ? __ldcg(p.counts + (size_t)b * p.V + v) : 0u;
-                const bool ban = p.s.ngram > 0 &&
-                                 ((__ldcg(p.banned + (size_t)b * nwords + (v >> 5)) >> (v & 31)) & 1u);
-                const float tv = transform_value(lg, cnt, ban, p.s);
-                if (better(tv, v, bv[0][i], bi[0][i])) { bv[0][i] = tv; bi[0][i] = v; }
-                if (p.s.ngram > 0) {
-                    const float tn = transform_value(lg, cnt, false, p.s);
-                    if (better(tn, v, bv[1][i], bi[1][i])) { bv[1][i] = tn; bi[1][i] = v; }
-                }
-            }
-        }
-#pragma unroll
-        for (int i = 0; i < kBCMax; i++) {
-            if (i >= nh) continue;
-#pragma unroll
-            for (int k = 0; k < 2; k++) {
-                float v = bv[k][i];
-                int id = bi[k][i];
-                warp_argmax(v, id);
-                if (lane == 0) { red[(k * kBCMax + i) * kWarps + warp] = v; ints[64 + (k * kBCMax + i) * kWarps + warp] = id; }
-            }
+        switch (nh <= 1 ? 1 : nh <= 2 ? 2 : nh <= 4 ? 4 : 8) {
+        case 1: hc_rows<1>(cp, emb, xs, hl, hg, nh, r0, nr, red, ints); break;
+        case 2: hc_rows<2>(cp, emb, xs, hl, hg, nh, r0, nr, red, ints); break;
+        case 4: hc_rows<4>(cp, emb, xs, hl, hg, nh, r0, nr, red, ints); break;
+        default: hc_rows<8>(cp, emb, xs, hl, hg, nh, r0, nr, red, ints); break;
         }
         __syncthreads();
-        if (threadIdx.x < 2 * nh) {
+        if (threadIdx.x < (p.s.ngram > 0 ? 2 : 1) * nh) {
             const int k = threadIdx.x / nh, i = threadIdx.x % nh;
             const int base = (k * kBCMax + i) * kWarps;
             float v = red[base];
