@@ -560,28 +560,37 @@ __device__ bool lc_attention(const ClusterParams& cp, LcState& S, cg::cluster_gr
     // (async proxy) in other CTAs: order them before the cluster barrier
     if (wrote_kv) asm volatile("fence.proxy.async.global;" ::: "memory");
     if (!lc_sync(cl, S, cs)) return false;
-    // combine the splits (every CTA): a warp per (sequence, head)
+    // combine the splits (every CTA): per (sequence, head) the split weights
+    // exp(m_s - M) and 1 / sum, then every output element
     if (ns > 1) {
-        for (int pr = warp; pr < nf * H; pr += kWarps) {
+        // ns > 1 implies nf K <= cs / 2, so nf H <= G cs / 2 <= 32 pairs and nf H ns <= 64
+        float* wgt = S.sc;                                         // [pairs][ns]
+        float* rden = S.sc + 64;                                   // [pairs]
+        int* src = reinterpret_cast<int*>(S.sc + 96);              // [pairs] attp offset
+        int* dsto = reinterpret_cast<int*>(S.sc + 128);            // [pairs] att offset
+        for (int pr = threadIdx.x; pr < nf * H; pr += blockDim.x) {
             const int i = pr / H, h = pr - i * H, g = h / G, hh = h - g * G;
-            const float* pp = S.attp + (size_t)((i * K + g) * ns) * pwp;
+            const float* pp = S.attp + (size_t)((i * K + g) * ns) * pwp + ghd + 2 * hh;
             float M = -INFINITY;
-            for (int s2 = 0; s2 < ns; s2++) M = fmaxf(M, pp[s2 * pwp + ghd + 2 * hh]);
-            float den = 0.0f, num[kAttMaxND];
-#pragma unroll
-            for (int j = 0; j < kAttMaxND; j++) num[j] = 0.0f;
+            for (int s2 = 0; s2 < ns; s2++) M = fmaxf(M, pp[s2 * pwp]);
+            float den = 0.0f;
             for (int s2 = 0; s2 < ns; s2++) {
-                const float* ps = pp + s2 * pwp;
-                const float ms = ps[ghd + 2 * hh];
+                const float ms = pp[s2 * pwp];
                 const float c = ms == -INFINITY ? 0.0f : expf(ms - M);   // a split may see no keys
-                den += c * ps[ghd + 2 * hh + 1];
-#pragma unroll
-                for (int j = 0; j < kAttMaxND; j++)
-                    if (lane + 32 * j < hd) num[j] += c * ps[hh * hd + lane + 32 * j];
+                wgt[pr * ns + s2] = c;
+                den += c * pp[s2 * pwp + 1];
             }
-#pragma unroll
-            for (int j = 0; j < kAttMaxND; j++)
-                if (lane + 32 * j < hd) S.att[fl[i] * D + h * hd + lane + 32 * j] = num[j] / den;
+            rden[pr] = den;
+            src[pr] = ((i * K + g) * ns) * pwp + hh * hd;
+            dsto[pr] = fl[i] * D + h * hd;
+        }
+        __syncthreads();
+        for (int e = threadIdx.x; e < nf * H * hd; e += blockDim.x) {
+            const int pr = e / hd, d = e - pr * hd;
+            const float* ps = S.attp + src[pr] + d;
+            float num = 0.0f;
+            for (int s2 = 0; s2 < ns; s2++) num += wgt[pr * ns + s2] * ps[s2 * pwp];
+            S.att[dsto[pr] + d] = num / rden[pr];
         }
         __syncthreads();
     }
