@@ -118,6 +118,19 @@ def algorithmic_bytes(P, nnew, B, t0=0, weight_bytes_per=4):
     return total
 
 
+def profiled_traffic(kernel_name):
+    """DRAM bytes per launch of `kernel_name` from the ncu summaries under
+    profiles/ (one *_traffic.json per captured kernel); None when that kernel
+    has no capture."""
+    import glob
+    for tf in sorted(glob.glob(os.path.join(ROOT, "profiles", "*_traffic.json"))):
+        with open(tf) as fh:
+            rec = json.load(fh)
+        if rec.get("kernel", "").split("<")[0] == (kernel_name or "").split("<")[0]:
+            return rec.get("dram_bytes_per_launch")
+    return None
+
+
 def measured_hbm():
     path = os.path.join(ROOT, "MEASURED_PEAKS.json")
     if os.path.exists(path):
@@ -334,11 +347,7 @@ def native_arm(args):
         kms = statistics.mean(kernel_ms) - prefill_ms
         peak, peak_src = measured_hbm()
         achieved = algo / (kms / 1e3) / 1e9
-        traffic = None
-        tf = os.path.join(ROOT, "profiles", "token_loop_c2_traffic.json")
-        if os.path.exists(tf):
-            with open(tf) as fh:
-                traffic = json.load(fh).get("dram_bytes_per_launch")
+        traffic = profiled_traffic(kernel_name)
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": total_ms / args.steps,

@@ -629,8 +629,12 @@ mc_status run_cluster(mc_session* s, mc::LoopParams<float>& p) {
     MC_CUDA(cudaMemsetAsync(s->stamps, 0, ((size_t)p.T + 1) * 8, s->stream));
     MC_CUDA(cudaMemsetAsync(s->status, 0, 256, s->stream));
     MC_CUDA(cudaMemsetAsync(s->hsync, 0, 64 * 4, s->stream));
-    cudaError_t e = launch_cluster(cp, s->cl_cs, s->cl_nc, s->cl_smem, s->stream, true);
-    if (e != cudaSuccess) {
+    // MINIMA_CUDA_CLUSTER_NONCOOP=1 skips the cooperative attribute (kernel
+    // profilers that cannot instrument cooperative cluster launches)
+    const char* noncoop = getenv("MINIMA_CUDA_CLUSTER_NONCOOP");
+    const bool coop = !(noncoop && noncoop[0] == '1');
+    cudaError_t e = launch_cluster(cp, s->cl_cs, s->cl_nc, s->cl_smem, s->stream, coop);
+    if (e != cudaSuccess && coop) {
         // cooperative scheduling of clusters unsupported: the plan already
         // checked that every cluster can be resident, and every wait is bounded
         cudaGetLastError();
