@@ -212,6 +212,50 @@ mc_status mc_generate_static(const mc_model_desc* w, int batch,
     uint16_t* out_ids, int out_cap, const mc_sampling* opts,
     uint64_t* rng_states, int* out_counts, int max_seq, void* stream);
 
+/*
+ * Checkpoints — the reference's on-disk format (checkpoint.c:154-234):
+ * "MINIMA04" / "MINIMA05", a 112-byte header (v5: 116, the optimizer type
+ * appended), the nine model arrays in MODEL_ARRAYS order (checkpoint.c:43-52),
+ * then the optimizer moments (m, and v for AdamW, per array), all fp32
+ * little-endian, nothing after them.
+ *
+ * mc_checkpoint_inspect    <- the header and length checks of checkpoint_load
+ *                             (checkpoint.c:301-400); reads no array, touches
+ *                             no device.  Fills *info when it returns MC_OK.
+ * mc_model_load_checkpoint <- checkpoint_load's model half, straight to the
+ *                             device: the file streams through pinned staging
+ *                             buffers into the model's device arrays (bf16
+ *                             RNE on the device when weights_dtype is
+ *                             MC_WEIGHTS_BF16); the moments stream through
+ *                             too, because checkpoint_load rejects a file with
+ *                             any non-finite float (checkpoint.c:403-405) and
+ *                             that check runs on the device.  Transactional:
+ *                             on failure *out stays NULL.  The tokenizer
+ *                             fingerprint must equal expected_tokenizer_hash
+ *                             (checkpoint.c:376) unless flags has
+ *                             MC_CKPT_ANY_TOKENIZER.  The optimizer type is
+ *                             reported, not matched (a decoder has none).
+ * Rejections return MC_ERR_INVALID and name the failed check.
+ */
+#define MC_CKPT_ANY_TOKENIZER 0x1u
+typedef struct {
+    uint32_t version;                  /* 4 or 5 */
+    int32_t vocab_size, dim, n_layers, n_heads, ffn_dim, max_seq;
+    uint64_t n_params;                 /* model floats (checkpoint.c:33-41) */
+    int64_t step;
+    uint64_t rng_state;                /* as checkpoint_load restores it: 0 -> 0x123456789abcdef0 */
+    uint64_t tokenizer_hash;
+    float lr, beta1, beta2, eps, weight_decay, schedule_base_lr;
+    int64_t schedule_total_steps, schedule_warmup_steps;
+    int32_t schedule_type;             /* 0 cosine, 1 constant */
+    int32_t optimizer_type;            /* 0 AdamW, 1 Lion (v4: AdamW) */
+    uint64_t header_bytes, file_bytes;
+} mc_checkpoint_info;
+mc_status mc_checkpoint_inspect(const char* path, mc_checkpoint_info* info);
+mc_status mc_model_load_checkpoint(const char* path, int weights_dtype,
+    uint64_t expected_tokenizer_hash, unsigned flags, mc_model** out,
+    mc_checkpoint_info* info);
+
 const char* mc_last_error(void);
 
 #ifdef __cplusplus

@@ -30,7 +30,8 @@ LIB_HOST = os.path.join(PKG, "libminima_host.so")
 CUDA_SYMBOLS = ("mc_init", "mc_model_create", "mc_model_update", "mc_model_destroy",
                 "mc_session_create", "mc_session_destroy", "mc_generate", "mc_forward_logits",
                 "mc_last_kernel_ms", "mc_last_launch_count", "mc_last_step_times",
-                "mc_last_kernel_name", "mc_last_prefill", "mc_session_stream", "mc_last_error")
+                "mc_last_kernel_name", "mc_last_prefill", "mc_session_stream", "mc_last_error",
+                "mc_checkpoint_inspect", "mc_model_load_checkpoint")
 GENERATE_SYMBOLS = ("kvcache_init", "kvcache_reset", "generation_check_kv_cache",
                     "generation_inspect_next_tokens", "generate", "generate_with_options",
                     "generate_ex", "generate_batch_with_options", "minima_cuda_select_device",
@@ -207,6 +208,9 @@ def _declare(host, cuda, gen):
     cuda.mc_last_kernel_name.restype = C.c_char_p
     cuda.mc_last_kernel_name.argtypes = [vp]
     cuda.mc_last_error.restype = C.c_char_p
+    cuda.mc_checkpoint_inspect.argtypes = [C.c_char_p, C.POINTER(CheckpointInfo)]
+    cuda.mc_model_load_checkpoint.argtypes = [C.c_char_p, C.c_int, C.c_uint64, C.c_uint,
+                                              C.POINTER(vp), C.POINTER(CheckpointInfo)]
 
     gen.kvcache_init.restype = C.c_bool
     gen.kvcache_init.argtypes = [C.POINTER(KVCache), C.POINTER(Arena), C.POINTER(Model), C.c_int]
@@ -388,6 +392,35 @@ def generate_batch(hm: HostModel, tok: Tokenizer, caches: Caches, prompts, promp
 
 
 # ------------------------------------------------------------ C ABI layer
+MC_CKPT_ANY_TOKENIZER = 0x1
+
+
+class CheckpointInfo(C.Structure):
+    """mc_checkpoint_info: a checkpoint's header (checkpoint.c:154-234)."""
+    _fields_ = [("version", C.c_uint32), ("vocab_size", C.c_int32), ("dim", C.c_int32),
+                ("n_layers", C.c_int32), ("n_heads", C.c_int32), ("ffn_dim", C.c_int32),
+                ("max_seq", C.c_int32), ("n_params", C.c_uint64), ("step", C.c_int64),
+                ("rng_state", C.c_uint64), ("tokenizer_hash", C.c_uint64), ("lr", C.c_float),
+                ("beta1", C.c_float), ("beta2", C.c_float), ("eps", C.c_float),
+                ("weight_decay", C.c_float), ("schedule_base_lr", C.c_float),
+                ("schedule_total_steps", C.c_int64), ("schedule_warmup_steps", C.c_int64),
+                ("schedule_type", C.c_int32), ("optimizer_type", C.c_int32),
+                ("header_bytes", C.c_uint64), ("file_bytes", C.c_uint64)]
+
+    def as_dict(self):
+        return {k: getattr(self, k) for k, _ in self._fields_}
+
+
+def checkpoint_inspect(path):
+    """mc_checkpoint_inspect: header and length checks of checkpoint_load, no
+    device work.  Returns the header as a dict; raises MinimaCudaError when
+    the file would be rejected."""
+    _, cuda, _ = libs()
+    info = CheckpointInfo()
+    _check(cuda.mc_checkpoint_inspect(os.fsencode(path), C.byref(info)), "mc_checkpoint_inspect")
+    return info.as_dict()
+
+
 class DeviceModel:
     """mc_model: weights of a HostModel resident on the current device."""
 
@@ -396,7 +429,30 @@ class DeviceModel:
         _check(cuda.mc_init(device), "mc_init")
         self.h = C.c_void_p()
         self._desc = hm.desc()
+        self.info = None
         _check(cuda.mc_model_create(C.byref(self._desc), dtype, C.byref(self.h)), "mc_model_create")
+
+    @classmethod
+    def from_checkpoint(cls, path, dtype=MC_WEIGHTS_F32, tokenizer_hash=None, device=0):
+        """mc_model_load_checkpoint: the model arrays of a reference
+        checkpoint streamed to the device.  tokenizer_hash=None accepts any
+        fingerprint.  The header is kept in .info."""
+        _, cuda, _ = libs()
+        _check(cuda.mc_init(device), "mc_init")
+        self = cls.__new__(cls)
+        self.h = C.c_void_p()
+        info = CheckpointInfo()
+        flags = MC_CKPT_ANY_TOKENIZER if tokenizer_hash is None else 0
+        _check(cuda.mc_model_load_checkpoint(os.fsencode(path), dtype, tokenizer_hash or 0, flags,
+                                             C.byref(self.h), C.byref(info)),
+               "mc_model_load_checkpoint")
+        self.info = info.as_dict()
+        # dimensions only: the weights live on the device
+        K = kv_head_count(info.n_heads)
+        hd = info.dim // info.n_heads
+        self._desc = ModelDesc(info.vocab_size, info.dim, info.n_layers, info.n_heads, K, hd,
+                               K * hd, info.dim + 2 * K * hd, info.ffn_dim, info.max_seq)
+        return self
 
     def close(self):
         if self.h:

@@ -18,6 +18,7 @@
 #include "mc_token_loop.cuh"
 #include "mc_cluster_loop.cuh"
 #include "mc_prefill.cuh"
+#include "mc_checkpoint.cuh"
 
 namespace {
 
@@ -291,7 +292,7 @@ bool plan_cluster(mc_session* s, const cudaDeviceProp& prop) {
     return false;
 }
 
-mc_status validate_desc(const mc_model_desc* d) {
+mc_status validate_dims(const mc_model_desc* d) {
     if (!d) return fail(MC_ERR_INVALID, "null model description");
     if (d->vocab_size < 5 || d->vocab_size > MC_MAX_VOCAB || d->dim <= 0 || d->dim > MC_MAX_DIM ||
         d->n_layers <= 0 || d->n_layers > MC_MAX_LAYERS || d->n_heads <= 0 ||
@@ -303,6 +304,12 @@ mc_status validate_desc(const mc_model_desc* d) {
     if (d->head_dim != hd || d->n_kv_heads != K || d->kv_dim != K * hd ||
         d->qkv_dim != d->dim + 2 * K * hd)
         return fail(MC_ERR_INVALID, "derived model dimensions inconsistent (model.c:55-89)");
+    return MC_OK;
+}
+
+mc_status validate_desc(const mc_model_desc* d) {
+    const mc_status st = validate_dims(d);
+    if (st) return st;
     if (!d->tok_emb || !d->attn_qkv || !d->attn_proj || !d->ffn_up || !d->ffn_gate ||
         !d->ffn_down || !d->rms1_scale || !d->rms2_scale || !d->rms_final_scale)
         return fail(MC_ERR_INVALID, "null weight pointer");
@@ -351,11 +358,13 @@ mc_status mc_init(int device) {
     return MC_OK;
 }
 
-mc_status mc_model_create(const mc_model_desc* d, int dtype, mc_model** out) {
-    if (!out) return fail(MC_ERR_INVALID, "null output handle");
-    *out = nullptr;
-    mc_status st = validate_desc(d);
-    if (st) return st;
+}  // extern "C"
+
+namespace {
+
+// Device buffers and RoPE table of a model with d's dimensions (weights not
+// yet written).
+mc_status model_alloc(const mc_model_desc* d, int dtype, mc_model** out) {
     if (dtype != MC_WEIGHTS_F32 && dtype != MC_WEIGHTS_BF16)
         return fail(MC_ERR_INVALID, "unknown weight dtype %d", dtype);
     mc_model* m = new mc_model();
@@ -398,6 +407,22 @@ mc_status mc_model_create(const mc_model_desc* d, int dtype, mc_model** out) {
             return fail(MC_ERR_CUDA, "rope upload: %s", cudaGetErrorString(e));
         }
     }
+    *out = m;
+    return MC_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+mc_status mc_model_create(const mc_model_desc* d, int dtype, mc_model** out) {
+    if (!out) return fail(MC_ERR_INVALID, "null output handle");
+    *out = nullptr;
+    mc_status st = validate_desc(d);
+    if (st) return st;
+    mc_model* m = nullptr;
+    st = model_alloc(d, dtype, &m);
+    if (st) return st;
     st = upload_weights(m, d);
     if (st) {
         mc_model_destroy(m);
@@ -1282,3 +1307,238 @@ extern "C" mc_status mc_generate_static(const mc_model_desc* w, int batch,
         return fail(MC_ERR_DEVICE, "mc_generate_static: kernel status %d", g_static_status);
     return MC_OK;
 }
+
+// ------------------------------------------------------------- checkpoints
+namespace {
+
+constexpr char kCkptMagicV4[8] = {'M', 'I', 'N', 'I', 'M', 'A', '0', '4'};
+constexpr char kCkptMagicV5[8] = {'M', 'I', 'N', 'I', 'M', 'A', '0', '5'};
+constexpr size_t kCkptChunkFloats = (size_t)8 << 20;   // 32 MiB per staging buffer
+
+template <typename T>
+void take_le(const unsigned char*& p, T& v) {
+    std::memcpy(&v, p, sizeof(T));
+    p += sizeof(T);
+}
+
+// Dimensions derived as model_init_config derives them (model.c:55-89).
+mc_model_desc ckpt_desc(const mc_checkpoint_info& in) {
+    mc_model_desc d{};
+    d.vocab_size = in.vocab_size;
+    d.dim = in.dim;
+    d.n_layers = in.n_layers;
+    d.n_heads = in.n_heads;
+    d.ffn_dim = in.ffn_dim;
+    d.max_seq = in.max_seq;
+    if (in.n_heads > 0 && in.dim % in.n_heads == 0) {
+        d.n_kv_heads = kv_head_count(in.n_heads);
+        d.head_dim = in.dim / in.n_heads;
+        d.kv_dim = d.n_kv_heads * d.head_dim;
+        d.qkv_dim = in.dim + 2 * d.kv_dim;
+    }
+    return d;
+}
+
+// Floats per model array, MODEL_ARRAYS order (checkpoint.c:43-52).
+void ckpt_counts(const mc_model_desc& d, size_t (&c)[9]) {
+    const size_t V = d.vocab_size, D = d.dim, L = d.n_layers, Q = d.qkv_dim, F = d.ffn_dim;
+    const size_t v[9] = {V * D, L * Q * D, L * D * D, L * F * D, L * F * D, L * D * F, L * D, L * D, D};
+    for (int i = 0; i < 9; i++) c[i] = v[i];
+}
+
+// The header and length checks of checkpoint_load (checkpoint.c:319-400),
+// in its order.  Leaves f positioned after the header.
+mc_status ckpt_header(FILE* f, mc_checkpoint_info* out) {
+    unsigned char h[116];
+    if (std::fread(h, 1, 12, f) != 12) return fail(MC_ERR_INVALID, "checkpoint: short header");
+    mc_checkpoint_info in{};
+    const unsigned char* p = h + 8;
+    take_le(p, in.version);
+    const bool v4 = in.version == 4 && std::memcmp(h, kCkptMagicV4, 8) == 0;
+    const bool v5 = in.version == 5 && std::memcmp(h, kCkptMagicV5, 8) == 0;
+    if (!v4 && !v5) return fail(MC_ERR_INVALID, "checkpoint: bad magic or version");
+    in.header_bytes = v5 ? 116 : 112;
+    if (std::fread(h + 12, 1, in.header_bytes - 12, f) != in.header_bytes - 12)
+        return fail(MC_ERR_INVALID, "checkpoint: short header");
+    uint32_t dims[6];
+    for (int i = 0; i < 6; i++) take_le(p, dims[i]);
+    take_le(p, in.n_params);
+    take_le(p, in.step);
+    uint64_t rng = 0;
+    take_le(p, rng);
+    take_le(p, in.tokenizer_hash);
+    take_le(p, in.lr);
+    take_le(p, in.beta1);
+    take_le(p, in.beta2);
+    take_le(p, in.eps);
+    take_le(p, in.weight_decay);
+    take_le(p, in.schedule_base_lr);
+    take_le(p, in.schedule_total_steps);
+    take_le(p, in.schedule_warmup_steps);
+    take_le(p, in.schedule_type);
+    in.optimizer_type = 0;
+    if (v5) take_le(p, in.optimizer_type);
+    if (in.optimizer_type != 0 && in.optimizer_type != 1)
+        return fail(MC_ERR_INVALID, "checkpoint: unknown optimizer type %d", in.optimizer_type);
+    for (int i = 0; i < 6; i++)
+        if (dims[i] > 0x7fffffffu) return fail(MC_ERR_INVALID, "checkpoint: dimension out of range");
+    in.vocab_size = (int32_t)dims[0];
+    in.dim = (int32_t)dims[1];
+    in.n_layers = (int32_t)dims[2];
+    in.n_heads = (int32_t)dims[3];
+    in.ffn_dim = (int32_t)dims[4];
+    in.max_seq = (int32_t)dims[5];
+    in.rng_state = rng ? rng : 0x123456789abcdef0ULL;   // checkpoint.c:413
+    const mc_model_desc d = ckpt_desc(in);
+    mc_status st = validate_dims(&d);
+    if (st) return st;
+    size_t c[9];
+    ckpt_counts(d, c);
+    uint64_t params = 0;
+    for (int i = 0; i < 9; i++) params += c[i];
+    if (in.n_params != params)
+        return fail(MC_ERR_INVALID, "checkpoint: %llu parameters stored, the dimensions give %llu",
+                    (unsigned long long)in.n_params, (unsigned long long)params);
+    const bool hyper_ok =
+        in.step >= 0 && std::isfinite(in.lr) && in.lr >= 0.0f && std::isfinite(in.beta1) &&
+        in.beta1 >= 0.0f && in.beta1 < 1.0f && std::isfinite(in.beta2) && in.beta2 >= 0.0f &&
+        in.beta2 < 1.0f && std::isfinite(in.eps) && in.eps > 0.0f &&
+        std::isfinite(in.weight_decay) && in.weight_decay >= 0.0f &&
+        std::isfinite(in.schedule_base_lr) && in.schedule_base_lr > 0.0f &&
+        in.schedule_total_steps >= 1 && in.step <= in.schedule_total_steps &&
+        in.schedule_warmup_steps >= 0 && in.schedule_warmup_steps < in.schedule_total_steps &&
+        (in.schedule_type == 0 || in.schedule_type == 1);
+    if (!hyper_ok) return fail(MC_ERR_INVALID, "checkpoint: optimizer state out of range");
+    // model arrays, then m (and v for AdamW) per array, then end of file
+    const uint64_t floats = params * (in.optimizer_type == 0 ? 3u : 2u);
+    in.file_bytes = in.header_bytes + floats * 4;
+    const long here = std::ftell(f);
+    if (here < 0 || std::fseek(f, 0, SEEK_END) != 0) return fail(MC_ERR_INVALID, "checkpoint: cannot seek");
+    const long end = std::ftell(f);
+    if (end < 0 || std::fseek(f, here, SEEK_SET) != 0) return fail(MC_ERR_INVALID, "checkpoint: cannot seek");
+    if ((uint64_t)end < in.file_bytes) return fail(MC_ERR_INVALID, "checkpoint: truncated file");
+    if ((uint64_t)end > in.file_bytes) return fail(MC_ERR_INVALID, "checkpoint: trailing bytes");
+    *out = in;
+    return MC_OK;
+}
+
+struct CkptStaging {
+    float* pinned[2] = {nullptr, nullptr};
+    float* dev[2] = {nullptr, nullptr};
+    unsigned* bad = nullptr;
+    cudaStream_t stream = nullptr;
+    cudaEvent_t done[2] = {nullptr, nullptr};
+    ~CkptStaging() {
+        if (stream) cudaStreamSynchronize(stream);
+        for (int i = 0; i < 2; i++) {
+            if (pinned[i]) cudaFreeHost(pinned[i]);
+            if (dev[i]) cudaFree(dev[i]);
+            if (done[i]) cudaEventDestroy(done[i]);
+        }
+        if (bad) cudaFree(bad);
+        if (stream) cudaStreamDestroy(stream);
+    }
+};
+
+// Stream the arrays of an already validated file into m (fp32 or bf16).
+mc_status ckpt_stream(FILE* f, const mc_checkpoint_info& in, mc_model* m) {
+    CkptStaging st;
+    MC_CUDA(cudaStreamCreateWithFlags(&st.stream, cudaStreamNonBlocking));
+    for (int i = 0; i < 2; i++) {
+        if (cudaHostAlloc(&st.pinned[i], kCkptChunkFloats * 4, cudaHostAllocDefault) != cudaSuccess ||
+            cudaMalloc(&st.dev[i], kCkptChunkFloats * 4) != cudaSuccess) {
+            cudaGetLastError();
+            return fail(MC_ERR_NOMEM, "checkpoint: staging buffers");
+        }
+        MC_CUDA(cudaEventCreateWithFlags(&st.done[i], cudaEventDisableTiming));
+    }
+    MC_CUDA(cudaMalloc(&st.bad, 4));
+    MC_CUDA(cudaMemsetAsync(st.bad, 0, 4, st.stream));
+    const mc_model_desc d = ckpt_desc(in);
+    size_t c[9];
+    ckpt_counts(d, c);
+    const size_t L = m->L, D = m->D;
+    char* wb = static_cast<char*>(m->wblock);
+    const bool bf16 = m->dtype == MC_WEIGHTS_BF16;
+    // destinations: six matrices in wblock, three norm arrays in norms, then
+    // the moments (checked only)
+    struct Run {
+        size_t n;
+        float* f32;
+        __nv_bfloat16* b16;
+    };
+    std::vector<Run> runs;
+    for (int i = 0; i < 6; i++)
+        runs.push_back({c[i], bf16 ? nullptr : reinterpret_cast<float*>(wb + m->off[i]),
+                        bf16 ? reinterpret_cast<__nv_bfloat16*>(wb + m->off[i]) : nullptr});
+    runs.push_back({c[6], m->norms, nullptr});
+    runs.push_back({c[7], m->norms + L * D, nullptr});
+    runs.push_back({c[8], m->norms + 2 * L * D, nullptr});
+    runs.push_back({(size_t)in.n_params * (in.optimizer_type == 0 ? 2u : 1u), nullptr, nullptr});
+    int k = 0;
+    for (const Run& r : runs) {
+        for (size_t o = 0; o < r.n; o += kCkptChunkFloats, k++) {
+            const size_t n = std::min(kCkptChunkFloats, r.n - o);
+            const int b = k & 1;
+            MC_CUDA(cudaEventSynchronize(st.done[b]));     // its last copy has left the buffer
+            if (std::fread(st.pinned[b], 4, n, f) != n) return fail(MC_ERR_INVALID, "checkpoint: read failed");
+            MC_CUDA(cudaMemcpyAsync(st.dev[b], st.pinned[b], n * 4, cudaMemcpyHostToDevice, st.stream));
+            const int grid = (int)std::min<size_t>((n + 255) / 256, 148 * 8);
+            mc::ckpt_ingest_kernel<<<grid, 256, 0, st.stream>>>(st.dev[b], n, r.f32 ? r.f32 + o : nullptr,
+                                                               r.b16 ? r.b16 + o : nullptr, st.bad);
+            MC_CUDA(cudaGetLastError());
+            MC_CUDA(cudaEventRecord(st.done[b], st.stream));
+        }
+    }
+    unsigned bad = 0;
+    MC_CUDA(cudaMemcpyAsync(&bad, st.bad, 4, cudaMemcpyDeviceToHost, st.stream));
+    MC_CUDA(cudaStreamSynchronize(st.stream));
+    if (bad) return fail(MC_ERR_INVALID, "checkpoint: non-finite values");
+    return MC_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+mc_status mc_checkpoint_inspect(const char* path, mc_checkpoint_info* info) {
+    if (!path || !info) return fail(MC_ERR_INVALID, "null argument");
+    FILE* f = std::fopen(path, "rb");
+    if (!f) return fail(MC_ERR_INVALID, "checkpoint: cannot open %s", path);
+    mc_checkpoint_info in{};
+    const mc_status st = ckpt_header(f, &in);
+    std::fclose(f);
+    if (st) return st;
+    *info = in;
+    return MC_OK;
+}
+
+mc_status mc_model_load_checkpoint(const char* path, int weights_dtype, uint64_t expected_tokenizer_hash,
+                                   unsigned flags, mc_model** out, mc_checkpoint_info* info) {
+    if (!path || !out) return fail(MC_ERR_INVALID, "null argument");
+    *out = nullptr;
+    if (weights_dtype != MC_WEIGHTS_F32 && weights_dtype != MC_WEIGHTS_BF16)
+        return fail(MC_ERR_INVALID, "unknown weight dtype %d", weights_dtype);
+    FILE* f = std::fopen(path, "rb");
+    if (!f) return fail(MC_ERR_INVALID, "checkpoint: cannot open %s", path);
+    mc_checkpoint_info in{};
+    mc_status st = ckpt_header(f, &in);
+    if (!st && !(flags & MC_CKPT_ANY_TOKENIZER) && in.tokenizer_hash != expected_tokenizer_hash)
+        st = fail(MC_ERR_INVALID, "checkpoint: tokenizer fingerprint differs");
+    mc_model* m = nullptr;
+    if (!st) {
+        const mc_model_desc d = ckpt_desc(in);
+        st = model_alloc(&d, weights_dtype, &m);
+    }
+    if (!st) st = ckpt_stream(f, in, m);
+    std::fclose(f);
+    if (st) {
+        if (m) mc_model_destroy(m);
+        return st;
+    }
+    *out = m;
+    if (info) *info = in;
+    return MC_OK;
+}
+
+}  // extern "C"

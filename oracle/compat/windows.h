@@ -149,4 +149,43 @@ static inline BOOL MoveFileExA(const char* from, const char* to, DWORD flags) {
     return rename(from, to) == 0;
 }
 
+/* checkpoint.c: archive slots and the atomic save. */
+#define FALSE 0
+#define TRUE 1
+#define MAX_PATH 260
+#define ERROR_FILE_NOT_FOUND 2u   /* == ENOENT, which GetLastError returns here */
+#define ERROR_PATH_NOT_FOUND 3u
+#define _TRUNCATE ((size_t)-1)
+
+#include <stdarg.h>
+/* _snprintf_s(buf, size, _TRUNCATE, ...): -1 when the output was truncated. */
+static inline int compat_snprintf_s(char* buf, size_t size, size_t count, const char* fmt, ...) {
+    (void)count;
+    va_list ap;
+    va_start(ap, fmt);
+    const int n = vsnprintf(buf, size, fmt, ap);
+    va_end(ap);
+    return (n < 0 || (size_t)n >= size) ? -1 : n;
+}
+#define _snprintf_s compat_snprintf_s
+
+static inline BOOL DeleteFileA(const char* path) { return unlink(path) == 0; }
+
+static inline BOOL CopyFileA(const char* from, const char* to, BOOL fail_if_exists) {
+    if (fail_if_exists && access(to, F_OK) == 0) return 0;
+    FILE* in = fopen(from, "rb");
+    if (!in) return 0;
+    FILE* out = fopen(to, "wb");
+    if (!out) { fclose(in); return 0; }
+    char buf[65536];
+    size_t n;
+    BOOL ok = 1;
+    while ((n = fread(buf, 1, sizeof(buf), in)) > 0)
+        if (fwrite(buf, 1, n, out) != n) { ok = 0; break; }
+    if (ferror(in)) ok = 0;
+    fclose(in);
+    if (fclose(out) != 0) ok = 0;
+    return ok;
+}
+
 #endif

@@ -156,6 +156,12 @@ def _load_ref():
         lib.refsh_forward_logits.argtypes = [C.c_void_p, _u16p, C.c_int, _f32p]
         lib.refsh_check_kv_cache.restype = C.c_int
         lib.refsh_check_kv_cache.argtypes = [C.c_void_p, _u16p, C.c_int, C.c_float]
+        lib.refsh_checkpoint_save.restype = C.c_int
+        lib.refsh_checkpoint_save.argtypes = [C.c_void_p, C.c_char_p, C.c_int, C.c_int64,
+                                              C.c_int64, C.c_uint64, C.c_uint64, C.c_float]
+        lib.refsh_checkpoint_load.restype = C.c_int
+        lib.refsh_checkpoint_load.argtypes = [C.c_void_p, C.c_char_p, C.c_int, C.c_uint64,
+                                              _u64p, C.POINTER(C.c_int64)]
         lib.rng_seed.argtypes = [C.c_void_p, C.c_uint64]
         lib.rng_u64.restype = C.c_uint64
         lib.rng_u64.argtypes = [C.c_void_p]
@@ -272,6 +278,23 @@ class RefModel(_ModelBase):
     def check_kv_cache(self, tokens, tol):
         t, tp = _u16(tokens)
         return bool(self.lib.refsh_check_kv_cache(self.h, tp, len(t), tol))
+
+    def checkpoint_save(self, path, optimizer=0, step=3, total_steps=10, rng_state=77,
+                        tokenizer_hash=0x1234, moment_fill=0.0):
+        """The reference's checkpoint_save (checkpoint.c:154-234) of these
+        weights with a fresh optimizer of type `optimizer` (0 AdamW, 1 Lion)."""
+        return bool(self.lib.refsh_checkpoint_save(self.h, os.fsencode(path), optimizer, step,
+                                                   total_steps, rng_state, tokenizer_hash,
+                                                   moment_fill))
+
+    def checkpoint_load(self, path, optimizer=0, tokenizer_hash=0x1234):
+        """The reference's checkpoint_load (checkpoint.c:301-426) into this
+        model; returns (rng_state, step) or None when it rejects the file."""
+        rng = C.c_uint64(0)
+        step = C.c_int64(0)
+        ok = self.lib.refsh_checkpoint_load(self.h, os.fsencode(path), optimizer, tokenizer_hash,
+                                            C.byref(rng), C.byref(step))
+        return (rng.value, step.value) if ok else None
 
     def close(self):
         if self.h:

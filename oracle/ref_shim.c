@@ -7,10 +7,14 @@
  * Every call goes through the reference's public functions:
  * model_init_config (model.h:45), kvcache_init (generate.h:26),
  * generate_with_options (generate.h:65), activations_init/model_forward
- * (forward.h:43-57) and generation_check_kv_cache (generate.h:31).
+ * (forward.h:43-57), generation_check_kv_cache (generate.h:31),
+ * optim_init_type (optim.h:62) and checkpoint_save / checkpoint_load
+ * (checkpoint.h:10-24).
  */
 #include "generate.h"
 #include "forward.h"
+#include "checkpoint.h"
+#include "optim.h"
 
 #include <stdlib.h>
 #include <string.h>
@@ -137,5 +141,67 @@ int refsh_check_kv_cache(void* p, const uint16_t* tokens, int seq, float tol) {
         generation_check_kv_cache(m, &cache, &temp, tokens, seq, tol);
     arena_free(&cache_arena);
     arena_free(&temp);
+    return ok;
+}
+
+/* A freshly initialised optimizer (optim_init_type, optim.h:62) of `type`
+   in its own arena, with a valid schedule and every moment set to `fill`. */
+static int shim_optim(Arena* a, Optim* opt, const Model* m, int type, int64_t step,
+    int64_t total_steps, float fill) {
+    const size_t n = model_param_count(m);
+    if (!arena_init(a, pages(2 * n * sizeof(float) + 32 * 64))) return 0;
+    if (!optim_init_type(opt, m, a, (OptimizerType)type, 1e-3f, 0.9f, 0.95f, 1e-8f, 0.1f)) {
+        arena_free(a);
+        return 0;
+    }
+    opt->step = step;
+    opt->schedule_base_lr = 1e-3f;
+    opt->schedule_total_steps = total_steps;
+    opt->schedule_warmup_steps = 0;
+    opt->schedule_type = 0;
+    float* moments[18] = {
+        opt->m_tok_emb, opt->m_attn_qkv, opt->m_attn_proj, opt->m_ffn_up, opt->m_ffn_gate,
+        opt->m_ffn_down, opt->m_rms1_scale, opt->m_rms2_scale, opt->m_rms_final_scale,
+        opt->v_tok_emb, opt->v_attn_qkv, opt->v_attn_proj, opt->v_ffn_up, opt->v_ffn_gate,
+        opt->v_ffn_down, opt->v_rms1_scale, opt->v_rms2_scale, opt->v_rms_final_scale };
+    const size_t D = (size_t)m->dim, L = (size_t)m->n_layers, F = (size_t)m->ffn_dim;
+    const size_t counts[9] = { (size_t)m->vocab_size * D, L * (size_t)m->qkv_dim * D, L * D * D,
+        L * F * D, L * F * D, L * D * F, L * D, L * D, D };
+    for (int k = 0; k < 18; k++)
+        if (moments[k])
+            for (size_t i = 0; i < counts[k % 9]; i++) moments[k][i] = fill;
+    return 1;
+}
+
+/* checkpoint_save of this model with an optimizer of `type` (0 AdamW,
+   1 Lion) at global step `step` of `total_steps`, RNG state and tokenizer
+   fingerprint as given. */
+int refsh_checkpoint_save(void* p, const char* path, int type, int64_t step, int64_t total_steps,
+    uint64_t rng_state, uint64_t tokenizer_hash, float moment_fill) {
+    RefModel* h = (RefModel*)p;
+    Arena a;
+    Optim opt;
+    if (!shim_optim(&a, &opt, &h->model, type, step, total_steps, moment_fill)) return 0;
+    Rng rng = { rng_state };
+    const int ok = checkpoint_save(path, &h->model, &opt, &rng, tokenizer_hash) ? 1 : 0;
+    arena_free(&a);
+    return ok;
+}
+
+/* checkpoint_load into this model and a fresh optimizer of `type`; the
+   RNG state and step it restores are returned. */
+int refsh_checkpoint_load(void* p, const char* path, int type, uint64_t tokenizer_hash,
+    uint64_t* rng_out, int64_t* step_out) {
+    RefModel* h = (RefModel*)p;
+    Arena a;
+    Optim opt;
+    if (!shim_optim(&a, &opt, &h->model, type, 0, 1, 0.0f)) return 0;
+    Rng rng = { 1 };
+    const int ok = checkpoint_load(path, &h->model, &opt, &rng, tokenizer_hash) ? 1 : 0;
+    if (ok) {
+        *rng_out = rng.state;
+        *step_out = opt.step;
+    }
+    arena_free(&a);
     return ok;
 }
