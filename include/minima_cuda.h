@@ -256,6 +256,22 @@ mc_status mc_model_load_checkpoint(const char* path, int weights_dtype,
     uint64_t expected_tokenizer_hash, unsigned flags, mc_model** out,
     mc_checkpoint_info* info);
 
+/*
+ * mc_gemm — C[M][N] = A[M][K] . B[N][K]^T on the tensor cores (tcgen05.mma,
+ * TMEM accumulator, TMA-fed 128 x 128 tiles): the kernel the prefill uses
+ * with MINIMA_CUDA_PREFILL=tcgen05, exposed for tests and measurement.
+ * No reference counterpart (the reference's matmul is forward.c:24-40 on the
+ * CPU).  MC_GEMM_TF32: A, B fp32 (multiplied as tf32, fp32 accumulate);
+ * MC_GEMM_BF16: A, B bf16 bit patterns (uint16).  C is fp32, row-major with
+ * leading dimension N.  K * element size must be a multiple of 16 bytes.
+ * Host pointers unless flags has MC_DEVICE_POINTERS (then 16-byte aligned
+ * device pointers).  *ms (optional) receives the kernel's device time.
+ */
+#define MC_GEMM_TF32 0
+#define MC_GEMM_BF16 1
+mc_status mc_gemm(int kind, const void* A, const void* B, float* C, int M, int N, int K,
+    unsigned flags, float* ms);
+
 const char* mc_last_error(void);
 
 #ifdef __cplusplus

@@ -31,7 +31,7 @@ CUDA_SYMBOLS = ("mc_init", "mc_model_create", "mc_model_update", "mc_model_destr
                 "mc_session_create", "mc_session_destroy", "mc_generate", "mc_forward_logits",
                 "mc_last_kernel_ms", "mc_last_launch_count", "mc_last_step_times",
                 "mc_last_kernel_name", "mc_last_prefill", "mc_session_stream", "mc_last_error",
-                "mc_checkpoint_inspect", "mc_model_load_checkpoint")
+                "mc_checkpoint_inspect", "mc_model_load_checkpoint", "mc_gemm")
 GENERATE_SYMBOLS = ("kvcache_init", "kvcache_reset", "generation_check_kv_cache",
                     "generation_inspect_next_tokens", "generate", "generate_with_options",
                     "generate_ex", "generate_batch_with_options", "minima_cuda_select_device",
@@ -208,6 +208,7 @@ def _declare(host, cuda, gen):
     cuda.mc_last_kernel_name.restype = C.c_char_p
     cuda.mc_last_kernel_name.argtypes = [vp]
     cuda.mc_last_error.restype = C.c_char_p
+    cuda.mc_gemm.argtypes = [C.c_int, vp, vp, _f32p, C.c_int, C.c_int, C.c_int, C.c_uint, _f32p]
     cuda.mc_checkpoint_inspect.argtypes = [C.c_char_p, C.POINTER(CheckpointInfo)]
     cuda.mc_model_load_checkpoint.argtypes = [C.c_char_p, C.c_int, C.c_uint64, C.c_uint,
                                               C.POINTER(vp), C.POINTER(CheckpointInfo)]
@@ -393,6 +394,25 @@ def generate_batch(hm: HostModel, tok: Tokenizer, caches: Caches, prompts, promp
 
 # ------------------------------------------------------------ C ABI layer
 MC_CKPT_ANY_TOKENIZER = 0x1
+MC_GEMM_TF32, MC_GEMM_BF16 = 0, 1
+
+
+def gemm(a, b, kind=MC_GEMM_TF32, device=0):
+    """mc_gemm: a[M][K] . b[N][K]^T on the tensor cores (host arrays).  For
+    MC_GEMM_BF16, a and b are uint16 arrays of bf16 bit patterns.  Returns
+    (C fp32 [M][N], kernel milliseconds)."""
+    _, cuda, _ = libs()
+    _check(cuda.mc_init(device), "mc_init")
+    dt = np.float32 if kind == MC_GEMM_TF32 else np.uint16
+    a = np.ascontiguousarray(a, dtype=dt)
+    b = np.ascontiguousarray(b, dtype=dt)
+    (M, K), (N, K2) = a.shape, b.shape
+    assert K == K2
+    c = np.zeros((M, N), dtype=np.float32)
+    ms = C.c_float(0.0)
+    _check(cuda.mc_gemm(kind, a.ctypes.data, b.ctypes.data, c.ctypes.data_as(_f32p), M, N, K, 0,
+                        C.byref(ms)), "mc_gemm")
+    return c, ms.value
 
 
 class CheckpointInfo(C.Structure):

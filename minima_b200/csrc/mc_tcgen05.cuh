@@ -1,0 +1,326 @@
+// mc_tcgen05.cuh — tensor-core GEMMs for sm_100a: TMA-fed shared-memory
+// tiles, tcgen05.mma with the accumulator in tensor memory (TMEM), and the
+// prefill's fused epilogues applied straight out of TMEM.
+//
+//   C[M][N] = A[M][K] . B[N][K]^T      (A: activations, B: a weight matrix in
+//                                       the reference's [out][in] layout)
+//
+// One CTA per 128 x 128 output tile, 128 threads:
+//   thread 0   issues the TMA loads of a 4-stage ring (A and B tiles of 128
+//              rows x 128 bytes of K, 128-byte swizzle),
+//   thread 32  issues tcgen05.mma (kind::tf32 for fp32 operands, kind::f16
+//              for bf16 operands; M = N = 128, 32 bytes of K per
+//              instruction) and frees each stage with tcgen05.commit,
+//   all 4 warps then drain TMEM with tcgen05.ld (warp w owns lanes
+//              32w..32w+31 = output rows) and apply the epilogue.
+// For SwiGLU the up and gate tiles share the A tile and accumulate into two
+// TMEM column ranges.  Every wait is bounded by the caller's deadline; a
+// wait that expires sets the status word, stops the pipeline, drains the
+// copies in flight and still frees TMEM.
+//
+// Numerics: kind::tf32 multiplies with 10-bit mantissas (fp32 accumulate),
+// kind::f16 with bf16 operands; both are looser than the fp32 CUDA-core
+// path, and the prefill uses them only when asked to.
+#pragma once
+
+#include <cuda.h>
+
+#include "mc_device.cuh"
+#include "mc_cluster_loop.cuh"
+#include "mc_prefill.cuh"
+
+namespace mc {
+
+constexpr int TC_BM = 128, TC_BN = 128;
+constexpr int TC_BKB = 128;                 // bytes of K per stage (one swizzle row)
+constexpr int TC_STAGES = 4;
+constexpr int TC_THREADS = 128;
+constexpr uint32_t TC_TILE = TC_BM * TC_BKB;   // 16 KB: A tile; B tiles are the same size
+enum TcKind { TC_TF32 = 0, TC_BF16 = 1 };
+constexpr int TCE_STORE = 3;                // plain C = A.B^T (the prefill kinds are 0..2)
+
+struct TcArgs {
+    int M, N, K;               // problem
+    int layer;                 // z coordinate of the weight tensor maps
+    float* C;
+    int ldc;
+    PrefillArgs pa;            // rows <-> (sequence, position) for the QKV epilogue
+    int* status;
+    unsigned long long timeout_ns;
+};
+
+// Dynamic shared memory of a launch with `btiles` B tiles per stage (1, or
+// 2 for SwiGLU): alignment slack, the ring, barriers and control words.
+__host__ __device__ constexpr size_t tc_smem_bytes(int btiles) {
+    return 1024 + (size_t)TC_STAGES * TC_TILE * (1 + btiles) + 256;
+}
+
+// Shared-memory matrix descriptor of a K-major tile of 8-row groups of
+// 128-byte rows with the 128-byte swizzle (sm_100 format: start >> 4 at
+// [0,14), leading offset [16,30) unused for swizzled K-major, stride offset
+// 1024 B >> 4 at [32,46), version 1 at [46,48), layout 2 = SWIZZLE_128B at
+// [61,64)).
+__device__ __forceinline__ uint64_t tc_sw128_desc(uint32_t saddr) {
+    return (uint64_t)((saddr & 0x3FFFFu) >> 4) | (1ull << 16) | (64ull << 32) | (1ull << 46) |
+           (2ull << 61);
+}
+
+// Instruction descriptor: fp32 accumulate, A/B format (tf32 = 2, bf16 = 1),
+// both K-major, N >> 3 at [17,23), M >> 4 at [24,29).
+template <int KIND>
+__device__ __forceinline__ uint32_t tc_idesc() {
+    constexpr uint32_t fmt = KIND == TC_TF32 ? 2u : 1u;
+    return (1u << 4) | (fmt << 7) | (fmt << 10) | ((uint32_t)(TC_BN >> 3) << 17) |
+           ((uint32_t)(TC_BM >> 4) << 24);
+}
+
+__device__ __forceinline__ void tc_tma_2d(uint32_t dst, const CUtensorMap* map, int x, int y,
+                                          uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
+        : "memory");
+}
+__device__ __forceinline__ void tc_tma_3d(uint32_t dst, const CUtensorMap* map, int x, int y, int z,
+                                          uint32_t bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(dst),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(bar)
+        : "memory");
+}
+
+template <int KIND>
+__device__ __forceinline__ void tc_mma(uint32_t tmem, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                       uint32_t accumulate) {
+    if constexpr (KIND == TC_TF32) {
+        asm volatile(
+            "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+            " tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n}\n" ::"r"(tmem),
+            "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(0), "r"(0), "r"(0), "r"(0));
+    } else {
+        asm volatile(
+            "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+            " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, {%5, %6, %7, %8}, p;\n}\n" ::"r"(tmem),
+            "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(0), "r"(0), "r"(0), "r"(0));
+    }
+}
+
+__device__ __forceinline__ void tc_commit(uint32_t bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
+                 : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() {
+    asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+__device__ __forceinline__ void tc_fence_after() {
+    asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+// 32 consecutive TMEM columns of this warp's 32 lanes: lane l gets row
+// (32 w + l), columns [col, col + 32).
+__device__ __forceinline__ void tc_tmem_ld32(uint32_t taddr, float (&v)[32]) {
+    uint32_t r[32];
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, "
+        "%12, %13, %14, %15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, "
+        "%30, %31}, [%32];"
+        : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+          "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+          "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+          "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
+          "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+        : "r"(taddr));
+#pragma unroll
+    for (int i = 0; i < 32; i++) v[i] = __uint_as_float(r[i]);
+}
+__device__ __forceinline__ void tc_tmem_wait_ld() {
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+// Epilogue of 32 consecutive columns [n, n + 32) of row m (m < M).
+template <int EPI>
+__device__ __forceinline__ void tc_epilogue(const TcArgs& g, int m, int n, const float (&u)[32],
+                                            const float (&gt)[32]) {
+    if constexpr (EPI == EPI_QKV) {
+        const PrefillArgs& a = g.pa;
+        int b, t;
+        pf_row(a, m, b, t);
+#pragma unroll
+        for (int j = 0; j < 32; j += 2) {
+            const int c = n + j;                 // even: c, c + 1 are a RoPE pair
+            if (c >= g.N) break;
+            float v0 = u[j], v1 = u[j + 1];
+            const int slot = c / a.hd, dd = c - slot * a.hd;
+            if (slot < a.H + a.K) {
+                const float2 r = a.rope[(size_t)t * (a.hd / 2) + dd / 2];
+                const float x0 = v0 * r.x - v1 * r.y, x1 = v0 * r.y + v1 * r.x;
+                v0 = x0;
+                v1 = x1;
+            }
+            if (slot < a.H) {
+                a.QB[(size_t)m * a.D + c] = v0;
+                a.QB[(size_t)m * a.D + c + 1] = v1;
+            } else {
+                const bool isk = slot < a.H + a.K;
+                const int gk = isk ? slot - a.H : slot - a.H - a.K;
+                float* dst = (isk ? a.kc : a.vc) +
+                             ((((size_t)g.layer * a.Bcap + b) * a.K + gk) * a.cap + t) * a.hd + dd;
+                dst[0] = v0;
+                dst[1] = v1;
+            }
+        }
+    } else {
+        float* crow = g.C + (size_t)m * g.ldc;
+#pragma unroll
+        for (int j = 0; j < 32; j++) {
+            const int c = n + j;
+            if (c >= g.N) break;
+            if constexpr (EPI == EPI_RESID) crow[c] += u[j];
+            else if constexpr (EPI == EPI_SWIGLU) crow[c] = (gt[j] / (1.0f + expf(-gt[j]))) * u[j];
+            else crow[c] = u[j];
+        }
+    }
+}
+
+template <int KIND, int EPI>
+__global__ void __launch_bounds__(TC_THREADS, 1)
+    tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   const __grid_constant__ CUtensorMap tmB2, const TcArgs g) {
+    constexpr int DUAL = EPI == EPI_SWIGLU ? 2 : 1;
+    constexpr int ES = KIND == TC_TF32 ? 4 : 2;
+    constexpr int BKE = TC_BKB / ES;                       // K elements per stage
+    constexpr uint32_t STAGE = TC_TILE * (1 + DUAL);
+    extern __shared__ unsigned char tc_smem_raw[];
+    unsigned char* base =
+        reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(tc_smem_raw) + 1023) & ~uintptr_t(1023));
+    unsigned long long* full = reinterpret_cast<unsigned long long*>(base + TC_STAGES * STAGE);
+    unsigned long long* empty = full + TC_STAGES;
+    unsigned long long* done = empty + TC_STAGES;
+    volatile int* ctl = reinterpret_cast<volatile int*>(done + 1);   // 0 tmem, 1 error, 2 issued, 3 consumed
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int m0 = blockIdx.y * TC_BM, n0 = blockIdx.x * TC_BN;
+    const int nk = (g.K + BKE - 1) / BKE;
+
+    // the ring and the control words must lie inside the dynamic shared
+    // memory this launch received; nothing is touched otherwise
+    uint32_t dyn = 0;
+    asm volatile("mov.u32 %0, %%dynamic_smem_size;" : "=r"(dyn));
+    const unsigned char* ctl_end = reinterpret_cast<const unsigned char*>(const_cast<int*>(ctl) + 4);
+    if ((size_t)(ctl_end - tc_smem_raw) > dyn || smem_addr(ctl_end) >= (1u << 18)) {
+        if (threadIdx.x == 0) atomicMax(g.status, (int)ST_DEVICE);
+        return;
+    }
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < TC_STAGES; s++) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        mbar_init(done, 1);
+        ctl[1] = 0;
+        ctl[2] = 0;
+        ctl[3] = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncwarp();                                  // tcgen05.alloc is warp-collective
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                         smem_addr((const void*)ctl)),
+                     "r"(DUAL * TC_BN));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = (uint32_t)ctl[0];
+    // an allocation is lane 0 and a column range inside the 512 columns
+    const bool tmem_ok = (tmem >> 16) == 0 && (tmem & 0xFFFFu) + DUAL * TC_BN <= 512;
+    if (!tmem_ok) {
+        if (threadIdx.x == 0) {
+            ctl[1] = 1;
+            atomicMax(g.status, (int)ST_DEVICE);
+        }
+        __syncthreads();
+        return;
+    }
+
+    if (threadIdx.x == 0) {
+        // ---- producer: TMA ring
+        int issued = 0;
+        for (int kb = 0; kb < nk; kb++) {
+            const int s = kb % TC_STAGES;
+            if (kb >= TC_STAGES &&
+                !mbar_wait(&empty[s], (uint32_t)((kb / TC_STAGES) - 1) & 1u, g.timeout_ns)) {
+                ctl[1] = 1;
+                atomicMax(g.status, (int)ST_TIMEOUT);
+                break;
+            }
+            if (ctl[1]) break;
+            const uint32_t st = smem_addr(base + (size_t)s * STAGE);
+            mbar_expect_tx(&full[s], STAGE);
+            const uint32_t fb = smem_addr(&full[s]);
+            tc_tma_2d(st, &tmA, kb * BKE, m0, fb);
+            tc_tma_3d(st + TC_TILE, &tmB, kb * BKE, n0, g.layer, fb);
+            if constexpr (DUAL == 2) tc_tma_3d(st + 2 * TC_TILE, &tmB2, kb * BKE, n0, g.layer, fb);
+            issued++;
+        }
+        ctl[2] = issued;
+    } else if (threadIdx.x == 32) {
+        // ---- MMA issuer
+        const uint32_t idesc = tc_idesc<KIND>();
+        int consumed = 0;
+        for (int kb = 0; kb < nk; kb++) {
+            const int s = kb % TC_STAGES;
+            if (!mbar_wait(&full[s], (uint32_t)(kb / TC_STAGES) & 1u, g.timeout_ns)) {
+                ctl[1] = 1;
+                atomicMax(g.status, (int)ST_TIMEOUT);
+                break;
+            }
+            consumed++;
+            tc_fence_after();
+            const uint32_t a_addr = smem_addr(base + (size_t)s * STAGE);
+#pragma unroll
+            for (int k = 0; k < TC_BKB / 32; k++) {
+                const uint64_t ad = tc_sw128_desc(a_addr + 32 * k);
+                const uint32_t acc = (kb | k) != 0;
+                tc_mma<KIND>(tmem, ad, tc_sw128_desc(a_addr + TC_TILE + 32 * k), idesc, acc);
+                if constexpr (DUAL == 2)
+                    tc_mma<KIND>(tmem + TC_BN, ad, tc_sw128_desc(a_addr + 2 * TC_TILE + 32 * k), idesc, acc);
+            }
+            tc_commit(smem_addr(&empty[s]));     // the stage is free once these MMAs are done
+        }
+        ctl[3] = consumed;
+        tc_commit(smem_addr(done));              // every MMA issued above has completed
+    }
+    __syncwarp();
+    // ---- epilogue: TMEM -> registers -> global
+    const bool finished = mbar_wait(done, 0, g.timeout_ns);
+    if (!finished) atomicMax(g.status, (int)ST_TIMEOUT);
+    tc_fence_after();
+    // block-uniform decision: tcgen05.ld is warp-collective
+    const bool store = __syncthreads_and(finished) && ctl[1] == 0 && nk > 0;
+    const int row = m0 + warp * 32 + lane;
+    const uint32_t trow = tmem + ((uint32_t)(warp * 32) << 16);
+#pragma unroll 1
+    for (int c0 = 0; c0 < TC_BN; c0 += 32) {
+        if (!store || n0 + c0 >= g.N) break;               // block-uniform
+        float u[32], gt[32] = {};
+        tc_tmem_ld32(trow + c0, u);
+        if constexpr (DUAL == 2) tc_tmem_ld32(trow + TC_BN + c0, gt);
+        tc_tmem_wait_ld();
+        if (row < g.M) tc_epilogue<EPI>(g, row, n0 + c0, u, gt);
+    }
+    // ---- drain copies still in flight (only after a failed wait), free TMEM
+    if (threadIdx.x == 0)
+        for (int kb = ctl[3]; kb < ctl[2]; kb++)
+            if (!mbar_wait(&full[kb % TC_STAGES], (uint32_t)(kb / TC_STAGES) & 1u, g.timeout_ns)) break;
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0)
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                     "r"(DUAL * TC_BN));
+}
+
+}  // namespace mc

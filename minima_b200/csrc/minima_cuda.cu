@@ -19,6 +19,9 @@
 #include "mc_cluster_loop.cuh"
 #include "mc_prefill.cuh"
 #include "mc_checkpoint.cuh"
+#include "mc_tcgen05.cuh"
+
+#include <cudaTypedefs.h>
 
 namespace {
 
@@ -109,6 +112,9 @@ struct mc_session {
     // batched prefill work buffers (allocated on first use)
     float *pf_x, *pf_xn, *pf_q, *pf_att, *pf_f;
     size_t pf_rows;               // rows the buffers hold
+    bool pf_tc;                   // prefill GEMMs on tcgen05 (kind::tf32), MINIMA_CUDA_PREFILL=tcgen05
+    bool pf_maps_ok;              // tensor maps below match the current buffers
+    CUtensorMap pf_map[8];        // A: xn, att, f; B: qkv, proj, up, gate, down
     cudaEvent_t ev_mid;           // end of prefill
     int last_prefill_pos;         // positions prefilled by the last call
     float last_prefill_ms;
@@ -475,6 +481,10 @@ mc_status mc_session_create(mc_model* m, int max_batch, int max_seq, mc_session*
         return fail(MC_ERR_INVALID, "session batch %d / max_seq %d outside [1,%d] / [1,%d]",
                     max_batch, max_seq, MC_MAX_BATCH, m->max_seq);
     mc_session* s = new mc_session();
+    {
+        const char* pe = getenv("MINIMA_CUDA_PREFILL");
+        s->pf_tc = pe && std::strcmp(pe, "tcgen05") == 0;
+    }
     s->m = m;
     s->Bcap = max_batch;
     s->cap = max_seq;
@@ -687,6 +697,77 @@ bool prefill_ok(const mc_model* m) {
 
 constexpr int kPrefillChunk = 256;   // positions per prefill pass
 
+// cuTensorMapEncodeTiled from the driver, looked up once through the runtime.
+PFN_cuTensorMapEncodeTiled_v12000 tc_encoder() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    if (!fn) {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+        else
+            cudaGetLastError();
+    }
+    return fn;
+}
+
+// Tensor map of a row-major [layers][rows][inner] array (layers == 0: 2-D)
+// read as 128-row x 128-byte boxes with the 128-byte swizzle.  The caller
+// guarantees a 16-byte aligned base and inner * es % 16 == 0.
+mc_status tc_map(CUtensorMap* map, const void* base, int es, uint64_t inner, uint64_t rows,
+                 uint64_t layers) {
+    auto enc = tc_encoder();
+    if (!enc) return fail(MC_ERR_UNSUPPORTED, "cuTensorMapEncodeTiled unavailable");
+    const cuuint64_t dims[3] = {inner, rows, layers ? layers : 1};
+    const cuuint64_t strides[2] = {inner * es, inner * rows * es};
+    const cuuint32_t box[3] = {(cuuint32_t)(mc::TC_BKB / es), (cuuint32_t)mc::TC_BM, 1};
+    const cuuint32_t estr[3] = {1, 1, 1};
+    const CUresult r = enc(map, es == 4 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
+                           layers ? 3 : 2, const_cast<void*>(base), dims, strides, box, estr,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return fail(MC_ERR_INVALID, "tensor map encode failed (%d)", (int)r);
+    return MC_OK;
+}
+
+template <int KIND, int EPI>
+cudaError_t tc_launch(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& b2,
+                      const mc::TcArgs& g, cudaStream_t st) {
+    const size_t smem = mc::tc_smem_bytes(EPI == mc::EPI_SWIGLU ? 2 : 1);
+    static unsigned long long attr_set = 0;    // one bit per device
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 64 && !((attr_set >> dev) & 1ull)) {
+        e = cudaFuncSetAttribute(mc::tc_gemm_kernel<KIND, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)smem);
+        if (e != cudaSuccess) return e;
+        attr_set |= 1ull << dev;
+    }
+    const dim3 grid((g.N + mc::TC_BN - 1) / mc::TC_BN, (g.M + mc::TC_BM - 1) / mc::TC_BM);
+    mc::tc_gemm_kernel<KIND, EPI><<<grid, mc::TC_THREADS, smem, st>>>(a, b, b2, g);
+    return cudaGetLastError();
+}
+
+// Tensor maps of the prefill buffers and weight matrices (fp32, kind::tf32).
+mc_status pf_tc_maps(mc_session* s) {
+    const mc_model* m = s->m;
+    const char* wb = static_cast<const char*>(m->wblock);
+    const uint64_t R = s->pf_rows, D = m->D, F = m->F, Q = m->Q, L = m->L;
+    mc_status st = MC_OK;
+    if (!st) st = tc_map(&s->pf_map[0], s->pf_xn, 4, D, R, 0);
+    if (!st) st = tc_map(&s->pf_map[1], s->pf_att, 4, D, R, 0);
+    if (!st) st = tc_map(&s->pf_map[2], s->pf_f, 4, F, R, 0);
+    if (!st) st = tc_map(&s->pf_map[3], wb + m->off[1], 4, D, Q, L);
+    if (!st) st = tc_map(&s->pf_map[4], wb + m->off[2], 4, D, D, L);
+    if (!st) st = tc_map(&s->pf_map[5], wb + m->off[3], 4, D, F, L);
+    if (!st) st = tc_map(&s->pf_map[6], wb + m->off[4], 4, D, F, L);
+    if (!st) st = tc_map(&s->pf_map[7], wb + m->off[5], 4, F, D, L);
+    s->pf_maps_ok = st == MC_OK;
+    return st;
+}
+
 // Batched forward of positions [0, Pf) of every sequence (mc_prefill.cuh):
 // fills the KV cache so that the token loop can start at position Pf.
 template <typename WT>
@@ -705,6 +786,12 @@ mc_status run_prefill(mc_session* s, int batch, const uint16_t* prompts, int str
         MC_CUDA(cudaMalloc(&s->pf_att, rows * D * 4));
         MC_CUDA(cudaMalloc(&s->pf_f, rows * F * 4));
         s->pf_rows = rows;
+        s->pf_maps_ok = false;
+    }
+    const bool tc = s->pf_tc && std::is_same<WT, float>::value;
+    if (tc && !s->pf_maps_ok) {
+        const mc_status st = pf_tc_maps(s);
+        if (st) return st;
     }
     mc::PrefillArgs a{};
     a.V = m->V; a.D = m->D; a.L = m->L; a.H = m->H; a.K = m->K; a.hd = m->hd; a.kvd = m->kvd;
@@ -737,6 +824,33 @@ mc_status run_prefill(mc_session* s, int batch, const uint16_t* prompts, int str
         const int M = batch * a.chunk;
         for (int l = 0; l < m->L; l++) {
             mc::pf_norm_kernel<WT><<<(M + 7) / 8, 256, 0, st>>>(a, emb, rms1 + l * D, l == 0);
+            if (tc) {
+                mc::TcArgs g{};
+                g.M = M;
+                g.layer = l;
+                g.pa = a;
+                g.status = s->status;
+                g.timeout_ns = 1000ull * 1000ull * 1000ull;
+                const CUtensorMap* mp = s->pf_map;
+                cudaError_t e;
+                g.N = m->Q; g.K = m->D; g.C = nullptr; g.ldc = 0;
+                e = tc_launch<mc::TC_TF32, mc::EPI_QKV>(mp[0], mp[3], mp[3], g, st);
+                if (e != cudaSuccess) return fail(MC_ERR_CUDA, "tcgen05 prefill: %s", cudaGetErrorString(e));
+                mc::pf_attention_kernel<<<dim3((a.chunk + QT - 1) / QT, m->K, batch), 256, att_smem, st>>>(
+                    a, l, QT);
+                g.N = m->D; g.K = m->D; g.C = a.X; g.ldc = m->D;
+                e = tc_launch<mc::TC_TF32, mc::EPI_RESID>(mp[1], mp[4], mp[4], g, st);
+                if (e != cudaSuccess) return fail(MC_ERR_CUDA, "tcgen05 prefill: %s", cudaGetErrorString(e));
+                mc::pf_norm_kernel<WT><<<(M + 7) / 8, 256, 0, st>>>(a, emb, rms2 + l * D, 0);
+                g.N = m->F; g.K = m->D; g.C = a.FH; g.ldc = m->F;
+                e = tc_launch<mc::TC_TF32, mc::EPI_SWIGLU>(mp[0], mp[5], mp[6], g, st);
+                if (e != cudaSuccess) return fail(MC_ERR_CUDA, "tcgen05 prefill: %s", cudaGetErrorString(e));
+                g.N = m->D; g.K = m->F; g.C = a.X; g.ldc = m->D;
+                e = tc_launch<mc::TC_TF32, mc::EPI_RESID>(mp[2], mp[7], mp[7], g, st);
+                if (e != cudaSuccess) return fail(MC_ERR_CUDA, "tcgen05 prefill: %s", cudaGetErrorString(e));
+                launches += 7;
+                continue;
+            }
             mc::pf_gemm_kernel<WT, mc::EPI_QKV><<<grid2(m->Q, M), 256, 0, st>>>(
                 a, a.XN, M, m->Q, m->D, wqkv + l * Q * D, nullptr, nullptr, 0, l);
             mc::pf_attention_kernel<<<dim3((a.chunk + QT - 1) / QT, m->K, batch), 256, att_smem, st>>>(
@@ -1542,3 +1656,78 @@ mc_status mc_model_load_checkpoint(const char* path, int weights_dtype, uint64_t
 }
 
 }  // extern "C"
+
+// ------------------------------------------------------------ plain GEMM
+extern "C" mc_status mc_gemm(int kind, const void* A, const void* B, float* C, int M, int N, int K,
+                             unsigned flags, float* ms) {
+    if (kind != MC_GEMM_TF32 && kind != MC_GEMM_BF16) return fail(MC_ERR_INVALID, "unknown GEMM kind %d", kind);
+    const int es = kind == MC_GEMM_TF32 ? 4 : 2;
+    if (!A || !B || !C || M <= 0 || N <= 0 || K <= 0 || ((size_t)K * es) % 16 != 0)
+        return fail(MC_ERR_INVALID, "mc_gemm: bad shape or null pointer (K * element size must be a multiple of 16)");
+    const bool dev = flags & MC_DEVICE_POINTERS;
+    const void* dA = A;
+    const void* dB = B;
+    float* dC = C;
+    void* own[3] = {nullptr, nullptr, nullptr};
+    int* dstatus = nullptr;
+    mc_status st = MC_OK;
+    auto cleanup = [&]() {
+        for (void* p : own) cudaFree(p);
+        cudaFree(dstatus);
+    };
+    if (!dev) {
+        if (cudaMalloc(&own[0], (size_t)M * K * es) != cudaSuccess ||
+            cudaMalloc(&own[1], (size_t)N * K * es) != cudaSuccess ||
+            cudaMalloc(&own[2], (size_t)M * N * 4) != cudaSuccess) {
+            cudaGetLastError();
+            cleanup();
+            return fail(MC_ERR_NOMEM, "mc_gemm: device buffers");
+        }
+        dA = own[0];
+        dB = own[1];
+        dC = static_cast<float*>(own[2]);
+        if (cudaMemcpy(own[0], A, (size_t)M * K * es, cudaMemcpyHostToDevice) != cudaSuccess ||
+            cudaMemcpy(own[1], B, (size_t)N * K * es, cudaMemcpyHostToDevice) != cudaSuccess) {
+            cleanup();
+            return fail(MC_ERR_CUDA, "mc_gemm: upload");
+        }
+    } else if ((reinterpret_cast<uintptr_t>(A) | reinterpret_cast<uintptr_t>(B)) & 15) {
+        return fail(MC_ERR_INVALID, "mc_gemm: device operands must be 16-byte aligned");
+    }
+    CUtensorMap ma, mb;
+    st = tc_map(&ma, dA, es, (uint64_t)K, (uint64_t)M, 0);
+    if (!st) st = tc_map(&mb, dB, es, (uint64_t)K, (uint64_t)N, 1);
+    if (!st && cudaMalloc(&dstatus, 4) != cudaSuccess) {
+        cudaGetLastError();
+        st = fail(MC_ERR_NOMEM, "mc_gemm: status word");
+    }
+    if (st) {
+        cleanup();
+        return st;
+    }
+    cudaEvent_t e0, e1;
+    cudaEventCreate(&e0);
+    cudaEventCreate(&e1);
+    cudaMemset(dstatus, 0, 4);
+    mc::TcArgs g{};
+    g.M = M; g.N = N; g.K = K; g.layer = 0; g.C = dC; g.ldc = N;
+    g.status = dstatus;
+    g.timeout_ns = 1000ull * 1000ull * 1000ull;
+    cudaEventRecord(e0, 0);
+    const cudaError_t le = kind == MC_GEMM_TF32 ? tc_launch<mc::TC_TF32, mc::TCE_STORE>(ma, mb, mb, g, 0)
+                                                : tc_launch<mc::TC_BF16, mc::TCE_STORE>(ma, mb, mb, g, 0);
+    cudaEventRecord(e1, 0);
+    cudaError_t e = le != cudaSuccess ? le : cudaEventSynchronize(e1);
+    int status = 0;
+    if (e == cudaSuccess) e = cudaMemcpy(&status, dstatus, 4, cudaMemcpyDeviceToHost);
+    if (e == cudaSuccess && ms) cudaEventElapsedTime(ms, e0, e1);
+    if (e == cudaSuccess && !dev) e = cudaMemcpy(C, dC, (size_t)M * N * 4, cudaMemcpyDeviceToHost);
+    cudaEventDestroy(e0);
+    cudaEventDestroy(e1);
+    cleanup();
+    if (e != cudaSuccess) return fail(MC_ERR_CUDA, "mc_gemm: %s", cudaGetErrorString(e));
+    if (status == mc::ST_TIMEOUT) return fail(MC_ERR_TIMEOUT, "mc_gemm: a pipeline wait passed its deadline");
+    if (status != 0) return fail(MC_ERR_DEVICE, "mc_gemm: kernel status %d", status);
+    return MC_OK;
+}
+
