@@ -5,11 +5,11 @@
 //   C[M][N] = A[M][K] . B[N][K]^T      (A: activations, B: a weight matrix in
 //                                       the reference's [out][in] layout)
 //
-// One CTA per 128 x 128 output tile, 128 threads:
-//   thread 0   issues the TMA loads of a 4-stage ring (A and B tiles of 128
-//              rows x 128 bytes of K, 128-byte swizzle),
+// One CTA per 128 x BN output tile (BN = 128 or 256), 128 threads:
+//   thread 0   issues the TMA loads of a 4-stage ring (A tiles of 128 rows,
+//              B tiles of BN rows, 128 bytes of K each, 128-byte swizzle),
 //   thread 32  issues tcgen05.mma (kind::tf32 for fp32 operands, kind::f16
-//              for bf16 operands; M = N = 128, 32 bytes of K per
+//              for bf16 operands; M = 128, N = BN, 32 bytes of K per
 //              instruction) and frees each stage with tcgen05.commit,
 //   all 4 warps then drain TMEM with tcgen05.ld (warp w owns lanes
 //              32w..32w+31 = output rows) and apply the epilogue.
@@ -31,11 +31,12 @@
 
 namespace mc {
 
-constexpr int TC_BM = 128, TC_BN = 128;
+constexpr int TC_BM = 128;                  // output rows per CTA (TMEM lanes)
 constexpr int TC_BKB = 128;                 // bytes of K per stage (one swizzle row)
 constexpr int TC_STAGES = 4;
 constexpr int TC_THREADS = 128;
-constexpr uint32_t TC_TILE = TC_BM * TC_BKB;   // 16 KB: A tile; B tiles are the same size
+constexpr int TC_GROUP_M = 8;               // tile rows per rasterization group (L2 reuse)
+constexpr uint32_t TC_TILE = TC_BM * TC_BKB;   // 16 KB: A tile; a B tile is BN x 128 B
 enum TcKind { TC_TF32 = 0, TC_BF16 = 1 };
 constexpr int TCE_STORE = 3;                // plain C = A.B^T (the prefill kinds are 0..2)
 
@@ -49,10 +50,11 @@ struct TcArgs {
     unsigned long long timeout_ns;
 };
 
-// Dynamic shared memory of a launch with `btiles` B tiles per stage (1, or
-// 2 for SwiGLU): alignment slack, the ring, barriers and control words.
-__host__ __device__ constexpr size_t tc_smem_bytes(int btiles) {
-    return 1024 + (size_t)TC_STAGES * TC_TILE * (1 + btiles) + 256;
+// Dynamic shared memory of a launch with `btiles` B tiles of `bn` rows per
+// stage (1, or 2 for SwiGLU): alignment slack, the ring, barriers and
+// control words.
+__host__ __device__ constexpr size_t tc_smem_bytes(int btiles, int bn) {
+    return 1024 + (size_t)TC_STAGES * (TC_TILE + (size_t)btiles * bn * TC_BKB) + 256;
 }
 
 // Shared-memory matrix descriptor of a K-major tile of 8-row groups of
@@ -67,10 +69,10 @@ __device__ __forceinline__ uint64_t tc_sw128_desc(uint32_t saddr) {
 
 // Instruction descriptor: fp32 accumulate, A/B format (tf32 = 2, bf16 = 1),
 // both K-major, N >> 3 at [17,23), M >> 4 at [24,29).
-template <int KIND>
+template <int KIND, int BN>
 __device__ __forceinline__ uint32_t tc_idesc() {
     constexpr uint32_t fmt = KIND == TC_TF32 ? 2u : 1u;
-    return (1u << 4) | (fmt << 7) | (fmt << 10) | ((uint32_t)(TC_BN >> 3) << 17) |
+    return (1u << 4) | (fmt << 7) | (fmt << 10) | ((uint32_t)(BN >> 3) << 17) |
            ((uint32_t)(TC_BM >> 4) << 24);
 }
 
@@ -184,14 +186,16 @@ __device__ __forceinline__ void tc_epilogue(const TcArgs& g, int m, int n, const
     }
 }
 
-template <int KIND, int EPI>
+template <int KIND, int EPI, int BN>
 __global__ void __launch_bounds__(TC_THREADS, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmB2, const TcArgs g) {
     constexpr int DUAL = EPI == EPI_SWIGLU ? 2 : 1;
     constexpr int ES = KIND == TC_TF32 ? 4 : 2;
     constexpr int BKE = TC_BKB / ES;                       // K elements per stage
-    constexpr uint32_t STAGE = TC_TILE * (1 + DUAL);
+    constexpr uint32_t BTILE = (uint32_t)BN * TC_BKB;      // bytes of one B tile
+    constexpr uint32_t STAGE = TC_TILE + DUAL * BTILE;
+    static_assert(DUAL * BN <= 512, "TMEM holds 512 fp32 columns");
     extern __shared__ unsigned char tc_smem_raw[];
     unsigned char* base =
         reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(tc_smem_raw) + 1023) & ~uintptr_t(1023));
@@ -200,7 +204,17 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     unsigned long long* done = empty + TC_STAGES;
     volatile int* ctl = reinterpret_cast<volatile int*>(done + 1);   // 0 tmem, 1 error, 2 issued, 3 consumed
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int m0 = blockIdx.y * TC_BM, n0 = blockIdx.x * TC_BN;
+    // tiles in groups of TC_GROUP_M tile rows, column-major inside a group,
+    // so that the CTAs resident at one time share their A and B tiles in L2
+    int m0, n0;
+    {
+        const int tiles_m = (g.M + TC_BM - 1) / TC_BM, tiles_n = (g.N + BN - 1) / BN;
+        const int t = blockIdx.x, per_group = TC_GROUP_M * tiles_n;
+        const int first = (t / per_group) * TC_GROUP_M, rows = min(tiles_m - first, TC_GROUP_M);
+        const int r = t % per_group;
+        m0 = (first + r % rows) * TC_BM;
+        n0 = (r / rows) * BN;
+    }
     const int nk = (g.K + BKE - 1) / BKE;
 
     // the ring and the control words must lie inside the dynamic shared
@@ -228,7 +242,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     if (warp == 0) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
                          smem_addr((const void*)ctl)),
-                     "r"(DUAL * TC_BN));
+                     "r"(DUAL * BN));
         asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
     }
     tc_fence_before();
@@ -236,7 +250,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     tc_fence_after();
     const uint32_t tmem = (uint32_t)ctl[0];
     // an allocation is lane 0 and a column range inside the 512 columns
-    const bool tmem_ok = (tmem >> 16) == 0 && (tmem & 0xFFFFu) + DUAL * TC_BN <= 512;
+    const bool tmem_ok = (tmem >> 16) == 0 && (tmem & 0xFFFFu) + DUAL * BN <= 512;
     if (!tmem_ok) {
         if (threadIdx.x == 0) {
             ctl[1] = 1;
@@ -263,13 +277,13 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             const uint32_t fb = smem_addr(&full[s]);
             tc_tma_2d(st, &tmA, kb * BKE, m0, fb);
             tc_tma_3d(st + TC_TILE, &tmB, kb * BKE, n0, g.layer, fb);
-            if constexpr (DUAL == 2) tc_tma_3d(st + 2 * TC_TILE, &tmB2, kb * BKE, n0, g.layer, fb);
+            if constexpr (DUAL == 2) tc_tma_3d(st + TC_TILE + BTILE, &tmB2, kb * BKE, n0, g.layer, fb);
             issued++;
         }
         ctl[2] = issued;
     } else if (threadIdx.x == 32) {
         // ---- MMA issuer
-        const uint32_t idesc = tc_idesc<KIND>();
+        const uint32_t idesc = tc_idesc<KIND, BN>();
         int consumed = 0;
         for (int kb = 0; kb < nk; kb++) {
             const int s = kb % TC_STAGES;
@@ -287,7 +301,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 const uint32_t acc = (kb | k) != 0;
                 tc_mma<KIND>(tmem, ad, tc_sw128_desc(a_addr + TC_TILE + 32 * k), idesc, acc);
                 if constexpr (DUAL == 2)
-                    tc_mma<KIND>(tmem + TC_BN, ad, tc_sw128_desc(a_addr + 2 * TC_TILE + 32 * k), idesc, acc);
+                    tc_mma<KIND>(tmem + BN, ad, tc_sw128_desc(a_addr + TC_TILE + BTILE + 32 * k), idesc,
+                                 acc);
             }
             tc_commit(smem_addr(&empty[s]));     // the stage is free once these MMAs are done
         }
@@ -304,11 +319,11 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     const int row = m0 + warp * 32 + lane;
     const uint32_t trow = tmem + ((uint32_t)(warp * 32) << 16);
 #pragma unroll 1
-    for (int c0 = 0; c0 < TC_BN; c0 += 32) {
+    for (int c0 = 0; c0 < BN; c0 += 32) {
         if (!store || n0 + c0 >= g.N) break;               // block-uniform
         float u[32], gt[32] = {};
         tc_tmem_ld32(trow + c0, u);
-        if constexpr (DUAL == 2) tc_tmem_ld32(trow + TC_BN + c0, gt);
+        if constexpr (DUAL == 2) tc_tmem_ld32(trow + BN + c0, gt);
         tc_tmem_wait_ld();
         if (row < g.M) tc_epilogue<EPI>(g, row, n0 + c0, u, gt);
     }
@@ -320,7 +335,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     __syncthreads();
     if (warp == 0)
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
-                     "r"(DUAL * TC_BN));
+                     "r"(DUAL * BN));
 }
 
 }  // namespace mc

@@ -713,15 +713,15 @@ PFN_cuTensorMapEncodeTiled_v12000 tc_encoder() {
 }
 
 // Tensor map of a row-major [layers][rows][inner] array (layers == 0: 2-D)
-// read as 128-row x 128-byte boxes with the 128-byte swizzle.  The caller
-// guarantees a 16-byte aligned base and inner * es % 16 == 0.
+// read as box_rows-row x 128-byte boxes with the 128-byte swizzle.  The
+// caller guarantees a 16-byte aligned base and inner * es % 16 == 0.
 mc_status tc_map(CUtensorMap* map, const void* base, int es, uint64_t inner, uint64_t rows,
-                 uint64_t layers) {
+                 uint64_t layers, uint32_t box_rows = mc::TC_BM) {
     auto enc = tc_encoder();
     if (!enc) return fail(MC_ERR_UNSUPPORTED, "cuTensorMapEncodeTiled unavailable");
     const cuuint64_t dims[3] = {inner, rows, layers ? layers : 1};
     const cuuint64_t strides[2] = {inner * es, inner * rows * es};
-    const cuuint32_t box[3] = {(cuuint32_t)(mc::TC_BKB / es), (cuuint32_t)mc::TC_BM, 1};
+    const cuuint32_t box[3] = {(cuuint32_t)(mc::TC_BKB / es), box_rows, 1};
     const cuuint32_t estr[3] = {1, 1, 1};
     const CUresult r = enc(map, es == 4 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
                            layers ? 3 : 2, const_cast<void*>(base), dims, strides, box, estr,
@@ -731,22 +731,23 @@ mc_status tc_map(CUtensorMap* map, const void* base, int es, uint64_t inner, uin
     return MC_OK;
 }
 
-template <int KIND, int EPI>
+// B maps must be built with box_rows == BN.
+template <int KIND, int EPI, int BN = 128>
 cudaError_t tc_launch(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& b2,
                       const mc::TcArgs& g, cudaStream_t st) {
-    const size_t smem = mc::tc_smem_bytes(EPI == mc::EPI_SWIGLU ? 2 : 1);
+    const size_t smem = mc::tc_smem_bytes(EPI == mc::EPI_SWIGLU ? 2 : 1, BN);
     static unsigned long long attr_set = 0;    // one bit per device
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
     if (dev < 64 && !((attr_set >> dev) & 1ull)) {
-        e = cudaFuncSetAttribute(mc::tc_gemm_kernel<KIND, EPI>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        e = cudaFuncSetAttribute(mc::tc_gemm_kernel<KIND, EPI, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)smem);
         if (e != cudaSuccess) return e;
         attr_set |= 1ull << dev;
     }
-    const dim3 grid((g.N + mc::TC_BN - 1) / mc::TC_BN, (g.M + mc::TC_BM - 1) / mc::TC_BM);
-    mc::tc_gemm_kernel<KIND, EPI><<<grid, mc::TC_THREADS, smem, st>>>(a, b, b2, g);
+    const unsigned tiles = (unsigned)((g.N + BN - 1) / BN) * (unsigned)((g.M + mc::TC_BM - 1) / mc::TC_BM);
+    mc::tc_gemm_kernel<KIND, EPI, BN><<<tiles, mc::TC_THREADS, smem, st>>>(a, b, b2, g);
     return cudaGetLastError();
 }
 
@@ -1696,7 +1697,7 @@ extern "C" mc_status mc_gemm(int kind, const void* A, const void* B, float* C, i
     }
     CUtensorMap ma, mb;
     st = tc_map(&ma, dA, es, (uint64_t)K, (uint64_t)M, 0);
-    if (!st) st = tc_map(&mb, dB, es, (uint64_t)K, (uint64_t)N, 1);
+    if (!st) st = tc_map(&mb, dB, es, (uint64_t)K, (uint64_t)N, 1, 256);
     if (!st && cudaMalloc(&dstatus, 4) != cudaSuccess) {
         cudaGetLastError();
         st = fail(MC_ERR_NOMEM, "mc_gemm: status word");
@@ -1714,8 +1715,8 @@ extern "C" mc_status mc_gemm(int kind, const void* A, const void* B, float* C, i
     g.status = dstatus;
     g.timeout_ns = 1000ull * 1000ull * 1000ull;
     cudaEventRecord(e0, 0);
-    const cudaError_t le = kind == MC_GEMM_TF32 ? tc_launch<mc::TC_TF32, mc::TCE_STORE>(ma, mb, mb, g, 0)
-                                                : tc_launch<mc::TC_BF16, mc::TCE_STORE>(ma, mb, mb, g, 0);
+    const cudaError_t le = kind == MC_GEMM_TF32 ? tc_launch<mc::TC_TF32, mc::TCE_STORE, 256>(ma, mb, mb, g, 0)
+                                                : tc_launch<mc::TC_BF16, mc::TCE_STORE, 256>(ma, mb, mb, g, 0);
     cudaEventRecord(e1, 0);
     cudaError_t e = le != cudaSuccess ? le : cudaEventSynchronize(e1);
     int status = 0;
