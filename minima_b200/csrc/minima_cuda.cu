@@ -760,11 +760,12 @@ mc_status pf_tc_maps(mc_session* s) {
     if (!st) st = tc_map(&s->pf_map[0], s->pf_xn, 4, D, R, 0);
     if (!st) st = tc_map(&s->pf_map[1], s->pf_att, 4, D, R, 0);
     if (!st) st = tc_map(&s->pf_map[2], s->pf_f, 4, F, R, 0);
-    if (!st) st = tc_map(&s->pf_map[3], wb + m->off[1], 4, D, Q, L);
-    if (!st) st = tc_map(&s->pf_map[4], wb + m->off[2], 4, D, D, L);
-    if (!st) st = tc_map(&s->pf_map[5], wb + m->off[3], 4, D, F, L);
-    if (!st) st = tc_map(&s->pf_map[6], wb + m->off[4], 4, D, F, L);
-    if (!st) st = tc_map(&s->pf_map[7], wb + m->off[5], 4, F, D, L);
+    // single-B GEMMs run 128 x 256 tiles, the SwiGLU pair 128 x 128
+    if (!st) st = tc_map(&s->pf_map[3], wb + m->off[1], 4, D, Q, L, 256);
+    if (!st) st = tc_map(&s->pf_map[4], wb + m->off[2], 4, D, D, L, 256);
+    if (!st) st = tc_map(&s->pf_map[5], wb + m->off[3], 4, D, F, L, 128);
+    if (!st) st = tc_map(&s->pf_map[6], wb + m->off[4], 4, D, F, L, 128);
+    if (!st) st = tc_map(&s->pf_map[7], wb + m->off[5], 4, F, D, L, 256);
     s->pf_maps_ok = st == MC_OK;
     return st;
 }
@@ -835,19 +836,19 @@ mc_status run_prefill(mc_session* s, int batch, const uint16_t* prompts, int str
                 const CUtensorMap* mp = s->pf_map;
                 cudaError_t e;
                 g.N = m->Q; g.K = m->D; g.C = nullptr; g.ldc = 0;
-                e = tc_launch<mc::TC_TF32, mc::EPI_QKV>(mp[0], mp[3], mp[3], g, st);
+                e = tc_launch<mc::TC_TF32, mc::EPI_QKV, 256>(mp[0], mp[3], mp[3], g, st);
                 if (e != cudaSuccess) return fail(MC_ERR_CUDA, "tcgen05 prefill: %s", cudaGetErrorString(e));
                 mc::pf_attention_kernel<<<dim3((a.chunk + QT - 1) / QT, m->K, batch), 256, att_smem, st>>>(
                     a, l, QT);
                 g.N = m->D; g.K = m->D; g.C = a.X; g.ldc = m->D;
-                e = tc_launch<mc::TC_TF32, mc::EPI_RESID>(mp[1], mp[4], mp[4], g, st);
+                e = tc_launch<mc::TC_TF32, mc::EPI_RESID, 256>(mp[1], mp[4], mp[4], g, st);
                 if (e != cudaSuccess) return fail(MC_ERR_CUDA, "tcgen05 prefill: %s", cudaGetErrorString(e));
                 mc::pf_norm_kernel<WT><<<(M + 7) / 8, 256, 0, st>>>(a, emb, rms2 + l * D, 0);
                 g.N = m->F; g.K = m->D; g.C = a.FH; g.ldc = m->F;
                 e = tc_launch<mc::TC_TF32, mc::EPI_SWIGLU>(mp[0], mp[5], mp[6], g, st);
                 if (e != cudaSuccess) return fail(MC_ERR_CUDA, "tcgen05 prefill: %s", cudaGetErrorString(e));
                 g.N = m->D; g.K = m->F; g.C = a.X; g.ldc = m->D;
-                e = tc_launch<mc::TC_TF32, mc::EPI_RESID>(mp[2], mp[7], mp[7], g, st);
+                e = tc_launch<mc::TC_TF32, mc::EPI_RESID, 256>(mp[2], mp[7], mp[7], g, st);
                 if (e != cudaSuccess) return fail(MC_ERR_CUDA, "tcgen05 prefill: %s", cudaGetErrorString(e));
                 launches += 7;
                 continue;
