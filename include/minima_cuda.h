@@ -148,6 +148,17 @@ mc_status mc_generate(mc_session* session, int batch,
 mc_status mc_forward_logits(mc_session* session, int batch, const uint16_t* tokens,
     int n, float* logits_out);
 
+/* Batched causal forward of tokens[b*seq .. b*seq+seq) at every position —
+   the logits of model_forward (forward.c:176-274), equal to forward_one per
+   prefix (generate.c:76-194) within fp32 rounding: logits_out[(b*seq+t)*V].
+   Runs the prefill kernels plus the final norm and tied lm_head (tcgen05
+   GEMMs with MINIMA_CUDA_PREFILL=tcgen05 and fp32 weights); the session's KV
+   cache is overwritten.  Token ids >= vocab are rejected (MC_ERR_INVALID) as
+   forward.c:179-186 rejects them.  With MC_DEVICE_POINTERS, tokens and
+   logits_out are device pointers. */
+mc_status mc_model_forward(mc_session* session, int batch, int seq, const uint16_t* tokens,
+    float* logits_out, unsigned flags);
+
 /* Kernel time of the last mc_generate / mc_forward_logits on this session,
    measured with CUDA events on the launching stream (milliseconds). */
 mc_status mc_last_kernel_ms(mc_session* session, float* ms);

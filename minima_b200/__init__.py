@@ -31,7 +31,8 @@ CUDA_SYMBOLS = ("mc_init", "mc_model_create", "mc_model_update", "mc_model_destr
                 "mc_session_create", "mc_session_destroy", "mc_generate", "mc_forward_logits",
                 "mc_last_kernel_ms", "mc_last_launch_count", "mc_last_step_times",
                 "mc_last_kernel_name", "mc_last_prefill", "mc_session_stream", "mc_last_error",
-                "mc_checkpoint_inspect", "mc_model_load_checkpoint", "mc_gemm")
+                "mc_checkpoint_inspect", "mc_model_load_checkpoint", "mc_gemm",
+                "mc_model_forward")
 GENERATE_SYMBOLS = ("kvcache_init", "kvcache_reset", "generation_check_kv_cache",
                     "generation_inspect_next_tokens", "generate", "generate_with_options",
                     "generate_ex", "generate_batch_with_options", "minima_cuda_select_device",
@@ -208,6 +209,7 @@ def _declare(host, cuda, gen):
     cuda.mc_last_kernel_name.restype = C.c_char_p
     cuda.mc_last_kernel_name.argtypes = [vp]
     cuda.mc_last_error.restype = C.c_char_p
+    cuda.mc_model_forward.argtypes = [vp, C.c_int, C.c_int, u16p, _f32p, C.c_uint]
     cuda.mc_gemm.argtypes = [C.c_int, vp, vp, _f32p, C.c_int, C.c_int, C.c_int, C.c_uint, _f32p]
     cuda.mc_checkpoint_inspect.argtypes = [C.c_char_p, C.POINTER(CheckpointInfo)]
     cuda.mc_model_load_checkpoint.argtypes = [C.c_char_p, C.c_int, C.c_uint64, C.c_uint,
@@ -555,6 +557,18 @@ class Session:
         _check(libs()[1].mc_last_step_times(self.h, buf.ctypes.data_as(C.POINTER(C.c_uint64)),
                                             cap, C.byref(n)), "mc_last_step_times")
         return buf[:n.value]
+
+    def model_forward(self, tokens):
+        """mc_model_forward: logits [B][S][V] of every position (batched causal
+        forward) for tokens [B][S]."""
+        _, cuda, _ = libs()
+        t = np.ascontiguousarray(tokens, dtype=np.uint16)
+        B, S = t.shape
+        V = self.dm._desc.vocab_size
+        out = np.zeros((B, S, V), dtype=np.float32)
+        _check(cuda.mc_model_forward(self.h, B, S, t.ctypes.data_as(C.POINTER(C.c_uint16)),
+                                     out.ctypes.data_as(_f32p), 0), "mc_model_forward")
+        return out
 
     def last_prefill(self):
         """(positions prefilled in one batch, prefill device ms) of the last call."""

@@ -70,12 +70,13 @@ __global__ void __launch_bounds__(256) pf_norm_kernel(PrefillArgs a, const WT* t
     for (int k = lane; k < a.D; k += 32) a.XN[(size_t)m * a.D + k] = x[k] * inv * scale[k];
 }
 
-enum PfEpi { EPI_QKV = 0, EPI_RESID = 1, EPI_SWIGLU = 2 };
+enum PfEpi { EPI_QKV = 0, EPI_RESID = 1, EPI_SWIGLU = 2, EPI_STORE = 3 };
 
 constexpr int GBM = 64, GBN = 64, GBK = 32;
 
 // C[M][N] = A[M][K] . W[N][K]^T with a fused epilogue.  For EPI_SWIGLU, W2 is
-// the gate matrix and the output is silu(A.W2) * (A.W).  K % 4 == 0.
+// the gate matrix and the output is silu(A.W2) * (A.W); EPI_STORE writes
+// C as is (the lm_head of model_forward).  K % 4 == 0.
 template <typename WT, int EPI>
 __global__ void __launch_bounds__(256, 1) pf_gemm_kernel(PrefillArgs a, const float* A, int M, int N,
                                                       int Kd, const WT* W, const WT* W2, float* C,
@@ -171,6 +172,8 @@ __global__ void __launch_bounds__(256, 1) pf_gemm_kernel(PrefillArgs a, const fl
                 if (n >= N) continue;
                 if constexpr (EPI == EPI_RESID) {
                     C[(size_t)m * ldc + n] += acc[0][i][j];
+                } else if constexpr (EPI == EPI_STORE) {
+                    C[(size_t)m * ldc + n] = acc[0][i][j];
                 } else {
                     const float up = acc[0][i][j], g = acc[DUAL - 1][i][j];
                     C[(size_t)m * ldc + n] = (g / (1.0f + expf(-g))) * up;

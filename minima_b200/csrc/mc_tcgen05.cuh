@@ -38,7 +38,7 @@ constexpr int TC_THREADS = 128;
 constexpr int TC_GROUP_M = 8;               // tile rows per rasterization group (L2 reuse)
 constexpr uint32_t TC_TILE = TC_BM * TC_BKB;   // 16 KB: A tile; a B tile is BN x 128 B
 enum TcKind { TC_TF32 = 0, TC_BF16 = 1 };
-constexpr int TCE_STORE = 3;                // plain C = A.B^T (the prefill kinds are 0..2)
+constexpr int TCE_STORE = EPI_STORE;        // plain C = A.B^T
 
 struct TcArgs {
     int M, N, K;               // problem

@@ -114,7 +114,8 @@ struct mc_session {
     size_t pf_rows;               // rows the buffers hold
     bool pf_tc;                   // prefill GEMMs on tcgen05 (kind::tf32), MINIMA_CUDA_PREFILL=tcgen05
     bool pf_maps_ok;              // tensor maps below match the current buffers
-    CUtensorMap pf_map[8];        // A: xn, att, f; B: qkv, proj, up, gate, down
+    CUtensorMap pf_map[9];        // A: xn, att, f; B: qkv, proj, up, gate, down, tok_emb
+    float* pf_logits;             // [pf_rows][V] lm_head scratch of mc_model_forward
     cudaEvent_t ev_mid;           // end of prefill
     int last_prefill_pos;         // positions prefilled by the last call
     float last_prefill_ms;
@@ -463,7 +464,7 @@ mc_status mc_session_destroy(mc_session* s) {
                     s->part_l, s->amax_v, s->amax_i, s->att_cnt, s->counts, s->banned, s->bar,
                     s->status, s->seq, s->prompts, s->out, s->stop, s->trace, s->stamps,
                     s->xfin, s->hgen, s->hsync, s->hpv, s->hpi,
-                    s->pf_x, s->pf_xn, s->pf_q, s->pf_att, s->pf_f};
+                    s->pf_x, s->pf_xn, s->pf_q, s->pf_att, s->pf_f, s->pf_logits};
     for (void* b : bufs) cudaFree(b);
     if (s->ev_mid) cudaEventDestroy(s->ev_mid);
     if (s->ev0) cudaEventDestroy(s->ev0);
@@ -766,15 +767,19 @@ mc_status pf_tc_maps(mc_session* s) {
     if (!st) st = tc_map(&s->pf_map[5], wb + m->off[3], 4, D, F, L, 128);
     if (!st) st = tc_map(&s->pf_map[6], wb + m->off[4], 4, D, F, L, 128);
     if (!st) st = tc_map(&s->pf_map[7], wb + m->off[5], 4, F, D, L, 256);
+    if (!st) st = tc_map(&s->pf_map[8], wb + m->off[0], 4, D, m->V, 1, 256);
     s->pf_maps_ok = st == MC_OK;
     return st;
 }
 
 // Batched forward of positions [0, Pf) of every sequence (mc_prefill.cuh):
 // fills the KV cache so that the token loop can start at position Pf.
+// With `logits` set (mc_model_forward), every chunk also applies the final
+// norm and the tied lm_head (forward.c:253-270) and copies the chunk's rows
+// to logits[b][t][V] (sequence length S, host or device memory).
 template <typename WT>
 mc_status run_prefill(mc_session* s, int batch, const uint16_t* prompts, int stride, int Pf,
-                      int& launches) {
+                      int& launches, float* logits = nullptr, bool logits_dev = false, int S = 0) {
     const mc_model* m = s->m;
     const size_t rows = (size_t)s->Bcap * std::min(kPrefillChunk, s->cap);
     if (s->pf_rows < rows) {
@@ -789,6 +794,15 @@ mc_status run_prefill(mc_session* s, int batch, const uint16_t* prompts, int str
         MC_CUDA(cudaMalloc(&s->pf_f, rows * F * 4));
         s->pf_rows = rows;
         s->pf_maps_ok = false;
+        cudaFree(s->pf_logits);
+        s->pf_logits = nullptr;
+    }
+    if (logits && !s->pf_logits) {
+        const size_t bytes = s->pf_rows * (size_t)m->V * 4;
+        if (cudaMalloc(&s->pf_logits, bytes) != cudaSuccess) {
+            cudaGetLastError();
+            return fail(MC_ERR_NOMEM, "model_forward: lm_head scratch (%zu bytes)", bytes);
+        }
     }
     const bool tc = s->pf_tc && std::is_same<WT, float>::value;
     if (tc && !s->pf_maps_ok) {
@@ -865,6 +879,30 @@ mc_status run_prefill(mc_session* s, int batch, const uint16_t* prompts, int str
             mc::pf_gemm_kernel<WT, mc::EPI_RESID><<<grid2(m->D, M), 256, 0, st>>>(
                 a, a.FH, M, m->D, m->F, wdown + l * D * F, nullptr, a.X, m->D, l);
             launches += 7;
+        }
+        if (logits) {
+            const float* rmsf = m->norms + 2 * (size_t)m->L * m->D;
+            mc::pf_norm_kernel<WT><<<(M + 7) / 8, 256, 0, st>>>(a, emb, rmsf, 0);
+            if (tc) {
+                mc::TcArgs g{};
+                g.M = M; g.N = m->V; g.K = m->D; g.layer = 0; g.C = s->pf_logits; g.ldc = m->V;
+                g.pa = a;
+                g.status = s->status;
+                g.timeout_ns = 1000ull * 1000ull * 1000ull;
+                const cudaError_t e = tc_launch<mc::TC_TF32, mc::TCE_STORE, 256>(s->pf_map[0], s->pf_map[8],
+                                                                                 s->pf_map[8], g, st);
+                if (e != cudaSuccess) return fail(MC_ERR_CUDA, "tcgen05 lm_head: %s", cudaGetErrorString(e));
+            } else {
+                mc::pf_gemm_kernel<WT, mc::EPI_STORE><<<grid2(m->V, M), 256, 0, st>>>(
+                    a, a.XN, M, m->V, m->D, emb, nullptr, s->pf_logits, m->V, 0);
+            }
+            launches += 2;
+            // rows of sequence b are contiguous in the chunk and in the output
+            const size_t n = a.chunk, V = m->V;
+            for (int b = 0; b < batch; b++)
+                MC_CUDA(cudaMemcpyAsync(logits + ((size_t)b * S + a.c0) * V, s->pf_logits + (size_t)b * n * V,
+                                        n * V * 4, logits_dev ? cudaMemcpyDeviceToDevice : cudaMemcpyDeviceToHost,
+                                        st));
         }
     }
     const cudaError_t e = cudaGetLastError();
@@ -1108,6 +1146,56 @@ mc_status mc_generate(mc_session* s, int batch, const uint16_t* prompts, int pro
                                          trace_logits, trace_steps);
     return generate_t<float>(s, batch, prompts, prompt_stride, prompt_lens, out_ids, out_cap, o,
                              rng_states, out_counts, final_pos, flags, trace_logits, trace_steps);
+}
+
+}  // extern "C"
+
+namespace {
+
+template <typename WT>
+mc_status model_forward_t(mc_session* s, int batch, int seq, const uint16_t* tokens, float* logits,
+                          bool dev) {
+    const mc_model* m = s->m;
+    const uint16_t* dtok = tokens;
+    if (!dev) {
+        for (size_t i = 0; i < (size_t)batch * seq; i++)   // forward.c:179-186
+            if (tokens[i] >= m->V) return fail(MC_ERR_INVALID, "model_forward: token id %d >= vocab", tokens[i]);
+        MC_CUDA(cudaMemcpyAsync(s->prompts, tokens, (size_t)batch * seq * 2, cudaMemcpyHostToDevice, s->stream));
+        dtok = s->prompts;
+    }
+    MC_CUDA(cudaMemsetAsync(s->status, 0, 256, s->stream));
+    MC_CUDA(cudaEventRecord(s->ev0, s->stream));
+    int launches = 0;
+    const mc_status st = run_prefill<WT>(s, batch, dtok, seq, seq, launches, logits, dev, seq);
+    if (st) return st;
+    MC_CUDA(cudaEventRecord(s->ev1, s->stream));
+    int status = 0;
+    MC_CUDA(cudaMemcpyAsync(&status, s->status, 4, cudaMemcpyDeviceToHost, s->stream));
+    MC_CUDA(cudaStreamSynchronize(s->stream));
+    MC_CUDA(cudaEventElapsedTime(&s->last_ms, s->ev0, s->ev1));
+    s->last_launches = launches;
+    s->last_T = 0;
+    if (status == mc::ST_DEVICE) return fail(MC_ERR_INVALID, "model_forward: token id outside the vocabulary");
+    if (status != 0) return fail(MC_ERR_DEVICE, "model_forward: kernel status %d", status);
+    return MC_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+mc_status mc_model_forward(mc_session* s, int batch, int seq, const uint16_t* tokens, float* logits_out,
+                           unsigned flags) {
+    if (!s || !tokens || !logits_out) return fail(MC_ERR_INVALID, "null argument");
+    if (batch <= 0 || batch > s->Bcap || seq <= 0 || seq > s->cap)
+        return fail(MC_ERR_INVALID, "model_forward: batch %d, seq %d outside [1, %d] x [1, %d]", batch, seq,
+                    s->Bcap, s->cap);
+    if (!prefill_ok(s->m)) return fail(MC_ERR_UNSUPPORTED, "model_forward: no batched kernels for this shape");
+    MC_CUDA(cudaSetDevice(s->m->device));
+    const bool dev = flags & MC_DEVICE_POINTERS;
+    if (s->m->dtype == MC_WEIGHTS_BF16)
+        return model_forward_t<__nv_bfloat16>(s, batch, seq, tokens, logits_out, dev);
+    return model_forward_t<float>(s, batch, seq, tokens, logits_out, dev);
 }
 
 mc_status mc_forward_logits(mc_session* s, int batch, const uint16_t* tokens, int n, float* out) {
