@@ -701,11 +701,32 @@ __device__ bool lc_layer(const ClusterParams& cp, const CSlice& sl, LcState& S,
     if (!lc_sync(cl, S, cs)) return false;
 
     // ---- down + residual (generate.c:181-184)
-    for (int r0 = sl.p0 + 4 * warp; r0 < sl.p1; r0 += 4 * kWarps) {
-        const float* w0 = wd + (size_t)(r0 - sl.p0) * F;
-        const float val = lc_gemv4(w0, w0 + F, w0 + 2 * F, w0 + 3 * F, F, S.f, F, fl, nf);
-        const int i = lane & 7;
-        if (i < nf) S.x[fl[i] * D + r0 + (lane >> 3)] += val;
+    // With fewer 4-row groups than warps, each group's F-long rows are split
+    // into nks slices over nks warps and the partial sums meet in shared
+    // memory (S.sc is free after the attention phase).
+    const int ngroups = (sl.p1 - sl.p0) >> 2;
+    const int nks = ngroups > 0 ? kWarps / ngroups : 1;
+    if (nks >= 2 && F % (4 * nks) == 0) {
+        const int grp = warp % ngroups, ks = warp / ngroups, kl = F / nks;
+        if (ks < nks) {
+            const int k0 = ks * kl;
+            const float* w0 = wd + (size_t)(4 * grp) * F + k0;
+            S.sc[warp * 32 + lane] = lc_gemv4(w0, w0 + F, w0 + 2 * F, w0 + 3 * F, kl, S.f + k0, F, fl, nf);
+        }
+        __syncthreads();
+        if (ks == 0) {
+            float val = 0.0f;
+            for (int s2 = 0; s2 < nks; s2++) val += S.sc[(s2 * ngroups + grp) * 32 + lane];
+            const int i = lane & 7;
+            if (i < nf) S.x[fl[i] * D + sl.p0 + 4 * grp + (lane >> 3)] += val;
+        }
+    } else {
+        for (int r0 = sl.p0 + 4 * warp; r0 < sl.p1; r0 += 4 * kWarps) {
+            const float* w0 = wd + (size_t)(r0 - sl.p0) * F;
+            const float val = lc_gemv4(w0, w0 + F, w0 + 2 * F, w0 + 3 * F, F, S.f, F, fl, nf);
+            const int i = lane & 7;
+            if (i < nf) S.x[fl[i] * D + r0 + (lane >> 3)] += val;
+        }
     }
     __syncthreads();
     push_rows(cl, S.x, D, sl.p0, sl.p1, fl, nf, cs, crank);
