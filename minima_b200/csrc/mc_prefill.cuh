@@ -32,6 +32,11 @@ struct PrefillArgs {
     float* QB;                 // [B*chunk][D] rotated queries
     float* ATT;                // [B*chunk][D]
     float* FH;                 // [B*chunk][F]
+    // bf16 copies of the GEMM inputs for the tensor-core path with bf16
+    // weights (kind::f16 needs both operands in bf16); null otherwise
+    __nv_bfloat16* XN16;
+    __nv_bfloat16* ATT16;
+    __nv_bfloat16* FH16;
     int* status;
 };
 
@@ -67,7 +72,11 @@ __global__ void __launch_bounds__(256) pf_norm_kernel(PrefillArgs a, const WT* t
     for (int k = lane; k < a.D; k += 32) ss += x[k] * x[k];
     ss = warp_sum(ss);
     const float inv = 1.0f / sqrtf(ss / (float)a.D + 1e-5f);
-    for (int k = lane; k < a.D; k += 32) a.XN[(size_t)m * a.D + k] = x[k] * inv * scale[k];
+    for (int k = lane; k < a.D; k += 32) {
+        const float v = x[k] * inv * scale[k];
+        a.XN[(size_t)m * a.D + k] = v;
+        if (a.XN16) a.XN16[(size_t)m * a.D + k] = __float2bfloat16_rn(v);
+    }
 }
 
 enum PfEpi { EPI_QKV = 0, EPI_RESID = 1, EPI_SWIGLU = 2, EPI_STORE = 3 };
@@ -266,10 +275,16 @@ __global__ void __launch_bounds__(256) pf_attention_kernel(PrefillArgs a, int la
         if (r >= rows) break;
         const int h = r / QT, t = qt0 + r % QT;
         if (t >= qt1) continue;
-        float* dst = a.ATT + ((size_t)b * n + (t - a.c0)) * a.D + (g * G + h) * hd;
+        const size_t off = ((size_t)b * n + (t - a.c0)) * a.D + (g * G + h) * hd;
+        float* dst = a.ATT + off;
         const float inv = 1.0f / l_run[k];
-        if (lane < hd) dst[lane] = o_acc[k][0] * inv;
-        if (lane + 32 < hd) dst[lane + 32] = o_acc[k][1] * inv;
+        const float v0 = o_acc[k][0] * inv, v1 = o_acc[k][1] * inv;
+        if (lane < hd) dst[lane] = v0;
+        if (lane + 32 < hd) dst[lane + 32] = v1;
+        if (a.ATT16) {
+            if (lane < hd) a.ATT16[off + lane] = __float2bfloat16_rn(v0);
+            if (lane + 32 < hd) a.ATT16[off + lane + 32] = __float2bfloat16_rn(v1);
+        }
     }
 }
 

@@ -179,9 +179,15 @@ __device__ __forceinline__ void tc_epilogue(const TcArgs& g, int m, int n, const
         for (int j = 0; j < 32; j++) {
             const int c = n + j;
             if (c >= g.N) break;
-            if constexpr (EPI == EPI_RESID) crow[c] += u[j];
-            else if constexpr (EPI == EPI_SWIGLU) crow[c] = (gt[j] / (1.0f + expf(-gt[j]))) * u[j];
-            else crow[c] = u[j];
+            if constexpr (EPI == EPI_RESID) {
+                crow[c] += u[j];
+            } else if constexpr (EPI == EPI_SWIGLU) {
+                const float v = (gt[j] / (1.0f + expf(-gt[j]))) * u[j];
+                crow[c] = v;
+                if (g.pa.FH16) g.pa.FH16[(size_t)m * g.ldc + c] = __float2bfloat16_rn(v);
+            } else {
+                crow[c] = u[j];
+            }
         }
     }
 }

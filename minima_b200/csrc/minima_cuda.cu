@@ -112,10 +112,11 @@ struct mc_session {
     // batched prefill work buffers (allocated on first use)
     float *pf_x, *pf_xn, *pf_q, *pf_att, *pf_f;
     size_t pf_rows;               // rows the buffers hold
-    bool pf_tc;                   // prefill GEMMs on tcgen05 (kind::tf32), MINIMA_CUDA_PREFILL=tcgen05
+    bool pf_tc;                   // prefill GEMMs on tcgen05 (tf32 / bf16), MINIMA_CUDA_PREFILL=tcgen05
     bool pf_maps_ok;              // tensor maps below match the current buffers
     CUtensorMap pf_map[9];        // A: xn, att, f; B: qkv, proj, up, gate, down, tok_emb
     float* pf_logits;             // [pf_rows][V] lm_head scratch of mc_model_forward
+    __nv_bfloat16 *pf_xn16, *pf_att16, *pf_f16;   // bf16 GEMM inputs (tensor cores, bf16 weights)
     cudaEvent_t ev_mid;           // end of prefill
     int last_prefill_pos;         // positions prefilled by the last call
     float last_prefill_ms;
@@ -464,7 +465,8 @@ mc_status mc_session_destroy(mc_session* s) {
                     s->part_l, s->amax_v, s->amax_i, s->att_cnt, s->counts, s->banned, s->bar,
                     s->status, s->seq, s->prompts, s->out, s->stop, s->trace, s->stamps,
                     s->xfin, s->hgen, s->hsync, s->hpv, s->hpi,
-                    s->pf_x, s->pf_xn, s->pf_q, s->pf_att, s->pf_f, s->pf_logits};
+                    s->pf_x, s->pf_xn, s->pf_q, s->pf_att, s->pf_f, s->pf_logits,
+                    s->pf_xn16, s->pf_att16, s->pf_f16};
     for (void* b : bufs) cudaFree(b);
     if (s->ev_mid) cudaEventDestroy(s->ev_mid);
     if (s->ev0) cudaEventDestroy(s->ev0);
@@ -752,22 +754,29 @@ cudaError_t tc_launch(const CUtensorMap& a, const CUtensorMap& b, const CUtensor
     return cudaGetLastError();
 }
 
-// Tensor maps of the prefill buffers and weight matrices (fp32, kind::tf32).
+// Tensor maps of the prefill buffers and weight matrices: fp32 operands
+// (kind::tf32) for fp32 weights, bf16 operands (kind::f16; the activations'
+// bf16 copies) for bf16 weights.
 mc_status pf_tc_maps(mc_session* s) {
     const mc_model* m = s->m;
     const char* wb = static_cast<const char*>(m->wblock);
     const uint64_t R = s->pf_rows, D = m->D, F = m->F, Q = m->Q, L = m->L;
+    const bool b16 = m->dtype == MC_WEIGHTS_BF16;
+    const int es = b16 ? 2 : 4;
+    const void* xn = b16 ? (const void*)s->pf_xn16 : (const void*)s->pf_xn;
+    const void* att = b16 ? (const void*)s->pf_att16 : (const void*)s->pf_att;
+    const void* fh = b16 ? (const void*)s->pf_f16 : (const void*)s->pf_f;
     mc_status st = MC_OK;
-    if (!st) st = tc_map(&s->pf_map[0], s->pf_xn, 4, D, R, 0);
-    if (!st) st = tc_map(&s->pf_map[1], s->pf_att, 4, D, R, 0);
-    if (!st) st = tc_map(&s->pf_map[2], s->pf_f, 4, F, R, 0);
+    if (!st) st = tc_map(&s->pf_map[0], xn, es, D, R, 0);
+    if (!st) st = tc_map(&s->pf_map[1], att, es, D, R, 0);
+    if (!st) st = tc_map(&s->pf_map[2], fh, es, F, R, 0);
     // single-B GEMMs run 128 x 256 tiles, the SwiGLU pair 128 x 128
-    if (!st) st = tc_map(&s->pf_map[3], wb + m->off[1], 4, D, Q, L, 256);
-    if (!st) st = tc_map(&s->pf_map[4], wb + m->off[2], 4, D, D, L, 256);
-    if (!st) st = tc_map(&s->pf_map[5], wb + m->off[3], 4, D, F, L, 128);
-    if (!st) st = tc_map(&s->pf_map[6], wb + m->off[4], 4, D, F, L, 128);
-    if (!st) st = tc_map(&s->pf_map[7], wb + m->off[5], 4, F, D, L, 256);
-    if (!st) st = tc_map(&s->pf_map[8], wb + m->off[0], 4, D, m->V, 1, 256);
+    if (!st) st = tc_map(&s->pf_map[3], wb + m->off[1], es, D, Q, L, 256);
+    if (!st) st = tc_map(&s->pf_map[4], wb + m->off[2], es, D, D, L, 256);
+    if (!st) st = tc_map(&s->pf_map[5], wb + m->off[3], es, D, F, L, 128);
+    if (!st) st = tc_map(&s->pf_map[6], wb + m->off[4], es, D, F, L, 128);
+    if (!st) st = tc_map(&s->pf_map[7], wb + m->off[5], es, F, D, L, 256);
+    if (!st) st = tc_map(&s->pf_map[8], wb + m->off[0], es, D, m->V, 1, 256);
     s->pf_maps_ok = st == MC_OK;
     return st;
 }
@@ -796,6 +805,23 @@ mc_status run_prefill(mc_session* s, int batch, const uint16_t* prompts, int str
         s->pf_maps_ok = false;
         cudaFree(s->pf_logits);
         s->pf_logits = nullptr;
+        for (__nv_bfloat16** b : {&s->pf_xn16, &s->pf_att16, &s->pf_f16}) {
+            cudaFree(*b);
+            *b = nullptr;
+        }
+    }
+    constexpr bool kB16 = std::is_same<WT, __nv_bfloat16>::value;
+    constexpr int KD = kB16 ? mc::TC_BF16 : mc::TC_TF32;
+    // bf16 operands need rows of a multiple of 8 elements (16-byte strides)
+    const bool tc = s->pf_tc && (!kB16 || (m->D % 8 == 0 && m->F % 8 == 0));
+    if (tc && kB16 && !s->pf_xn16) {
+        const size_t D = m->D, F = m->F, R = s->pf_rows;
+        if (cudaMalloc(&s->pf_xn16, R * D * 2) != cudaSuccess || cudaMalloc(&s->pf_att16, R * D * 2) != cudaSuccess ||
+            cudaMalloc(&s->pf_f16, R * F * 2) != cudaSuccess) {
+            cudaGetLastError();
+            return fail(MC_ERR_NOMEM, "prefill bf16 buffers");
+        }
+        s->pf_maps_ok = false;
     }
     if (logits && !s->pf_logits) {
         const size_t bytes = s->pf_rows * (size_t)m->V * 4;
@@ -804,7 +830,6 @@ mc_status run_prefill(mc_session* s, int batch, const uint16_t* prompts, int str
             return fail(MC_ERR_NOMEM, "model_forward: lm_head scratch (%zu bytes)", bytes);
         }
     }
-    const bool tc = s->pf_tc && std::is_same<WT, float>::value;
     if (tc && !s->pf_maps_ok) {
         const mc_status st = pf_tc_maps(s);
         if (st) return st;
@@ -816,6 +841,11 @@ mc_status run_prefill(mc_session* s, int batch, const uint16_t* prompts, int str
     a.prompts = prompts; a.prompt_stride = stride;
     a.rope = m->rope; a.kc = s->kc; a.vc = s->vc;
     a.X = s->pf_x; a.XN = s->pf_xn; a.QB = s->pf_q; a.ATT = s->pf_att; a.FH = s->pf_f;
+    if (tc && kB16) {
+        a.XN16 = s->pf_xn16;
+        a.ATT16 = s->pf_att16;
+        a.FH16 = s->pf_f16;
+    }
     a.status = s->status;
     const char* wb = static_cast<const char*>(m->wblock);
     const WT* emb = reinterpret_cast<const WT*>(wb + m->off[0]);
@@ -850,19 +880,19 @@ mc_status run_prefill(mc_session* s, int batch, const uint16_t* prompts, int str
                 const CUtensorMap* mp = s->pf_map;
                 cudaError_t e;
                 g.N = m->Q; g.K = m->D; g.C = nullptr; g.ldc = 0;
-                e = tc_launch<mc::TC_TF32, mc::EPI_QKV, 256>(mp[0], mp[3], mp[3], g, st);
+                e = tc_launch<KD, mc::EPI_QKV, 256>(mp[0], mp[3], mp[3], g, st);
                 if (e != cudaSuccess) return fail(MC_ERR_CUDA, "tcgen05 prefill: %s", cudaGetErrorString(e));
                 mc::pf_attention_kernel<<<dim3((a.chunk + QT - 1) / QT, m->K, batch), 256, att_smem, st>>>(
                     a, l, QT);
                 g.N = m->D; g.K = m->D; g.C = a.X; g.ldc = m->D;
-                e = tc_launch<mc::TC_TF32, mc::EPI_RESID, 256>(mp[1], mp[4], mp[4], g, st);
+                e = tc_launch<KD, mc::EPI_RESID, 256>(mp[1], mp[4], mp[4], g, st);
                 if (e != cudaSuccess) return fail(MC_ERR_CUDA, "tcgen05 prefill: %s", cudaGetErrorString(e));
                 mc::pf_norm_kernel<WT><<<(M + 7) / 8, 256, 0, st>>>(a, emb, rms2 + l * D, 0);
                 g.N = m->F; g.K = m->D; g.C = a.FH; g.ldc = m->F;
-                e = tc_launch<mc::TC_TF32, mc::EPI_SWIGLU>(mp[0], mp[5], mp[6], g, st);
+                e = tc_launch<KD, mc::EPI_SWIGLU>(mp[0], mp[5], mp[6], g, st);
                 if (e != cudaSuccess) return fail(MC_ERR_CUDA, "tcgen05 prefill: %s", cudaGetErrorString(e));
                 g.N = m->D; g.K = m->F; g.C = a.X; g.ldc = m->D;
-                e = tc_launch<mc::TC_TF32, mc::EPI_RESID, 256>(mp[2], mp[7], mp[7], g, st);
+                e = tc_launch<KD, mc::EPI_RESID, 256>(mp[2], mp[7], mp[7], g, st);
                 if (e != cudaSuccess) return fail(MC_ERR_CUDA, "tcgen05 prefill: %s", cudaGetErrorString(e));
                 launches += 7;
                 continue;
@@ -889,7 +919,7 @@ mc_status run_prefill(mc_session* s, int batch, const uint16_t* prompts, int str
                 g.pa = a;
                 g.status = s->status;
                 g.timeout_ns = 1000ull * 1000ull * 1000ull;
-                const cudaError_t e = tc_launch<mc::TC_TF32, mc::TCE_STORE, 256>(s->pf_map[0], s->pf_map[8],
+                const cudaError_t e = tc_launch<KD, mc::TCE_STORE, 256>(s->pf_map[0], s->pf_map[8],
                                                                                  s->pf_map[8], g, st);
                 if (e != cudaSuccess) return fail(MC_ERR_CUDA, "tcgen05 lm_head: %s", cudaGetErrorString(e));
             } else {

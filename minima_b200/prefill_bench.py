@@ -1,5 +1,6 @@
 """Batched-prefill time with the CUDA-core fp32 GEMMs and with the tcgen05
-(kind::tf32) GEMMs, on a seeded random-init Minima-architecture model.
+GEMMs (kind::tf32 for fp32 weights, kind::f16 with --bf16), on a seeded
+random-init Minima-architecture model.
 
     python -m minima_b200.prefill_bench --dim 768 --layers 12 --heads 12 --ffn 3072 \\
         --vocab 16384 --batch 64 --prompt 256
@@ -31,10 +32,11 @@ def main():
     ap.add_argument("--prompt", type=int, default=256)
     ap.add_argument("--iters", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=2)
+    ap.add_argument("--bf16", action="store_true", help="bf16 weights (tensor-core arm: kind::f16)")
     args = ap.parse_args()
     cap = args.prompt + 8
-    hm = M.HostModel(args.vocab, args.dim, args.layers, args.heads, args.ffn, cap, seed=2)
-    dm = M.DeviceModel(hm)
+    hm = M.HostModel(args.vocab, args.dim, args.layers, args.heads, args.ffn, cap, seed=2, bf16=args.bf16)
+    dm = M.DeviceModel(hm, M.MC_WEIGHTS_BF16 if args.bf16 else M.MC_WEIGHTS_F32)
     # non-special ids (generate.c:567 rejects none of them), seeded
     prompts = np.random.default_rng(1000).integers(4, args.vocab, (args.batch, args.prompt), dtype=np.uint16)
     opts = M.options(top_k=1, max_new_tokens=1)
@@ -43,8 +45,9 @@ def main():
     Q = args.dim + 2 * K * hd
     rows = args.batch * (args.prompt - 1)
     flops = 2.0 * rows * args.layers * (Q * args.dim + args.dim * args.dim + 3 * args.ffn * args.dim)
-    for arm in ("cuda_cores_fp32", "tcgen05_tf32"):
-        if arm == "tcgen05_tf32":
+    arms = ("cuda_cores", "tcgen05_bf16" if args.bf16 else "tcgen05_tf32")
+    for arm in arms:
+        if arm != "cuda_cores":
             os.environ["MINIMA_CUDA_PREFILL"] = "tcgen05"
         else:
             os.environ.pop("MINIMA_CUDA_PREFILL", None)

@@ -9,7 +9,9 @@ Bounds of the tensor-core path (looser than the fp32 path by design):
                exact, so only the fp32 accumulation rounds)
   prefill      decode-step logits after a tf32 prefill: |gpu - ref| <=
                TC_ATOL + TC_RTOL * |ref| against the fp32 oracle (measured
-               max |err| 3.8e-4 on this model).
+               max |err| 3.8e-4 on this model); after a bf16 (kind::f16)
+               prefill, TC16_ATOL + TC16_RTOL * |ref| against the oracle with
+               the same bf16 weights and fp32 activations (measured 7.1e-4).
 """
 import numpy as np
 import pytest
@@ -20,6 +22,7 @@ from oracle import oracle as O
 pytestmark = pytest.mark.gpu
 
 TC_ATOL, TC_RTOL = 2e-3, 2e-3
+TC16_ATOL, TC16_RTOL = 5e-3, 5e-3
 
 
 def to_bf16_bits(x):
@@ -99,3 +102,28 @@ def test_tcgen05_prefill_logits(gpu, monkeypatch):
         bound = TC_ATOL + TC_RTOL * np.abs(want[finite])
         assert np.all(err <= bound), f"max err {err.max():.3e}"
         assert np.array_equal(out_f[b, :counts_f[b]], ref_ids)
+
+
+def test_tcgen05_bf16_prefill_logits(gpu, monkeypatch):
+    """bf16 weights: the prefill GEMMs run as kind::f16 on bf16 copies of the
+    activations; decode logits against the oracle with the same bf16-rounded
+    weights and fp32 activations stay within TC16_ATOL + TC16_RTOL |ref|."""
+    dims = O.Dims(4096, 128, 2, 4, 512, 256)
+    hm = M.HostModel(dims.vocab, dims.dim, dims.n_layers, dims.n_heads, dims.ffn_dim, dims.max_seq,
+                     seed=12, bf16=True)
+    orc = O.OrcModel(dims, 12, bf16=True)
+    prompts = np.stack([O.random_prompt(150, dims.vocab, 30 + b) for b in range(2)])
+    monkeypatch.setenv("MINIMA_CUDA_PREFILL", "tcgen05")
+    sess = M.Session(M.DeviceModel(hm, M.MC_WEIGHTS_BF16), 2, 256)
+    _, _, _, _, tr = sess.generate(prompts, [150, 150], 256, M.options(top_k=1, max_new_tokens=8),
+                                   [1, 2], trace_steps=8)
+    assert sess.last_prefill()[0] == 149
+    for b in range(2):
+        _, _, _, ref_tr = orc.generate(prompts[b], 256, 256, O.make_options(top_k=1, max_new_tokens=8),
+                                       b + 1, trace_steps=8)
+        got, want = tr[b].astype(np.float64), ref_tr.astype(np.float64)
+        finite = np.isfinite(want)
+        assert np.array_equal(np.isfinite(got), finite)
+        err = np.abs(got[finite] - want[finite])
+        bound = TC16_ATOL + TC16_RTOL * np.abs(want[finite])
+        assert np.all(err <= bound), f"max err {err.max():.3e}"
