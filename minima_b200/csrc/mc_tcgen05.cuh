@@ -46,6 +46,10 @@ struct TcArgs {
     float* C;
     int ldc;
     PrefillArgs pa;            // rows <-> (sequence, position) for the QKV epilogue
+    // decode mode (batched token loop): row m is sequence m at the position
+    // *tpos; rows whose act[m] is 0 are not written.  act == null: prefill.
+    const int* act;
+    const int* tpos;
     int* status;
     unsigned long long timeout_ns;
 };
@@ -145,10 +149,16 @@ __device__ __forceinline__ void tc_tmem_wait_ld() {
 template <int EPI>
 __device__ __forceinline__ void tc_epilogue(const TcArgs& g, int m, int n, const float (&u)[32],
                                             const float (&gt)[32]) {
+    if (g.act && !g.act[m]) return;
     if constexpr (EPI == EPI_QKV) {
         const PrefillArgs& a = g.pa;
         int b, t;
-        pf_row(a, m, b, t);
+        if (g.act) {
+            b = m;
+            t = *g.tpos;
+        } else {
+            pf_row(a, m, b, t);
+        }
 #pragma unroll
         for (int j = 0; j < 32; j += 2) {
             const int c = n + j;                 // even: c, c + 1 are a RoPE pair

@@ -277,46 +277,82 @@ __device__ void phase_qkv(const LoopParams<WT>& p, int l, int t, LoopSmem& sm, i
     }
 }
 
+// Shared memory of the attention phase: queries [G][hd], scores
+// [G][kSplitLen], and the split's K and V rows staged [kSplitLen][hd] each.
+__host__ __device__ inline size_t att_phase_bytes(int G, int hd) {
+    return ((size_t)G * hd + (size_t)G * kSplitLen + 2 * (size_t)kSplitLen * hd) * 4;
+}
+
 template <typename WT>
 __device__ void phase_att(const LoopParams<WT>& p, int l, int t, LoopSmem& sm, int nfwd) {
     const int nkeys = t + 1;
     const int nsplit = (nkeys + kSplitLen - 1) / kSplitLen;
     const int units = nfwd * p.K * nsplit;
-    const int G = p.G, hd = p.hd;
+    const int G = p.G, hd = p.hd, q4 = hd / 4;
     const float scale = 1.0f / sqrtf((float)hd);
     float* qs = sm.xs;                       // [G][hd]
     float* sc = sm.xs + G * hd;              // [G][kSplitLen]
+    float* ks = sc + G * kSplitLen;          // [kSplitLen][hd]
+    float* vs = ks + kSplitLen * hd;         // [kSplitLen][hd]
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const bool combine = nsplit > 1 || G > 32;
     for (int u = blockIdx.x; u < units; u += gridDim.x) {
         const int s = u % nsplit;
         const int g = (u / nsplit) % p.K;
         const int b = sm.fwd[u / (nsplit * p.K)];
-        const int j0 = s * kSplitLen, j1 = min(nkeys, j0 + kSplitLen);
+        const int j0 = s * kSplitLen, j1 = min(nkeys, j0 + kSplitLen), n = j1 - j0;
         const size_t cache_off = (((size_t)l * p.Bcap + b) * p.K + g) * p.cap;
-        const float* kb = p.kc + cache_off * hd;
-        const float* vb = p.vc + cache_off * hd;
+        const float* kb = p.kc + (cache_off + j0) * hd;
+        const float* vb = p.vc + (cache_off + j0) * hd;
+        // stage q, and the split's K and V rows, with coalesced L2 reads
+        // (rows written by other CTAs earlier in this launch)
         for (int i = threadIdx.x; i < G * hd; i += blockDim.x)
             qs[i] = ldcg(p.q + (size_t)b * p.D + (size_t)g * G * hd + i);
-        __syncthreads();
-        // scores
-        for (int j = j0 + warp; j < j1; j += kWarps) {
-            const float* kr = kb + (size_t)j * hd;
-            for (int h = 0; h < G; h++) {
-                float part = 0.0f;
-                for (int d = lane; d < hd; d += 32) part += qs[h * hd + d] * ldcg(kr + d);
-                part = warp_sum(part);
-                if (lane == 0) sc[h * kSplitLen + (j - j0)] = part * scale;
+        if ((hd & 3) == 0) {
+            for (int e = threadIdx.x; e < n * q4; e += blockDim.x) {
+                reinterpret_cast<float4*>(ks)[e] = ldcg4(kb + 4 * e);
+                reinterpret_cast<float4*>(vs)[e] = ldcg4(vb + 4 * e);
             }
+        } else {
+            for (int e = threadIdx.x; e < n * hd; e += blockDim.x) {
+                ks[e] = ldcg(kb + e);
+                vs[e] = ldcg(vb + e);
+            }
+        }
+        __syncthreads();
+        // scores: a thread per (head, key); its key row is read starting at
+        // element (j mod hd) so that neighbouring keys fall in different banks
+        for (int e = threadIdx.x; e < G * n; e += blockDim.x) {
+            const int h = e / n, j = e - h * n;
+            const float* kr = ks + j * hd;
+            const float* qh = qs + h * hd;
+            float part = 0.0f;
+            if ((hd & 3) == 0) {
+                int cc = j % q4;
+#pragma unroll 4
+                for (int c = 0; c < q4; c++) {
+                    const float4 k4 = *reinterpret_cast<const float4*>(kr + 4 * cc);
+                    const float4 x4 = *reinterpret_cast<const float4*>(qh + 4 * cc);
+                    part += x4.x * k4.x + x4.y * k4.y + x4.z * k4.z + x4.w * k4.w;
+                    cc = cc + 1 == q4 ? 0 : cc + 1;
+                }
+            } else {
+                int d = j % hd;
+                for (int c = 0; c < hd; c++) {
+                    part += qh[d] * kr[d];
+                    d = d + 1 == hd ? 0 : d + 1;
+                }
+            }
+            sc[h * kSplitLen + j] = part * scale;
         }
         __syncthreads();
         // local softmax statistics per head
         for (int h = warp; h < G; h += kWarps) {
             float m = -INFINITY;
-            for (int j = lane; j < j1 - j0; j += 32) m = fmaxf(m, sc[h * kSplitLen + j]);
+            for (int j = lane; j < n; j += 32) m = fmaxf(m, sc[h * kSplitLen + j]);
             m = warp_max(m);
             float lsum = 0.0f;
-            for (int j = lane; j < j1 - j0; j += 32) {
+            for (int j = lane; j < n; j += 32) {
                 const float e = expf(sc[h * kSplitLen + j] - m);
                 sc[h * kSplitLen + j] = e;
                 lsum += e;
@@ -333,7 +369,8 @@ __device__ void phase_att(const LoopParams<WT>& p, int l, int t, LoopSmem& sm, i
         for (int i = threadIdx.x; i < G * hd; i += blockDim.x) {
             const int h = i / hd, d = i % hd;
             float o = 0.0f;
-            for (int j = j0; j < j1; j++) o += sc[h * kSplitLen + (j - j0)] * ldcg(vb + (size_t)j * hd + d);
+#pragma unroll 8
+            for (int j = 0; j < n; j++) o += sc[h * kSplitLen + j] * vs[j * hd + d];
             if (!combine) {
                 p.att[(size_t)b * p.D + (g * G + h) * hd + d] = o / sm.red[h];
             } else {
@@ -656,6 +693,30 @@ __device__ void phase_sample(const LoopParams<WT>& p, int t, LoopSmem& sm, int n
     }
 }
 
+// Prologue of a generate call: one CTA per sequence copies the prompt into
+// its history, seeds penalty counts and first-draw n-gram bans.
+template <typename WT>
+__device__ void loop_prologue(const LoopParams<WT>& p) {
+    for (int b = blockIdx.x; b < p.B; b += gridDim.x) {
+        const SeqState* st = p.seq + b;
+        if (st->done) continue;
+        const int P = st->P;
+        uint16_t* out = p.out_ids + (size_t)b * p.out_cap;
+        for (int i = threadIdx.x; i < P; i += blockDim.x) out[i] = p.prompts[(size_t)b * p.prompt_stride + i];
+        if (p.s.pen_active) {
+            unsigned* cnt = p.counts + (size_t)b * p.V;
+            for (int v = threadIdx.x; v < p.V; v += blockDim.x) cnt[v] = 0u;
+            __syncthreads();
+            for (int i = threadIdx.x; i < P; i += blockDim.x) {
+                const int id = p.prompts[(size_t)b * p.prompt_stride + i];
+                if (id < p.V) atomicAdd(&cnt[id], 1u);
+            }
+        }
+        __syncthreads();
+        if (p.s.ngram > 0) compute_bans(p, b, P);
+    }
+}
+
 // ------------------------------------------------------------------ kernel
 template <typename WT, bool VEC>
 __global__ void __launch_bounds__(kThreads, 1) token_loop_kernel(const LoopParams<WT> p) {
@@ -668,29 +729,7 @@ __global__ void __launch_bounds__(kThreads, 1) token_loop_kernel(const LoopParam
     sm.xs = smem_f + loop_fixed_bytes(p.Bcap) / 4;
     GridSync gs{p.bar, p.status, gridDim.x + p.extra_arrivals, 0u, p.timeout_ns};
 
-    // Prologue: one CTA per sequence copies the prompt into its history,
-    // seeds penalty counts and first-draw n-gram bans.
-    if (!p.all_logits) {
-        for (int b = blockIdx.x; b < p.B; b += gridDim.x) {
-            const SeqState* st = p.seq + b;
-            if (st->done) continue;
-            const int P = st->P;
-            uint16_t* out = p.out_ids + (size_t)b * p.out_cap;
-            for (int i = threadIdx.x; i < P; i += blockDim.x)
-                out[i] = p.prompts[(size_t)b * p.prompt_stride + i];
-            if (p.s.pen_active) {
-                unsigned* cnt = p.counts + (size_t)b * p.V;
-                for (int v = threadIdx.x; v < p.V; v += blockDim.x) cnt[v] = 0u;
-                __syncthreads();
-                for (int i = threadIdx.x; i < P; i += blockDim.x) {
-                    const int id = p.prompts[(size_t)b * p.prompt_stride + i];
-                    if (id < p.V) atomicAdd(&cnt[id], 1u);
-                }
-            }
-            __syncthreads();
-            if (p.s.ngram > 0) compute_bans(p, b, P);
-        }
-    }
+    if (!p.all_logits) loop_prologue(p);
     if (!gs.sync()) return;
 
     for (int t = p.t0; t < p.T; t++) {

@@ -20,6 +20,7 @@
 #include "mc_prefill.cuh"
 #include "mc_checkpoint.cuh"
 #include "mc_tcgen05.cuh"
+#include "mc_batched.cuh"
 
 #include <cudaTypedefs.h>
 
@@ -114,7 +115,16 @@ struct mc_session {
     size_t pf_rows;               // rows the buffers hold
     bool pf_tc;                   // prefill GEMMs on tcgen05 (tf32 / bf16), MINIMA_CUDA_PREFILL=tcgen05
     bool pf_maps_ok;              // tensor maps below match the current buffers
-    CUtensorMap pf_map[9];        // A: xn, att, f; B: qkv, proj, up, gate, down, tok_emb
+    CUtensorMap pf_map[3];        // A operands of the prefill GEMMs: xn, att, f
+    bool w_maps_ok;
+    CUtensorMap w_map[6];         // B operands: qkv, proj, up, gate, down, tok_emb
+    // batched decode on tcgen05 (mc_batched.cuh), MINIMA_CUDA_DECODE=tcgen05
+    bool bd_tc;
+    int* bd_lists;
+    float* bd_xn;                 // [Bcap][D]
+    __nv_bfloat16 *bd_xn16, *bd_att16, *bd_f16;
+    bool bd_maps_ok;
+    CUtensorMap bd_map[3];        // A operands: xn, att, f ([Bcap] rows)
     float* pf_logits;             // [pf_rows][V] lm_head scratch of mc_model_forward
     __nv_bfloat16 *pf_xn16, *pf_att16, *pf_f16;   // bf16 GEMM inputs (tensor cores, bf16 weights)
     cudaEvent_t ev_mid;           // end of prefill
@@ -466,7 +476,8 @@ mc_status mc_session_destroy(mc_session* s) {
                     s->status, s->seq, s->prompts, s->out, s->stop, s->trace, s->stamps,
                     s->xfin, s->hgen, s->hsync, s->hpv, s->hpi,
                     s->pf_x, s->pf_xn, s->pf_q, s->pf_att, s->pf_f, s->pf_logits,
-                    s->pf_xn16, s->pf_att16, s->pf_f16};
+                    s->pf_xn16, s->pf_att16, s->pf_f16, s->bd_lists, s->bd_xn,
+                    s->bd_xn16, s->bd_att16, s->bd_f16};
     for (void* b : bufs) cudaFree(b);
     if (s->ev_mid) cudaEventDestroy(s->ev_mid);
     if (s->ev0) cudaEventDestroy(s->ev0);
@@ -487,6 +498,8 @@ mc_status mc_session_create(mc_model* m, int max_batch, int max_seq, mc_session*
     {
         const char* pe = getenv("MINIMA_CUDA_PREFILL");
         s->pf_tc = pe && std::strcmp(pe, "tcgen05") == 0;
+        const char* de = getenv("MINIMA_CUDA_DECODE");
+        s->bd_tc = de && std::strcmp(de, "tcgen05") == 0;
     }
     s->m = m;
     s->Bcap = max_batch;
@@ -499,7 +512,7 @@ mc_status mc_session_create(mc_model* m, int max_batch, int max_seq, mc_session*
     // largest of GEMV chunk, attention split and sampler.
     const int G = m->H / m->K;
     s->xs_ld = (int)align_up((size_t)std::max(m->D, m->F), 4);
-    const size_t att_bytes = (size_t)(G * m->hd + G * mc::kSplitLen) * 4;
+    const size_t att_bytes = mc::att_phase_bytes(G, m->hd);
     const size_t samp_bytes = mc::sampler_smem_bytes(m->V);
     const size_t limit = (size_t)prop.sharedMemPerBlockOptin;
     const size_t fixed = mc::loop_fixed_bytes(max_batch);
@@ -754,29 +767,39 @@ cudaError_t tc_launch(const CUtensorMap& a, const CUtensorMap& b, const CUtensor
     return cudaGetLastError();
 }
 
-// Tensor maps of the prefill buffers and weight matrices: fp32 operands
-// (kind::tf32) for fp32 weights, bf16 operands (kind::f16; the activations'
-// bf16 copies) for bf16 weights.
-mc_status pf_tc_maps(mc_session* s) {
+// Tensor maps of the weight matrices: fp32 operands (kind::tf32) for fp32
+// weights, bf16 operands (kind::f16) for bf16 weights.  Single-matrix GEMMs
+// run 128 x 256 tiles, the SwiGLU pair 128 x 128.
+mc_status tc_weight_maps(mc_session* s) {
+    if (s->w_maps_ok) return MC_OK;
     const mc_model* m = s->m;
     const char* wb = static_cast<const char*>(m->wblock);
-    const uint64_t R = s->pf_rows, D = m->D, F = m->F, Q = m->Q, L = m->L;
+    const uint64_t D = m->D, F = m->F, Q = m->Q, L = m->L;
+    const int es = m->dtype == MC_WEIGHTS_BF16 ? 2 : 4;
+    mc_status st = MC_OK;
+    if (!st) st = tc_map(&s->w_map[0], wb + m->off[1], es, D, Q, L, 256);
+    if (!st) st = tc_map(&s->w_map[1], wb + m->off[2], es, D, D, L, 256);
+    if (!st) st = tc_map(&s->w_map[2], wb + m->off[3], es, D, F, L, 128);
+    if (!st) st = tc_map(&s->w_map[3], wb + m->off[4], es, D, F, L, 128);
+    if (!st) st = tc_map(&s->w_map[4], wb + m->off[5], es, F, D, L, 256);
+    if (!st) st = tc_map(&s->w_map[5], wb + m->off[0], es, D, m->V, 1, 256);
+    s->w_maps_ok = st == MC_OK;
+    return st;
+}
+
+// A-operand maps of the prefill buffers (their bf16 copies for bf16 weights).
+mc_status pf_tc_maps(mc_session* s) {
+    const mc_model* m = s->m;
+    const uint64_t R = s->pf_rows, D = m->D, F = m->F;
     const bool b16 = m->dtype == MC_WEIGHTS_BF16;
     const int es = b16 ? 2 : 4;
     const void* xn = b16 ? (const void*)s->pf_xn16 : (const void*)s->pf_xn;
     const void* att = b16 ? (const void*)s->pf_att16 : (const void*)s->pf_att;
     const void* fh = b16 ? (const void*)s->pf_f16 : (const void*)s->pf_f;
-    mc_status st = MC_OK;
+    mc_status st = tc_weight_maps(s);
     if (!st) st = tc_map(&s->pf_map[0], xn, es, D, R, 0);
     if (!st) st = tc_map(&s->pf_map[1], att, es, D, R, 0);
     if (!st) st = tc_map(&s->pf_map[2], fh, es, F, R, 0);
-    // single-B GEMMs run 128 x 256 tiles, the SwiGLU pair 128 x 128
-    if (!st) st = tc_map(&s->pf_map[3], wb + m->off[1], es, D, Q, L, 256);
-    if (!st) st = tc_map(&s->pf_map[4], wb + m->off[2], es, D, D, L, 256);
-    if (!st) st = tc_map(&s->pf_map[5], wb + m->off[3], es, D, F, L, 128);
-    if (!st) st = tc_map(&s->pf_map[6], wb + m->off[4], es, D, F, L, 128);
-    if (!st) st = tc_map(&s->pf_map[7], wb + m->off[5], es, F, D, L, 256);
-    if (!st) st = tc_map(&s->pf_map[8], wb + m->off[0], es, D, m->V, 1, 256);
     s->pf_maps_ok = st == MC_OK;
     return st;
 }
@@ -878,21 +901,22 @@ mc_status run_prefill(mc_session* s, int batch, const uint16_t* prompts, int str
                 g.status = s->status;
                 g.timeout_ns = 1000ull * 1000ull * 1000ull;
                 const CUtensorMap* mp = s->pf_map;
+                const CUtensorMap* wm = s->w_map;
                 cudaError_t e;
                 g.N = m->Q; g.K = m->D; g.C = nullptr; g.ldc = 0;
-                e = tc_launch<KD, mc::EPI_QKV, 256>(mp[0], mp[3], mp[3], g, st);
+                e = tc_launch<KD, mc::EPI_QKV, 256>(mp[0], wm[0], wm[0], g, st);
                 if (e != cudaSuccess) return fail(MC_ERR_CUDA, "tcgen05 prefill: %s", cudaGetErrorString(e));
                 mc::pf_attention_kernel<<<dim3((a.chunk + QT - 1) / QT, m->K, batch), 256, att_smem, st>>>(
                     a, l, QT);
                 g.N = m->D; g.K = m->D; g.C = a.X; g.ldc = m->D;
-                e = tc_launch<KD, mc::EPI_RESID, 256>(mp[1], mp[4], mp[4], g, st);
+                e = tc_launch<KD, mc::EPI_RESID, 256>(mp[1], wm[1], wm[1], g, st);
                 if (e != cudaSuccess) return fail(MC_ERR_CUDA, "tcgen05 prefill: %s", cudaGetErrorString(e));
                 mc::pf_norm_kernel<WT><<<(M + 7) / 8, 256, 0, st>>>(a, emb, rms2 + l * D, 0);
                 g.N = m->F; g.K = m->D; g.C = a.FH; g.ldc = m->F;
-                e = tc_launch<KD, mc::EPI_SWIGLU>(mp[0], mp[5], mp[6], g, st);
+                e = tc_launch<KD, mc::EPI_SWIGLU>(mp[0], wm[2], wm[3], g, st);
                 if (e != cudaSuccess) return fail(MC_ERR_CUDA, "tcgen05 prefill: %s", cudaGetErrorString(e));
                 g.N = m->D; g.K = m->F; g.C = a.X; g.ldc = m->D;
-                e = tc_launch<KD, mc::EPI_RESID, 256>(mp[2], mp[7], mp[7], g, st);
+                e = tc_launch<KD, mc::EPI_RESID, 256>(mp[2], wm[4], wm[4], g, st);
                 if (e != cudaSuccess) return fail(MC_ERR_CUDA, "tcgen05 prefill: %s", cudaGetErrorString(e));
                 launches += 7;
                 continue;
@@ -919,8 +943,8 @@ mc_status run_prefill(mc_session* s, int batch, const uint16_t* prompts, int str
                 g.pa = a;
                 g.status = s->status;
                 g.timeout_ns = 1000ull * 1000ull * 1000ull;
-                const cudaError_t e = tc_launch<KD, mc::TCE_STORE, 256>(s->pf_map[0], s->pf_map[8],
-                                                                                 s->pf_map[8], g, st);
+                const cudaError_t e = tc_launch<KD, mc::TCE_STORE, 256>(s->pf_map[0], s->w_map[5],
+                                                                                 s->w_map[5], g, st);
                 if (e != cudaSuccess) return fail(MC_ERR_CUDA, "tcgen05 lm_head: %s", cudaGetErrorString(e));
             } else {
                 mc::pf_gemm_kernel<WT, mc::EPI_STORE><<<grid2(m->V, M), 256, 0, st>>>(
@@ -937,6 +961,122 @@ mc_status run_prefill(mc_session* s, int batch, const uint16_t* prompts, int str
     }
     const cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return fail(MC_ERR_CUDA, "prefill launch: %s", cudaGetErrorString(e));
+    return MC_OK;
+}
+
+// Shapes the batched tensor-core decode handles: TMA rows of 16 bytes
+// (bf16: multiples of 8 elements) and the attention phase's limits.
+bool batched_ok(const mc_model* m) {
+    const int mult = m->dtype == MC_WEIGHTS_BF16 ? 8 : 4;
+    return m->D % mult == 0 && m->F % mult == 0;
+}
+
+// The token loop as one launch sequence per step with every matrix product
+// a batch-wide tcgen05 GEMM (mc_batched.cuh).
+template <typename WT>
+mc_status run_batched(mc_session* s, mc::LoopParams<WT>& p) {
+    const mc_model* m = s->m;
+    constexpr bool kB16 = std::is_same<WT, __nv_bfloat16>::value;
+    constexpr int KD = kB16 ? mc::TC_BF16 : mc::TC_TF32;
+    fill_params(p, s);
+    p.stamps = s->stamps;
+    s->last_T = p.T;
+    const size_t Bc = s->Bcap, D = m->D, F = m->F;
+    if (!s->bd_lists) {
+        bool ok = cudaMalloc(&s->bd_lists, mc::bd_lists_ints(s->Bcap) * 4) == cudaSuccess &&
+                  cudaMalloc(&s->bd_xn, Bc * D * 4) == cudaSuccess;
+        if (ok && kB16)
+            ok = cudaMalloc(&s->bd_xn16, Bc * D * 2) == cudaSuccess &&
+                 cudaMalloc(&s->bd_att16, Bc * D * 2) == cudaSuccess &&
+                 cudaMalloc(&s->bd_f16, Bc * F * 2) == cudaSuccess;
+        if (!ok) {
+            cudaGetLastError();
+            return fail(MC_ERR_NOMEM, "batched decode buffers");
+        }
+        s->bd_maps_ok = false;
+    }
+    if (!s->bd_maps_ok) {
+        const int es = kB16 ? 2 : 4;
+        mc_status st = tc_weight_maps(s);
+        if (!st) st = tc_map(&s->bd_map[0], kB16 ? (const void*)s->bd_xn16 : (const void*)s->bd_xn, es, D, Bc, 0);
+        if (!st) st = tc_map(&s->bd_map[1], kB16 ? (const void*)s->bd_att16 : (const void*)s->att, es, D, Bc, 0);
+        if (!st) st = tc_map(&s->bd_map[2], kB16 ? (const void*)s->bd_f16 : (const void*)s->f, es, F, Bc, 0);
+        if (st) return st;
+        s->bd_maps_ok = true;
+    }
+    cudaStream_t st = s->stream;
+    MC_CUDA(cudaMemsetAsync(s->stamps, 0, ((size_t)p.T + 1) * 8, st));
+    MC_CUDA(cudaMemsetAsync(s->status, 0, 256, st));
+    MC_CUDA(cudaMemsetAsync(s->att_cnt, 0, (size_t)s->Bcap * m->K * 4, st));
+    static unsigned long long attr_set = 0;     // dynamic shared memory limits, per device
+    int dev = 0;
+    MC_CUDA(cudaGetDevice(&dev));
+    if (dev < 64 && !((attr_set >> dev) & 1ull)) {
+        int lim = 0;     // the device maximum, shared by every session on the device
+        MC_CUDA(cudaDeviceGetAttribute(&lim, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev));
+        MC_CUDA(cudaFuncSetAttribute(mc::bd_att_kernel<WT>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim));
+        MC_CUDA(cudaFuncSetAttribute(mc::bd_sample_kernel<WT>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim));
+        attr_set |= 1ull << dev;
+    }
+    const mc::BdLists L{s->bd_lists, s->Bcap};
+    mc::TcArgs g{};
+    g.M = p.B;
+    g.act = L.base + 4 + 2 * (size_t)s->Bcap;      // act_fwd
+    g.tpos = L.base + 2;
+    g.status = s->status;
+    g.timeout_ns = p.timeout_ns;
+    g.pa.D = m->D; g.pa.H = m->H; g.pa.K = m->K; g.pa.hd = m->hd; g.pa.Bcap = s->Bcap; g.pa.cap = s->cap;
+    g.pa.rope = m->rope; g.pa.kc = s->kc; g.pa.vc = s->vc; g.pa.QB = s->q;
+    g.pa.FH16 = kB16 ? s->bd_f16 : nullptr;
+    const CUtensorMap* am = s->bd_map;
+    const CUtensorMap* wm = s->w_map;
+    const float* rmsf = m->norms + 2 * (size_t)m->L * m->D;
+    int launches = 0;
+    mc::bd_prologue_kernel<WT><<<s->grid, mc::kThreads, 0, st>>>(p);
+    launches++;
+    cudaError_t e = cudaSuccess;
+    for (int t = p.t0; t < p.T && e == cudaSuccess; t++) {
+        mc::bd_lists_kernel<WT><<<1, 32, 0, st>>>(p, L, t == p.t0);
+        for (int l = 0; l < m->L; l++) {
+            mc::bd_norm_kernel<WT><<<p.B, mc::kThreads, 0, st>>>(p, L, 0, m->norms + (size_t)l * D, l == 0,
+                                                                  s->bd_xn, kB16 ? s->bd_xn16 : nullptr);
+            g.layer = l;
+            g.N = m->Q; g.K = m->D; g.C = nullptr; g.ldc = 0;
+            if ((e = tc_launch<KD, mc::EPI_QKV, 256>(am[0], wm[0], wm[0], g, st)) != cudaSuccess) break;
+            mc::bd_att_kernel<WT><<<s->grid, mc::kThreads, s->smem, st>>>(p, L, l);
+            if (kB16) mc::bd_cvt_kernel<WT><<<p.B, mc::kThreads, 0, st>>>(p, L, s->bd_att16);
+            g.N = m->D; g.K = m->D; g.C = s->x; g.ldc = m->D;
+            if ((e = tc_launch<KD, mc::EPI_RESID, 256>(am[1], wm[1], wm[1], g, st)) != cudaSuccess) break;
+            mc::bd_norm_kernel<WT><<<p.B, mc::kThreads, 0, st>>>(p, L, 0, m->norms + ((size_t)m->L + l) * D, 0,
+                                                                  s->bd_xn, kB16 ? s->bd_xn16 : nullptr);
+            g.N = m->F; g.K = m->D; g.C = s->f; g.ldc = m->F;
+            if ((e = tc_launch<KD, mc::EPI_SWIGLU>(am[0], wm[2], wm[3], g, st)) != cudaSuccess) break;
+            g.N = m->D; g.K = m->F; g.C = s->x; g.ldc = m->D;
+            if ((e = tc_launch<KD, mc::EPI_RESID, 256>(am[2], wm[4], wm[4], g, st)) != cudaSuccess) break;
+            launches += kB16 ? 8 : 7;
+        }
+        if (e != cudaSuccess) break;
+        mc::bd_norm_kernel<WT><<<p.B, mc::kThreads, 0, st>>>(p, L, 1, rmsf, 0, s->bd_xn,
+                                                              kB16 ? s->bd_xn16 : nullptr);
+        mc::TcArgs gh = g;
+        gh.act = nullptr;
+        gh.N = m->V; gh.K = m->D; gh.C = s->logits; gh.ldc = m->V; gh.layer = 0;
+        if ((e = tc_launch<KD, mc::TCE_STORE, 256>(am[0], wm[5], wm[5], gh, st)) != cudaSuccess) break;
+        mc::bd_head_kernel<WT><<<s->grid, mc::kThreads, 0, st>>>(p, L);
+        mc::bd_sample_kernel<WT><<<s->grid, mc::kThreads, s->smem, st>>>(p, L);
+        launches += 6;
+        e = cudaGetLastError();
+    }
+    if (e != cudaSuccess) return fail(MC_ERR_CUDA, "batched decode launch: %s", cudaGetErrorString(e));
+    MC_CUDA(cudaEventRecord(s->ev1, st));
+    s->last_launches = launches;
+    s->last_path = 2;
+    int status = 0;
+    MC_CUDA(cudaMemcpyAsync(&status, s->status, 4, cudaMemcpyDeviceToHost, st));
+    MC_CUDA(cudaStreamSynchronize(st));
+    MC_CUDA(cudaEventElapsedTime(&s->last_ms, s->ev0, s->ev1));
+    if (status == mc::ST_TIMEOUT) return fail(MC_ERR_TIMEOUT, "batched decode: a pipeline wait passed its deadline");
+    if (status != 0) return fail(MC_ERR_DEVICE, "batched decode reported status %d", status);
     return MC_OK;
 }
 
@@ -1057,7 +1197,9 @@ mc_status generate_t(mc_session* s, int batch, const uint16_t* prompts, int prom
         MC_CUDA(cudaEventRecord(s->ev_mid, s->stream));
         p.t0 = Pf;
         mc_status st;
-        if constexpr (std::is_same<WT, float>::value) {
+        if (s->bd_tc && batched_ok(m)) {
+            st = run_batched<WT>(s, p);
+        } else if constexpr (std::is_same<WT, float>::value) {
             if (s->cl_ok && p.s.top_k == 1 && batch <= mc::kBCMax) st = run_cluster(s, p);
             else st = run_loop<WT>(s, p);
         } else {
@@ -1268,7 +1410,7 @@ mc_status mc_last_step_times(mc_session* s, unsigned long long* ns, int cap, int
 
 const char* mc_last_kernel_name(mc_session* s) {
     if (!s || s->last_launches == 0) return "";
-    return s->last_path == 1 ? "mc::cluster_loop_kernel" : "mc::token_loop_kernel";
+    return s->last_path == 2 ? "mc::tc_gemm_kernel" : s->last_path == 1 ? "mc::cluster_loop_kernel" : "mc::token_loop_kernel";
 }
 
 mc_status mc_session_stream(mc_session* s, void** stream) {
@@ -1351,7 +1493,7 @@ StaticPlan static_plan(const mc_model_desc* d, int batch, int cap, int grid, siz
     pl.total = off;
     const int G = d->n_heads / d->n_kv_heads;
     pl.xs_ld = (int)align_up((size_t)std::max(d->dim, d->ffn_dim), 4);
-    const size_t att_bytes = (size_t)(G * d->head_dim + G * mc::kSplitLen) * 4;
+    const size_t att_bytes = mc::att_phase_bytes(G, d->head_dim);
     const size_t samp_bytes = mc::sampler_smem_bytes(d->vocab_size);
     const size_t fixed = mc::loop_fixed_bytes(batch);
     const size_t wi_bytes = mc::kWarps * mc::kBCMax * 4;
