@@ -39,34 +39,43 @@ struct BdLists {
 // sample after it (the token loop's step lists), the ids they feed, and the
 // position itself (first call: t0; then one more per call).
 template <typename WT>
-__global__ void __launch_bounds__(kThreads) bd_lists_kernel(const LoopParams<WT> p, BdLists L, int first) {
-    if (threadIdx.x != 0) return;
+__global__ void __launch_bounds__(1024) bd_lists_kernel(const LoopParams<WT> p, BdLists L, int first) {
+    __shared__ int flag[1024];
     const int t = first ? p.t0 : L.base[2] + 1;
-    int nf = 0, nh = 0;
-    for (int b = 0; b < p.B; b++) {
-        L.act_fwd()[b] = 0;
-        L.act_head()[b] = 0;
+    __syncthreads();                     // every thread has read the previous position
+    // a thread per sequence: does it run a forward, does it sample, which id
+    for (int b = threadIdx.x; b < p.B; b += blockDim.x) {
         const SeqState* st = p.seq + b;
-        if (st->done) continue;
-        const int P = st->P, nnew = st->nnew;
-        if (t >= P + nnew - 1) continue;
-        L.fwd()[nf++] = b;
-        L.act_fwd()[b] = 1;
-        if (t >= P - 1) {
-            L.head()[nh++] = b;
-            L.act_head()[b] = 1;
+        int f = 0;
+        if (!st->done) {
+            const int P = st->P, nnew = st->nnew;
+            if (t < P + nnew - 1) {
+                f = 1 | (t >= P - 1 ? 2 : 0);
+                int tok = t < P ? (int)p.prompts[(size_t)b * p.prompt_stride + t] : st->tok;
+                if (tok < 0 || tok >= p.V) {
+                    atomicMax(p.status, (int)ST_DEVICE);
+                    tok = 0;
+                }
+                L.tok()[b] = tok;
+            }
         }
-        int tok = t < P ? (int)p.prompts[(size_t)b * p.prompt_stride + t] : st->tok;
-        if (tok < 0 || tok >= p.V) {
-            atomicMax(p.status, (int)ST_DEVICE);
-            tok = 0;
-        }
-        L.tok()[b] = tok;
+        L.act_fwd()[b] = f & 1;
+        L.act_head()[b] = (f >> 1) & 1;
+        if (b < 1024) flag[b] = f;
     }
-    L.base[0] = nf;
-    L.base[1] = nh;
-    L.base[2] = t;
-    if (p.stamps && t < p.T) p.stamps[t] = globaltimer_ns();
+    __syncthreads();
+    if (threadIdx.x == 0) {              // compact, in sequence order
+        int nf = 0, nh = 0;
+        for (int b = 0; b < p.B; b++) {
+            const int f = b < 1024 ? flag[b] : (L.act_fwd()[b] | (L.act_head()[b] << 1));
+            if (f & 1) L.fwd()[nf++] = b;
+            if (f & 2) L.head()[nh++] = b;
+        }
+        L.base[0] = nf;
+        L.base[1] = nh;
+        L.base[2] = t;
+        if (p.stamps && t < p.T) p.stamps[t] = globaltimer_ns();
+    }
 }
 
 // xn[b] = rmsnorm(x[b]) * scale (generate.c:57-63) for the listed sequences,
@@ -133,20 +142,19 @@ __global__ void __launch_bounds__(kThreads) bd_cvt_kernel(const LoopParams<WT> p
 // vocabulary (generate.c:438-460), the partials phase_sample reduces.
 template <typename WT>
 __global__ void __launch_bounds__(kThreads) bd_head_kernel(const LoopParams<WT> p, BdLists L) {
-    __shared__ float rv[kWarps];
-    __shared__ int ri[kWarps];
     const int nh = L.base[1];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int per = (p.V + gridDim.x - 1) / gridDim.x;
     const int v0 = min(p.V, blockIdx.x * per), v1 = min(p.V, v0 + per);
     const int nwords = (p.V + 31) >> 5;
     const bool greedy = p.s.top_k == 1;
-    for (int i = 0; i < nh; i++) {
+    // a warp per head sequence over this CTA's share of the vocabulary
+    for (int i = warp; i < nh; i += kWarps) {
         const int b = L.head()[i];
         float* lg = p.logits + (size_t)b * p.V;
         float bv = -INFINITY;
         int bi = 0x7fffffff;
-        for (int v = v0 + threadIdx.x; v < v1; v += blockDim.x) {
+        for (int v = v0 + lane; v < v1; v += 32) {
             float x = lg[v];
             if (v < 4) {
                 x = -INFINITY;
@@ -161,17 +169,10 @@ __global__ void __launch_bounds__(kThreads) bd_head_kernel(const LoopParams<WT> 
         }
         if (!greedy) continue;
         warp_argmax(bv, bi);
-        if (lane == 0) { rv[warp] = bv; ri[warp] = bi; }
-        __syncthreads();
-        if (threadIdx.x == 0) {
-            float v = rv[0];
-            int id = ri[0];
-            for (int w = 1; w < kWarps; w++)
-                if (better(rv[w], ri[w], v, id)) { v = rv[w]; id = ri[w]; }
-            p.amax_v[(size_t)b * gridDim.x + blockIdx.x] = v;
-            p.amax_i[(size_t)b * gridDim.x + blockIdx.x] = id;
+        if (lane == 0) {
+            p.amax_v[(size_t)b * gridDim.x + blockIdx.x] = bv;
+            p.amax_i[(size_t)b * gridDim.x + blockIdx.x] = bi;
         }
-        __syncthreads();
     }
 }
 

@@ -125,6 +125,7 @@ struct mc_session {
     __nv_bfloat16 *bd_xn16, *bd_att16, *bd_f16;
     bool bd_maps_ok;
     CUtensorMap bd_map[3];        // A operands: xn, att, f ([Bcap] rows)
+    CUtensorMap bd_wmap[6];       // B operands as 64-row boxes (more CTAs for skinny GEMMs)
     float* pf_logits;             // [pf_rows][V] lm_head scratch of mc_model_forward
     __nv_bfloat16 *pf_xn16, *pf_att16, *pf_f16;   // bf16 GEMM inputs (tensor cores, bf16 weights)
     cudaEvent_t ev_mid;           // end of prefill
@@ -1001,6 +1002,16 @@ mc_status run_batched(mc_session* s, mc::LoopParams<WT>& p) {
         if (!st) st = tc_map(&s->bd_map[0], kB16 ? (const void*)s->bd_xn16 : (const void*)s->bd_xn, es, D, Bc, 0);
         if (!st) st = tc_map(&s->bd_map[1], kB16 ? (const void*)s->bd_att16 : (const void*)s->att, es, D, Bc, 0);
         if (!st) st = tc_map(&s->bd_map[2], kB16 ? (const void*)s->bd_f16 : (const void*)s->f, es, F, Bc, 0);
+        // a decode GEMM has at most a tile of rows: 64-column tiles spread
+        // the weight stream over 4x more CTAs than the prefill's
+        const char* wb = static_cast<const char*>(m->wblock);
+        const uint64_t Q = m->Q, L = m->L;
+        if (!st) st = tc_map(&s->bd_wmap[0], wb + m->off[1], es, D, Q, L, 64);
+        if (!st) st = tc_map(&s->bd_wmap[1], wb + m->off[2], es, D, D, L, 64);
+        if (!st) st = tc_map(&s->bd_wmap[2], wb + m->off[3], es, D, F, L, 64);
+        if (!st) st = tc_map(&s->bd_wmap[3], wb + m->off[4], es, D, F, L, 64);
+        if (!st) st = tc_map(&s->bd_wmap[4], wb + m->off[5], es, F, D, L, 64);
+        if (!st) st = tc_map(&s->bd_wmap[5], wb + m->off[0], es, D, m->V, 1, 64);
         if (st) return st;
         s->bd_maps_ok = true;
     }
@@ -1029,30 +1040,33 @@ mc_status run_batched(mc_session* s, mc::LoopParams<WT>& p) {
     g.pa.rope = m->rope; g.pa.kc = s->kc; g.pa.vc = s->vc; g.pa.QB = s->q;
     g.pa.FH16 = kB16 ? s->bd_f16 : nullptr;
     const CUtensorMap* am = s->bd_map;
-    const CUtensorMap* wm = s->w_map;
+    const CUtensorMap* wm = s->bd_wmap;
     const float* rmsf = m->norms + 2 * (size_t)m->L * m->D;
+    // the attention kernel needs only its lists and the attention phase region,
+    // so several CTAs share an SM
+    const size_t att_smem = mc::loop_fixed_bytes(s->Bcap) + mc::att_phase_bytes(m->H / m->K, m->hd);
     int launches = 0;
     mc::bd_prologue_kernel<WT><<<s->grid, mc::kThreads, 0, st>>>(p);
     launches++;
     cudaError_t e = cudaSuccess;
     for (int t = p.t0; t < p.T && e == cudaSuccess; t++) {
-        mc::bd_lists_kernel<WT><<<1, 32, 0, st>>>(p, L, t == p.t0);
+        mc::bd_lists_kernel<WT><<<1, 1024, 0, st>>>(p, L, t == p.t0);
         for (int l = 0; l < m->L; l++) {
             mc::bd_norm_kernel<WT><<<p.B, mc::kThreads, 0, st>>>(p, L, 0, m->norms + (size_t)l * D, l == 0,
                                                                   s->bd_xn, kB16 ? s->bd_xn16 : nullptr);
             g.layer = l;
             g.N = m->Q; g.K = m->D; g.C = nullptr; g.ldc = 0;
-            if ((e = tc_launch<KD, mc::EPI_QKV, 256>(am[0], wm[0], wm[0], g, st)) != cudaSuccess) break;
-            mc::bd_att_kernel<WT><<<s->grid, mc::kThreads, s->smem, st>>>(p, L, l);
+            if ((e = tc_launch<KD, mc::EPI_QKV, 64>(am[0], wm[0], wm[0], g, st)) != cudaSuccess) break;
+            mc::bd_att_kernel<WT><<<4 * s->grid, mc::kThreads, att_smem, st>>>(p, L, l);
             if (kB16) mc::bd_cvt_kernel<WT><<<p.B, mc::kThreads, 0, st>>>(p, L, s->bd_att16);
             g.N = m->D; g.K = m->D; g.C = s->x; g.ldc = m->D;
-            if ((e = tc_launch<KD, mc::EPI_RESID, 256>(am[1], wm[1], wm[1], g, st)) != cudaSuccess) break;
+            if ((e = tc_launch<KD, mc::EPI_RESID, 64>(am[1], wm[1], wm[1], g, st)) != cudaSuccess) break;
             mc::bd_norm_kernel<WT><<<p.B, mc::kThreads, 0, st>>>(p, L, 0, m->norms + ((size_t)m->L + l) * D, 0,
                                                                   s->bd_xn, kB16 ? s->bd_xn16 : nullptr);
             g.N = m->F; g.K = m->D; g.C = s->f; g.ldc = m->F;
-            if ((e = tc_launch<KD, mc::EPI_SWIGLU>(am[0], wm[2], wm[3], g, st)) != cudaSuccess) break;
+            if ((e = tc_launch<KD, mc::EPI_SWIGLU, 64>(am[0], wm[2], wm[3], g, st)) != cudaSuccess) break;
             g.N = m->D; g.K = m->F; g.C = s->x; g.ldc = m->D;
-            if ((e = tc_launch<KD, mc::EPI_RESID, 256>(am[2], wm[4], wm[4], g, st)) != cudaSuccess) break;
+            if ((e = tc_launch<KD, mc::EPI_RESID, 64>(am[2], wm[4], wm[4], g, st)) != cudaSuccess) break;
             launches += kB16 ? 8 : 7;
         }
         if (e != cudaSuccess) break;
@@ -1061,7 +1075,7 @@ mc_status run_batched(mc_session* s, mc::LoopParams<WT>& p) {
         mc::TcArgs gh = g;
         gh.act = nullptr;
         gh.N = m->V; gh.K = m->D; gh.C = s->logits; gh.ldc = m->V; gh.layer = 0;
-        if ((e = tc_launch<KD, mc::TCE_STORE, 256>(am[0], wm[5], wm[5], gh, st)) != cudaSuccess) break;
+        if ((e = tc_launch<KD, mc::TCE_STORE, 64>(am[0], wm[5], wm[5], gh, st)) != cudaSuccess) break;
         mc::bd_head_kernel<WT><<<s->grid, mc::kThreads, 0, st>>>(p, L);
         mc::bd_sample_kernel<WT><<<s->grid, mc::kThreads, s->smem, st>>>(p, L);
         launches += 6;
