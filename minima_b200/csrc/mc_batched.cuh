@@ -79,23 +79,33 @@ __global__ void __launch_bounds__(1024) bd_lists_kernel(const LoopParams<WT> p, 
 }
 
 // xn[b] = rmsnorm(x[b]) * scale (generate.c:57-63) for the listed sequences,
-// plus a bf16 copy when xn16 is set; with embed, x[b] is first set to the
-// embedding row of the id fed (generate.c:86-88).  One CTA per sequence.
+// plus a bf16 copy when xn16 is set.  With embed, x[b] is first set to the
+// embedding row of the id fed (generate.c:86-88); with nparts > 0, the
+// K-slice partials of the residual GEMM before it are first added to x[b]
+// in slice order (part + (s * B + b) * D).  One CTA per sequence.
 template <typename WT>
 __global__ void __launch_bounds__(kThreads) bd_norm_kernel(const LoopParams<WT> p, BdLists L, int head,
                                                            const float* scale, int embed, float* xn,
-                                                           __nv_bfloat16* xn16) {
+                                                           __nv_bfloat16* xn16, const float* part,
+                                                           int nparts) {
     __shared__ float red[32];
     const int b = blockIdx.x;
     if (b >= p.B || !(head ? L.act_head() : L.act_fwd())[b]) return;
     float* x = p.x + (size_t)b * p.D;
-    if (embed) {
-        const int tok = L.tok()[b];
-        for (int k = threadIdx.x; k < p.D; k += blockDim.x) x[k] = wload1(p.tok_emb + (size_t)tok * p.D + k);
-        __syncthreads();
-    }
     float ss = 0.0f;
-    for (int k = threadIdx.x; k < p.D; k += blockDim.x) ss += x[k] * x[k];
+    for (int k = threadIdx.x; k < p.D; k += blockDim.x) {
+        float v;
+        if (embed) {
+            v = wload1(p.tok_emb + (size_t)L.tok()[b] * p.D + k);
+        } else {
+            v = x[k];
+            float r = 0.0f;
+            for (int s = 0; s < nparts; s++) r += __ldcg(part + ((size_t)s * p.B + b) * p.D + k);
+            v += r;
+        }
+        if (embed || nparts > 0) x[k] = v;
+        ss += v * v;
+    }
     ss = block_sum(ss, red);
     const float inv = 1.0f / sqrtf(ss / (float)p.D + 1e-5f);
     for (int k = threadIdx.x; k < p.D; k += blockDim.x) {
@@ -115,16 +125,164 @@ __device__ inline LoopSmem bd_smem(float* smem_f, int Bcap) {
     return sm;
 }
 
-// Attention of the listed sequences at position t (the token loop's phase).
+// Attention of the listed sequences at position t (generate.c:122-160), one
+// CTA per (sequence, KV head, split of kSplitLen keys): the split's K and V
+// rows (contiguous in the cache) and the queries are staged in shared
+// memory with coalesced 16-byte loads; scores, the split's softmax
+// statistics and P.V follow, and the last split of a (sequence, KV head) to
+// finish merges the partial states (flash-decoding).  Small CTAs let
+// several units per SM overlap their loads with math.
+constexpr int kBdAttThreads = 128;
+
+// [flag | pad] then K, V [kSplitLen][hd], q [G][hd], scores [G][kSplitLen],
+// row sums [G]
+__host__ __device__ inline size_t bd_att_smem(int G, int hd) {
+    return 16 + ((size_t)2 * kSplitLen * hd + (size_t)G * hd + (size_t)G * kSplitLen + G) * 4;
+}
+
 template <typename WT>
-__global__ void __launch_bounds__(kThreads, 1) bd_att_kernel(const LoopParams<WT> p, BdLists L, int l) {
+__global__ void __launch_bounds__(kBdAttThreads) bd_att_kernel(const LoopParams<WT> p, BdLists L, int l) {
     extern __shared__ __align__(16) float smem_f[];
-    LoopSmem sm = bd_smem(smem_f, p.Bcap);
     const int nf = L.base[0], t = L.base[2];
-    for (int i = threadIdx.x; i < nf; i += blockDim.x) sm.fwd[i] = L.fwd()[i];
+    const int nkeys = t + 1;
+    const int nsplit = (nkeys + kSplitLen - 1) / kSplitLen;
+    const int u = blockIdx.x;
+    if (u >= nf * p.K * nsplit) return;
+    const int G = p.G, hd = p.hd, q4 = hd / 4;
+    const int s = u % nsplit;
+    const int g = (u / nsplit) % p.K;
+    const int b = L.fwd()[u / (nsplit * p.K)];
+    const int j0 = s * kSplitLen, j1 = min(nkeys, j0 + kSplitLen), n = j1 - j0;
+    const size_t cache_off = (((size_t)l * p.Bcap + b) * p.K + g) * p.cap;
+    const float* kb = p.kc + (cache_off + j0) * hd;
+    const float* vb = p.vc + (cache_off + j0) * hd;
+    int* flag = reinterpret_cast<int*>(smem_f);
+    float* ks = smem_f + 4;                  // 16-byte aligned
+    float* vs = ks + kSplitLen * hd;
+    float* qs = vs + kSplitLen * hd;
+    float* sc = qs + G * hd;
+    float* red = sc + G * kSplitLen;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    constexpr int nwarps = kBdAttThreads / 32;
+    const bool vec = (hd & 3) == 0;          // rows are whole 16-byte units
+    {
+        // every access below stays inside the launch's shared memory, the
+        // cache and the query rows; a failed check records its number in
+        // lists[3] and the CTA returns before touching anything
+        uint32_t dyn = 0;
+        asm volatile("mov.u32 %0, %%dynamic_smem_size;" : "=r"(dyn));
+        int bad = 0;
+        if ((size_t)dyn < bd_att_smem(G, hd)) bad = 1;
+        else if (b < 0 || b >= p.Bcap || g >= p.K || l < 0 || l >= p.L) bad = 2;
+        else if (nkeys > p.cap || n <= 0) bad = 3;
+        else if (vec && ((reinterpret_cast<uintptr_t>(kb) | reinterpret_cast<uintptr_t>(vb)) & 15)) bad = 4;
+        else if (vec && (reinterpret_cast<uintptr_t>(ks) & 15)) bad = 5;
+        else if ((size_t)g * G * hd + (size_t)G * hd > (size_t)p.D) bad = 6;
+        else if (s >= p.max_split) bad = 7;
+        if (bad) {
+            if (threadIdx.x == 0) {
+                atomicMax(L.base + 3, bad);
+                atomicMax(p.status, (int)ST_DEVICE);
+            }
+            return;
+        }
+    }
+    for (int i = threadIdx.x; i < G * hd; i += blockDim.x)
+        qs[i] = ldcg(p.q + (size_t)b * p.D + (size_t)g * G * hd + i);
+    if (vec) {
+#pragma unroll 4
+        for (int e = threadIdx.x; e < n * q4; e += blockDim.x) {
+            reinterpret_cast<float4*>(ks)[e] = ldcg4(kb + 4 * e);
+            reinterpret_cast<float4*>(vs)[e] = ldcg4(vb + 4 * e);
+        }
+    } else {
+        for (int e = threadIdx.x; e < n * hd; e += blockDim.x) {
+            ks[e] = ldcg(kb + e);
+            vs[e] = ldcg(vb + e);
+        }
+    }
     __syncthreads();
-    if (nf == 0) return;
-    phase_att<WT>(p, l, t, sm, nf);
+    const float scale = 1.0f / sqrtf((float)hd);
+    const bool combine = nsplit > 1 || G > 32;
+    // scores: a thread per (head, key); its key row is read starting at
+    // element (j mod hd) so that neighbouring keys fall in different banks
+    for (int e = threadIdx.x; e < G * n; e += blockDim.x) {
+        const int h = e / n, j = e - h * n;
+        const float* kr = ks + j * hd;
+        const float* qh = qs + h * hd;
+        float part = 0.0f;
+        if (vec) {
+            int cc = j % q4;
+#pragma unroll 4
+            for (int c = 0; c < q4; c++) {
+                const float4 k4 = *reinterpret_cast<const float4*>(kr + 4 * cc);
+                const float4 x4 = *reinterpret_cast<const float4*>(qh + 4 * cc);
+                part += x4.x * k4.x + x4.y * k4.y + x4.z * k4.z + x4.w * k4.w;
+                cc = cc + 1 == q4 ? 0 : cc + 1;
+            }
+        } else {
+            int d = j % hd;
+            for (int c = 0; c < hd; c++) {
+                part += qh[d] * kr[d];
+                d = d + 1 == hd ? 0 : d + 1;
+            }
+        }
+        sc[h * kSplitLen + j] = part * scale;
+    }
+    __syncthreads();
+    // the split's softmax statistics per head
+    for (int h = warp; h < G; h += nwarps) {
+        float m = -INFINITY;
+        for (int j = lane; j < n; j += 32) m = fmaxf(m, sc[h * kSplitLen + j]);
+        m = warp_max(m);
+        float lsum = 0.0f;
+        for (int j = lane; j < n; j += 32) {
+            const float e = expf(sc[h * kSplitLen + j] - m);
+            sc[h * kSplitLen + j] = e;
+            lsum += e;
+        }
+        lsum = warp_sum(lsum);
+        if (lane == 0) {
+            const size_t pi = ((size_t)b * p.H + g * G + h) * p.max_split + s;
+            if (combine) { p.part_m[pi] = m; p.part_l[pi] = lsum; }
+            else red[h] = lsum;
+        }
+    }
+    __syncthreads();
+    // P.V
+    for (int i = threadIdx.x; i < G * hd; i += blockDim.x) {
+        const int h = i / hd, d = i - h * hd;
+        float o = 0.0f;
+#pragma unroll 8
+        for (int j = 0; j < n; j++) o += sc[h * kSplitLen + j] * vs[j * hd + d];
+        if (!combine) p.att[(size_t)b * p.D + (g * G + h) * hd + d] = o / red[h];
+        else p.part_o[(((size_t)b * p.H + g * G + h) * p.max_split + s) * hd + d] = o;
+    }
+    if (!combine) return;
+    // the last split to finish merges (flash-decoding reduction)
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        const unsigned prev = atomicAdd(&p.att_cnt[b * p.K + g], 1u);
+        *flag = prev == (unsigned)nsplit - 1;
+    }
+    __syncthreads();
+    if (!*flag) return;
+    __threadfence();
+    for (int i = threadIdx.x; i < G * hd; i += blockDim.x) {
+        const int h = i / hd, d = i - h * hd;
+        const size_t pb = ((size_t)b * p.H + g * G + h) * p.max_split;
+        float M = -INFINITY;
+        for (int s2 = 0; s2 < nsplit; s2++) M = fmaxf(M, ldcg(p.part_m + pb + s2));
+        float num = 0.0f, den = 0.0f;
+        for (int s2 = 0; s2 < nsplit; s2++) {
+            const float w = expf(ldcg(p.part_m + pb + s2) - M);
+            den += w * ldcg(p.part_l + pb + s2);
+            num += w * ldcg(p.part_o + (pb + s2) * hd + d);
+        }
+        p.att[(size_t)b * p.D + (g * G + h) * hd + d] = num / den;
+    }
+    if (threadIdx.x == 0) p.att_cnt[b * p.K + g] = 0u;
 }
 
 // bf16 copy of the attention output of the listed sequences (the A operand

@@ -14,7 +14,13 @@
 //   all 4 warps then drain TMEM with tcgen05.ld (warp w owns lanes
 //              32w..32w+31 = output rows) and apply the epilogue.
 // For SwiGLU the up and gate tiles share the A tile and accumulate into two
-// TMEM column ranges.  Every wait is bounded by the caller's deadline; a
+// TMEM column ranges.
+//
+// Split K (decode GEMMs: a few dozen rows against a whole weight matrix):
+// with ksplit > 1 the grid holds ksplit CTAs per output tile, CTA r
+// accumulating the r-th slice of K and storing its partial tile with plain
+// stores to C + r * M * ldc (EPI_PART); the kernel that next reads the
+// result sums the partials in slice order.  Every wait is bounded by the caller's deadline; a
 // wait that expires sets the status word, stops the pipeline, drains the
 // copies in flight and still frees TMEM.
 //
@@ -39,6 +45,7 @@ constexpr int TC_GROUP_M = 8;               // tile rows per rasterization group
 constexpr uint32_t TC_TILE = TC_BM * TC_BKB;   // 16 KB: A tile; a B tile is BN x 128 B
 enum TcKind { TC_TF32 = 0, TC_BF16 = 1 };
 constexpr int TCE_STORE = EPI_STORE;        // plain C = A.B^T
+constexpr int EPI_PART = 4;                 // partial tile of K slice r at C + r * M * ldc
 
 struct TcArgs {
     int M, N, K;               // problem
@@ -52,6 +59,7 @@ struct TcArgs {
     const int* tpos;
     int* status;
     unsigned long long timeout_ns;
+    int ksplit;                // CTAs splitting K per tile (<= 1: no split; EPI_PART only)
 };
 
 // Dynamic shared memory of a launch with `btiles` B tiles of `bn` rows per
@@ -145,10 +153,10 @@ __device__ __forceinline__ void tc_tmem_wait_ld() {
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
-// Epilogue of 32 consecutive columns [n, n + 32) of row m (m < M).
-template <int EPI>
-__device__ __forceinline__ void tc_epilogue(const TcArgs& g, int m, int n, const float (&u)[32],
-                                            const float (&gt)[32]) {
+// Epilogue of W consecutive columns [n, n + W) of row m (m < M; n, W even).
+template <int EPI, int W>
+__device__ __forceinline__ void tc_epilogue(const TcArgs& g, int m, int n, const float (&u)[W],
+                                            const float (&gt)[W], int split) {
     if (g.act && !g.act[m]) return;
     if constexpr (EPI == EPI_QKV) {
         const PrefillArgs& a = g.pa;
@@ -160,7 +168,7 @@ __device__ __forceinline__ void tc_epilogue(const TcArgs& g, int m, int n, const
             pf_row(a, m, b, t);
         }
 #pragma unroll
-        for (int j = 0; j < 32; j += 2) {
+        for (int j = 0; j < W; j += 2) {
             const int c = n + j;                 // even: c, c + 1 are a RoPE pair
             if (c >= g.N) break;
             float v0 = u[j], v1 = u[j + 1];
@@ -183,10 +191,17 @@ __device__ __forceinline__ void tc_epilogue(const TcArgs& g, int m, int n, const
                 dst[1] = v1;
             }
         }
+    } else if constexpr (EPI == EPI_PART) {
+        float* crow = g.C + ((size_t)split * g.M + m) * g.ldc;
+#pragma unroll
+        for (int j = 0; j < W; j++) {
+            if (n + j >= g.N) break;
+            crow[n + j] = u[j];
+        }
     } else {
         float* crow = g.C + (size_t)m * g.ldc;
 #pragma unroll
-        for (int j = 0; j < 32; j++) {
+        for (int j = 0; j < W; j++) {
             const int c = n + j;
             if (c >= g.N) break;
             if constexpr (EPI == EPI_RESID) {
@@ -220,18 +235,23 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     unsigned long long* done = empty + TC_STAGES;
     volatile int* ctl = reinterpret_cast<volatile int*>(done + 1);   // 0 tmem, 1 error, 2 issued, 3 consumed
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int ks = g.ksplit > 1 ? g.ksplit : 1;
+    const int split = blockIdx.x % ks;                     // slice of K
     // tiles in groups of TC_GROUP_M tile rows, column-major inside a group,
     // so that the CTAs resident at one time share their A and B tiles in L2
     int m0, n0;
     {
         const int tiles_m = (g.M + TC_BM - 1) / TC_BM, tiles_n = (g.N + BN - 1) / BN;
-        const int t = blockIdx.x, per_group = TC_GROUP_M * tiles_n;
+        const int t = blockIdx.x / ks, per_group = TC_GROUP_M * tiles_n;
         const int first = (t / per_group) * TC_GROUP_M, rows = min(tiles_m - first, TC_GROUP_M);
         const int r = t % per_group;
         m0 = (first + r % rows) * TC_BM;
         n0 = (r / rows) * BN;
     }
-    const int nk = (g.K + BKE - 1) / BKE;
+    const int nk_all = (g.K + BKE - 1) / BKE;
+    // this CTA's K blocks [kb0, kb0 + nk); non-empty while ksplit <= nk_all
+    const int kb0 = (int)((long long)split * nk_all / ks);
+    const int nk = (int)((long long)(split + 1) * nk_all / ks) - kb0;
 
     // the ring and the control words must lie inside the dynamic shared
     // memory this launch received; nothing is touched otherwise
@@ -291,9 +311,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             const uint32_t st = smem_addr(base + (size_t)s * STAGE);
             mbar_expect_tx(&full[s], STAGE);
             const uint32_t fb = smem_addr(&full[s]);
-            tc_tma_2d(st, &tmA, kb * BKE, m0, fb);
-            tc_tma_3d(st + TC_TILE, &tmB, kb * BKE, n0, g.layer, fb);
-            if constexpr (DUAL == 2) tc_tma_3d(st + TC_TILE + BTILE, &tmB2, kb * BKE, n0, g.layer, fb);
+            const int kx = (kb0 + kb) * BKE;
+            tc_tma_2d(st, &tmA, kx, m0, fb);
+            tc_tma_3d(st + TC_TILE, &tmB, kx, n0, g.layer, fb);
+            if constexpr (DUAL == 2) tc_tma_3d(st + TC_TILE + BTILE, &tmB2, kx, n0, g.layer, fb);
             issued++;
         }
         ctl[2] = issued;
@@ -341,7 +362,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         tc_tmem_ld32(trow + c0, u);
         if constexpr (DUAL == 2) tc_tmem_ld32(trow + BN + c0, gt);
         tc_tmem_wait_ld();
-        if (row < g.M) tc_epilogue<EPI>(g, row, n0 + c0, u, gt);
+        if (row < g.M) tc_epilogue<EPI, 32>(g, row, n0 + c0, u, gt, split);
     }
     // ---- drain copies still in flight (only after a failed wait), free TMEM
     if (threadIdx.x == 0)

@@ -126,6 +126,7 @@ struct mc_session {
     bool bd_maps_ok;
     CUtensorMap bd_map[3];        // A operands: xn, att, f ([Bcap] rows)
     CUtensorMap bd_wmap[6];       // B operands as 64-row boxes (more CTAs for skinny GEMMs)
+    float* bd_part;               // [kMaxKSplit][Bcap][D] K-slice partials of the residual GEMMs
     float* pf_logits;             // [pf_rows][V] lm_head scratch of mc_model_forward
     __nv_bfloat16 *pf_xn16, *pf_att16, *pf_f16;   // bf16 GEMM inputs (tensor cores, bf16 weights)
     cudaEvent_t ev_mid;           // end of prefill
@@ -478,7 +479,7 @@ mc_status mc_session_destroy(mc_session* s) {
                     s->xfin, s->hgen, s->hsync, s->hpv, s->hpi,
                     s->pf_x, s->pf_xn, s->pf_q, s->pf_att, s->pf_f, s->pf_logits,
                     s->pf_xn16, s->pf_att16, s->pf_f16, s->bd_lists, s->bd_xn,
-                    s->bd_xn16, s->bd_att16, s->bd_f16};
+                    s->bd_xn16, s->bd_att16, s->bd_f16, s->bd_part};
     for (void* b : bufs) cudaFree(b);
     if (s->ev_mid) cudaEventDestroy(s->ev_mid);
     if (s->ev0) cudaEventDestroy(s->ev0);
@@ -764,8 +765,22 @@ cudaError_t tc_launch(const CUtensorMap& a, const CUtensorMap& b, const CUtensor
         attr_set |= 1ull << dev;
     }
     const unsigned tiles = (unsigned)((g.N + BN - 1) / BN) * (unsigned)((g.M + mc::TC_BM - 1) / mc::TC_BM);
-    mc::tc_gemm_kernel<KIND, EPI, BN><<<tiles, mc::TC_THREADS, smem, st>>>(a, b, b2, g);
+    // split K only for partial-tile launches: ksplit CTAs per tile
+    const unsigned ks = g.ksplit > 1 ? (unsigned)g.ksplit : 1u;
+    if (ks > 1 && EPI != mc::EPI_PART) return cudaErrorInvalidValue;
+    mc::tc_gemm_kernel<KIND, EPI, BN><<<tiles * ks, mc::TC_THREADS, smem, st>>>(a, b, b2, g);
     return cudaGetLastError();
+}
+
+// CTAs splitting K for a decode GEMM of `tiles` output tiles and nk K
+// blocks: about one CTA per SM in all, at most 8 partials per element and
+// at least one K block each.
+constexpr int kMaxKSplit = 8;
+int tc_ksplit(int tiles, int nk, int sms) {
+    int ks = sms / std::max(tiles, 1);
+    ks = std::min(ks, kMaxKSplit);
+    ks = std::min(ks, nk);
+    return std::max(ks, 1);
 }
 
 // Tensor maps of the weight matrices: fp32 operands (kind::tf32) for fp32
@@ -985,7 +1000,8 @@ mc_status run_batched(mc_session* s, mc::LoopParams<WT>& p) {
     const size_t Bc = s->Bcap, D = m->D, F = m->F;
     if (!s->bd_lists) {
         bool ok = cudaMalloc(&s->bd_lists, mc::bd_lists_ints(s->Bcap) * 4) == cudaSuccess &&
-                  cudaMalloc(&s->bd_xn, Bc * D * 4) == cudaSuccess;
+                  cudaMalloc(&s->bd_xn, Bc * D * 4) == cudaSuccess &&
+                  cudaMalloc(&s->bd_part, (size_t)kMaxKSplit * Bc * D * 4) == cudaSuccess;
         if (ok && kB16)
             ok = cudaMalloc(&s->bd_xn16, Bc * D * 2) == cudaSuccess &&
                  cudaMalloc(&s->bd_att16, Bc * D * 2) == cudaSuccess &&
@@ -1042,39 +1058,59 @@ mc_status run_batched(mc_session* s, mc::LoopParams<WT>& p) {
     const CUtensorMap* am = s->bd_map;
     const CUtensorMap* wm = s->bd_wmap;
     const float* rmsf = m->norms + 2 * (size_t)m->L * m->D;
-    // the attention kernel needs only its lists and the attention phase region,
-    // so several CTAs share an SM
-    const size_t att_smem = mc::loop_fixed_bytes(s->Bcap) + mc::att_phase_bytes(m->H / m->K, m->hd);
+    const size_t att_smem = mc::bd_att_smem(m->H / m->K, m->hd);
+    int ks_proj, ks_down;
+    {
+        int dev = 0, optin = 0, sms = 0;
+        MC_CUDA(cudaGetDevice(&dev));
+        MC_CUDA(cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev));
+        MC_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+        const int bke = mc::TC_BKB / (kB16 ? 2 : 4), tm = (p.B + mc::TC_BM - 1) / mc::TC_BM;
+        auto tiles = [&](int n) { return tm * ((n + 63) / 64); };
+        ks_proj = tc_ksplit(tiles(m->D), (m->D + bke - 1) / bke, sms);
+        ks_down = tc_ksplit(tiles(m->D), (m->F + bke - 1) / bke, sms);
+        if (att_smem > (size_t)optin)
+            return fail(MC_ERR_UNSUPPORTED, "batched attention needs %zu B of shared memory", att_smem);
+        MC_CUDA(cudaFuncSetAttribute(mc::bd_att_kernel<WT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)att_smem));
+    }
     int launches = 0;
+    MC_CUDA(cudaMemsetAsync(s->bd_lists + 3, 0, 4, st));
     mc::bd_prologue_kernel<WT><<<s->grid, mc::kThreads, 0, st>>>(p);
     launches++;
     cudaError_t e = cudaSuccess;
     for (int t = p.t0; t < p.T && e == cudaSuccess; t++) {
         mc::bd_lists_kernel<WT><<<1, 1024, 0, st>>>(p, L, t == p.t0);
+        // units of the attention launches: the device's position is t too
+        const unsigned att_units = (unsigned)p.B * m->K * ((t + mc::kSplitLen) / mc::kSplitLen);
+        // the residual GEMMs (proj, down) leave K-slice partials in bd_part;
+        // the norm that follows adds them to x in slice order
         for (int l = 0; l < m->L; l++) {
             mc::bd_norm_kernel<WT><<<p.B, mc::kThreads, 0, st>>>(p, L, 0, m->norms + (size_t)l * D, l == 0,
-                                                                  s->bd_xn, kB16 ? s->bd_xn16 : nullptr);
+                                                                  s->bd_xn, kB16 ? s->bd_xn16 : nullptr,
+                                                                  s->bd_part, l == 0 ? 0 : ks_down);
             g.layer = l;
-            g.N = m->Q; g.K = m->D; g.C = nullptr; g.ldc = 0;
+            g.N = m->Q; g.K = m->D; g.C = nullptr; g.ldc = 0; g.ksplit = 1;
             if ((e = tc_launch<KD, mc::EPI_QKV, 64>(am[0], wm[0], wm[0], g, st)) != cudaSuccess) break;
-            mc::bd_att_kernel<WT><<<4 * s->grid, mc::kThreads, att_smem, st>>>(p, L, l);
+            mc::bd_att_kernel<WT><<<att_units, mc::kBdAttThreads, att_smem, st>>>(p, L, l);
             if (kB16) mc::bd_cvt_kernel<WT><<<p.B, mc::kThreads, 0, st>>>(p, L, s->bd_att16);
-            g.N = m->D; g.K = m->D; g.C = s->x; g.ldc = m->D;
-            if ((e = tc_launch<KD, mc::EPI_RESID, 64>(am[1], wm[1], wm[1], g, st)) != cudaSuccess) break;
+            g.N = m->D; g.K = m->D; g.C = s->bd_part; g.ldc = m->D; g.ksplit = ks_proj;
+            if ((e = tc_launch<KD, mc::EPI_PART, 64>(am[1], wm[1], wm[1], g, st)) != cudaSuccess) break;
             mc::bd_norm_kernel<WT><<<p.B, mc::kThreads, 0, st>>>(p, L, 0, m->norms + ((size_t)m->L + l) * D, 0,
-                                                                  s->bd_xn, kB16 ? s->bd_xn16 : nullptr);
-            g.N = m->F; g.K = m->D; g.C = s->f; g.ldc = m->F;
+                                                                  s->bd_xn, kB16 ? s->bd_xn16 : nullptr,
+                                                                  s->bd_part, ks_proj);
+            g.N = m->F; g.K = m->D; g.C = s->f; g.ldc = m->F; g.ksplit = 1;
             if ((e = tc_launch<KD, mc::EPI_SWIGLU, 64>(am[0], wm[2], wm[3], g, st)) != cudaSuccess) break;
-            g.N = m->D; g.K = m->F; g.C = s->x; g.ldc = m->D;
-            if ((e = tc_launch<KD, mc::EPI_RESID, 64>(am[2], wm[4], wm[4], g, st)) != cudaSuccess) break;
+            g.N = m->D; g.K = m->F; g.C = s->bd_part; g.ldc = m->D; g.ksplit = ks_down;
+            if ((e = tc_launch<KD, mc::EPI_PART, 64>(am[2], wm[4], wm[4], g, st)) != cudaSuccess) break;
             launches += kB16 ? 8 : 7;
         }
         if (e != cudaSuccess) break;
         mc::bd_norm_kernel<WT><<<p.B, mc::kThreads, 0, st>>>(p, L, 1, rmsf, 0, s->bd_xn,
-                                                              kB16 ? s->bd_xn16 : nullptr);
+                                                              kB16 ? s->bd_xn16 : nullptr, s->bd_part, ks_down);
         mc::TcArgs gh = g;
         gh.act = nullptr;
-        gh.N = m->V; gh.K = m->D; gh.C = s->logits; gh.ldc = m->V; gh.layer = 0;
+        gh.N = m->V; gh.K = m->D; gh.C = s->logits; gh.ldc = m->V; gh.layer = 0; gh.ksplit = 1;
         if ((e = tc_launch<KD, mc::TCE_STORE, 64>(am[0], wm[5], wm[5], gh, st)) != cudaSuccess) break;
         mc::bd_head_kernel<WT><<<s->grid, mc::kThreads, 0, st>>>(p, L);
         mc::bd_sample_kernel<WT><<<s->grid, mc::kThreads, s->smem, st>>>(p, L);
@@ -1090,7 +1126,11 @@ mc_status run_batched(mc_session* s, mc::LoopParams<WT>& p) {
     MC_CUDA(cudaStreamSynchronize(st));
     MC_CUDA(cudaEventElapsedTime(&s->last_ms, s->ev0, s->ev1));
     if (status == mc::ST_TIMEOUT) return fail(MC_ERR_TIMEOUT, "batched decode: a pipeline wait passed its deadline");
-    if (status != 0) return fail(MC_ERR_DEVICE, "batched decode reported status %d", status);
+    if (status != 0) {
+        int check = 0;
+        MC_CUDA(cudaMemcpy(&check, s->bd_lists + 3, 4, cudaMemcpyDeviceToHost));
+        return fail(MC_ERR_DEVICE, "batched decode reported status %d (check %d)", status, check);
+    }
     return MC_OK;
 }
 
