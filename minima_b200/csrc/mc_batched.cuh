@@ -125,43 +125,58 @@ __device__ inline LoopSmem bd_smem(float* smem_f, int Bcap) {
     return sm;
 }
 
-// Attention of the listed sequences at position t (generate.c:122-160), one
-// CTA per (sequence, KV head, split of kSplitLen keys): the split's K and V
-// rows (contiguous in the cache) and the queries are staged in shared
-// memory with coalesced 16-byte loads; scores, the split's softmax
-// statistics and P.V follow, and the last split of a (sequence, KV head) to
-// finish merges the partial states (flash-decoding).  Small CTAs let
-// several units per SM overlap their loads with math.
+// Attention of the running sequences at position t (generate.c:122-160).
+// One CTA per (sequence, KV head, key split) — a split is klen keys, and a
+// (sequence, KV head) has one split unless there are too few pairs to fill
+// the GPU.  The split's keys stream through shared memory in tiles of
+// kBdTile rows, double-buffered with cp.async (the next tile's K and V rows
+// are in flight while this one is scored), and each of the G query heads
+// keeps an online softmax (running max, sum and P.V rows).  With several
+// splits the last one to finish merges the partial states (flash-decoding).
+// The unit comes from blockIdx directly; sequences that do not run at t
+// return before writing anything.
 constexpr int kBdAttThreads = 128;
+constexpr int kBdTile = 64;                  // keys per shared-memory tile
+constexpr int kBdAttMaxO = 4;                // P.V outputs per thread (G * hd <= 512)
 
-// [flag | pad] then K, V [kSplitLen][hd], q [G][hd], scores [G][kSplitLen],
-// row sums [G]
+// [flag, pad x3] then K, V [2][kBdTile][hd], q [G][hd], probabilities
+// [G][kBdTile], running max / sum / rescale [G] each
 __host__ __device__ inline size_t bd_att_smem(int G, int hd) {
-    return 16 + ((size_t)2 * kSplitLen * hd + (size_t)G * hd + (size_t)G * kSplitLen + G) * 4;
+    return 16 + ((size_t)4 * kBdTile * hd + (size_t)G * hd + (size_t)G * kBdTile + 3 * (size_t)G) * 4;
 }
 
+__device__ __forceinline__ void cp_async16(void* dst, const void* src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(smem_addr(dst)), "l"(src) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
 template <typename WT>
-__global__ void __launch_bounds__(kBdAttThreads) bd_att_kernel(const LoopParams<WT> p, BdLists L, int l) {
+__global__ void __launch_bounds__(kBdAttThreads) bd_att_kernel(const LoopParams<WT> p, BdLists L, int l, int t,
+                                                               int klen) {
     extern __shared__ __align__(16) float smem_f[];
-    const int nf = L.base[0], t = L.base[2];
     const int nkeys = t + 1;
-    const int nsplit = (nkeys + kSplitLen - 1) / kSplitLen;
+    const int nsplit = (nkeys + klen - 1) / klen;
     const int u = blockIdx.x;
-    if (u >= nf * p.K * nsplit) return;
     const int G = p.G, hd = p.hd, q4 = hd / 4;
     const int s = u % nsplit;
     const int g = (u / nsplit) % p.K;
-    const int b = L.fwd()[u / (nsplit * p.K)];
-    const int j0 = s * kSplitLen, j1 = min(nkeys, j0 + kSplitLen), n = j1 - j0;
+    const int b = u / (nsplit * p.K);
+    if (b >= p.B) return;
+    const int j0 = s * klen, j1 = min(nkeys, j0 + klen);
+    const int ntiles = (j1 - j0 + kBdTile - 1) / kBdTile;
     const size_t cache_off = (((size_t)l * p.Bcap + b) * p.K + g) * p.cap;
     const float* kb = p.kc + (cache_off + j0) * hd;
     const float* vb = p.vc + (cache_off + j0) * hd;
     int* flag = reinterpret_cast<int*>(smem_f);
-    float* ks = smem_f + 4;                  // 16-byte aligned
-    float* vs = ks + kSplitLen * hd;
-    float* qs = vs + kSplitLen * hd;
+    float* kt = smem_f + 4;                  // [2][kBdTile][hd], 16-byte aligned
+    float* vt = kt + 2 * kBdTile * hd;
+    float* qs = vt + 2 * kBdTile * hd;
     float* sc = qs + G * hd;
-    float* red = sc + G * kSplitLen;
+    float* rm = sc + G * kBdTile;            // running max
+    float* rl = rm + G;                      // running sum
+    float* ra = rl + G;                      // rescale of this tile
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     constexpr int nwarps = kBdAttThreads / 32;
     const bool vec = (hd & 3) == 0;          // rows are whole 16-byte units
@@ -173,11 +188,11 @@ __global__ void __launch_bounds__(kBdAttThreads) bd_att_kernel(const LoopParams<
         asm volatile("mov.u32 %0, %%dynamic_smem_size;" : "=r"(dyn));
         int bad = 0;
         if ((size_t)dyn < bd_att_smem(G, hd)) bad = 1;
-        else if (b < 0 || b >= p.Bcap || g >= p.K || l < 0 || l >= p.L) bad = 2;
-        else if (nkeys > p.cap || n <= 0) bad = 3;
+        else if (b >= p.Bcap || l < 0 || l >= p.L) bad = 2;
+        else if (nkeys > p.cap || j1 <= j0) bad = 3;
         else if (vec && ((reinterpret_cast<uintptr_t>(kb) | reinterpret_cast<uintptr_t>(vb)) & 15)) bad = 4;
-        else if (vec && (reinterpret_cast<uintptr_t>(ks) & 15)) bad = 5;
-        else if ((size_t)g * G * hd + (size_t)G * hd > (size_t)p.D) bad = 6;
+        else if (G * hd > kBdAttMaxO * kBdAttThreads || G > kBdAttThreads || (size_t)p.K * G * hd > (size_t)p.D)
+            bad = 6;
         else if (s >= p.max_split) bad = 7;
         if (bad) {
             if (threadIdx.x == 0) {
@@ -187,78 +202,129 @@ __global__ void __launch_bounds__(kBdAttThreads) bd_att_kernel(const LoopParams<
             return;
         }
     }
-    for (int i = threadIdx.x; i < G * hd; i += blockDim.x)
-        qs[i] = ldcg(p.q + (size_t)b * p.D + (size_t)g * G * hd + i);
-    if (vec) {
-#pragma unroll 4
-        for (int e = threadIdx.x; e < n * q4; e += blockDim.x) {
-            reinterpret_cast<float4*>(ks)[e] = ldcg4(kb + 4 * e);
-            reinterpret_cast<float4*>(vs)[e] = ldcg4(vb + 4 * e);
-        }
-    } else {
-        for (int e = threadIdx.x; e < n * hd; e += blockDim.x) {
-            ks[e] = ldcg(kb + e);
-            vs[e] = ldcg(vb + e);
-        }
-    }
-    __syncthreads();
-    const float scale = 1.0f / sqrtf((float)hd);
-    const bool combine = nsplit > 1 || G > 32;
-    // scores: a thread per (head, key); its key row is read starting at
-    // element (j mod hd) so that neighbouring keys fall in different banks
-    for (int e = threadIdx.x; e < G * n; e += blockDim.x) {
-        const int h = e / n, j = e - h * n;
-        const float* kr = ks + j * hd;
-        const float* qh = qs + h * hd;
-        float part = 0.0f;
+    // tile i of this split -> buffer i & 1
+    auto load_tile = [&](int i) {
+        const int k0 = i * kBdTile, nt = min(kBdTile, j1 - j0 - k0);
+        float* kd = kt + (i & 1) * kBdTile * hd;
+        float* vd = vt + (i & 1) * kBdTile * hd;
         if (vec) {
-            int cc = j % q4;
-#pragma unroll 4
-            for (int c = 0; c < q4; c++) {
-                const float4 k4 = *reinterpret_cast<const float4*>(kr + 4 * cc);
-                const float4 x4 = *reinterpret_cast<const float4*>(qh + 4 * cc);
-                part += x4.x * k4.x + x4.y * k4.y + x4.z * k4.z + x4.w * k4.w;
-                cc = cc + 1 == q4 ? 0 : cc + 1;
+            for (int e = threadIdx.x; e < nt * q4; e += blockDim.x) {
+                cp_async16(kd + 4 * e, kb + (size_t)k0 * hd + 4 * e);
+                cp_async16(vd + 4 * e, vb + (size_t)k0 * hd + 4 * e);
             }
         } else {
-            int d = j % hd;
-            for (int c = 0; c < hd; c++) {
-                part += qh[d] * kr[d];
-                d = d + 1 == hd ? 0 : d + 1;
+            for (int e = threadIdx.x; e < nt * hd; e += blockDim.x) {
+                kd[e] = ldcg(kb + (size_t)k0 * hd + e);
+                vd[e] = ldcg(vb + (size_t)k0 * hd + e);
             }
         }
-        sc[h * kSplitLen + j] = part * scale;
+        cp_async_commit();
+    };
+    load_tile(0);
+    const int active = L.act_fwd()[b];       // in flight with the first tile
+    for (int i = threadIdx.x; i < G * hd; i += blockDim.x)
+        qs[i] = ldcg(p.q + (size_t)b * p.D + (size_t)g * G * hd + i);
+    if (threadIdx.x < G) {
+        rm[threadIdx.x] = -INFINITY;
+        rl[threadIdx.x] = 0.0f;
     }
-    __syncthreads();
-    // the split's softmax statistics per head
-    for (int h = warp; h < G; h += nwarps) {
-        float m = -INFINITY;
-        for (int j = lane; j < n; j += 32) m = fmaxf(m, sc[h * kSplitLen + j]);
-        m = warp_max(m);
-        float lsum = 0.0f;
-        for (int j = lane; j < n; j += 32) {
-            const float e = expf(sc[h * kSplitLen + j] - m);
-            sc[h * kSplitLen + j] = e;
-            lsum += e;
-        }
-        lsum = warp_sum(lsum);
-        if (lane == 0) {
-            const size_t pi = ((size_t)b * p.H + g * G + h) * p.max_split + s;
-            if (combine) { p.part_m[pi] = m; p.part_l[pi] = lsum; }
-            else red[h] = lsum;
-        }
+    if (!active) {                           // block-uniform
+        cp_async_wait<0>();
+        return;
     }
-    __syncthreads();
-    // P.V
-    for (int i = threadIdx.x; i < G * hd; i += blockDim.x) {
-        const int h = i / hd, d = i - h * hd;
-        float o = 0.0f;
+    const float scale = 1.0f / sqrtf((float)hd);
+    float o[kBdAttMaxO];
+#pragma unroll
+    for (int k = 0; k < kBdAttMaxO; k++) o[k] = 0.0f;
+    for (int it = 0; it < ntiles; it++) {
+        if (it + 1 < ntiles) {
+            load_tile(it + 1);
+            cp_async_wait<1>();
+        } else {
+            cp_async_wait<0>();
+        }
+        __syncthreads();                     // tile it (and q, stats) visible to all
+        const int nt = min(kBdTile, j1 - j0 - it * kBdTile);
+        const float* ks = kt + (it & 1) * kBdTile * hd;
+        const float* vs = vt + (it & 1) * kBdTile * hd;
+        // scores: a thread per (head, key); its key row is read starting at
+        // element (j mod hd) so that neighbouring keys fall in different banks
+        for (int e = threadIdx.x; e < G * nt; e += blockDim.x) {
+            const int h = e / nt, j = e - h * nt;
+            const float* kr = ks + j * hd;
+            const float* qh = qs + h * hd;
+            float part = 0.0f;
+            if (vec) {
+                int cc = j % q4;
+#pragma unroll 4
+                for (int c = 0; c < q4; c++) {
+                    const float4 k4 = *reinterpret_cast<const float4*>(kr + 4 * cc);
+                    const float4 x4 = *reinterpret_cast<const float4*>(qh + 4 * cc);
+                    part += x4.x * k4.x + x4.y * k4.y + x4.z * k4.z + x4.w * k4.w;
+                    cc = cc + 1 == q4 ? 0 : cc + 1;
+                }
+            } else {
+                int d = j % hd;
+                for (int c = 0; c < hd; c++) {
+                    part += qh[d] * kr[d];
+                    d = d + 1 == hd ? 0 : d + 1;
+                }
+            }
+            sc[h * kBdTile + j] = part * scale;
+        }
+        __syncthreads();
+        // online softmax per head: new max, rescale of the old state, exps
+        for (int h = warp; h < G; h += nwarps) {
+            float mx = -INFINITY;
+            for (int j = lane; j < nt; j += 32) mx = fmaxf(mx, sc[h * kBdTile + j]);
+            mx = warp_max(mx);
+            const float mold = rm[h], mnew = fmaxf(mold, mx);
+            float lsum = 0.0f;
+            for (int j = lane; j < nt; j += 32) {
+                const float e = expf(sc[h * kBdTile + j] - mnew);
+                sc[h * kBdTile + j] = e;
+                lsum += e;
+            }
+            lsum = warp_sum(lsum);
+            if (lane == 0) {
+                const float a = expf(mold - mnew);
+                ra[h] = a;
+                rl[h] = rl[h] * a + lsum;
+                rm[h] = mnew;
+            }
+        }
+        __syncthreads();
+        // P.V into the running rows
+#pragma unroll
+        for (int k = 0; k < kBdAttMaxO; k++) {
+            const int i = threadIdx.x + k * kBdAttThreads;
+            if (i < G * hd) {
+                const int h = i / hd, d = i - h * hd;
+                const float* ph = sc + h * kBdTile;
+                float acc = 0.0f;
 #pragma unroll 8
-        for (int j = 0; j < n; j++) o += sc[h * kSplitLen + j] * vs[j * hd + d];
-        if (!combine) p.att[(size_t)b * p.D + (g * G + h) * hd + d] = o / red[h];
-        else p.part_o[(((size_t)b * p.H + g * G + h) * p.max_split + s) * hd + d] = o;
+                for (int j = 0; j < nt; j++) acc += ph[j] * vs[j * hd + d];
+                o[k] = o[k] * ra[h] + acc;
+            }
+        }
+        __syncthreads();                     // buffer (it & 1) is refilled next
+    }
+    const bool combine = nsplit > 1;
+#pragma unroll
+    for (int k = 0; k < kBdAttMaxO; k++) {
+        const int i = threadIdx.x + k * kBdAttThreads;
+        if (i < G * hd) {
+            const int h = i / hd, d = i - h * hd;
+            if (!combine) p.att[(size_t)b * p.D + (g * G + h) * hd + d] = o[k] / rl[h];
+            else p.part_o[(((size_t)b * p.H + g * G + h) * p.max_split + s) * hd + d] = o[k];
+        }
     }
     if (!combine) return;
+    if (threadIdx.x < G) {
+        const size_t pi = ((size_t)b * p.H + g * G + threadIdx.x) * p.max_split + s;
+        p.part_m[pi] = rm[threadIdx.x];
+        p.part_l[pi] = rl[threadIdx.x];
+    }
     // the last split to finish merges (flash-decoding reduction)
     __threadfence();
     __syncthreads();

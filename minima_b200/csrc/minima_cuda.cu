@@ -984,7 +984,9 @@ mc_status run_prefill(mc_session* s, int batch, const uint16_t* prompts, int str
 // (bf16: multiples of 8 elements) and the attention phase's limits.
 bool batched_ok(const mc_model* m) {
     const int mult = m->dtype == MC_WEIGHTS_BF16 ? 8 : 4;
-    return m->D % mult == 0 && m->F % mult == 0;
+    const int G = m->H / m->K;
+    return m->D % mult == 0 && m->F % mult == 0 && G * m->hd <= mc::kBdAttMaxO * mc::kBdAttThreads &&
+           G <= mc::kBdAttThreads;
 }
 
 // The token loop as one launch sequence per step with every matrix product
@@ -1059,9 +1061,9 @@ mc_status run_batched(mc_session* s, mc::LoopParams<WT>& p) {
     const CUtensorMap* wm = s->bd_wmap;
     const float* rmsf = m->norms + 2 * (size_t)m->L * m->D;
     const size_t att_smem = mc::bd_att_smem(m->H / m->K, m->hd);
-    int ks_proj, ks_down;
+    int ks_proj, ks_down, sms = 0;
     {
-        int dev = 0, optin = 0, sms = 0;
+        int dev = 0, optin = 0;
         MC_CUDA(cudaGetDevice(&dev));
         MC_CUDA(cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev));
         MC_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
@@ -1081,8 +1083,13 @@ mc_status run_batched(mc_session* s, mc::LoopParams<WT>& p) {
     cudaError_t e = cudaSuccess;
     for (int t = p.t0; t < p.T && e == cudaSuccess; t++) {
         mc::bd_lists_kernel<WT><<<1, 1024, 0, st>>>(p, L, t == p.t0);
-        // units of the attention launches: the device's position is t too
-        const unsigned att_units = (unsigned)p.B * m->K * ((t + mc::kSplitLen) / mc::kSplitLen);
+        // attention units: (sequence, KV head) pairs, each split into
+        // klen-key pieces only when the pairs alone would not fill the GPU
+        // twice over (the device's position is t too)
+        const int pairs = p.B * m->K, nkeys = t + 1;
+        const int want = std::max(1, (2 * sms + pairs - 1) / pairs);
+        const int klen = std::max(mc::kBdTile, (nkeys + want - 1) / want + mc::kBdTile - 1) / mc::kBdTile * mc::kBdTile;
+        const unsigned att_units = (unsigned)pairs * (unsigned)((nkeys + klen - 1) / klen);
         // the residual GEMMs (proj, down) leave K-slice partials in bd_part;
         // the norm that follows adds them to x in slice order
         for (int l = 0; l < m->L; l++) {
@@ -1092,7 +1099,7 @@ mc_status run_batched(mc_session* s, mc::LoopParams<WT>& p) {
             g.layer = l;
             g.N = m->Q; g.K = m->D; g.C = nullptr; g.ldc = 0; g.ksplit = 1;
             if ((e = tc_launch<KD, mc::EPI_QKV, 64>(am[0], wm[0], wm[0], g, st)) != cudaSuccess) break;
-            mc::bd_att_kernel<WT><<<att_units, mc::kBdAttThreads, att_smem, st>>>(p, L, l);
+            mc::bd_att_kernel<WT><<<att_units, mc::kBdAttThreads, att_smem, st>>>(p, L, l, t, klen);
             if (kB16) mc::bd_cvt_kernel<WT><<<p.B, mc::kThreads, 0, st>>>(p, L, s->bd_att16);
             g.N = m->D; g.K = m->D; g.C = s->bd_part; g.ldc = m->D; g.ksplit = ks_proj;
             if ((e = tc_launch<KD, mc::EPI_PART, 64>(am[1], wm[1], wm[1], g, st)) != cudaSuccess) break;
