@@ -78,6 +78,8 @@ __global__ void __launch_bounds__(1024) bd_lists_kernel(const LoopParams<WT> p, 
     }
 }
 
+constexpr int kBdMaxParts = 8;               // K-slice partials of a residual GEMM
+
 // xn[b] = rmsnorm(x[b]) * scale (generate.c:57-63) for the listed sequences,
 // plus a bf16 copy when xn16 is set.  With embed, x[b] is first set to the
 // embedding row of the id fed (generate.c:86-88); with nparts > 0, the
@@ -100,7 +102,9 @@ __global__ void __launch_bounds__(kThreads) bd_norm_kernel(const LoopParams<WT> 
         } else {
             v = x[k];
             float r = 0.0f;
-            for (int s = 0; s < nparts; s++) r += __ldcg(part + ((size_t)s * p.B + b) * p.D + k);
+#pragma unroll
+            for (int s = 0; s < kBdMaxParts; s++)
+                if (s < nparts) r += __ldcg(part + ((size_t)s * p.B + b) * p.D + k);
             v += r;
         }
         if (embed || nparts > 0) x[k] = v;

@@ -5,8 +5,8 @@
 //   C[M][N] = A[M][K] . B[N][K]^T      (A: activations, B: a weight matrix in
 //                                       the reference's [out][in] layout)
 //
-// One CTA per 128 x BN output tile (BN = 128 or 256), 128 threads:
-//   thread 0   issues the TMA loads of a 4-stage ring (A tiles of 128 rows,
+// One CTA per 128 x BN output tile (BN = 64, 128 or 256), 128 threads:
+//   thread 0   issues the TMA loads of a STAGES-deep ring (A tiles of 128 rows,
 //              B tiles of BN rows, 128 bytes of K each, 128-byte swizzle),
 //   thread 32  issues tcgen05.mma (kind::tf32 for fp32 operands, kind::f16
 //              for bf16 operands; M = 128, N = BN, 32 bytes of K per
@@ -39,7 +39,7 @@ namespace mc {
 
 constexpr int TC_BM = 128;                  // output rows per CTA (TMEM lanes)
 constexpr int TC_BKB = 128;                 // bytes of K per stage (one swizzle row)
-constexpr int TC_STAGES = 4;
+constexpr int TC_STAGES = 4;                // ring depth of the prefill / mc_gemm launches
 constexpr int TC_THREADS = 128;
 constexpr int TC_GROUP_M = 8;               // tile rows per rasterization group (L2 reuse)
 constexpr uint32_t TC_TILE = TC_BM * TC_BKB;   // 16 KB: A tile; a B tile is BN x 128 B
@@ -63,10 +63,10 @@ struct TcArgs {
 };
 
 // Dynamic shared memory of a launch with `btiles` B tiles of `bn` rows per
-// stage (1, or 2 for SwiGLU): alignment slack, the ring, barriers and
-// control words.
-__host__ __device__ constexpr size_t tc_smem_bytes(int btiles, int bn) {
-    return 1024 + (size_t)TC_STAGES * (TC_TILE + (size_t)btiles * bn * TC_BKB) + 256;
+// stage (1, or 2 for SwiGLU) and `stages` stages: alignment slack, the
+// ring, barriers and control words.
+__host__ __device__ constexpr size_t tc_smem_bytes(int btiles, int bn, int stages) {
+    return 1024 + (size_t)stages * (TC_TILE + (size_t)btiles * bn * TC_BKB) + 256;
 }
 
 // Shared-memory matrix descriptor of a K-major tile of 8-row groups of
@@ -153,11 +153,11 @@ __device__ __forceinline__ void tc_tmem_wait_ld() {
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
-// Epilogue of W consecutive columns [n, n + W) of row m (m < M; n, W even).
+// Epilogue of W consecutive columns [n, n + W) of row m (m < M; n, W even;
+// in decode mode the caller has checked that row m runs).
 template <int EPI, int W>
 __device__ __forceinline__ void tc_epilogue(const TcArgs& g, int m, int n, const float (&u)[W],
                                             const float (&gt)[W], int split) {
-    if (g.act && !g.act[m]) return;
     if constexpr (EPI == EPI_QKV) {
         const PrefillArgs& a = g.pa;
         int b, t;
@@ -217,7 +217,7 @@ __device__ __forceinline__ void tc_epilogue(const TcArgs& g, int m, int n, const
     }
 }
 
-template <int KIND, int EPI, int BN>
+template <int KIND, int EPI, int BN, int STAGES>
 __global__ void __launch_bounds__(TC_THREADS, 1)
     tc_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                    const __grid_constant__ CUtensorMap tmB2, const TcArgs g) {
@@ -227,12 +227,16 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     constexpr uint32_t BTILE = (uint32_t)BN * TC_BKB;      // bytes of one B tile
     constexpr uint32_t STAGE = TC_TILE + DUAL * BTILE;
     static_assert(DUAL * BN <= 512, "TMEM holds 512 fp32 columns");
+    constexpr int TLD = DUAL * BN + 4;                     // epilogue tile row stride (floats)
+    static_assert((size_t)TC_BM * TLD * 4 <= (size_t)STAGES * STAGE, "epilogue tile fits the ring");
+    static_assert((2 * STAGES + 1) * 8 + 16 <= 256, "barriers and control words fit the tail");
+    static_assert(tc_smem_bytes(DUAL, BN, STAGES) <= 232448, "ring fits 227 KB of shared memory");
     extern __shared__ unsigned char tc_smem_raw[];
     unsigned char* base =
         reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(tc_smem_raw) + 1023) & ~uintptr_t(1023));
-    unsigned long long* full = reinterpret_cast<unsigned long long*>(base + TC_STAGES * STAGE);
-    unsigned long long* empty = full + TC_STAGES;
-    unsigned long long* done = empty + TC_STAGES;
+    unsigned long long* full = reinterpret_cast<unsigned long long*>(base + STAGES * STAGE);
+    unsigned long long* empty = full + STAGES;
+    unsigned long long* done = empty + STAGES;
     volatile int* ctl = reinterpret_cast<volatile int*>(done + 1);   // 0 tmem, 1 error, 2 issued, 3 consumed
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int ks = g.ksplit > 1 ? g.ksplit : 1;
@@ -264,7 +268,12 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     }
 
     if (threadIdx.x == 0) {
-        for (int s = 0; s < TC_STAGES; s++) {
+        // descriptors into the TMA unit's cache while the prologue runs
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmA)) : "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmB)) : "memory");
+        if constexpr (DUAL == 2)
+            asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmB2)) : "memory");
+        for (int s = 0; s < STAGES; s++) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], 1);
         }
@@ -300,9 +309,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         // ---- producer: TMA ring
         int issued = 0;
         for (int kb = 0; kb < nk; kb++) {
-            const int s = kb % TC_STAGES;
-            if (kb >= TC_STAGES &&
-                !mbar_wait(&empty[s], (uint32_t)((kb / TC_STAGES) - 1) & 1u, g.timeout_ns)) {
+            const int s = kb % STAGES;
+            if (kb >= STAGES &&
+                !mbar_wait(&empty[s], (uint32_t)((kb / STAGES) - 1) & 1u, g.timeout_ns)) {
                 ctl[1] = 1;
                 atomicMax(g.status, (int)ST_TIMEOUT);
                 break;
@@ -323,8 +332,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         const uint32_t idesc = tc_idesc<KIND, BN>();
         int consumed = 0;
         for (int kb = 0; kb < nk; kb++) {
-            const int s = kb % TC_STAGES;
-            if (!mbar_wait(&full[s], (uint32_t)(kb / TC_STAGES) & 1u, g.timeout_ns)) {
+            const int s = kb % STAGES;
+            if (!mbar_wait(&full[s], (uint32_t)(kb / STAGES) & 1u, g.timeout_ns)) {
                 ctl[1] = 1;
                 atomicMax(g.status, (int)ST_TIMEOUT);
                 break;
@@ -353,21 +362,47 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     tc_fence_after();
     // block-uniform decision: tcgen05.ld is warp-collective
     const bool store = __syncthreads_and(finished) && ctl[1] == 0 && nk > 0;
-    const int row = m0 + warp * 32 + lane;
     const uint32_t trow = tmem + ((uint32_t)(warp * 32) << 16);
+    // TMEM -> registers -> the ring, now idle, as a row-major tile (row
+    // stride TLD keeps the float4 writes of 8 consecutive rows in distinct
+    // banks); then a warp per row applies the epilogue to column pairs, so
+    // every global access of a warp covers consecutive addresses
+    float* tile = reinterpret_cast<float*>(base);
+    float* trow_s = tile + (size_t)(warp * 32 + lane) * TLD;
 #pragma unroll 1
-    for (int c0 = 0; c0 < BN; c0 += 32) {
-        if (!store || n0 + c0 >= g.N) break;               // block-uniform
-        float u[32], gt[32] = {};
+    for (int c0 = 0; c0 < DUAL * BN; c0 += 32) {
+        if (!store) break;                                 // block-uniform
+        float u[32];
         tc_tmem_ld32(trow + c0, u);
-        if constexpr (DUAL == 2) tc_tmem_ld32(trow + BN + c0, gt);
         tc_tmem_wait_ld();
-        if (row < g.M) tc_epilogue<EPI, 32>(g, row, n0 + c0, u, gt, split);
+#pragma unroll
+        for (int j = 0; j < 32; j += 4)
+            *reinterpret_cast<float4*>(trow_s + c0 + j) = make_float4(u[j], u[j + 1], u[j + 2], u[j + 3]);
+    }
+    __syncthreads();
+    for (int r = warp; r < TC_BM && store; r += TC_THREADS / 32) {
+        const int m = m0 + r;
+        if (m >= g.M) break;                               // rows ascend: warp-uniform
+        if (g.act && !g.act[m]) continue;
+        const float* src = tile + (size_t)r * TLD;
+#pragma unroll 1
+        for (int c = 2 * lane; c < BN; c += 64) {
+            if (n0 + c >= g.N) break;
+            const float2 uv = *reinterpret_cast<const float2*>(src + c);
+            const float u[2] = {uv.x, uv.y};
+            float gt[2] = {0.0f, 0.0f};
+            if constexpr (DUAL == 2) {
+                const float2 gv = *reinterpret_cast<const float2*>(src + BN + c);
+                gt[0] = gv.x;
+                gt[1] = gv.y;
+            }
+            tc_epilogue<EPI, 2>(g, m, n0 + c, u, gt, split);
+        }
     }
     // ---- drain copies still in flight (only after a failed wait), free TMEM
     if (threadIdx.x == 0)
         for (int kb = ctl[3]; kb < ctl[2]; kb++)
-            if (!mbar_wait(&full[kb % TC_STAGES], (uint32_t)(kb / TC_STAGES) & 1u, g.timeout_ns)) break;
+            if (!mbar_wait(&full[kb % STAGES], (uint32_t)(kb / STAGES) & 1u, g.timeout_ns)) break;
     tc_fence_before();
     __syncthreads();
     if (warp == 0)

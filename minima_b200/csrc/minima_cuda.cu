@@ -750,16 +750,16 @@ mc_status tc_map(CUtensorMap* map, const void* base, int es, uint64_t inner, uin
 }
 
 // B maps must be built with box_rows == BN.
-template <int KIND, int EPI, int BN = 128>
+template <int KIND, int EPI, int BN = 128, int STAGES = mc::TC_STAGES>
 cudaError_t tc_launch(const CUtensorMap& a, const CUtensorMap& b, const CUtensorMap& b2,
                       const mc::TcArgs& g, cudaStream_t st) {
-    const size_t smem = mc::tc_smem_bytes(EPI == mc::EPI_SWIGLU ? 2 : 1, BN);
+    const size_t smem = mc::tc_smem_bytes(EPI == mc::EPI_SWIGLU ? 2 : 1, BN, STAGES);
     static unsigned long long attr_set = 0;    // one bit per device
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return e;
     if (dev < 64 && !((attr_set >> dev) & 1ull)) {
-        e = cudaFuncSetAttribute(mc::tc_gemm_kernel<KIND, EPI, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        e = cudaFuncSetAttribute(mc::tc_gemm_kernel<KIND, EPI, BN, STAGES>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  (int)smem);
         if (e != cudaSuccess) return e;
         attr_set |= 1ull << dev;
@@ -768,14 +768,14 @@ cudaError_t tc_launch(const CUtensorMap& a, const CUtensorMap& b, const CUtensor
     // split K only for partial-tile launches: ksplit CTAs per tile
     const unsigned ks = g.ksplit > 1 ? (unsigned)g.ksplit : 1u;
     if (ks > 1 && EPI != mc::EPI_PART) return cudaErrorInvalidValue;
-    mc::tc_gemm_kernel<KIND, EPI, BN><<<tiles * ks, mc::TC_THREADS, smem, st>>>(a, b, b2, g);
+    mc::tc_gemm_kernel<KIND, EPI, BN, STAGES><<<tiles * ks, mc::TC_THREADS, smem, st>>>(a, b, b2, g);
     return cudaGetLastError();
 }
 
 // CTAs splitting K for a decode GEMM of `tiles` output tiles and nk K
 // blocks: about one CTA per SM in all, at most 8 partials per element and
 // at least one K block each.
-constexpr int kMaxKSplit = 8;
+constexpr int kMaxKSplit = mc::kBdMaxParts;
 int tc_ksplit(int tiles, int nk, int sms) {
     int ks = sms / std::max(tiles, 1);
     ks = std::min(ks, kMaxKSplit);
@@ -1098,18 +1098,18 @@ mc_status run_batched(mc_session* s, mc::LoopParams<WT>& p) {
                                                                   s->bd_part, l == 0 ? 0 : ks_down);
             g.layer = l;
             g.N = m->Q; g.K = m->D; g.C = nullptr; g.ldc = 0; g.ksplit = 1;
-            if ((e = tc_launch<KD, mc::EPI_QKV, 64>(am[0], wm[0], wm[0], g, st)) != cudaSuccess) break;
+            if ((e = tc_launch<KD, mc::EPI_QKV, 64, 8>(am[0], wm[0], wm[0], g, st)) != cudaSuccess) break;
             mc::bd_att_kernel<WT><<<att_units, mc::kBdAttThreads, att_smem, st>>>(p, L, l, t, klen);
             if (kB16) mc::bd_cvt_kernel<WT><<<p.B, mc::kThreads, 0, st>>>(p, L, s->bd_att16);
             g.N = m->D; g.K = m->D; g.C = s->bd_part; g.ldc = m->D; g.ksplit = ks_proj;
-            if ((e = tc_launch<KD, mc::EPI_PART, 64>(am[1], wm[1], wm[1], g, st)) != cudaSuccess) break;
+            if ((e = tc_launch<KD, mc::EPI_PART, 64, 8>(am[1], wm[1], wm[1], g, st)) != cudaSuccess) break;
             mc::bd_norm_kernel<WT><<<p.B, mc::kThreads, 0, st>>>(p, L, 0, m->norms + ((size_t)m->L + l) * D, 0,
                                                                   s->bd_xn, kB16 ? s->bd_xn16 : nullptr,
                                                                   s->bd_part, ks_proj);
             g.N = m->F; g.K = m->D; g.C = s->f; g.ldc = m->F; g.ksplit = 1;
-            if ((e = tc_launch<KD, mc::EPI_SWIGLU, 64>(am[0], wm[2], wm[3], g, st)) != cudaSuccess) break;
+            if ((e = tc_launch<KD, mc::EPI_SWIGLU, 64, 6>(am[0], wm[2], wm[3], g, st)) != cudaSuccess) break;
             g.N = m->D; g.K = m->F; g.C = s->bd_part; g.ldc = m->D; g.ksplit = ks_down;
-            if ((e = tc_launch<KD, mc::EPI_PART, 64>(am[2], wm[4], wm[4], g, st)) != cudaSuccess) break;
+            if ((e = tc_launch<KD, mc::EPI_PART, 64, 8>(am[2], wm[4], wm[4], g, st)) != cudaSuccess) break;
             launches += kB16 ? 8 : 7;
         }
         if (e != cudaSuccess) break;
@@ -1118,7 +1118,7 @@ mc_status run_batched(mc_session* s, mc::LoopParams<WT>& p) {
         mc::TcArgs gh = g;
         gh.act = nullptr;
         gh.N = m->V; gh.K = m->D; gh.C = s->logits; gh.ldc = m->V; gh.layer = 0; gh.ksplit = 1;
-        if ((e = tc_launch<KD, mc::TCE_STORE, 64>(am[0], wm[5], wm[5], gh, st)) != cudaSuccess) break;
+        if ((e = tc_launch<KD, mc::TCE_STORE, 64, 8>(am[0], wm[5], wm[5], gh, st)) != cudaSuccess) break;
         mc::bd_head_kernel<WT><<<s->grid, mc::kThreads, 0, st>>>(p, L);
         mc::bd_sample_kernel<WT><<<s->grid, mc::kThreads, s->smem, st>>>(p, L);
         launches += 6;
