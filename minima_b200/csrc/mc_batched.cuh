@@ -41,6 +41,8 @@ struct BdLists {
 template <typename WT>
 __global__ void __launch_bounds__(1024) bd_lists_kernel(const LoopParams<WT> p, BdLists L, int first) {
     __shared__ int flag[1024];
+    pdl_wait();
+    pdl_trigger();
     const int t = first ? p.t0 : L.base[2] + 1;
     __syncthreads();                     // every thread has read the previous position
     // a thread per sequence: does it run a forward, does it sample, which id
@@ -78,7 +80,7 @@ __global__ void __launch_bounds__(1024) bd_lists_kernel(const LoopParams<WT> p, 
     }
 }
 
-constexpr int kBdMaxParts = 8;               // K-slice partials of a residual GEMM
+constexpr int kBdMaxParts = 16;              // K-slice partials of a decode GEMM
 
 // xn[b] = rmsnorm(x[b]) * scale (generate.c:57-63) for the listed sequences,
 // plus a bf16 copy when xn16 is set.  With embed, x[b] is first set to the
@@ -91,6 +93,8 @@ __global__ void __launch_bounds__(kThreads) bd_norm_kernel(const LoopParams<WT> 
                                                            __nv_bfloat16* xn16, const float* part,
                                                            int nparts) {
     __shared__ float red[32];
+    pdl_wait();
+    pdl_trigger();
     const int b = blockIdx.x;
     if (b >= p.B || !(head ? L.act_head() : L.act_fwd())[b]) return;
     float* x = p.x + (size_t)b * p.D;
@@ -139,14 +143,21 @@ __device__ inline LoopSmem bd_smem(float* smem_f, int Bcap) {
 // splits the last one to finish merges the partial states (flash-decoding).
 // The unit comes from blockIdx directly; sequences that do not run at t
 // return before writing anything.
+// With nq > 0 the QKV GEMM left nq K-slice partials of each sequence's
+// [q | k | v] row in qkvp (slice r at qkvp + r * B * Q): every unit sums the
+// partials of its queries and rotates them (RoPE, rotary.h:26-40), and the
+// unit holding key t also builds that key's K (rotated) and V rows, appends
+// them to the cache (generate.c:108-120) and places them in its last tile.
 constexpr int kBdAttThreads = 128;
 constexpr int kBdTile = 64;                  // keys per shared-memory tile
 constexpr int kBdAttMaxO = 4;                // P.V outputs per thread (G * hd <= 512)
 
 // [flag, pad x3] then K, V [2][kBdTile][hd], q [G][hd], probabilities
-// [G][kBdTile], running max / sum / rescale [G] each
+// [G][kBdTile], the new K and V rows [hd] each, running max / sum / rescale
+// [G] each
 __host__ __device__ inline size_t bd_att_smem(int G, int hd) {
-    return 16 + ((size_t)4 * kBdTile * hd + (size_t)G * hd + (size_t)G * kBdTile + 3 * (size_t)G) * 4;
+    return 16 + ((size_t)4 * kBdTile * hd + (size_t)G * hd + (size_t)G * kBdTile + 2 * (size_t)hd +
+                 3 * (size_t)G) * 4;
 }
 
 __device__ __forceinline__ void cp_async16(void* dst, const void* src) {
@@ -158,7 +169,7 @@ __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_gr
 
 template <typename WT>
 __global__ void __launch_bounds__(kBdAttThreads) bd_att_kernel(const LoopParams<WT> p, BdLists L, int l, int t,
-                                                               int klen) {
+                                                               int klen, const float* qkvp, int nq) {
     extern __shared__ __align__(16) float smem_f[];
     const int nkeys = t + 1;
     const int nsplit = (nkeys + klen - 1) / klen;
@@ -178,7 +189,9 @@ __global__ void __launch_bounds__(kBdAttThreads) bd_att_kernel(const LoopParams<
     float* vt = kt + 2 * kBdTile * hd;
     float* qs = vt + 2 * kBdTile * hd;
     float* sc = qs + G * hd;
-    float* rm = sc + G * kBdTile;            // running max
+    float* krow = sc + G * kBdTile;          // key t's K and V rows (nq > 0)
+    float* vrow = krow + hd;
+    float* rm = vrow + hd;                   // running max
     float* rl = rm + G;                      // running sum
     float* ra = rl + G;                      // rescale of this tile
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -198,6 +211,7 @@ __global__ void __launch_bounds__(kBdAttThreads) bd_att_kernel(const LoopParams<
         else if (G * hd > kBdAttMaxO * kBdAttThreads || G > kBdAttThreads || (size_t)p.K * G * hd > (size_t)p.D)
             bad = 6;
         else if (s >= p.max_split) bad = 7;
+        else if (nq > kBdMaxParts || (nq > 0 && (t >= p.rope_len || (hd & 1)))) bad = 8;
         if (bad) {
             if (threadIdx.x == 0) {
                 atomicMax(L.base + 3, bad);
@@ -206,9 +220,12 @@ __global__ void __launch_bounds__(kBdAttThreads) bd_att_kernel(const LoopParams<
             return;
         }
     }
+    // key t (the last key of the last split) is built here when nq > 0
+    const bool has_t = nq > 0 && s == nsplit - 1;
     // tile i of this split -> buffer i & 1
     auto load_tile = [&](int i) {
-        const int k0 = i * kBdTile, nt = min(kBdTile, j1 - j0 - k0);
+        const int k0 = i * kBdTile;
+        const int nt = min(kBdTile, j1 - j0 - k0) - (has_t && i == ntiles - 1 ? 1 : 0);
         float* kd = kt + (i & 1) * kBdTile * hd;
         float* vd = vt + (i & 1) * kBdTile * hd;
         if (vec) {
@@ -224,10 +241,57 @@ __global__ void __launch_bounds__(kBdAttThreads) bd_att_kernel(const LoopParams<
         }
         cp_async_commit();
     };
+    // the first tile's rows precede t and were written at earlier steps, so
+    // they are requested before waiting for the previous kernel
     load_tile(0);
-    const int active = L.act_fwd()[b];       // in flight with the first tile
-    for (int i = threadIdx.x; i < G * hd; i += blockDim.x)
-        qs[i] = ldcg(p.q + (size_t)b * p.D + (size_t)g * G * hd + i);
+    pdl_wait();
+    pdl_trigger();
+    const int active = L.act_fwd()[b];
+    const int hp = hd / 2;
+    if (nq > 0) {
+        // q (and key t's rows): sums of the partials in slice order, then RoPE
+        const float* pb = qkvp + (size_t)b * p.Q;
+        const size_t pst = (size_t)p.B * p.Q;
+        const float2* rot = p.rope + (size_t)t * hp;
+        auto gather = [&](int col, float& x0, float& x1) {
+            x0 = 0.0f;
+            x1 = 0.0f;
+#pragma unroll
+            for (int r = 0; r < kBdMaxParts; r++)
+                if (r < nq) {
+                    const float2 v = __ldcg(reinterpret_cast<const float2*>(pb + r * pst + col));
+                    x0 += v.x;
+                    x1 += v.y;
+                }
+        };
+        for (int i = threadIdx.x; i < G * hp; i += blockDim.x) {
+            const int h = i / hp, pr = i - h * hp;
+            float x0, x1;
+            gather((g * G + h) * hd + 2 * pr, x0, x1);
+            const float2 r = rot[pr];
+            qs[h * hd + 2 * pr] = x0 * r.x - x1 * r.y;
+            qs[h * hd + 2 * pr + 1] = x0 * r.y + x1 * r.x;
+        }
+        if (has_t)
+            for (int i = threadIdx.x; i < hd; i += blockDim.x) {
+                const bool isk = i < hp;
+                const int pr = isk ? i : i - hp;
+                float x0, x1;
+                gather((isk ? p.H + g : p.H + p.K + g) * hd + 2 * pr, x0, x1);
+                float* row = isk ? krow : vrow;
+                if (isk) {
+                    const float2 r = rot[pr];
+                    row[2 * pr] = x0 * r.x - x1 * r.y;
+                    row[2 * pr + 1] = x0 * r.y + x1 * r.x;
+                } else {
+                    row[2 * pr] = x0;
+                    row[2 * pr + 1] = x1;
+                }
+            }
+    } else {
+        for (int i = threadIdx.x; i < G * hd; i += blockDim.x)
+            qs[i] = ldcg(p.q + (size_t)b * p.D + (size_t)g * G * hd + i);
+    }
     if (threadIdx.x < G) {
         rm[threadIdx.x] = -INFINITY;
         rl[threadIdx.x] = 0.0f;
@@ -236,6 +300,17 @@ __global__ void __launch_bounds__(kBdAttThreads) bd_att_kernel(const LoopParams<
         cp_async_wait<0>();
         return;
     }
+    // key t's rows into the cache (this thread's own entries)
+    const int tl = (t - j0) - (ntiles - 1) * kBdTile;       // its row in the last tile
+    if (has_t)
+        for (int i = threadIdx.x; i < hd; i += blockDim.x) {
+            const bool isk = i < hp;
+            const int d = 2 * (isk ? i : i - hp);
+            float* dst = (isk ? p.kc : p.vc) + (cache_off + t) * hd + d;
+            const float* row = isk ? krow : vrow;
+            dst[0] = row[d];
+            dst[1] = row[d + 1];
+        }
     const float scale = 1.0f / sqrtf((float)hd);
     float o[kBdAttMaxO];
 #pragma unroll
@@ -246,6 +321,15 @@ __global__ void __launch_bounds__(kBdAttThreads) bd_att_kernel(const LoopParams<
             cp_async_wait<1>();
         } else {
             cp_async_wait<0>();
+            if (has_t)                       // key t's rows (this thread's own entries)
+                for (int i = threadIdx.x; i < hd; i += blockDim.x) {
+                    const bool isk = i < hp;
+                    const int d = 2 * (isk ? i : i - hp);
+                    float* dst = (isk ? kt : vt) + (it & 1) * kBdTile * hd + tl * hd + d;
+                    const float* row = isk ? krow : vrow;
+                    dst[0] = row[d];
+                    dst[1] = row[d + 1];
+                }
         }
         __syncthreads();                     // tile it (and q, stats) visible to all
         const int nt = min(kBdTile, j1 - j0 - it * kBdTile);
@@ -355,10 +439,47 @@ __global__ void __launch_bounds__(kBdAttThreads) bd_att_kernel(const LoopParams<
     if (threadIdx.x == 0) p.att_cnt[b * p.K + g] = 0u;
 }
 
+// f[b] = SiLU(gate) * up (generate.c:165-179) of the running sequences, from
+// the nparts K-slice partials the up/gate GEMM left in part (slice r, row b
+// at part + (r * B + b) * 2F: up in [0, F), gate in [F, 2F)), summed in
+// slice order; plus a bf16 copy when f16 is set (the A operand of a
+// kind::f16 down GEMM).
+template <typename WT>
+__global__ void __launch_bounds__(kThreads) bd_swiglu_kernel(const LoopParams<WT> p, BdLists L, const float* part,
+                                                             int nparts, __nv_bfloat16* f16) {
+    pdl_wait();
+    pdl_trigger();
+    const int F4 = p.F / 4;
+    const size_t pst = (size_t)p.B * 2 * p.F;
+    for (int idx = blockIdx.x * blockDim.x + threadIdx.x; idx < p.B * F4; idx += gridDim.x * blockDim.x) {
+        const int b = idx / F4, c = (idx - b * F4) * 4;
+        if (!L.act_fwd()[b]) continue;
+        const float* pb = part + (size_t)b * 2 * p.F + c;
+        float u[4] = {0.0f, 0.0f, 0.0f, 0.0f}, gt[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+        for (int r = 0; r < kBdMaxParts; r++)
+            if (r < nparts) {
+                const float4 a = __ldcg(reinterpret_cast<const float4*>(pb + r * pst));
+                const float4 z = __ldcg(reinterpret_cast<const float4*>(pb + r * pst + p.F));
+                u[0] += a.x; u[1] += a.y; u[2] += a.z; u[3] += a.w;
+                gt[0] += z.x; gt[1] += z.y; gt[2] += z.z; gt[3] += z.w;
+            }
+        float v[4];
+#pragma unroll
+        for (int j = 0; j < 4; j++) v[j] = (gt[j] / (1.0f + expf(-gt[j]))) * u[j];
+        *reinterpret_cast<float4*>(p.f + (size_t)b * p.F + c) = make_float4(v[0], v[1], v[2], v[3]);
+        if (f16)
+#pragma unroll
+            for (int j = 0; j < 4; j++) f16[(size_t)b * p.F + c + j] = __float2bfloat16_rn(v[j]);
+    }
+}
+
 // bf16 copy of the attention output of the listed sequences (the A operand
 // of a kind::f16 proj GEMM).
 template <typename WT>
 __global__ void __launch_bounds__(kThreads) bd_cvt_kernel(const LoopParams<WT> p, BdLists L, __nv_bfloat16* dst) {
+    pdl_wait();
+    pdl_trigger();
     const int b = blockIdx.x;
     if (b >= p.B || !L.act_fwd()[b]) return;
     for (int k = threadIdx.x; k < p.D; k += blockDim.x)
@@ -370,6 +491,8 @@ __global__ void __launch_bounds__(kThreads) bd_cvt_kernel(const LoopParams<WT> p
 // vocabulary (generate.c:438-460), the partials phase_sample reduces.
 template <typename WT>
 __global__ void __launch_bounds__(kThreads) bd_head_kernel(const LoopParams<WT> p, BdLists L) {
+    pdl_wait();
+    pdl_trigger();
     const int nh = L.base[1];
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int per = (p.V + gridDim.x - 1) / gridDim.x;
@@ -408,6 +531,8 @@ __global__ void __launch_bounds__(kThreads) bd_head_kernel(const LoopParams<WT> 
 template <typename WT>
 __global__ void __launch_bounds__(kThreads, 1) bd_sample_kernel(const LoopParams<WT> p, BdLists L) {
     extern __shared__ __align__(16) float smem_f[];
+    pdl_wait();
+    pdl_trigger();
     LoopSmem sm = bd_smem(smem_f, p.Bcap);
     const int nh = L.base[1], t = L.base[2];
     for (int i = threadIdx.x; i < nh; i += blockDim.x) sm.head[i] = L.head()[i];
@@ -418,6 +543,8 @@ __global__ void __launch_bounds__(kThreads, 1) bd_sample_kernel(const LoopParams
 
 template <typename WT>
 __global__ void __launch_bounds__(kThreads) bd_prologue_kernel(const LoopParams<WT> p) {
+    pdl_wait();
+    pdl_trigger();
     loop_prologue(p);
 }
 

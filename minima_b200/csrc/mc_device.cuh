@@ -15,6 +15,16 @@ namespace mc {
 // Device status word values (mirrors MC_* in minima_cuda.h).
 enum : int { ST_OK = 0, ST_TIMEOUT = 4, ST_DEVICE = 5 };
 
+// Programmatic dependent launch (kernels launched with the programmatic
+// stream serialization attribute): pdl_wait returns once the previous kernel
+// in the stream has completed and its memory operations are visible (at
+// once for an ordinary launch); pdl_trigger lets the next kernel's CTAs be
+// scheduled.  Kernels call pdl_trigger only after pdl_wait, so the next
+// kernel's work before its own pdl_wait overlaps this kernel alone and may
+// read only what the kernels before this one wrote, or constant data.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 __device__ __forceinline__ unsigned long long globaltimer_ns() {
     unsigned long long t;
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));

@@ -46,6 +46,7 @@ constexpr uint32_t TC_TILE = TC_BM * TC_BKB;   // 16 KB: A tile; a B tile is BN 
 enum TcKind { TC_TF32 = 0, TC_BF16 = 1 };
 constexpr int TCE_STORE = EPI_STORE;        // plain C = A.B^T
 constexpr int EPI_PART = 4;                 // partial tile of K slice r at C + r * M * ldc
+constexpr int EPI_PART2 = 5;                // the same for a matrix pair: [0, N) and [N, 2N) of a row
 
 struct TcArgs {
     int M, N, K;               // problem
@@ -191,12 +192,13 @@ __device__ __forceinline__ void tc_epilogue(const TcArgs& g, int m, int n, const
                 dst[1] = v1;
             }
         }
-    } else if constexpr (EPI == EPI_PART) {
+    } else if constexpr (EPI == EPI_PART || EPI == EPI_PART2) {
         float* crow = g.C + ((size_t)split * g.M + m) * g.ldc;
 #pragma unroll
         for (int j = 0; j < W; j++) {
             if (n + j >= g.N) break;
             crow[n + j] = u[j];
+            if constexpr (EPI == EPI_PART2) crow[g.N + n + j] = gt[j];
         }
     } else {
         float* crow = g.C + (size_t)m * g.ldc;
@@ -400,6 +402,212 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         }
     }
     // ---- drain copies still in flight (only after a failed wait), free TMEM
+    if (threadIdx.x == 0)
+        for (int kb = ctl[3]; kb < ctl[2]; kb++)
+            if (!mbar_wait(&full[kb % STAGES], (uint32_t)(kb / STAGES) & 1u, g.timeout_ns)) break;
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0)
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                     "r"(DUAL * BN));
+}
+
+// ---------------------------------------------------------------------------
+// Decode GEMM with the operands swapped: C[M][N] = X[M][K] . W[N][K]^T where
+// M (sequences, at most a few dozen to a few hundred) is small.  The MMA's
+// 128-row operand is a tile of 128 weight rows (output features) and the
+// N = BN operand a tile of BN sequences, so no MMA row is spent on padding
+// and the tensor pipe reads each weight byte once per BN sequences.  The
+// accumulator is feature-major in TMEM (lane = feature, column = sequence);
+// the epilogue turns it sequence-major through shared memory and applies
+// the same per-row epilogues as the prefill kernel.  With ksplit > 1 (only
+// for the partial epilogues) CTA r of a tile accumulates the r-th K slice.
+// For a matrix pair (EPI_PART2: up and gate) two weight tiles share the
+// sequence tile and accumulate into two TMEM column ranges.
+template <int KIND, int EPI, int BN, int STAGES>
+__global__ void __launch_bounds__(TC_THREADS, 1)
+    tc_dec_kernel(const __grid_constant__ CUtensorMap tmX, const __grid_constant__ CUtensorMap tmW,
+                  const __grid_constant__ CUtensorMap tmW2, const TcArgs g) {
+    constexpr int DUAL = EPI == EPI_PART2 ? 2 : 1;
+    constexpr int ES = KIND == TC_TF32 ? 4 : 2;
+    constexpr int BKE = TC_BKB / ES;                       // K elements per stage
+    constexpr uint32_t XTILE = (uint32_t)BN * TC_BKB;      // bytes of the sequence tile
+    constexpr uint32_t STAGE = DUAL * TC_TILE + XTILE;
+    constexpr int TLD = DUAL * TC_BM + 4;                  // epilogue tile row stride (floats)
+    static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "N of an M = 128 MMA");
+    static_assert(DUAL * BN <= 512 && (DUAL * BN & (DUAL * BN - 1)) == 0 && DUAL * BN >= 32,
+                  "TMEM allocation: a power of two from 32 to 512 columns");
+    static_assert(STAGE % 1024 == 0, "stages stay 1024-byte aligned for the 128-byte swizzle");
+    static_assert((size_t)BN * TLD * 4 <= (size_t)STAGES * STAGE, "epilogue tile fits the ring");
+    static_assert((2 * STAGES + 1) * 8 + 16 <= 256, "barriers and control words fit the tail");
+    static_assert(1024 + (size_t)STAGES * STAGE + 256 <= 232448, "ring fits 227 KB of shared memory");
+    extern __shared__ unsigned char tc_smem_raw[];
+    unsigned char* base =
+        reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(tc_smem_raw) + 1023) & ~uintptr_t(1023));
+    unsigned long long* full = reinterpret_cast<unsigned long long*>(base + STAGES * STAGE);
+    unsigned long long* empty = full + STAGES;
+    unsigned long long* done = empty + STAGES;
+    volatile int* ctl = reinterpret_cast<volatile int*>(done + 1);   // 0 tmem, 1 error, 2 issued, 3 consumed
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int ks = g.ksplit > 1 ? g.ksplit : 1;
+    const int split = blockIdx.x % ks;                     // slice of K
+    const int tiles_f = (g.N + TC_BM - 1) / TC_BM;
+    const int tile = blockIdx.x / ks;
+    const int f0 = (tile % tiles_f) * TC_BM;               // first feature (weight row)
+    const int s0 = (tile / tiles_f) * BN;                  // first sequence
+    const int nk_all = (g.K + BKE - 1) / BKE;
+    const int kb0 = (int)((long long)split * nk_all / ks);
+    const int nk = (int)((long long)(split + 1) * nk_all / ks) - kb0;
+
+    uint32_t dyn = 0;
+    asm volatile("mov.u32 %0, %%dynamic_smem_size;" : "=r"(dyn));
+    const unsigned char* ctl_end = reinterpret_cast<const unsigned char*>(const_cast<int*>(ctl) + 4);
+    if ((size_t)(ctl_end - tc_smem_raw) > dyn || smem_addr(ctl_end) >= (1u << 18)) {
+        if (threadIdx.x == 0) atomicMax(g.status, (int)ST_DEVICE);
+        return;
+    }
+    if (threadIdx.x == 0) {
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmX)) : "memory");
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmW)) : "memory");
+        if constexpr (DUAL == 2)
+            asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&tmW2)) : "memory");
+        for (int st = 0; st < STAGES; st++) {
+            mbar_init(&full[st], 1);
+            mbar_init(&empty[st], 1);
+        }
+        mbar_init(done, 1);
+        ctl[1] = 0;
+        ctl[2] = 0;
+        ctl[3] = 0;
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    }
+    __syncwarp();
+    if (warp == 0) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                         smem_addr((const void*)ctl)),
+                     "r"(DUAL * BN));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = (uint32_t)ctl[0];
+    const bool tmem_ok = (tmem >> 16) == 0 && (tmem & 0xFFFFu) + DUAL * BN <= 512;
+    if (!tmem_ok) {
+        if (threadIdx.x == 0) {
+            ctl[1] = 1;
+            atomicMax(g.status, (int)ST_DEVICE);
+        }
+        __syncthreads();
+        return;
+    }
+
+    // weights are constant: the first ring's worth of weight tiles is
+    // requested before waiting for the kernel that produces X
+    const int pre = min(nk, STAGES);
+    if (threadIdx.x == 0)
+        for (int kb = 0; kb < pre; kb++) {
+            const uint32_t sa = smem_addr(base + (size_t)kb * STAGE);
+            mbar_expect_tx(&full[kb], STAGE);
+            const int kx = (kb0 + kb) * BKE;
+            tc_tma_3d(sa, &tmW, kx, f0, g.layer, smem_addr(&full[kb]));
+            if constexpr (DUAL == 2) tc_tma_3d(sa + TC_TILE, &tmW2, kx, f0, g.layer, smem_addr(&full[kb]));
+        }
+    pdl_wait();
+    pdl_trigger();
+    if (threadIdx.x == 0) {
+        // ---- producer: weight tile(s) and the sequence tile of each K block
+        int issued = 0;
+        for (int kb = 0; kb < nk; kb++) {
+            const int st = kb % STAGES;
+            if (kb >= STAGES &&
+                !mbar_wait(&empty[st], (uint32_t)((kb / STAGES) - 1) & 1u, g.timeout_ns)) {
+                ctl[1] = 1;
+                atomicMax(g.status, (int)ST_TIMEOUT);
+                break;
+            }
+            if (kb >= pre && ctl[1]) break;      // pre-issued stages always get their X tile
+            const uint32_t sa = smem_addr(base + (size_t)st * STAGE);
+            const uint32_t fb = smem_addr(&full[st]);
+            const int kx = (kb0 + kb) * BKE;
+            if (kb >= pre) {
+                mbar_expect_tx(&full[st], STAGE);
+                tc_tma_3d(sa, &tmW, kx, f0, g.layer, fb);
+                if constexpr (DUAL == 2) tc_tma_3d(sa + TC_TILE, &tmW2, kx, f0, g.layer, fb);
+            }
+            tc_tma_2d(sa + DUAL * TC_TILE, &tmX, kx, s0, fb);
+            issued++;
+        }
+        ctl[2] = issued;
+    } else if (threadIdx.x == 32) {
+        // ---- MMA issuer: D[feature][sequence] += W . X^T
+        const uint32_t idesc = tc_idesc<KIND, BN>();
+        int consumed = 0;
+        for (int kb = 0; kb < nk; kb++) {
+            const int st = kb % STAGES;
+            if (!mbar_wait(&full[st], (uint32_t)(kb / STAGES) & 1u, g.timeout_ns)) {
+                ctl[1] = 1;
+                atomicMax(g.status, (int)ST_TIMEOUT);
+                break;
+            }
+            consumed++;
+            tc_fence_after();
+            const uint32_t sa = smem_addr(base + (size_t)st * STAGE);
+#pragma unroll
+            for (int k = 0; k < TC_BKB / 32; k++) {
+                const uint64_t xd = tc_sw128_desc(sa + DUAL * TC_TILE + 32 * k);
+                const uint32_t acc = (kb | k) != 0;
+                tc_mma<KIND>(tmem, tc_sw128_desc(sa + 32 * k), xd, idesc, acc);
+                if constexpr (DUAL == 2)
+                    tc_mma<KIND>(tmem + BN, tc_sw128_desc(sa + TC_TILE + 32 * k), xd, idesc, acc);
+            }
+            tc_commit(smem_addr(&empty[st]));
+        }
+        ctl[3] = consumed;
+        tc_commit(smem_addr(done));
+    }
+    __syncwarp();
+    const bool finished = mbar_wait(done, 0, g.timeout_ns);
+    if (!finished) atomicMax(g.status, (int)ST_TIMEOUT);
+    tc_fence_after();
+    const bool store = __syncthreads_and(finished) && ctl[1] == 0 && nk > 0;
+    // TMEM (lane = feature, column = sequence) -> a sequence-major tile in
+    // the idle ring: a warp's 32 lanes write 32 consecutive features of one
+    // sequence per store, so neither side has bank conflicts
+    const uint32_t tlane = tmem + ((uint32_t)(warp * 32) << 16);
+    float* tilep = reinterpret_cast<float*>(base);
+    const int fl = warp * 32 + lane;
+#pragma unroll 1
+    for (int c0 = 0; c0 < DUAL * BN; c0 += 32) {
+        if (!store) break;                                 // block-uniform
+        float v[32];
+        tc_tmem_ld32(tlane + c0, v);
+        tc_tmem_wait_ld();
+        const int part = c0 / BN, sq = c0 - part * BN;     // which matrix, first sequence
+#pragma unroll
+        for (int j = 0; j < 32; j++) tilep[(size_t)(sq + j) * TLD + part * TC_BM + fl] = v[j];
+    }
+    __syncthreads();
+    // a warp per sequence, lanes over feature pairs
+    for (int r = warp; r < BN && store; r += TC_THREADS / 32) {
+        const int m = s0 + r;
+        if (m >= g.M) break;                               // sequences ascend: warp-uniform
+        if (g.act && !g.act[m]) continue;
+        const float* src = tilep + (size_t)r * TLD;
+#pragma unroll
+        for (int c = 2 * lane; c < TC_BM; c += 64) {
+            if (f0 + c >= g.N) break;
+            const float2 uv = *reinterpret_cast<const float2*>(src + c);
+            const float u[2] = {uv.x, uv.y};
+            float gt[2] = {0.0f, 0.0f};
+            if constexpr (DUAL == 2) {
+                const float2 gv = *reinterpret_cast<const float2*>(src + TC_BM + c);
+                gt[0] = gv.x;
+                gt[1] = gv.y;
+            }
+            tc_epilogue<EPI, 2>(g, m, f0 + c, u, gt, split);
+        }
+    }
     if (threadIdx.x == 0)
         for (int kb = ctl[3]; kb < ctl[2]; kb++)
             if (!mbar_wait(&full[kb % STAGES], (uint32_t)(kb / STAGES) & 1u, g.timeout_ns)) break;

@@ -125,8 +125,10 @@ struct mc_session {
     __nv_bfloat16 *bd_xn16, *bd_att16, *bd_f16;
     bool bd_maps_ok;
     CUtensorMap bd_map[3];        // A operands: xn, att, f ([Bcap] rows)
-    CUtensorMap bd_wmap[6];       // B operands as 64-row boxes (more CTAs for skinny GEMMs)
-    float* bd_part;               // [kMaxKSplit][Bcap][D] K-slice partials of the residual GEMMs
+    CUtensorMap bd_wmap[6];       // weights as 128-row boxes (the MMA's M side in decode)
+    CUtensorMap bd_xmap[3];       // xn, att, f as 64-row boxes (the MMA's N side in decode)
+    float* bd_part;               // K-slice partials of the decode GEMMs
+    size_t bd_part_floats;
     float* pf_logits;             // [pf_rows][V] lm_head scratch of mc_model_forward
     __nv_bfloat16 *pf_xn16, *pf_att16, *pf_f16;   // bf16 GEMM inputs (tensor cores, bf16 weights)
     cudaEvent_t ev_mid;           // end of prefill
@@ -775,6 +777,48 @@ cudaError_t tc_launch(const CUtensorMap& a, const CUtensorMap& b, const CUtensor
 // CTAs splitting K for a decode GEMM of `tiles` output tiles and nk K
 // blocks: about one CTA per SM in all, at most 8 partials per element and
 // at least one K block each.
+// Launch with programmatic stream serialization: the kernel may start while
+// the previous one in the stream finishes (its pdl_wait orders the rest).
+template <typename... KArgs, typename... Args>
+cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                       Args&&... args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
+// Decode GEMM launch (tc_dec_kernel): X maps with BN-row boxes, weight maps
+// with 128-row boxes; ksplit CTAs per (128 features x BN sequences) tile.
+template <int KIND, int EPI, int BN, int STAGES>
+cudaError_t tc_dec_launch(const CUtensorMap& x, const CUtensorMap& w, const CUtensorMap& w2,
+                          const mc::TcArgs& g, cudaStream_t st) {
+    constexpr int DUAL = EPI == mc::EPI_PART2 ? 2 : 1;
+    const size_t smem = 1024 + (size_t)STAGES * (DUAL * mc::TC_TILE + (size_t)BN * mc::TC_BKB) + 256;
+    static unsigned long long attr_set = 0;    // one bit per device
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return e;
+    if (dev < 64 && !((attr_set >> dev) & 1ull)) {
+        e = cudaFuncSetAttribute(mc::tc_dec_kernel<KIND, EPI, BN, STAGES>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
+        attr_set |= 1ull << dev;
+    }
+    const unsigned ks = g.ksplit > 1 ? (unsigned)g.ksplit : 1u;
+    if (ks > 1 && EPI != mc::EPI_PART && EPI != mc::EPI_PART2) return cudaErrorInvalidValue;
+    const unsigned tiles = (unsigned)((g.N + mc::TC_BM - 1) / mc::TC_BM) * (unsigned)((g.M + BN - 1) / BN);
+    return launch_pdl(mc::tc_dec_kernel<KIND, EPI, BN, STAGES>, dim3(tiles * ks), dim3(mc::TC_THREADS), smem, st,
+                      x, w, w2, g);
+}
+
 constexpr int kMaxKSplit = mc::kBdMaxParts;
 int tc_ksplit(int tiles, int nk, int sms) {
     int ks = sms / std::max(tiles, 1);
@@ -996,14 +1040,29 @@ mc_status run_batched(mc_session* s, mc::LoopParams<WT>& p) {
     const mc_model* m = s->m;
     constexpr bool kB16 = std::is_same<WT, __nv_bfloat16>::value;
     constexpr int KD = kB16 ? mc::TC_BF16 : mc::TC_TF32;
+    constexpr int BN = 64;                       // sequences per decode GEMM tile
     fill_params(p, s);
     p.stamps = s->stamps;
     s->last_T = p.T;
-    const size_t Bc = s->Bcap, D = m->D, F = m->F;
+    const size_t Bc = s->Bcap, D = m->D, F = m->F, Q = m->Q;
+    int dev = 0, optin = 0, sms = 0;
+    MC_CUDA(cudaGetDevice(&dev));
+    MC_CUDA(cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev));
+    MC_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+    // K splits: about one CTA per SM for every GEMM but the lm_head, whose
+    // V/128 feature tiles fill the GPU by themselves
+    const int bke = mc::TC_BKB / (kB16 ? 2 : 4), tsq = (p.B + BN - 1) / BN;
+    auto tiles = [&](size_t n) { return tsq * (int)((n + mc::TC_BM - 1) / mc::TC_BM); };
+    auto nkb = [&](size_t k) { return (int)((k + bke - 1) / bke); };
+    const int ks_qkv = tc_ksplit(tiles(Q), nkb(D), sms);
+    const int ks_proj = tc_ksplit(tiles(D), nkb(D), sms);
+    const int ks_up = tc_ksplit(tiles(F), nkb(D), sms);
+    const int ks_down = tc_ksplit(tiles(D), nkb(F), sms);
+    const size_t part_need = std::max({(size_t)ks_qkv * p.B * Q, (size_t)ks_proj * p.B * D,
+                                       (size_t)ks_up * p.B * 2 * F, (size_t)ks_down * p.B * D});
     if (!s->bd_lists) {
         bool ok = cudaMalloc(&s->bd_lists, mc::bd_lists_ints(s->Bcap) * 4) == cudaSuccess &&
-                  cudaMalloc(&s->bd_xn, Bc * D * 4) == cudaSuccess &&
-                  cudaMalloc(&s->bd_part, (size_t)kMaxKSplit * Bc * D * 4) == cudaSuccess;
+                  cudaMalloc(&s->bd_xn, Bc * D * 4) == cudaSuccess;
         if (ok && kB16)
             ok = cudaMalloc(&s->bd_xn16, Bc * D * 2) == cudaSuccess &&
                  cudaMalloc(&s->bd_att16, Bc * D * 2) == cudaSuccess &&
@@ -1014,37 +1073,46 @@ mc_status run_batched(mc_session* s, mc::LoopParams<WT>& p) {
         }
         s->bd_maps_ok = false;
     }
+    if (s->bd_part_floats < part_need) {
+        cudaFree(s->bd_part);
+        s->bd_part = nullptr;
+        s->bd_part_floats = 0;
+        if (cudaMalloc(&s->bd_part, part_need * 4) != cudaSuccess) {
+            cudaGetLastError();
+            return fail(MC_ERR_NOMEM, "batched decode partials (%zu B)", part_need * 4);
+        }
+        s->bd_part_floats = part_need;
+    }
     if (!s->bd_maps_ok) {
         const int es = kB16 ? 2 : 4;
-        mc_status st = tc_weight_maps(s);
-        if (!st) st = tc_map(&s->bd_map[0], kB16 ? (const void*)s->bd_xn16 : (const void*)s->bd_xn, es, D, Bc, 0);
-        if (!st) st = tc_map(&s->bd_map[1], kB16 ? (const void*)s->bd_att16 : (const void*)s->att, es, D, Bc, 0);
-        if (!st) st = tc_map(&s->bd_map[2], kB16 ? (const void*)s->bd_f16 : (const void*)s->f, es, F, Bc, 0);
-        // a decode GEMM has at most a tile of rows: 64-column tiles spread
-        // the weight stream over 4x more CTAs than the prefill's
+        mc_status st = MC_OK;
+        if (!st) st = tc_map(&s->bd_xmap[0], kB16 ? (const void*)s->bd_xn16 : (const void*)s->bd_xn, es, D, Bc, 0, BN);
+        if (!st) st = tc_map(&s->bd_xmap[1], kB16 ? (const void*)s->bd_att16 : (const void*)s->att, es, D, Bc, 0, BN);
+        if (!st) st = tc_map(&s->bd_xmap[2], kB16 ? (const void*)s->bd_f16 : (const void*)s->f, es, F, Bc, 0, BN);
         const char* wb = static_cast<const char*>(m->wblock);
-        const uint64_t Q = m->Q, L = m->L;
-        if (!st) st = tc_map(&s->bd_wmap[0], wb + m->off[1], es, D, Q, L, 64);
-        if (!st) st = tc_map(&s->bd_wmap[1], wb + m->off[2], es, D, D, L, 64);
-        if (!st) st = tc_map(&s->bd_wmap[2], wb + m->off[3], es, D, F, L, 64);
-        if (!st) st = tc_map(&s->bd_wmap[3], wb + m->off[4], es, D, F, L, 64);
-        if (!st) st = tc_map(&s->bd_wmap[4], wb + m->off[5], es, F, D, L, 64);
-        if (!st) st = tc_map(&s->bd_wmap[5], wb + m->off[0], es, D, m->V, 1, 64);
+        const uint64_t L = m->L;
+        if (!st) st = tc_map(&s->bd_wmap[0], wb + m->off[1], es, D, Q, L, mc::TC_BM);
+        if (!st) st = tc_map(&s->bd_wmap[1], wb + m->off[2], es, D, D, L, mc::TC_BM);
+        if (!st) st = tc_map(&s->bd_wmap[2], wb + m->off[3], es, D, F, L, mc::TC_BM);
+        if (!st) st = tc_map(&s->bd_wmap[3], wb + m->off[4], es, D, F, L, mc::TC_BM);
+        if (!st) st = tc_map(&s->bd_wmap[4], wb + m->off[5], es, F, D, L, mc::TC_BM);
+        if (!st) st = tc_map(&s->bd_wmap[5], wb + m->off[0], es, D, m->V, 1, mc::TC_BM);
         if (st) return st;
         s->bd_maps_ok = true;
     }
+    const size_t att_smem = mc::bd_att_smem(m->H / m->K, m->hd);
+    if (att_smem > (size_t)optin)
+        return fail(MC_ERR_UNSUPPORTED, "batched attention needs %zu B of shared memory", att_smem);
     cudaStream_t st = s->stream;
     MC_CUDA(cudaMemsetAsync(s->stamps, 0, ((size_t)p.T + 1) * 8, st));
     MC_CUDA(cudaMemsetAsync(s->status, 0, 256, st));
     MC_CUDA(cudaMemsetAsync(s->att_cnt, 0, (size_t)s->Bcap * m->K * 4, st));
+    MC_CUDA(cudaMemsetAsync(s->bd_lists + 3, 0, 4, st));
     static unsigned long long attr_set = 0;     // dynamic shared memory limits, per device
-    int dev = 0;
-    MC_CUDA(cudaGetDevice(&dev));
     if (dev < 64 && !((attr_set >> dev) & 1ull)) {
-        int lim = 0;     // the device maximum, shared by every session on the device
-        MC_CUDA(cudaDeviceGetAttribute(&lim, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev));
-        MC_CUDA(cudaFuncSetAttribute(mc::bd_att_kernel<WT>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim));
-        MC_CUDA(cudaFuncSetAttribute(mc::bd_sample_kernel<WT>, cudaFuncAttributeMaxDynamicSharedMemorySize, lim));
+        // the device maximum, shared by every session on the device
+        MC_CUDA(cudaFuncSetAttribute(mc::bd_att_kernel<WT>, cudaFuncAttributeMaxDynamicSharedMemorySize, optin));
+        MC_CUDA(cudaFuncSetAttribute(mc::bd_sample_kernel<WT>, cudaFuncAttributeMaxDynamicSharedMemorySize, optin));
         attr_set |= 1ull << dev;
     }
     const mc::BdLists L{s->bd_lists, s->Bcap};
@@ -1054,35 +1122,22 @@ mc_status run_batched(mc_session* s, mc::LoopParams<WT>& p) {
     g.tpos = L.base + 2;
     g.status = s->status;
     g.timeout_ns = p.timeout_ns;
-    g.pa.D = m->D; g.pa.H = m->H; g.pa.K = m->K; g.pa.hd = m->hd; g.pa.Bcap = s->Bcap; g.pa.cap = s->cap;
-    g.pa.rope = m->rope; g.pa.kc = s->kc; g.pa.vc = s->vc; g.pa.QB = s->q;
-    g.pa.FH16 = kB16 ? s->bd_f16 : nullptr;
-    const CUtensorMap* am = s->bd_map;
+    g.C = s->bd_part;
+    const CUtensorMap* xm = s->bd_xmap;
     const CUtensorMap* wm = s->bd_wmap;
     const float* rmsf = m->norms + 2 * (size_t)m->L * m->D;
-    const size_t att_smem = mc::bd_att_smem(m->H / m->K, m->hd);
-    int ks_proj, ks_down, sms = 0;
-    {
-        int dev = 0, optin = 0;
-        MC_CUDA(cudaGetDevice(&dev));
-        MC_CUDA(cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev));
-        MC_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
-        const int bke = mc::TC_BKB / (kB16 ? 2 : 4), tm = (p.B + mc::TC_BM - 1) / mc::TC_BM;
-        auto tiles = [&](int n) { return tm * ((n + 63) / 64); };
-        ks_proj = tc_ksplit(tiles(m->D), (m->D + bke - 1) / bke, sms);
-        ks_down = tc_ksplit(tiles(m->D), (m->F + bke - 1) / bke, sms);
-        if (att_smem > (size_t)optin)
-            return fail(MC_ERR_UNSUPPORTED, "batched attention needs %zu B of shared memory", att_smem);
-        MC_CUDA(cudaFuncSetAttribute(mc::bd_att_kernel<WT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     (int)att_smem));
-    }
+    const unsigned swiglu_blocks = (unsigned)std::max(1, std::min(4 * sms, (int)((p.B * F / 4 + 255) / 256)));
+    __nv_bfloat16* xn16 = kB16 ? s->bd_xn16 : nullptr;
+    __nv_bfloat16* f16 = kB16 ? s->bd_f16 : nullptr;
     int launches = 0;
-    MC_CUDA(cudaMemsetAsync(s->bd_lists + 3, 0, 4, st));
     mc::bd_prologue_kernel<WT><<<s->grid, mc::kThreads, 0, st>>>(p);
     launches++;
     cudaError_t e = cudaSuccess;
     for (int t = p.t0; t < p.T && e == cudaSuccess; t++) {
-        mc::bd_lists_kernel<WT><<<1, 1024, 0, st>>>(p, L, t == p.t0);
+        if ((e = launch_pdl(mc::bd_lists_kernel<WT>, dim3(1), dim3(1024), 0, st, p, L, (int)(t == p.t0))) !=
+            cudaSuccess)
+            break;
+        launches++;
         // attention units: (sequence, KV head) pairs, each split into
         // klen-key pieces only when the pairs alone would not fill the GPU
         // twice over (the device's position is t too)
@@ -1090,38 +1145,52 @@ mc_status run_batched(mc_session* s, mc::LoopParams<WT>& p) {
         const int want = std::max(1, (2 * sms + pairs - 1) / pairs);
         const int klen = std::max(mc::kBdTile, (nkeys + want - 1) / want + mc::kBdTile - 1) / mc::kBdTile * mc::kBdTile;
         const unsigned att_units = (unsigned)pairs * (unsigned)((nkeys + klen - 1) / klen);
-        // the residual GEMMs (proj, down) leave K-slice partials in bd_part;
-        // the norm that follows adds them to x in slice order
+        // every GEMM leaves K-slice partials in bd_part; the kernel after it
+        // sums them in slice order (norm: residual; attention: q and the
+        // new K/V row with RoPE; swiglu: f)
         for (int l = 0; l < m->L; l++) {
-            mc::bd_norm_kernel<WT><<<p.B, mc::kThreads, 0, st>>>(p, L, 0, m->norms + (size_t)l * D, l == 0,
-                                                                  s->bd_xn, kB16 ? s->bd_xn16 : nullptr,
-                                                                  s->bd_part, l == 0 ? 0 : ks_down);
+            if ((e = launch_pdl(mc::bd_norm_kernel<WT>, dim3(p.B), dim3(mc::kThreads), 0, st, p, L, 0,
+                                m->norms + (size_t)l * D, (int)(l == 0), s->bd_xn, xn16, s->bd_part,
+                                l == 0 ? 0 : ks_down)) != cudaSuccess)
+                break;
             g.layer = l;
-            g.N = m->Q; g.K = m->D; g.C = nullptr; g.ldc = 0; g.ksplit = 1;
-            if ((e = tc_launch<KD, mc::EPI_QKV, 64, 8>(am[0], wm[0], wm[0], g, st)) != cudaSuccess) break;
-            mc::bd_att_kernel<WT><<<att_units, mc::kBdAttThreads, att_smem, st>>>(p, L, l, t, klen);
-            if (kB16) mc::bd_cvt_kernel<WT><<<p.B, mc::kThreads, 0, st>>>(p, L, s->bd_att16);
-            g.N = m->D; g.K = m->D; g.C = s->bd_part; g.ldc = m->D; g.ksplit = ks_proj;
-            if ((e = tc_launch<KD, mc::EPI_PART, 64, 8>(am[1], wm[1], wm[1], g, st)) != cudaSuccess) break;
-            mc::bd_norm_kernel<WT><<<p.B, mc::kThreads, 0, st>>>(p, L, 0, m->norms + ((size_t)m->L + l) * D, 0,
-                                                                  s->bd_xn, kB16 ? s->bd_xn16 : nullptr,
-                                                                  s->bd_part, ks_proj);
-            g.N = m->F; g.K = m->D; g.C = s->f; g.ldc = m->F; g.ksplit = 1;
-            if ((e = tc_launch<KD, mc::EPI_SWIGLU, 64, 6>(am[0], wm[2], wm[3], g, st)) != cudaSuccess) break;
-            g.N = m->D; g.K = m->F; g.C = s->bd_part; g.ldc = m->D; g.ksplit = ks_down;
-            if ((e = tc_launch<KD, mc::EPI_PART, 64, 8>(am[2], wm[4], wm[4], g, st)) != cudaSuccess) break;
-            launches += kB16 ? 8 : 7;
+            g.N = m->Q; g.K = m->D; g.ldc = m->Q; g.ksplit = ks_qkv;
+            if ((e = tc_dec_launch<KD, mc::EPI_PART, BN, 8>(xm[0], wm[0], wm[0], g, st)) != cudaSuccess) break;
+            if ((e = launch_pdl(mc::bd_att_kernel<WT>, dim3(att_units), dim3(mc::kBdAttThreads), att_smem, st, p,
+                                L, l, t, klen, (const float*)s->bd_part, ks_qkv)) != cudaSuccess)
+                break;
+            if (kB16 && (e = launch_pdl(mc::bd_cvt_kernel<WT>, dim3(p.B), dim3(mc::kThreads), 0, st, p, L,
+                                        s->bd_att16)) != cudaSuccess)
+                break;
+            g.N = m->D; g.K = m->D; g.ldc = m->D; g.ksplit = ks_proj;
+            if ((e = tc_dec_launch<KD, mc::EPI_PART, BN, 8>(xm[1], wm[1], wm[1], g, st)) != cudaSuccess) break;
+            if ((e = launch_pdl(mc::bd_norm_kernel<WT>, dim3(p.B), dim3(mc::kThreads), 0, st, p, L, 0,
+                                m->norms + ((size_t)m->L + l) * D, 0, s->bd_xn, xn16, s->bd_part, ks_proj)) !=
+                cudaSuccess)
+                break;
+            g.N = m->F; g.K = m->D; g.ldc = 2 * m->F; g.ksplit = ks_up;
+            if ((e = tc_dec_launch<KD, mc::EPI_PART2, BN, 5>(xm[0], wm[2], wm[3], g, st)) != cudaSuccess) break;
+            if ((e = launch_pdl(mc::bd_swiglu_kernel<WT>, dim3(swiglu_blocks), dim3(mc::kThreads), 0, st, p, L,
+                                (const float*)s->bd_part, ks_up, f16)) != cudaSuccess)
+                break;
+            g.N = m->D; g.K = m->F; g.ldc = m->D; g.ksplit = ks_down;
+            if ((e = tc_dec_launch<KD, mc::EPI_PART, BN, 8>(xm[2], wm[4], wm[4], g, st)) != cudaSuccess) break;
+            launches += kB16 ? 9 : 8;
         }
         if (e != cudaSuccess) break;
-        mc::bd_norm_kernel<WT><<<p.B, mc::kThreads, 0, st>>>(p, L, 1, rmsf, 0, s->bd_xn,
-                                                              kB16 ? s->bd_xn16 : nullptr, s->bd_part, ks_down);
+        if ((e = launch_pdl(mc::bd_norm_kernel<WT>, dim3(p.B), dim3(mc::kThreads), 0, st, p, L, 1, rmsf, 0,
+                            s->bd_xn, xn16, s->bd_part, ks_down)) != cudaSuccess)
+            break;
         mc::TcArgs gh = g;
         gh.act = nullptr;
         gh.N = m->V; gh.K = m->D; gh.C = s->logits; gh.ldc = m->V; gh.layer = 0; gh.ksplit = 1;
-        if ((e = tc_launch<KD, mc::TCE_STORE, 64, 8>(am[0], wm[5], wm[5], gh, st)) != cudaSuccess) break;
-        mc::bd_head_kernel<WT><<<s->grid, mc::kThreads, 0, st>>>(p, L);
-        mc::bd_sample_kernel<WT><<<s->grid, mc::kThreads, s->smem, st>>>(p, L);
-        launches += 6;
+        if ((e = tc_dec_launch<KD, mc::TCE_STORE, BN, 8>(xm[0], wm[5], wm[5], gh, st)) != cudaSuccess) break;
+        if ((e = launch_pdl(mc::bd_head_kernel<WT>, dim3(s->grid), dim3(mc::kThreads), 0, st, p, L)) != cudaSuccess)
+            break;
+        if ((e = launch_pdl(mc::bd_sample_kernel<WT>, dim3(s->grid), dim3(mc::kThreads), s->smem, st, p, L)) !=
+            cudaSuccess)
+            break;
+        launches += 4;
         e = cudaGetLastError();
     }
     if (e != cudaSuccess) return fail(MC_ERR_CUDA, "batched decode launch: %s", cudaGetErrorString(e));
