@@ -11,7 +11,7 @@
 //   per layer: norm -> QKV GEMM (+RoPE, K/V append) -> attention (the grid
 //              loop's phase_att) -> proj GEMM (+residual) -> norm ->
 //              up/gate GEMM (+SwiGLU) -> down GEMM (+residual)
-//   final norm -> lm_head GEMM -> reserved-id mask + greedy partials ->
+//   final norm -> lm_head GEMM (+ reserved-id mask and greedy partials) ->
 //   sampler and bookkeeping (the grid loop's phase_sample)
 //
 // The step's position lives in device memory (lists[2]), so every step
@@ -486,50 +486,9 @@ __global__ void __launch_bounds__(kThreads) bd_cvt_kernel(const LoopParams<WT> p
         dst[(size_t)b * p.D + k] = __float2bfloat16_rn(p.att[(size_t)b * p.D + k]);
 }
 
-// After the lm_head GEMM: ids 0..3 masked (generate.c:580-581) and, for
-// greedy sampling, each CTA's best transformed value over its share of the
-// vocabulary (generate.c:438-460), the partials phase_sample reduces.
-template <typename WT>
-__global__ void __launch_bounds__(kThreads) bd_head_kernel(const LoopParams<WT> p, BdLists L) {
-    pdl_wait();
-    pdl_trigger();
-    const int nh = L.base[1];
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int per = (p.V + gridDim.x - 1) / gridDim.x;
-    const int v0 = min(p.V, blockIdx.x * per), v1 = min(p.V, v0 + per);
-    const int nwords = (p.V + 31) >> 5;
-    const bool greedy = p.s.top_k == 1;
-    // a warp per head sequence over this CTA's share of the vocabulary
-    for (int i = warp; i < nh; i += kWarps) {
-        const int b = L.head()[i];
-        float* lg = p.logits + (size_t)b * p.V;
-        float bv = -INFINITY;
-        int bi = 0x7fffffff;
-        for (int v = v0 + lane; v < v1; v += 32) {
-            float x = lg[v];
-            if (v < 4) {
-                x = -INFINITY;
-                lg[v] = x;
-            }
-            if (greedy) {
-                const unsigned cnt = p.s.pen_active ? p.counts[(size_t)b * p.V + v] : 0u;
-                const bool ban = p.s.ngram > 0 && ((p.banned[(size_t)b * nwords + (v >> 5)] >> (v & 31)) & 1u);
-                const float tv = transform_value(x, cnt, ban, p.s);
-                if (better(tv, v, bv, bi)) { bv = tv; bi = v; }
-            }
-        }
-        if (!greedy) continue;
-        warp_argmax(bv, bi);
-        if (lane == 0) {
-            p.amax_v[(size_t)b * gridDim.x + blockIdx.x] = bv;
-            p.amax_i[(size_t)b * gridDim.x + blockIdx.x] = bi;
-        }
-    }
-}
-
 // Sampling and bookkeeping of the head sequences (the token loop's phase).
 template <typename WT>
-__global__ void __launch_bounds__(kThreads, 1) bd_sample_kernel(const LoopParams<WT> p, BdLists L) {
+__global__ void __launch_bounds__(kThreads, 1) bd_sample_kernel(const LoopParams<WT> p, BdLists L, int nparts) {
     extern __shared__ __align__(16) float smem_f[];
     pdl_wait();
     pdl_trigger();
@@ -537,7 +496,7 @@ __global__ void __launch_bounds__(kThreads, 1) bd_sample_kernel(const LoopParams
     const int nh = L.base[1], t = L.base[2];
     for (int i = threadIdx.x; i < nh; i += blockDim.x) sm.head[i] = L.head()[i];
     __syncthreads();
-    if (nh > 0) phase_sample<WT>(p, t, sm, nh);
+    if (nh > 0) phase_sample<WT>(p, t, sm, nh, nparts);
     if (p.stamps && t + 1 == p.T && blockIdx.x == 0 && threadIdx.x == 0) p.stamps[p.T] = globaltimer_ns();
 }
 

@@ -61,6 +61,16 @@ struct TcArgs {
     int* status;
     unsigned long long timeout_ns;
     int ksplit;                // CTAs splitting K per tile (<= 1: no split; EPI_PART only)
+    // decode lm_head (tc_dec_kernel with TCE_STORE and head != 0): ids 0..3
+    // are stored as -inf (generate.c:580-581) and, for greedy sampling, each
+    // (sequence, 128-id tile)'s best transformed value and its id
+    // (generate.c:438-460) go to amax_v/amax_i at [sequence][tile]
+    int head;
+    SamplingArgs sa;
+    const unsigned* counts;    // [B][N] ids sampled so far (penalties)
+    const unsigned* banned;    // [B][ceil(N/32)] n-gram bans
+    float* amax_v;
+    int* amax_i;
 };
 
 // Dynamic shared memory of a launch with `btiles` B tiles of `bn` rows per
@@ -594,6 +604,45 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         if (m >= g.M) break;                               // sequences ascend: warp-uniform
         if (g.act && !g.act[m]) continue;
         const float* src = tilep + (size_t)r * TLD;
+        if constexpr (EPI == TCE_STORE) {
+            if (g.head) {
+                const bool greedy = g.sa.top_k == 1;
+                const int nwords = (g.N + 31) >> 5;
+                float* crow = g.C + (size_t)m * g.ldc;
+                float bv = -INFINITY;
+                int bi = 0x7fffffff;
+#pragma unroll
+                for (int c = 2 * lane; c < TC_BM; c += 64) {
+                    const float2 uv = *reinterpret_cast<const float2*>(src + c);
+                    const float x2[2] = {uv.x, uv.y};
+#pragma unroll
+                    for (int j = 0; j < 2; j++) {
+                        const int n = f0 + c + j;
+                        if (n >= g.N) break;
+                        const float x = n < 4 ? -INFINITY : x2[j];
+                        crow[n] = x;
+                        if (greedy) {
+                            const unsigned cnt = g.sa.pen_active ? __ldg(g.counts + (size_t)m * g.N + n) : 0u;
+                            const bool ban = g.sa.ngram > 0 &&
+                                             ((__ldg(g.banned + (size_t)m * nwords + (n >> 5)) >> (n & 31)) & 1u);
+                            const float tv = transform_value(x, cnt, ban, g.sa);
+                            if (better(tv, n, bv, bi)) {
+                                bv = tv;
+                                bi = n;
+                            }
+                        }
+                    }
+                }
+                if (greedy) {
+                    warp_argmax(bv, bi);
+                    if (lane == 0) {
+                        g.amax_v[(size_t)m * tiles_f + f0 / TC_BM] = bv;
+                        g.amax_i[(size_t)m * tiles_f + f0 / TC_BM] = bi;
+                    }
+                }
+                continue;
+            }
+        }
 #pragma unroll
         for (int c = 2 * lane; c < TC_BM; c += 64) {
             if (f0 + c >= g.N) break;

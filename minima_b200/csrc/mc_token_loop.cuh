@@ -572,7 +572,7 @@ __device__ void compute_bans(const LoopParams<WT>& p, int b, int hlen) {
 }
 
 template <typename WT>
-__device__ void phase_sample(const LoopParams<WT>& p, int t, LoopSmem& sm, int nhead) {
+__device__ void phase_sample(const LoopParams<WT>& p, int t, LoopSmem& sm, int nhead, int nparts) {
     SamplerSmem ss = sampler_carve(sm.xs, p.V);
     const int nwords = (p.V + 31) >> 5;
     for (int i = blockIdx.x; i < nhead; i += gridDim.x) {
@@ -587,17 +587,27 @@ __device__ void phase_sample(const LoopParams<WT>& p, int t, LoopSmem& sm, int n
         unsigned long long rng = ld_volatile_u64(&st->rng);
         int id = 0;
         if (p.s.top_k == 1) {
-            if (threadIdx.x == 0) {
+            // the best of the nparts greedy partials: better() is a total
+            // order, so the parallel reduction picks the same (value, id)
+            {
                 float v = -INFINITY;
                 int best = 0x7fffffff;
-                for (int c = 0; c < (int)gridDim.x; c++) {
-                    const float cv = ldcg(p.amax_v + (size_t)b * gridDim.x + c);
-                    const int ci = __ldcg(p.amax_i + (size_t)b * gridDim.x + c);
+                for (int c = threadIdx.x; c < nparts; c += blockDim.x) {
+                    const float cv = ldcg(p.amax_v + (size_t)b * nparts + c);
+                    const int ci = __ldcg(p.amax_i + (size_t)b * nparts + c);
                     if (better(cv, ci, v, best)) { v = cv; best = ci; }
                 }
-                if (best == 0x7fffffff) { best = 0; }
-                sm.red[0] = v;
-                sm.ints[1] = best;
+                warp_argmax(v, best);
+                const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+                if (lane == 0) { sm.red[warp] = v; sm.ints[16 + warp] = best; }
+                __syncthreads();
+                if (threadIdx.x == 0) {
+                    for (int w = 1; w < kWarps; w++)
+                        if (better(sm.red[w], sm.ints[16 + w], v, best)) { v = sm.red[w]; best = sm.ints[16 + w]; }
+                    if (best == 0x7fffffff) { best = 0; }
+                    sm.red[0] = v;
+                    sm.ints[1] = best;
+                }
             }
             __syncthreads();
             float v = sm.red[0];
@@ -769,7 +779,7 @@ __global__ void __launch_bounds__(kThreads, 1) token_loop_kernel(const LoopParam
             phase_head<WT, VEC>(p, t, sm, nh);
             if (!gs.sync()) return;
             if (!p.all_logits) {
-                phase_sample<WT>(p, t, sm, nh);
+                phase_sample<WT>(p, t, sm, nh, (int)gridDim.x);
                 if (!gs.sync()) return;
             }
         }

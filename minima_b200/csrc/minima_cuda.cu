@@ -575,8 +575,10 @@ mc_status mc_session_create(mc_model* m, int max_batch, int max_seq, mc_session*
         {(void**)&s->part_o, B * H * ms * hd * 4},
         {(void**)&s->part_m, B * H * ms * 4},
         {(void**)&s->part_l, B * H * ms * 4},
-        {(void**)&s->amax_v, B * s->grid * 4},
-        {(void**)&s->amax_i, B * s->grid * 4},
+        // greedy partials: one per CTA of the grid loop, or per 128-id tile
+        // of the batched decode's lm_head
+        {(void**)&s->amax_v, B * std::max<size_t>(s->grid, (V + 127) / 128) * 4},
+        {(void**)&s->amax_i, B * std::max<size_t>(s->grid, (V + 127) / 128) * 4},
         {(void**)&s->att_cnt, B * K * 4},
         {(void**)&s->counts, B * V * 4},
         {(void**)&s->banned, B * ((V + 31) / 32) * 4},
@@ -1181,16 +1183,18 @@ mc_status run_batched(mc_session* s, mc::LoopParams<WT>& p) {
         if ((e = launch_pdl(mc::bd_norm_kernel<WT>, dim3(p.B), dim3(mc::kThreads), 0, st, p, L, 1, rmsf, 0,
                             s->bd_xn, xn16, s->bd_part, ks_down)) != cudaSuccess)
             break;
+        // lm_head for the sequences that sample, with the reserved-id mask and
+        // the greedy partials in its epilogue
         mc::TcArgs gh = g;
-        gh.act = nullptr;
+        gh.act = L.base + 4 + 3 * (size_t)s->Bcap;     // act_head
         gh.N = m->V; gh.K = m->D; gh.C = s->logits; gh.ldc = m->V; gh.layer = 0; gh.ksplit = 1;
+        gh.head = 1; gh.sa = p.s; gh.counts = s->counts; gh.banned = s->banned;
+        gh.amax_v = s->amax_v; gh.amax_i = s->amax_i;
         if ((e = tc_dec_launch<KD, mc::TCE_STORE, BN, 8>(xm[0], wm[5], wm[5], gh, st)) != cudaSuccess) break;
-        if ((e = launch_pdl(mc::bd_head_kernel<WT>, dim3(s->grid), dim3(mc::kThreads), 0, st, p, L)) != cudaSuccess)
+        if ((e = launch_pdl(mc::bd_sample_kernel<WT>, dim3(s->grid), dim3(mc::kThreads), s->smem, st, p, L,
+                            (int)((m->V + mc::TC_BM - 1) / mc::TC_BM))) != cudaSuccess)
             break;
-        if ((e = launch_pdl(mc::bd_sample_kernel<WT>, dim3(s->grid), dim3(mc::kThreads), s->smem, st, p, L)) !=
-            cudaSuccess)
-            break;
-        launches += 4;
+        launches += 3;
         e = cudaGetLastError();
     }
     if (e != cudaSuccess) return fail(MC_ERR_CUDA, "batched decode launch: %s", cudaGetErrorString(e));
