@@ -81,12 +81,15 @@ __global__ void __launch_bounds__(1024) bd_lists_kernel(const LoopParams<WT> p, 
 }
 
 constexpr int kBdMaxParts = 16;              // K-slice partials of a decode GEMM
+constexpr int kBdNormCols = 4;               // float4 columns per norm thread (D <= 16 * kThreads)
 
 // xn[b] = rmsnorm(x[b]) * scale (generate.c:57-63) for the listed sequences,
 // plus a bf16 copy when xn16 is set.  With embed, x[b] is first set to the
 // embedding row of the id fed (generate.c:86-88); with nparts > 0, the
 // K-slice partials of the residual GEMM before it are first added to x[b]
-// in slice order (part + (s * B + b) * D).  One CTA per sequence.
+// in slice order (part + (s * B + b) * D).  One CTA per sequence; a thread
+// keeps its float4 columns in registers and issues all partial loads of a
+// column before adding them.
 template <typename WT>
 __global__ void __launch_bounds__(kThreads) bd_norm_kernel(const LoopParams<WT> p, BdLists L, int head,
                                                            const float* scale, int embed, float* xn,
@@ -98,28 +101,54 @@ __global__ void __launch_bounds__(kThreads) bd_norm_kernel(const LoopParams<WT> 
     const int b = blockIdx.x;
     if (b >= p.B || !(head ? L.act_head() : L.act_fwd())[b]) return;
     float* x = p.x + (size_t)b * p.D;
+    const int nv = p.D >> 2;
+    float4 keep[kBdNormCols];
     float ss = 0.0f;
-    for (int k = threadIdx.x; k < p.D; k += blockDim.x) {
-        float v;
+#pragma unroll
+    for (int i = 0; i < kBdNormCols; i++) {
+        const int c = threadIdx.x + i * blockDim.x;
+        keep[i] = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        if (c >= nv) continue;
+        float4 v;
         if (embed) {
-            v = wload1(p.tok_emb + (size_t)L.tok()[b] * p.D + k);
+            const WT* e = p.tok_emb + (size_t)L.tok()[b] * p.D + 4 * c;
+            v = make_float4(wload1(e), wload1(e + 1), wload1(e + 2), wload1(e + 3));
         } else {
-            v = x[k];
-            float r = 0.0f;
+            v = ldcg4(x + 4 * c);
+            float4 r[kBdMaxParts];
 #pragma unroll
             for (int s = 0; s < kBdMaxParts; s++)
-                if (s < nparts) r += __ldcg(part + ((size_t)s * p.B + b) * p.D + k);
-            v += r;
+                r[s] = s < nparts ? ldcg4(part + ((size_t)s * p.B + b) * p.D + 4 * c)
+                                  : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+            float4 a = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+#pragma unroll
+            for (int s = 0; s < kBdMaxParts; s++)
+                if (s < nparts) {
+                    a.x += r[s].x; a.y += r[s].y; a.z += r[s].z; a.w += r[s].w;
+                }
+            v.x += a.x; v.y += a.y; v.z += a.z; v.w += a.w;
         }
-        if (embed || nparts > 0) x[k] = v;
-        ss += v * v;
+        if (embed || nparts > 0) *reinterpret_cast<float4*>(x + 4 * c) = v;
+        ss += v.x * v.x + v.y * v.y + v.z * v.z + v.w * v.w;
+        keep[i] = v;
     }
     ss = block_sum(ss, red);
     const float inv = 1.0f / sqrtf(ss / (float)p.D + 1e-5f);
-    for (int k = threadIdx.x; k < p.D; k += blockDim.x) {
-        const float v = x[k] * inv * scale[k];
-        xn[(size_t)b * p.D + k] = v;
-        if (xn16) xn16[(size_t)b * p.D + k] = __float2bfloat16_rn(v);
+#pragma unroll
+    for (int i = 0; i < kBdNormCols; i++) {
+        const int c = threadIdx.x + i * blockDim.x;
+        if (c >= nv) continue;
+        const float4 sc4 = *reinterpret_cast<const float4*>(scale + 4 * c);
+        const float4 v = make_float4(keep[i].x * inv * sc4.x, keep[i].y * inv * sc4.y, keep[i].z * inv * sc4.z,
+                                     keep[i].w * inv * sc4.w);
+        *reinterpret_cast<float4*>(xn + (size_t)b * p.D + 4 * c) = v;
+        if (xn16) {
+            __nv_bfloat16* o = xn16 + (size_t)b * p.D + 4 * c;
+            o[0] = __float2bfloat16_rn(v.x);
+            o[1] = __float2bfloat16_rn(v.y);
+            o[2] = __float2bfloat16_rn(v.z);
+            o[3] = __float2bfloat16_rn(v.w);
+        }
     }
 }
 

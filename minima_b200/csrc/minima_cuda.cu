@@ -1032,7 +1032,7 @@ bool batched_ok(const mc_model* m) {
     const int mult = m->dtype == MC_WEIGHTS_BF16 ? 8 : 4;
     const int G = m->H / m->K;
     return m->D % mult == 0 && m->F % mult == 0 && G * m->hd <= mc::kBdAttMaxO * mc::kBdAttThreads &&
-           G <= mc::kBdAttThreads;
+           G <= mc::kBdAttThreads && m->D <= 4 * mc::kBdNormCols * mc::kThreads;
 }
 
 // The token loop as one launch sequence per step with every matrix product

@@ -64,3 +64,19 @@ def test_batched_greedy_matches_oracle(gpu, monkeypatch, bf16):
 def test_batched_sampled_runs(gpu, monkeypatch):
     worst, agree = run(monkeypatch, False, 33, 8, temperature=0.8, top_k=40, top_p=0.9)
     print(f"sampled: worst err/bound {worst:.3f}")
+
+
+def test_batched_two_sequence_tiles(gpu, monkeypatch):
+    """80 sequences: the decode GEMMs run two 64-sequence tiles."""
+    worst, agree = run(monkeypatch, False, 80, 6, top_k=1)
+    print(f"B=80: worst err/bound {worst:.3f}")
+    assert sum(a == 6 for a in agree) >= 72
+
+
+def test_batched_penalties_and_bans(gpu, monkeypatch):
+    """Greedy with repetition/frequency/presence penalties and n-gram bans:
+    the lm_head epilogue's transformed values (generate.c:438-460)."""
+    worst, agree = run(monkeypatch, False, 36, 10, top_k=1, repetition_penalty=1.3,
+                       frequency_penalty=0.5, presence_penalty=0.2, no_repeat_ngram_size=2)
+    print(f"penalties: worst err/bound {worst:.3f}")
+    assert sum(a == 10 for a in agree) >= 32
