@@ -166,8 +166,9 @@ __device__ inline LoopSmem bd_smem(float* smem_f, int Bcap) {
 // One CTA per (sequence, KV head, key split) — a split is klen keys, and a
 // (sequence, KV head) has one split unless there are too few pairs to fill
 // the GPU.  The split's keys stream through shared memory in tiles of
-// kBdTile rows, double-buffered with cp.async (the next tile's K and V rows
-// are in flight while this one is scored), and each of the G query heads
+// kBdTile rows through a ring of kBdRing buffers filled by cp.async (the
+// next tiles' K and V rows are in flight while one is scored), and each of
+// the G query heads
 // keeps an online softmax (running max, sum and P.V rows).  With several
 // splits the last one to finish merges the partial states (flash-decoding).
 // The unit comes from blockIdx directly; sequences that do not run at t
@@ -179,13 +180,14 @@ __device__ inline LoopSmem bd_smem(float* smem_f, int Bcap) {
 // them to the cache (generate.c:108-120) and places them in its last tile.
 constexpr int kBdAttThreads = 128;
 constexpr int kBdTile = 64;                  // keys per shared-memory tile
+constexpr int kBdRing = 2;                   // tiles in the ring
 constexpr int kBdAttMaxO = 4;                // P.V outputs per thread (G * hd <= 512)
 
-// [flag, pad x3] then K, V [2][kBdTile][hd], q [G][hd], probabilities
+// [flag, pad x3] then K, V [kBdRing][kBdTile][hd], q [G][hd], probabilities
 // [G][kBdTile], the new K and V rows [hd] each, running max / sum / rescale
 // [G] each
 __host__ __device__ inline size_t bd_att_smem(int G, int hd) {
-    return 16 + ((size_t)4 * kBdTile * hd + (size_t)G * hd + (size_t)G * kBdTile + 2 * (size_t)hd +
+    return 16 + ((size_t)2 * kBdRing * kBdTile * hd + (size_t)G * hd + (size_t)G * kBdTile + 2 * (size_t)hd +
                  3 * (size_t)G) * 4;
 }
 
@@ -214,9 +216,9 @@ __global__ void __launch_bounds__(kBdAttThreads) bd_att_kernel(const LoopParams<
     const float* kb = p.kc + (cache_off + j0) * hd;
     const float* vb = p.vc + (cache_off + j0) * hd;
     int* flag = reinterpret_cast<int*>(smem_f);
-    float* kt = smem_f + 4;                  // [2][kBdTile][hd], 16-byte aligned
-    float* vt = kt + 2 * kBdTile * hd;
-    float* qs = vt + 2 * kBdTile * hd;
+    float* kt = smem_f + 4;                  // [kBdRing][kBdTile][hd], 16-byte aligned
+    float* vt = kt + kBdRing * kBdTile * hd;
+    float* qs = vt + kBdRing * kBdTile * hd;
     float* sc = qs + G * hd;
     float* krow = sc + G * kBdTile;          // key t's K and V rows (nq > 0)
     float* vrow = krow + hd;
@@ -251,12 +253,14 @@ __global__ void __launch_bounds__(kBdAttThreads) bd_att_kernel(const LoopParams<
     }
     // key t (the last key of the last split) is built here when nq > 0
     const bool has_t = nq > 0 && s == nsplit - 1;
-    // tile i of this split -> buffer i & 1
+    // tile i of this split -> buffer i % kBdRing; one commit group per tile
+    // (empty past the last tile), so tile i is complete once at most
+    // kBdRing - 1 newer groups are pending
     auto load_tile = [&](int i) {
         const int k0 = i * kBdTile;
-        const int nt = min(kBdTile, j1 - j0 - k0) - (has_t && i == ntiles - 1 ? 1 : 0);
-        float* kd = kt + (i & 1) * kBdTile * hd;
-        float* vd = vt + (i & 1) * kBdTile * hd;
+        const int nt = i < ntiles ? min(kBdTile, j1 - j0 - k0) - (has_t && i == ntiles - 1 ? 1 : 0) : 0;
+        float* kd = kt + (i % kBdRing) * kBdTile * hd;
+        float* vd = vt + (i % kBdRing) * kBdTile * hd;
         if (vec) {
             for (int e = threadIdx.x; e < nt * q4; e += blockDim.x) {
                 cp_async16(kd + 4 * e, kb + (size_t)k0 * hd + 4 * e);
@@ -270,13 +274,14 @@ __global__ void __launch_bounds__(kBdAttThreads) bd_att_kernel(const LoopParams<
         }
         cp_async_commit();
     };
-    // the first tile's rows precede t and were written at earlier steps, so
+    // the first tiles' rows precede t and were written at earlier steps, so
     // they are requested before waiting for the previous kernel
-    load_tile(0);
+    for (int i = 0; i < kBdRing - 1; i++) load_tile(i);
     pdl_wait();
     pdl_trigger();
     const int active = L.act_fwd()[b];
     const int hp = hd / 2;
+    const int nitems = G * hp + (has_t ? hd : 0);   // gather items; K/V ones stay with their thread
     if (nq > 0) {
         // q (and key t's rows): sums of the partials in slice order, then RoPE
         const float* pb = qkvp + (size_t)b * p.Q;
@@ -293,18 +298,19 @@ __global__ void __launch_bounds__(kBdAttThreads) bd_att_kernel(const LoopParams<
                     x1 += v.y;
                 }
         };
-        for (int i = threadIdx.x; i < G * hp; i += blockDim.x) {
-            const int h = i / hp, pr = i - h * hp;
-            float x0, x1;
-            gather((g * G + h) * hd + 2 * pr, x0, x1);
-            const float2 r = rot[pr];
-            qs[h * hd + 2 * pr] = x0 * r.x - x1 * r.y;
-            qs[h * hd + 2 * pr + 1] = x0 * r.y + x1 * r.x;
-        }
-        if (has_t)
-            for (int i = threadIdx.x; i < hd; i += blockDim.x) {
-                const bool isk = i < hp;
-                const int pr = isk ? i : i - hp;
+        // one pass: q pairs, then (for the unit holding key t) K and V pairs
+        for (int i = threadIdx.x; i < nitems; i += blockDim.x) {
+            if (i < G * hp) {
+                const int h = i / hp, pr = i - h * hp;
+                float x0, x1;
+                gather((g * G + h) * hd + 2 * pr, x0, x1);
+                const float2 r = rot[pr];
+                qs[h * hd + 2 * pr] = x0 * r.x - x1 * r.y;
+                qs[h * hd + 2 * pr + 1] = x0 * r.y + x1 * r.x;
+            } else {
+                const int k = i - G * hp;
+                const bool isk = k < hp;
+                const int pr = isk ? k : k - hp;
                 float x0, x1;
                 gather((isk ? p.H + g : p.H + p.K + g) * hd + 2 * pr, x0, x1);
                 float* row = isk ? krow : vrow;
@@ -317,6 +323,7 @@ __global__ void __launch_bounds__(kBdAttThreads) bd_att_kernel(const LoopParams<
                     row[2 * pr + 1] = x1;
                 }
             }
+        }
     } else {
         for (int i = threadIdx.x; i < G * hd; i += blockDim.x)
             qs[i] = ldcg(p.q + (size_t)b * p.D + (size_t)g * G * hd + i);
@@ -332,9 +339,11 @@ __global__ void __launch_bounds__(kBdAttThreads) bd_att_kernel(const LoopParams<
     // key t's rows into the cache (this thread's own entries)
     const int tl = (t - j0) - (ntiles - 1) * kBdTile;       // its row in the last tile
     if (has_t)
-        for (int i = threadIdx.x; i < hd; i += blockDim.x) {
-            const bool isk = i < hp;
-            const int d = 2 * (isk ? i : i - hp);
+        for (int i = threadIdx.x; i < nitems; i += blockDim.x) {
+            if (i < G * hp) continue;
+            const int k = i - G * hp;
+            const bool isk = k < hp;
+            const int d = 2 * (isk ? k : k - hp);
             float* dst = (isk ? p.kc : p.vc) + (cache_off + t) * hd + d;
             const float* row = isk ? krow : vrow;
             dst[0] = row[d];
@@ -345,25 +354,23 @@ __global__ void __launch_bounds__(kBdAttThreads) bd_att_kernel(const LoopParams<
 #pragma unroll
     for (int k = 0; k < kBdAttMaxO; k++) o[k] = 0.0f;
     for (int it = 0; it < ntiles; it++) {
-        if (it + 1 < ntiles) {
-            load_tile(it + 1);
-            cp_async_wait<1>();
-        } else {
-            cp_async_wait<0>();
-            if (has_t)                       // key t's rows (this thread's own entries)
-                for (int i = threadIdx.x; i < hd; i += blockDim.x) {
-                    const bool isk = i < hp;
-                    const int d = 2 * (isk ? i : i - hp);
-                    float* dst = (isk ? kt : vt) + (it & 1) * kBdTile * hd + tl * hd + d;
-                    const float* row = isk ? krow : vrow;
-                    dst[0] = row[d];
-                    dst[1] = row[d + 1];
-                }
-        }
+        load_tile(it + kBdRing - 1);         // into the buffer tile it - 1 used
+        cp_async_wait<kBdRing - 1>();        // this thread's copies of tile it have landed
+        if (has_t && it == ntiles - 1)       // key t's rows (this thread's own entries)
+            for (int i = threadIdx.x; i < nitems; i += blockDim.x) {
+                if (i < G * hp) continue;
+                const int k = i - G * hp;
+                const bool isk = k < hp;
+                const int d = 2 * (isk ? k : k - hp);
+                float* dst = (isk ? kt : vt) + (it % kBdRing) * kBdTile * hd + tl * hd + d;
+                const float* row = isk ? krow : vrow;
+                dst[0] = row[d];
+                dst[1] = row[d + 1];
+            }
         __syncthreads();                     // tile it (and q, stats) visible to all
         const int nt = min(kBdTile, j1 - j0 - it * kBdTile);
-        const float* ks = kt + (it & 1) * kBdTile * hd;
-        const float* vs = vt + (it & 1) * kBdTile * hd;
+        const float* ks = kt + (it % kBdRing) * kBdTile * hd;
+        const float* vs = vt + (it % kBdRing) * kBdTile * hd;
         // scores: a thread per (head, key); its key row is read starting at
         // element (j mod hd) so that neighbouring keys fall in different banks
         for (int e = threadIdx.x; e < G * nt; e += blockDim.x) {
@@ -424,7 +431,7 @@ __global__ void __launch_bounds__(kBdAttThreads) bd_att_kernel(const LoopParams<
                 o[k] = o[k] * ra[h] + acc;
             }
         }
-        __syncthreads();                     // buffer (it & 1) is refilled next
+        __syncthreads();                     // buffer it % kBdRing is refilled next
     }
     const bool combine = nsplit > 1;
 #pragma unroll
@@ -464,6 +471,272 @@ __global__ void __launch_bounds__(kBdAttThreads) bd_att_kernel(const LoopParams<
             num += w * ldcg(p.part_o + (pb + s2) * hd + d);
         }
         p.att[(size_t)b * p.D + (g * G + h) * hd + d] = num / den;
+    }
+    if (threadIdx.x == 0) p.att_cnt[b * p.K + g] = 0u;
+}
+
+// The same attention with a lane per key, for head_dim 32 or 64 and at
+// most kBdWMaxG query heads per KV head.  A CTA of kBdWWarps warps takes one
+// (sequence, KV head, key split) unit; warp w takes the split's 32-key
+// chunks w, w + kBdWWarps, ...  Per chunk, the chunk's K and V rows stream
+// into the warp's shared-memory tiles by cp.async (coalesced; K rows padded
+// by 4 floats so that a lane reading its own key's row hits distinct banks),
+// each lane scores its key against the G queries (broadcast reads), the warp
+// updates its online softmax per head with shuffles, then P.V reads the
+// probabilities four keys at a time and V as one HD/32-float piece per lane
+// and key.  The warps' states merge in shared
+// memory in warp order, then as in bd_att_kernel (direct output, or split
+// partials merged by the last split to finish).  Key t's K and V rows are
+// built from the QKV partials and written to the cache before any warp
+// reads them.
+constexpr int kBdWWarps = 4;
+constexpr int kBdWMaxG = 4;
+
+// q [G][HD], then per warp: K tile [32][HD + 4], V tile [32][HD] and
+// probabilities [kBdWMaxG][32]; the merge reuses the tiles; flag at the end
+__host__ __device__ inline size_t bd_attw_warp_floats(int hd) { return 32 * (hd + 4) + 32 * (size_t)hd + kBdWMaxG * 32; }
+__host__ __device__ inline size_t bd_attw_smem(int G, int hd) {
+    return ((size_t)G * hd + (size_t)kBdWWarps * bd_attw_warp_floats(hd) + 4) * 4;
+}
+
+template <typename WT, int HD>
+__global__ void __launch_bounds__(kBdWWarps * 32) bd_attw_kernel(const LoopParams<WT> p, BdLists L, int l, int t,
+                                                                 int klen, const float* qkvp, int nq) {
+    static_assert(HD == 32 || HD == 64, "a lane holds HD/32 output dimensions");
+    constexpr int E = HD / 32;
+    constexpr int Q4 = HD / 4;
+    extern __shared__ __align__(16) float smem_f[];
+    const int nkeys = t + 1;
+    const int nsplit = (nkeys + klen - 1) / klen;
+    const int u = blockIdx.x;
+    const int G = p.G;
+    const int s = u % nsplit;
+    const int g = (u / nsplit) % p.K;
+    const int b = u / (nsplit * p.K);
+    if (b >= p.B) return;
+    const int j0 = s * klen, j1 = min(nkeys, j0 + klen);
+    const size_t cache_off = (((size_t)l * p.Bcap + b) * p.K + g) * p.cap;
+    const float* kbase = p.kc + cache_off * HD;
+    const float* vbase = p.vc + cache_off * HD;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    constexpr int KLD = HD + 4;                           // K tile row stride
+    float* qs = smem_f;                                   // [G][HD]
+    float* wk = qs + G * HD + warp * bd_attw_warp_floats(HD);   // this warp's K tile
+    float* wv = wk + 32 * KLD;                            // this warp's V tile
+    float* wp = wv + 32 * HD;                             // this warp's probabilities
+    int* flag = reinterpret_cast<int*>(smem_f + G * HD + kBdWWarps * bd_attw_warp_floats(HD));
+    {
+        uint32_t dyn = 0;
+        asm volatile("mov.u32 %0, %%dynamic_smem_size;" : "=r"(dyn));
+        int bad = 0;
+        if ((size_t)dyn < bd_attw_smem(G, HD)) bad = 11;
+        else if (b >= p.Bcap || l < 0 || l >= p.L || p.hd != HD || G > kBdWMaxG) bad = 12;
+        else if (nkeys > p.cap || j1 <= j0 || s >= p.max_split) bad = 13;
+        else if (nq > kBdMaxParts || (nq > 0 && t >= p.rope_len)) bad = 14;
+        if (bad) {
+            if (threadIdx.x == 0) {
+                atomicMax(L.base + 3, bad);
+                atomicMax(p.status, (int)ST_DEVICE);
+            }
+            return;
+        }
+    }
+    pdl_wait();
+    pdl_trigger();
+    if (!L.act_fwd()[b]) return;                          // block-uniform
+    const bool has_t = nq > 0 && s == nsplit - 1;
+    constexpr int HP = HD / 2;
+    if (nq > 0) {
+        // q pairs, then (for the unit holding key t) K and V pairs: sums of
+        // the partials in slice order, RoPE on q and K; key t's rows go to
+        // the cache, where the warps read them below
+        const float* pb = qkvp + (size_t)b * p.Q;
+        const size_t pst = (size_t)p.B * p.Q;
+        const float2* rot = p.rope + (size_t)t * HP;
+        const int nitems = G * HP + (has_t ? HD : 0);
+        for (int i = threadIdx.x; i < nitems; i += blockDim.x) {
+            int col;
+            bool rope = true;
+            float* dst;
+            if (i < G * HP) {
+                const int h = i / HP, pr = i - h * HP;
+                col = (g * G + h) * HD + 2 * pr;
+                dst = qs + h * HD + 2 * pr;
+            } else {
+                const int k = i - G * HP;
+                const bool isk = k < HP;
+                const int pr = isk ? k : k - HP;
+                col = (isk ? p.H + g : p.H + p.K + g) * HD + 2 * pr;
+                dst = (isk ? p.kc : p.vc) + (cache_off + t) * HD + 2 * pr;
+                rope = isk;
+            }
+            float x0 = 0.0f, x1 = 0.0f;
+#pragma unroll
+            for (int r = 0; r < kBdMaxParts; r++)
+                if (r < nq) {
+                    const float2 v = __ldcg(reinterpret_cast<const float2*>(pb + r * pst + col));
+                    x0 += v.x;
+                    x1 += v.y;
+                }
+            if (rope) {
+                const float2 r = rot[(col % HD) / 2];
+                const float y0 = x0 * r.x - x1 * r.y, y1 = x0 * r.y + x1 * r.x;
+                x0 = y0;
+                x1 = y1;
+            }
+            dst[0] = x0;
+            dst[1] = x1;
+        }
+        if (has_t) __threadfence();                       // key t's rows before any warp reads them
+    } else {
+        for (int i = threadIdx.x; i < G * HD; i += blockDim.x)
+            qs[i] = ldcg(p.q + (size_t)b * p.D + (size_t)g * G * HD + i);
+    }
+    __syncthreads();
+    const float scale = 1.0f / sqrtf((float)HD);
+    float m[kBdWMaxG], lsum[kBdWMaxG], o[kBdWMaxG][E];
+#pragma unroll
+    for (int h = 0; h < kBdWMaxG; h++) {
+        m[h] = -INFINITY;
+        lsum[h] = 0.0f;
+#pragma unroll
+        for (int e = 0; e < E; e++) o[h][e] = 0.0f;
+    }
+    const int nchunks = (j1 - j0 + 31) / 32;
+    for (int c = warp; c < nchunks; c += kBdWWarps) {
+        const int key0 = j0 + 32 * c;
+        const int nv = min(32, j1 - key0);               // warp-uniform
+        // this chunk's K and V rows -> the warp's tiles (16-byte pieces, coalesced)
+        const float* ksrc = kbase + (size_t)key0 * HD;
+        const float* vsrc = vbase + (size_t)key0 * HD;
+        for (int e = lane; e < nv * Q4; e += 32) {
+            const int r = e / Q4, c4 = e - r * Q4;
+            cp_async16(wk + r * KLD + 4 * c4, ksrc + 4 * e);
+            cp_async16(wv + 4 * e, vsrc + 4 * e);
+        }
+        cp_async_commit();
+        cp_async_wait<0>();
+        __syncwarp();                                     // the tiles are visible to the warp
+        // scores: lane = key
+        const bool valid = lane < nv;
+        const float* krow = wk + (valid ? lane : 0) * KLD;
+        float4 k4[Q4];
+#pragma unroll
+        for (int i = 0; i < Q4; i++) k4[i] = *reinterpret_cast<const float4*>(krow + 4 * i);
+        float sv[kBdWMaxG];
+#pragma unroll
+        for (int h = 0; h < kBdWMaxG; h++) {
+            sv[h] = -INFINITY;
+            if (h < G) {
+                const float4* q4p = reinterpret_cast<const float4*>(qs + h * HD);
+                float a = 0.0f;
+#pragma unroll
+                for (int i = 0; i < Q4; i++) {
+                    const float4 q = q4p[i];
+                    a += q.x * k4[i].x + q.y * k4[i].y + q.z * k4[i].z + q.w * k4[i].w;
+                }
+                if (valid) sv[h] = a * scale;
+            }
+        }
+        // online softmax per head
+#pragma unroll
+        for (int h = 0; h < kBdWMaxG; h++) {
+            if (h < G) {
+                const float mnew = fmaxf(m[h], warp_max(sv[h]));
+                const float alpha = expf(m[h] - mnew);
+                const float pv = valid ? expf(sv[h] - mnew) : 0.0f;
+                lsum[h] = lsum[h] * alpha + warp_sum(pv);
+                m[h] = mnew;
+#pragma unroll
+                for (int e = 0; e < E; e++) o[h][e] *= alpha;
+                wp[h * 32 + lane] = pv;
+            }
+        }
+        __syncwarp();                                     // probabilities visible to the warp
+        // P.V: lane owns dimensions [E * lane, E * lane + E)
+        for (int j = 0; j < nv; j += 4) {
+#pragma unroll
+            for (int h = 0; h < kBdWMaxG; h++) {
+                if (h < G) {
+                    const float4 p4 = *reinterpret_cast<const float4*>(wp + h * 32 + j);
+                    const float pj[4] = {p4.x, p4.y, p4.z, p4.w};
+#pragma unroll
+                    for (int jj = 0; jj < 4; jj++) {
+                        if (j + jj < nv) {
+                            const float* vr = wv + (j + jj) * HD + E * lane;
+#pragma unroll
+                            for (int e = 0; e < E; e++) o[h][e] += pj[jj] * vr[e];
+                        }
+                    }
+                }
+            }
+        }
+        __syncwarp();                                     // the tile is refilled by the next chunk
+    }
+    // merge the warps' states in warp order
+    __syncthreads();
+    float* ms = qs + G * HD;                              // [kBdWWarps][G] max, then sums, then outputs
+    float* ls = ms + kBdWWarps * kBdWMaxG;
+    float* os = ls + kBdWWarps * kBdWMaxG;                // [kBdWWarps][G][HD]
+#pragma unroll
+    for (int h = 0; h < kBdWMaxG; h++) {
+        if (h < G) {
+            if (lane == 0) {
+                ms[warp * kBdWMaxG + h] = m[h];
+                ls[warp * kBdWMaxG + h] = lsum[h];
+            }
+#pragma unroll
+            for (int e = 0; e < E; e++) os[(warp * G + h) * HD + E * lane + e] = o[h][e];
+        }
+    }
+    __syncthreads();
+    const bool combine = nsplit > 1;
+    for (int i = threadIdx.x; i < G * HD; i += blockDim.x) {
+        const int h = i / HD, d = i - h * HD;
+        float M = -INFINITY;
+        for (int w = 0; w < kBdWWarps; w++) M = fmaxf(M, ms[w * kBdWMaxG + h]);
+        float num = 0.0f, den = 0.0f;
+        for (int w = 0; w < kBdWWarps; w++) {
+            const float mw = ms[w * kBdWMaxG + h];
+            if (mw == -INFINITY) continue;                // a warp without keys
+            const float wgt = expf(mw - M);
+            den += wgt * ls[w * kBdWMaxG + h];
+            num += wgt * os[(w * G + h) * HD + d];
+        }
+        if (!combine) {
+            p.att[(size_t)b * p.D + (g * G + h) * HD + d] = num / den;
+        } else {
+            const size_t pi = ((size_t)b * p.H + g * G + h) * p.max_split + s;
+            p.part_o[pi * HD + d] = num;
+            if (d == 0) {
+                p.part_m[pi] = M;
+                p.part_l[pi] = den;
+            }
+        }
+    }
+    if (!combine) return;
+    // the last split to finish merges (flash-decoding reduction)
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        const unsigned prev = atomicAdd(&p.att_cnt[b * p.K + g], 1u);
+        *flag = prev == (unsigned)nsplit - 1;
+    }
+    __syncthreads();
+    if (!*flag) return;
+    __threadfence();
+    for (int i = threadIdx.x; i < G * HD; i += blockDim.x) {
+        const int h = i / HD, d = i - h * HD;
+        const size_t pb2 = ((size_t)b * p.H + g * G + h) * p.max_split;
+        float M = -INFINITY;
+        for (int s2 = 0; s2 < nsplit; s2++) M = fmaxf(M, ldcg(p.part_m + pb2 + s2));
+        float num = 0.0f, den = 0.0f;
+        for (int s2 = 0; s2 < nsplit; s2++) {
+            const float w = expf(ldcg(p.part_m + pb2 + s2) - M);
+            den += w * ldcg(p.part_l + pb2 + s2);
+            num += w * ldcg(p.part_o + (pb2 + s2) * HD + d);
+        }
+        p.att[(size_t)b * p.D + (g * G + h) * HD + d] = num / den;
     }
     if (threadIdx.x == 0) p.att_cnt[b * p.K + g] = 0u;
 }

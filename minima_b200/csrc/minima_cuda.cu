@@ -1102,7 +1102,11 @@ mc_status run_batched(mc_session* s, mc::LoopParams<WT>& p) {
         if (st) return st;
         s->bd_maps_ok = true;
     }
-    const size_t att_smem = mc::bd_att_smem(m->H / m->K, m->hd);
+    // attention: a lane per key for head_dim 32/64 and G <= kBdWMaxG, else
+    // the shared-memory tile kernel
+    const int G = m->H / m->K;
+    const bool att_lane = (m->hd == 32 || m->hd == 64) && G <= mc::kBdWMaxG;
+    const size_t att_smem = att_lane ? mc::bd_attw_smem(G, m->hd) : mc::bd_att_smem(G, m->hd);
     if (att_smem > (size_t)optin)
         return fail(MC_ERR_UNSUPPORTED, "batched attention needs %zu B of shared memory", att_smem);
     cudaStream_t st = s->stream;
@@ -1114,6 +1118,8 @@ mc_status run_batched(mc_session* s, mc::LoopParams<WT>& p) {
     if (dev < 64 && !((attr_set >> dev) & 1ull)) {
         // the device maximum, shared by every session on the device
         MC_CUDA(cudaFuncSetAttribute(mc::bd_att_kernel<WT>, cudaFuncAttributeMaxDynamicSharedMemorySize, optin));
+        MC_CUDA(cudaFuncSetAttribute(mc::bd_attw_kernel<WT, 32>, cudaFuncAttributeMaxDynamicSharedMemorySize, optin));
+        MC_CUDA(cudaFuncSetAttribute(mc::bd_attw_kernel<WT, 64>, cudaFuncAttributeMaxDynamicSharedMemorySize, optin));
         MC_CUDA(cudaFuncSetAttribute(mc::bd_sample_kernel<WT>, cudaFuncAttributeMaxDynamicSharedMemorySize, optin));
         attr_set |= 1ull << dev;
     }
@@ -1145,7 +1151,9 @@ mc_status run_batched(mc_session* s, mc::LoopParams<WT>& p) {
         // twice over (the device's position is t too)
         const int pairs = p.B * m->K, nkeys = t + 1;
         const int want = std::max(1, (2 * sms + pairs - 1) / pairs);
-        const int klen = std::max(mc::kBdTile, (nkeys + want - 1) / want + mc::kBdTile - 1) / mc::kBdTile * mc::kBdTile;
+        // (a multiple of the tile, and at least kSplitLen keys so that the
+        // splits fit the max_split partial slots)
+        const int klen = std::max(mc::kSplitLen, ((nkeys + want - 1) / want + mc::kBdTile - 1) / mc::kBdTile * mc::kBdTile);
         const unsigned att_units = (unsigned)pairs * (unsigned)((nkeys + klen - 1) / klen);
         // every GEMM leaves K-slice partials in bd_part; the kernel after it
         // sums them in slice order (norm: residual; attention: q and the
@@ -1158,9 +1166,14 @@ mc_status run_batched(mc_session* s, mc::LoopParams<WT>& p) {
             g.layer = l;
             g.N = m->Q; g.K = m->D; g.ldc = m->Q; g.ksplit = ks_qkv;
             if ((e = tc_dec_launch<KD, mc::EPI_PART, BN, 8>(xm[0], wm[0], wm[0], g, st)) != cudaSuccess) break;
-            if ((e = launch_pdl(mc::bd_att_kernel<WT>, dim3(att_units), dim3(mc::kBdAttThreads), att_smem, st, p,
-                                L, l, t, klen, (const float*)s->bd_part, ks_qkv)) != cudaSuccess)
-                break;
+            if (att_lane)
+                e = launch_pdl(m->hd == 32 ? mc::bd_attw_kernel<WT, 32> : mc::bd_attw_kernel<WT, 64>,
+                               dim3(att_units), dim3(mc::kBdWWarps * 32), att_smem, st, p, L, l, t, klen,
+                               (const float*)s->bd_part, ks_qkv);
+            else
+                e = launch_pdl(mc::bd_att_kernel<WT>, dim3(att_units), dim3(mc::kBdAttThreads), att_smem, st, p,
+                               L, l, t, klen, (const float*)s->bd_part, ks_qkv);
+            if (e != cudaSuccess) break;
             if (kB16 && (e = launch_pdl(mc::bd_cvt_kernel<WT>, dim3(p.B), dim3(mc::kThreads), 0, st, p, L,
                                         s->bd_att16)) != cudaSuccess)
                 break;
