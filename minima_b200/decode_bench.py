@@ -7,7 +7,8 @@ random-init Minima-architecture model.
         --vocab 16384 --batch 64 --prompt 256 --new 32
 
 Each arm runs generate_with_options for the batch (prompts of --prompt
-seeded non-special ids, --new greedy tokens); the per-step device time comes
+seeded non-special ids, --new tokens, greedy unless --top-k/--temperature
+say otherwise; sequence b is seeded b + 1); the per-step device time comes
 from the %globaltimer stamps the kernels write at each step start
 (mc_last_step_times), median over the decode steps after the first 8 (the
 first half when there are fewer than 16) of the last of --iters calls.
@@ -38,19 +39,21 @@ def main():
     ap.add_argument("--iters", type=int, default=2)
     ap.add_argument("--bf16", action="store_true", help="bf16 weights (tensor-core arm: kind::f16)")
     ap.add_argument("--arms", default="default,tcgen05")
+    ap.add_argument("--temperature", type=float, default=1.0)
+    ap.add_argument("--top-k", type=int, default=1, help="1 = greedy; config 3 samples with T=0.8, k=40")
     args = ap.parse_args()
     cap = args.prompt + args.new + 8
     hm = M.HostModel(args.vocab, args.dim, args.layers, args.heads, args.ffn, cap, seed=2, bf16=args.bf16)
     dm = M.DeviceModel(hm, M.MC_WEIGHTS_BF16 if args.bf16 else M.MC_WEIGHTS_F32)
     prompts = np.random.default_rng(5).integers(4, args.vocab, (args.batch, args.prompt), dtype=np.uint16)
-    opts = M.options(top_k=1, max_new_tokens=args.new)
+    opts = M.options(temperature=args.temperature, top_k=args.top_k, max_new_tokens=args.new)
     K = M.kv_head_count(args.heads)
     hd = args.dim // args.heads
     Q = args.dim + 2 * K * hd
     w = 2 if args.bf16 else 4
     weights = (args.layers * (Q * args.dim + args.dim * args.dim + 3 * args.ffn * args.dim)
                + args.vocab * args.dim) * w
-    t_mid = args.prompt + args.new // 2
+    t_mid = args.prompt + args.new // 2        # the mean position of the decode steps
     kv = args.batch * args.layers * 2 * t_mid * K * hd * 4
     for arm in args.arms.split(","):
         if arm == "tcgen05":
