@@ -19,23 +19,24 @@ DIMS = O.Dims(4096, 128, 2, 4, 512, 256)
 BD_ATOL, BD_RTOL = 1e-2, 1e-2
 
 
-def run(monkeypatch, bf16, batch, steps, **kw):
+def run(monkeypatch, bf16, batch, steps, dims=DIMS, lens=None, cap=128, **kw):
     monkeypatch.setenv("MINIMA_CUDA_DECODE", "tcgen05")
-    hm = M.HostModel(DIMS.vocab, DIMS.dim, DIMS.n_layers, DIMS.n_heads, DIMS.ffn_dim, DIMS.max_seq,
+    hm = M.HostModel(dims.vocab, dims.dim, dims.n_layers, dims.n_heads, dims.ffn_dim, dims.max_seq,
                      seed=21, bf16=bf16)
-    orc = O.OrcModel(DIMS, 21, bf16=bf16)
-    lens = [20 + (b * 7) % 23 for b in range(batch)]          # ragged prompts
+    orc = O.OrcModel(dims, 21, bf16=bf16)
+    if lens is None:
+        lens = [20 + (b * 7) % 23 for b in range(batch)]      # ragged prompts
     prompts = np.zeros((batch, max(lens)), dtype=np.uint16)
     for b, n in enumerate(lens):
-        prompts[b, :n] = O.random_prompt(n, DIMS.vocab, 300 + b)
-    sess = M.Session(M.DeviceModel(hm, M.MC_WEIGHTS_BF16 if bf16 else M.MC_WEIGHTS_F32), batch, 128)
+        prompts[b, :n] = O.random_prompt(n, dims.vocab, 300 + b)
+    sess = M.Session(M.DeviceModel(hm, M.MC_WEIGHTS_BF16 if bf16 else M.MC_WEIGHTS_F32), batch, cap)
     opts = M.options(max_new_tokens=steps, **kw)
-    out, counts, st, _, trace = sess.generate(prompts, lens, 128, opts, list(range(1, batch + 1)),
+    out, counts, st, _, trace = sess.generate(prompts, lens, cap, opts, list(range(1, batch + 1)),
                                               trace_steps=steps)
     assert sess.last_kernel_name() == "mc::tc_gemm_kernel"
     worst, agree = 0.0, []
     for b in range(batch):
-        ids, _, _, ref_tr = orc.generate(prompts[b, :lens[b]], 128, 128, O.make_options(max_new_tokens=steps, **kw),
+        ids, _, _, ref_tr = orc.generate(prompts[b, :lens[b]], cap, cap, O.make_options(max_new_tokens=steps, **kw),
                                          b + 1, trace_steps=steps)
         got = out[b, lens[b]:counts[b]]
         want = ids[lens[b]:]
@@ -80,3 +81,23 @@ def test_batched_penalties_and_bans(gpu, monkeypatch):
                        frequency_penalty=0.5, presence_penalty=0.2, no_repeat_ngram_size=2)
     print(f"penalties: worst err/bound {worst:.3f}")
     assert sum(a == 10 for a in agree) >= 32
+
+
+def test_batched_head_dim_64_key_splits(gpu, monkeypatch):
+    """head_dim 64 (the lane-per-key attention kernel's HD = 64 build) with
+    ~300-key contexts over 24 sequences: too few (sequence, KV head) pairs
+    to fill the GPU, so each pair's keys are split and merged."""
+    dims = O.Dims(4096, 256, 2, 4, 512, 512)
+    lens = [280 + (b * 5) % 31 for b in range(24)]
+    worst, agree = run(monkeypatch, False, 24, 6, dims=dims, lens=lens, cap=512, top_k=1)
+    print(f"hd=64 splits: worst err/bound {worst:.3f}")
+    assert sum(a == 6 for a in agree) >= 21
+
+
+def test_batched_wide_query_groups(gpu, monkeypatch):
+    """7 heads share one KV head (G = 7 > the lane-per-key kernel's limit):
+    the shared-memory tile attention kernel."""
+    dims = O.Dims(4096, 224, 2, 7, 512, 256)
+    worst, agree = run(monkeypatch, False, 33, 6, dims=dims, top_k=1)
+    print(f"G=7: worst err/bound {worst:.3f}")
+    assert sum(a == 6 for a in agree) >= 30
