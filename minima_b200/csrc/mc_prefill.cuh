@@ -262,7 +262,9 @@ __global__ void __launch_bounds__(256) pf_attention_kernel(PrefillArgs a, int la
             float o0 = o_acc[k][0] * corr, o1 = o_acc[k][1] * corr;
             for (int j = 0; j < kn; j++) {
                 const float pj = __shfl_sync(0xffffffffu, j < 32 ? p0 : p1, j & 31);
-                o0 += pj * Vs[j * hd + lane];
+                // lanes past head_dim own no output (and row kn - 1 + lane
+                // would fall past the tile when head_dim < 32)
+                if (lane < hd) o0 += pj * Vs[j * hd + lane];
                 if (lane + 32 < hd) o1 += pj * Vs[j * hd + lane + 32];
             }
             o_acc[k][0] = o0;

@@ -5,7 +5,9 @@
  * two builds read the same stdin and must print the same transcript.
  *
  *   chat_e2e console   chat_run_console (chat.c:179-366): the CHAT_* line
- *                      protocol the GUI drives, on stdin/stdout
+ *                      protocol the GUI drives, on stdin/stdout, with greedy
+ *                      replies (a penalty, n-gram bans and a stop sequence)
+ *   chat_e2e sampled   the same with seeded top-k/top-p sampling
  *   chat_e2e bench     chat_run_generation_benchmark (chat.c:457-556):
  *                      greedy and seeded sampled continuations of fixed
  *                      prompts plus their repetition statistics
@@ -23,7 +25,9 @@
 #include "tokenizer.h"
 #include "util.h"
 
+#include <stdbool.h>
 #include <stdio.h>
+#include <stdlib.h>
 #include <string.h>
 
 static const char kCorpus[] =
@@ -44,7 +48,16 @@ static const char kCorpus[] =
     "Human: thank you for the help.\n"
     "Assistant: you are welcome, have a pleasant day.\n";
 
+/* The drop-in's error text (absent from the reference build). */
+extern const char* minima_cuda_last_error(void) __attribute__((weak));
+
+static void report_drop_in_error(void) {
+    if (minima_cuda_last_error && minima_cuda_last_error()[0])
+        fprintf(stderr, "drop-in: %s\n", minima_cuda_last_error());
+}
+
 int main(int argc, char** argv) {
+    atexit(report_drop_in_error);
     const char* mode = argc > 1 ? argv[1] : "console";
     static Tokenizer tok;
     Arena model_arena, tok_arena, cache_arena;
@@ -70,14 +83,15 @@ int main(int argc, char** argv) {
         return 2;
     }
     if (strcmp(mode, "bench") == 0) return chat_run_generation_benchmark(&model, &tok, &cache) ? 0 : 1;
+    const bool sampled = strcmp(mode, "sampled") == 0;
     ChatOptions options;
     memset(&options, 0, sizeof(options));
     options.seed = 7;
     options.sampling_seed = 99;          /* fixed: the reply does not depend on clock() */
-    options.temperature = 0.8f;
-    options.top_p = 0.9f;
+    options.temperature = sampled ? 0.8f : 1.0f;
+    options.top_p = sampled ? 0.9f : 1.0f;
     options.repetition_penalty = 1.1f;
-    options.top_k = 40;
+    options.top_k = sampled ? 40 : 1;
     options.max_new_tokens = 48;
     options.no_repeat_ngram_size = 3;
     options.stop_sequence = "\nHuman:";
