@@ -56,7 +56,8 @@ __device__ __forceinline__ float transform_value(float logit, unsigned count, bo
         value = __fsub_rn(value, __fadd_rn(__fmul_rn(s.freq, c), s.pres));
     }
     if (banned) value = -INFINITY;
-    return __fdiv_rn(value, s.temperature);
+    // x / 1 is x exactly (infinities and NaN included): skip the division
+    return s.temperature == 1.0f ? value : __fdiv_rn(value, s.temperature);
 }
 
 __device__ __forceinline__ unsigned order_key(float v) {

@@ -598,51 +598,88 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
         for (int j = 0; j < 32; j++) tilep[(size_t)(sq + j) * TLD + part * TC_BM + fl] = v[j];
     }
     __syncthreads();
-    // a warp per sequence, lanes over feature pairs
-    for (int r = warp; r < BN && store; r += TC_THREADS / 32) {
-        const int m = s0 + r;
-        if (m >= g.M) break;                               // sequences ascend: warp-uniform
-        if (g.act && !g.act[m]) continue;
-        const float* src = tilep + (size_t)r * TLD;
-        if constexpr (EPI == TCE_STORE) {
-            if (g.head) {
-                const bool greedy = g.sa.top_k == 1;
-                const int nwords = (g.N + 31) >> 5;
-                float* crow = g.C + (size_t)m * g.ldc;
+    bool row_epilogue = true;
+    if constexpr (EPI == TCE_STORE) {
+        if (g.head) {
+            // lm_head: a thread per (sequence, 32-id chunk) of the tile
+            // (float4 reads of its row, conflict-free for 8 consecutive
+            // sequences), then the chunks' greedy partials are combined per
+            // sequence; better() is a total order, so the result does not
+            // depend on how the ids are grouped
+            row_epilogue = false;
+            constexpr int NQ = TC_BM / 32;
+            static_assert((size_t)BN * TLD * 4 + (size_t)NQ * BN * 8 <= (size_t)STAGES * STAGE,
+                          "tile and chunk partials fit the ring");
+            float* bestv = tilep + (size_t)BN * TLD;
+            int* besti = reinterpret_cast<int*>(bestv + NQ * BN);
+            const bool greedy = g.sa.top_k == 1;
+            const int nwords = (g.N + 31) >> 5;
+            for (int it = threadIdx.x; it < NQ * BN; it += TC_THREADS) {
+                const int r = it % BN, q = it / BN;
+                const int m = s0 + r;
+                const int n0 = f0 + 32 * q;
                 float bv = -INFINITY;
                 int bi = 0x7fffffff;
+                if (store && m < g.M && (!g.act || g.act[m]) && n0 < g.N) {
+                    const float* src = tilep + (size_t)r * TLD + 32 * q;
+                    float* crow = g.C + (size_t)m * g.ldc;
+                    const unsigned bw = greedy && g.sa.ngram > 0 ? __ldg(g.banned + (size_t)m * nwords + (n0 >> 5)) : 0u;
 #pragma unroll
-                for (int c = 2 * lane; c < TC_BM; c += 64) {
-                    const float2 uv = *reinterpret_cast<const float2*>(src + c);
-                    const float x2[2] = {uv.x, uv.y};
+                    for (int j4 = 0; j4 < 32; j4 += 4) {
+                        const float4 v4 = *reinterpret_cast<const float4*>(src + j4);
+                        float x[4] = {v4.x, v4.y, v4.z, v4.w};
 #pragma unroll
-                    for (int j = 0; j < 2; j++) {
-                        const int n = f0 + c + j;
-                        if (n >= g.N) break;
-                        const float x = n < 4 ? -INFINITY : x2[j];
-                        crow[n] = x;
+                        for (int j = 0; j < 4; j++)
+                            if (n0 + j4 + j < 4) x[j] = -INFINITY;   // generate.c:580-581
+                        if (n0 + j4 + 3 < g.N && (g.ldc & 3) == 0) {
+                            *reinterpret_cast<float4*>(crow + n0 + j4) = make_float4(x[0], x[1], x[2], x[3]);
+                        } else {
+#pragma unroll
+                            for (int j = 0; j < 4; j++)
+                                if (n0 + j4 + j < g.N) crow[n0 + j4 + j] = x[j];
+                        }
                         if (greedy) {
-                            const unsigned cnt = g.sa.pen_active ? __ldg(g.counts + (size_t)m * g.N + n) : 0u;
-                            const bool ban = g.sa.ngram > 0 &&
-                                             ((__ldg(g.banned + (size_t)m * nwords + (n >> 5)) >> (n & 31)) & 1u);
-                            const float tv = transform_value(x, cnt, ban, g.sa);
-                            if (better(tv, n, bv, bi)) {
-                                bv = tv;
-                                bi = n;
+#pragma unroll
+                            for (int j = 0; j < 4; j++) {
+                                const int n = n0 + j4 + j;
+                                if (n >= g.N) break;
+                                const unsigned cnt = g.sa.pen_active ? __ldg(g.counts + (size_t)m * g.N + n) : 0u;
+                                const bool ban = (bw >> (n & 31)) & 1u;
+                                const float tv = transform_value(x[j], cnt, ban, g.sa);
+                                if (better(tv, n, bv, bi)) {
+                                    bv = tv;
+                                    bi = n;
+                                }
                             }
                         }
                     }
                 }
-                if (greedy) {
-                    warp_argmax(bv, bi);
-                    if (lane == 0) {
-                        g.amax_v[(size_t)m * tiles_f + f0 / TC_BM] = bv;
-                        g.amax_i[(size_t)m * tiles_f + f0 / TC_BM] = bi;
-                    }
-                }
-                continue;
+                bestv[q * BN + r] = bv;
+                besti[q * BN + r] = bi;
             }
+            __syncthreads();
+            if (greedy && store)
+                for (int r = threadIdx.x; r < BN; r += TC_THREADS) {
+                    const int m = s0 + r;
+                    if (m >= g.M || (g.act && !g.act[m])) continue;
+                    float bv = bestv[r];
+                    int bi = besti[r];
+                    for (int q = 1; q < NQ; q++)
+                        if (better(bestv[q * BN + r], besti[q * BN + r], bv, bi)) {
+                            bv = bestv[q * BN + r];
+                            bi = besti[q * BN + r];
+                        }
+                    g.amax_v[(size_t)m * tiles_f + f0 / TC_BM] = bv;
+                    g.amax_i[(size_t)m * tiles_f + f0 / TC_BM] = bi;
+                }
         }
+    }
+    // a warp per sequence, lanes over feature pairs
+    for (int r = warp; r < BN && store && row_epilogue; r += TC_THREADS / 32) {
+        const int m = s0 + r;
+        if (m >= g.M) break;                               // sequences ascend: warp-uniform
+        if (g.act && !g.act[m]) continue;
+        const float* src = tilep + (size_t)r * TLD;
 #pragma unroll
         for (int c = 2 * lane; c < TC_BM; c += 64) {
             if (f0 + c >= g.N) break;
