@@ -541,10 +541,31 @@ __global__ void __launch_bounds__(kBdWWarps * 32) bd_attw_kernel(const LoopParam
             return;
         }
     }
+    const bool has_t = nq > 0 && s == nsplit - 1;
+    const int nchunks = (j1 - j0 + 31) / 32;
+    // K and V rows [r0, r1) of chunk c -> this warp's tiles (16-byte pieces, coalesced)
+    auto issue = [&](int c, int r0, int r1) {
+        const float* ksrc = kbase + (size_t)(j0 + 32 * c) * HD;
+        const float* vsrc = vbase + (size_t)(j0 + 32 * c) * HD;
+        for (int e = r0 * Q4 + lane; e < r1 * Q4; e += 32) {
+            const int r = e / Q4, c4 = e - r * Q4;
+            cp_async16(wk + r * KLD + 4 * c4, ksrc + 4 * e);
+            cp_async16(wv + 4 * e, vsrc + 4 * e);
+        }
+        cp_async_commit();
+    };
+    // Each warp's first chunk holds rows written at earlier steps (key t,
+    // built below, is held back), so it is requested before waiting for
+    // the previous kernel.
+    const int nv0 = warp < nchunks ? min(32, j1 - (j0 + 32 * warp)) : 0;
+    const bool t_first = has_t && warp < nchunks && j0 + 32 * warp + nv0 - 1 == t;
+    if (warp < nchunks) issue(warp, 0, nv0 - (t_first ? 1 : 0));
     pdl_wait();
     pdl_trigger();
-    if (!L.act_fwd()[b]) return;                          // block-uniform
-    const bool has_t = nq > 0 && s == nsplit - 1;
+    if (!L.act_fwd()[b]) {                                // block-uniform
+        cp_async_wait<0>();
+        return;
+    }
     constexpr int HP = HD / 2;
     if (nq > 0) {
         // q pairs, then (for the unit holding key t) K and V pairs: sums of
@@ -602,19 +623,11 @@ __global__ void __launch_bounds__(kBdWWarps * 32) bd_attw_kernel(const LoopParam
 #pragma unroll
         for (int e = 0; e < E; e++) o[h][e] = 0.0f;
     }
-    const int nchunks = (j1 - j0 + 31) / 32;
     for (int c = warp; c < nchunks; c += kBdWWarps) {
         const int key0 = j0 + 32 * c;
         const int nv = min(32, j1 - key0);               // warp-uniform
-        // this chunk's K and V rows -> the warp's tiles (16-byte pieces, coalesced)
-        const float* ksrc = kbase + (size_t)key0 * HD;
-        const float* vsrc = vbase + (size_t)key0 * HD;
-        for (int e = lane; e < nv * Q4; e += 32) {
-            const int r = e / Q4, c4 = e - r * Q4;
-            cp_async16(wk + r * KLD + 4 * c4, ksrc + 4 * e);
-            cp_async16(wv + 4 * e, vsrc + 4 * e);
-        }
-        cp_async_commit();
+        if (c != warp) issue(c, 0, nv);
+        else if (t_first) issue(c, nv - 1, nv);          // key t, now in the cache
         cp_async_wait<0>();
         __syncwarp();                                     // the tiles are visible to the warp
         // scores: lane = key
