@@ -153,22 +153,64 @@ __device__ void topk_replay(int V, int k, SamplerSmem& sm, int& n_out) {
 __device__ bool topk_fast(int V, int k, SamplerSmem& sm) {
     unsigned prefix = 0, mask = 0;
     int remaining = k;
+    const int lane = threadIdx.x & 31;
     for (int shift = 24; shift >= 0; shift -= 8) {
         for (int i = threadIdx.x; i < 256; i += blockDim.x) sm.hist[i] = 0;
         __syncthreads();
-        for (int i = threadIdx.x; i < V; i += blockDim.x) {
-            const unsigned key = order_key(sm.vals[i]);
-            if ((key & mask) == prefix) atomicAdd(&sm.hist[(key >> shift) & 255u], 1u);
+        // histogram of the next byte among keys under the prefix: lanes with
+        // the same byte add once (logits share their high bytes, so plain
+        // per-key atomics would queue on a few bins)
+        for (int i0 = 0; i0 < V; i0 += blockDim.x) {
+            const int i = i0 + threadIdx.x;
+            unsigned bin = 256u;                         // no bin
+            if (i < V) {
+                const unsigned key = order_key(sm.vals[i]);
+                if ((key & mask) == prefix) bin = (key >> shift) & 255u;
+            }
+            const unsigned peers = __match_any_sync(0xffffffffu, bin);
+            if (bin < 256u && lane == __ffs(peers) - 1) atomicAdd(&sm.hist[bin], (unsigned)__popc(peers));
         }
         __syncthreads();
-        if (threadIdx.x == 0) {
-            int cum = 0, bin = 255;
-            for (; bin > 0; --bin) {
-                if (cum + (int)sm.hist[bin] >= remaining) break;
-                cum += (int)sm.hist[bin];
+        // the first bin, from 255 down to 1, whose cumulative count reaches
+        // `remaining` (else bin 0): warp 0, eight bins per lane, lane 0
+        // holding the highest
+        if (threadIdx.x < 32) {
+            int c[8], tot = 0;
+#pragma unroll
+            for (int j = 0; j < 8; j++) {
+                c[j] = (int)sm.hist[255 - 8 * lane - j];
+                tot += c[j];
             }
-            sm.misc[2] = bin;
-            sm.misc[3] = remaining - cum;
+            int incl = tot;
+#pragma unroll
+            for (int off = 1; off < 32; off <<= 1) {
+                const int y = __shfl_up_sync(0xffffffffu, incl, off);
+                if (lane >= off) incl += y;
+            }
+            int cum = incl - tot, found = -1, rem = 0, before0 = 0;
+#pragma unroll
+            for (int j = 0; j < 8; j++) {
+                const int bin = 255 - 8 * lane - j;
+                if (bin == 0) before0 = cum;
+                if (bin >= 1 && found < 0 && cum + c[j] >= remaining) {
+                    found = bin;
+                    rem = remaining - cum;
+                }
+                cum += c[j];
+            }
+            const unsigned hit = __ballot_sync(0xffffffffu, found >= 0);
+            if (hit) {
+                const int src = __ffs(hit) - 1;
+                found = __shfl_sync(0xffffffffu, found, src);
+                rem = __shfl_sync(0xffffffffu, rem, src);
+            } else {
+                found = 0;
+                rem = remaining - __shfl_sync(0xffffffffu, before0, 31);
+            }
+            if (lane == 0) {
+                sm.misc[2] = found;
+                sm.misc[3] = rem;
+            }
         }
         __syncthreads();
         prefix |= (unsigned)sm.misc[2] << shift;
@@ -190,15 +232,17 @@ __device__ bool topk_fast(int V, int k, SamplerSmem& sm) {
     __syncthreads();
     const int cnt = sm.misc[4];
     if (cnt != k) return false;  // ties at the threshold
-    // bitonic sort of k (<= 256) entries by value descending, padded to 256
-    for (int i = threadIdx.x + k; i < 256; i += blockDim.x) {
+    // bitonic sort of the k entries padded to the next power of two
+    int npad = 2;
+    while (npad < k) npad <<= 1;
+    for (int i = threadIdx.x + k; i < npad; i += blockDim.x) {
         sm.kv[i] = -INFINITY;
         sm.ki[i] = 0x7fffffff;
     }
     __syncthreads();
-    for (int size = 2; size <= 256; size <<= 1) {
+    for (int size = 2; size <= npad; size <<= 1) {
         for (int stride = size >> 1; stride > 0; stride >>= 1) {
-            for (int i = threadIdx.x; i < 256; i += blockDim.x) {
+            for (int i = threadIdx.x; i < npad; i += blockDim.x) {
                 const int j = i ^ stride;
                 if (j > i) {
                     const bool desc = (i & size) == 0;
