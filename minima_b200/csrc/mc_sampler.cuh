@@ -97,13 +97,27 @@ __device__ bool sampler_fill(const float* logits, const unsigned* counts,
     if (threadIdx.x == 0) sm.misc[0] = 0;
     __syncthreads();
     int nan_seen = 0;
-    for (int i = threadIdx.x; i < V; i += blockDim.x) {
-        const float lg = ldcg(logits + i);
-        const unsigned c = s.pen_active ? __ldcg(counts + i) : 0u;
-        const bool ban = use_bans && ((__ldcg(banned + (i >> 5)) >> (i & 31)) & 1u);
-        const float v = transform_value(lg, c, ban, s);
-        sm.vals[i] = v;
-        nan_seen |= (v != v);
+    // eight elements per thread and round: their loads are all in flight
+    // before the first is transformed
+    constexpr int U = 8;
+    for (int i0 = threadIdx.x; i0 < V; i0 += U * blockDim.x) {
+        float lg[U];
+        unsigned c[U], w[U];
+#pragma unroll
+        for (int u = 0; u < U; u++) {
+            const int i = i0 + u * blockDim.x;
+            lg[u] = i < V ? ldcg(logits + i) : 0.0f;
+            c[u] = s.pen_active && i < V ? __ldcg(counts + i) : 0u;
+            w[u] = use_bans && i < V ? __ldcg(banned + (i >> 5)) : 0u;
+        }
+#pragma unroll
+        for (int u = 0; u < U; u++) {
+            const int i = i0 + u * blockDim.x;
+            if (i >= V) break;
+            const float v = transform_value(lg[u], c[u], (w[u] >> (i & 31)) & 1u, s);
+            sm.vals[i] = v;
+            nan_seen |= (v != v);
+        }
     }
     if (__syncthreads_or(nan_seen)) return true;
     return false;
@@ -147,19 +161,54 @@ __device__ void topk_replay(int V, int k, SamplerSmem& sm, int& n_out) {
     n_out = sm.misc[1];
 }
 
-// Fast exact top-k: radix-select the k-th largest key; succeed only when the
-// k largest values are distinct and strictly above the rest.  On success
-// sm.kv/sm.ki hold them in descending order and the function returns true.
-__device__ bool topk_fast(int V, int k, SamplerSmem& sm) {
+// Sort sm.kv/sm.ki[0, n) by value descending, then id ascending (bitonic,
+// padded to the next power of two), and check the order is exact: the k
+// first values distinct and, when n > k, strictly above the (k+1)-th.
+__device__ bool topk_sort_check(int n, int k, SamplerSmem& sm) {
+    int npad = 2;
+    while (npad < n) npad <<= 1;
+    for (int i = threadIdx.x + n; i < npad; i += blockDim.x) {
+        sm.kv[i] = -INFINITY;
+        sm.ki[i] = 0x7fffffff;
+    }
+    __syncthreads();
+    for (int size = 2; size <= npad; size <<= 1) {
+        for (int stride = size >> 1; stride > 0; stride >>= 1) {
+            for (int i = threadIdx.x; i < npad; i += blockDim.x) {
+                const int j = i ^ stride;
+                if (j > i) {
+                    const bool desc = (i & size) == 0;
+                    const unsigned ki_ = order_key(sm.kv[i]), kj_ = order_key(sm.kv[j]);
+                    const bool swap = desc ? (ki_ < kj_ || (ki_ == kj_ && sm.ki[i] > sm.ki[j]))
+                                           : (ki_ > kj_ || (ki_ == kj_ && sm.ki[i] < sm.ki[j]));
+                    if (swap) {
+                        const float tv = sm.kv[i]; sm.kv[i] = sm.kv[j]; sm.kv[j] = tv;
+                        const int ti = sm.ki[i]; sm.ki[i] = sm.ki[j]; sm.ki[j] = ti;
+                    }
+                }
+            }
+            __syncthreads();
+        }
+    }
+    int dup = 0;
+    for (int i = threadIdx.x; i < k && i + 1 < n; i += blockDim.x)
+        dup |= (order_key(sm.kv[i]) == order_key(sm.kv[i + 1]));
+    return !__syncthreads_or(dup);
+}
+
+// Exact top-k by radix select of the k-th largest key; succeeds only when
+// the k largest values are distinct and strictly above the rest.  On
+// success sm.kv/sm.ki hold them in descending order.
+__device__ bool topk_radix(int V, int k, SamplerSmem& sm) {
     unsigned prefix = 0, mask = 0;
     int remaining = k;
     const int lane = threadIdx.x & 31;
     for (int shift = 24; shift >= 0; shift -= 8) {
         for (int i = threadIdx.x; i < 256; i += blockDim.x) sm.hist[i] = 0;
         __syncthreads();
-        // histogram of the next byte among keys under the prefix: lanes with
-        // the same byte add once (logits share their high bytes, so plain
-        // per-key atomics would queue on a few bins)
+        // histogram of the next byte among keys under the prefix: the lanes
+        // that share lane 0's byte add once (logits share their high bytes,
+        // so plain per-key atomics would queue on a few bins)
         for (int i0 = 0; i0 < V; i0 += blockDim.x) {
             const int i = i0 + threadIdx.x;
             unsigned bin = 256u;                         // no bin
@@ -167,8 +216,10 @@ __device__ bool topk_fast(int V, int k, SamplerSmem& sm) {
                 const unsigned key = order_key(sm.vals[i]);
                 if ((key & mask) == prefix) bin = (key >> shift) & 255u;
             }
-            const unsigned peers = __match_any_sync(0xffffffffu, bin);
-            if (bin < 256u && lane == __ffs(peers) - 1) atomicAdd(&sm.hist[bin], (unsigned)__popc(peers));
+            const unsigned lead = __shfl_sync(0xffffffffu, bin, 0);
+            const unsigned same = __ballot_sync(0xffffffffu, bin == lead);
+            if (lane == 0 && lead < 256u) atomicAdd(&sm.hist[lead], (unsigned)__popc(same));
+            if (bin != lead && bin < 256u) atomicAdd(&sm.hist[bin], 1u);
         }
         __syncthreads();
         // the first bin, from 255 down to 1, whose cumulative count reaches
@@ -232,36 +283,99 @@ __device__ bool topk_fast(int V, int k, SamplerSmem& sm) {
     __syncthreads();
     const int cnt = sm.misc[4];
     if (cnt != k) return false;  // ties at the threshold
-    // bitonic sort of the k entries padded to the next power of two
-    int npad = 2;
-    while (npad < k) npad <<= 1;
-    for (int i = threadIdx.x + k; i < npad; i += blockDim.x) {
-        sm.kv[i] = -INFINITY;
-        sm.ki[i] = 0x7fffffff;
+    return topk_sort_check(k, k, sm);
+}
+
+// Fast exact top-k.  The values are bucketed by their distance below the
+// maximum (256 linear buckets spanning the finite range; bucket order is
+// monotone in the value, so the first buckets holding k values contain the
+// k largest); those candidates are collected and sorted.  More than 256
+// candidates: the radix path.  Succeeds only when the k largest values are
+// distinct and strictly above the rest; sm.kv/sm.ki then hold them in
+// descending order.
+__device__ bool topk_fast(int V, int k, SamplerSmem& sm) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int nw = (blockDim.x + 31) >> 5;
+    float mx = -INFINITY, mn = INFINITY;
+    for (int i = threadIdx.x; i < V; i += blockDim.x) {
+        const float v = sm.vals[i];
+        mx = fmaxf(mx, v);
+        if (v != -INFINITY) mn = fminf(mn, v);
+    }
+    for (int off = 16; off > 0; off >>= 1) {
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+        mn = fminf(mn, __shfl_xor_sync(0xffffffffu, mn, off));
+    }
+    for (int i = threadIdx.x; i < 256; i += blockDim.x) sm.hist[i] = 0;
+    if (lane == 0) {
+        sm.kv[warp] = mx;
+        sm.kv[32 + warp] = mn;
+    }
+    if (threadIdx.x == 0) sm.misc[4] = 0;
+    __syncthreads();
+    mx = -INFINITY;
+    mn = INFINITY;
+    for (int w = 0; w < nw; w++) {
+        mx = fmaxf(mx, sm.kv[w]);
+        mn = fminf(mn, sm.kv[32 + w]);
+    }
+    __syncthreads();                                     // kv is reused below
+    if (!(mx > mn) || !isfinite(mx) || !isfinite(mn)) return topk_radix(V, k, sm);
+    const float sc = 256.0f / (mx - mn);
+    auto bucket = [&](float v) -> int {
+        const float d = mx - v;
+        if (!(d > 0.0f)) return 0;
+        const float f = d * sc;
+        return f >= 255.0f ? 255 : (int)f;
+    };
+    for (int i = threadIdx.x; i < V; i += blockDim.x) atomicAdd(&sm.hist[bucket(sm.vals[i])], 1u);
+    __syncthreads();
+    // first bucket whose cumulative count reaches k: warp 0, eight per lane
+    if (threadIdx.x < 32) {
+        int c[8], tot = 0;
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+            c[j] = (int)sm.hist[8 * lane + j];
+            tot += c[j];
+        }
+        int incl = tot;
+#pragma unroll
+        for (int off = 1; off < 32; off <<= 1) {
+            const int y = __shfl_up_sync(0xffffffffu, incl, off);
+            if (lane >= off) incl += y;
+        }
+        int cum = incl - tot, found = -1;
+#pragma unroll
+        for (int j = 0; j < 8; j++) {
+            cum += c[j];
+            if (found < 0 && cum >= k) found = 8 * lane + j;
+        }
+        const unsigned hit = __ballot_sync(0xffffffffu, found >= 0);
+        const int bmax = hit ? __shfl_sync(0xffffffffu, found, __ffs(hit) - 1) : 255;
+        if (lane == 0) sm.misc[5] = bmax;
     }
     __syncthreads();
-    for (int size = 2; size <= npad; size <<= 1) {
-        for (int stride = size >> 1; stride > 0; stride >>= 1) {
-            for (int i = threadIdx.x; i < npad; i += blockDim.x) {
-                const int j = i ^ stride;
-                if (j > i) {
-                    const bool desc = (i & size) == 0;
-                    const unsigned ki_ = order_key(sm.kv[i]), kj_ = order_key(sm.kv[j]);
-                    const bool swap = desc ? (ki_ < kj_ || (ki_ == kj_ && sm.ki[i] > sm.ki[j]))
-                                           : (ki_ > kj_ || (ki_ == kj_ && sm.ki[i] < sm.ki[j]));
-                    if (swap) {
-                        const float tv = sm.kv[i]; sm.kv[i] = sm.kv[j]; sm.kv[j] = tv;
-                        const int ti = sm.ki[i]; sm.ki[i] = sm.ki[j]; sm.ki[j] = ti;
-                    }
-                }
+    const int bmax = sm.misc[5];
+    // collect the candidates (a warp reserves its slots at once)
+    for (int i0 = 0; i0 < V; i0 += blockDim.x) {
+        const int i = i0 + threadIdx.x;
+        const bool take = i < V && bucket(sm.vals[i]) <= bmax;
+        const unsigned bal = __ballot_sync(0xffffffffu, take);
+        int base = 0;
+        if (lane == 0 && bal) base = atomicAdd(&sm.misc[4], __popc(bal));
+        base = __shfl_sync(0xffffffffu, base, 0);
+        if (take) {
+            const int slot = base + __popc(bal & ((1u << lane) - 1u));
+            if (slot < 256) {
+                sm.kv[slot] = sm.vals[i];
+                sm.ki[slot] = i;
             }
-            __syncthreads();
         }
     }
-    int dup = 0;
-    for (int i = threadIdx.x; i + 1 < k; i += blockDim.x)
-        dup |= (order_key(sm.kv[i]) == order_key(sm.kv[i + 1]));
-    return !__syncthreads_or(dup);
+    __syncthreads();
+    const int cnt = sm.misc[4];
+    if (cnt > 256) return topk_radix(V, k, sm);
+    return topk_sort_check(cnt, k, sm);
 }
 
 // Tail of generate.c:469-515 on thread 0.  Returns the id; advances rng
