@@ -97,6 +97,38 @@ __device__ bool sampler_fill(const float* logits, const unsigned* counts,
     if (threadIdx.x == 0) sm.misc[0] = 0;
     __syncthreads();
     int nan_seen = 0;
+    if ((V & 3) == 0) {
+        // four consecutive ids per load, eight loads per thread in flight
+        constexpr int U = 8;
+        const int V4 = V >> 2;
+        for (int q0 = threadIdx.x; q0 < V4; q0 += U * blockDim.x) {
+            float4 lg[U];
+            uint4 c[U];
+            unsigned w[U];
+#pragma unroll
+            for (int u = 0; u < U; u++) {
+                const int q = q0 + u * blockDim.x;
+                lg[u] = q < V4 ? ldcg4(logits + 4 * q) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+                c[u] = s.pen_active && q < V4 ? __ldcg(reinterpret_cast<const uint4*>(counts) + q)
+                                              : make_uint4(0u, 0u, 0u, 0u);
+                w[u] = use_bans && q < V4 ? __ldcg(banned + ((4 * q) >> 5)) : 0u;
+            }
+#pragma unroll
+            for (int u = 0; u < U; u++) {
+                const int q = q0 + u * blockDim.x;
+                if (q >= V4) break;
+                const int i = 4 * q;
+                float4 v;
+                v.x = transform_value(lg[u].x, c[u].x, (w[u] >> (i & 31)) & 1u, s);
+                v.y = transform_value(lg[u].y, c[u].y, (w[u] >> ((i + 1) & 31)) & 1u, s);
+                v.z = transform_value(lg[u].z, c[u].z, (w[u] >> ((i + 2) & 31)) & 1u, s);
+                v.w = transform_value(lg[u].w, c[u].w, (w[u] >> ((i + 3) & 31)) & 1u, s);
+                *reinterpret_cast<float4*>(sm.vals + i) = v;
+                nan_seen |= (v.x != v.x) | (v.y != v.y) | (v.z != v.z) | (v.w != v.w);
+            }
+        }
+        return __syncthreads_or(nan_seen) != 0;
+    }
     // eight elements per thread and round: their loads are all in flight
     // before the first is transformed
     constexpr int U = 8;
@@ -297,10 +329,17 @@ __device__ bool topk_fast(int V, int k, SamplerSmem& sm) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int nw = (blockDim.x + 31) >> 5;
     float mx = -INFINITY, mn = INFINITY;
-    for (int i = threadIdx.x; i < V; i += blockDim.x) {
-        const float v = sm.vals[i];
+    auto extent = [&](float v) {
         mx = fmaxf(mx, v);
         if (v != -INFINITY) mn = fminf(mn, v);
+    };
+    if ((V & 3) == 0) {
+        for (int q = threadIdx.x; q < (V >> 2); q += blockDim.x) {
+            const float4 v = *reinterpret_cast<const float4*>(sm.vals + 4 * q);
+            extent(v.x); extent(v.y); extent(v.z); extent(v.w);
+        }
+    } else {
+        for (int i = threadIdx.x; i < V; i += blockDim.x) extent(sm.vals[i]);
     }
     for (int off = 16; off > 0; off >>= 1) {
         mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
@@ -328,7 +367,17 @@ __device__ bool topk_fast(int V, int k, SamplerSmem& sm) {
         const float f = d * sc;
         return f >= 255.0f ? 255 : (int)f;
     };
-    for (int i = threadIdx.x; i < V; i += blockDim.x) atomicAdd(&sm.hist[bucket(sm.vals[i])], 1u);
+    if ((V & 3) == 0) {
+        for (int q = threadIdx.x; q < (V >> 2); q += blockDim.x) {
+            const float4 v = *reinterpret_cast<const float4*>(sm.vals + 4 * q);
+            atomicAdd(&sm.hist[bucket(v.x)], 1u);
+            atomicAdd(&sm.hist[bucket(v.y)], 1u);
+            atomicAdd(&sm.hist[bucket(v.z)], 1u);
+            atomicAdd(&sm.hist[bucket(v.w)], 1u);
+        }
+    } else {
+        for (int i = threadIdx.x; i < V; i += blockDim.x) atomicAdd(&sm.hist[bucket(sm.vals[i])], 1u);
+    }
     __syncthreads();
     // first bucket whose cumulative count reaches k: warp 0, eight per lane
     if (threadIdx.x < 32) {
