@@ -207,18 +207,18 @@ __device__ void lc_issue_layer(const ClusterParams& cp, const CSlice& sl, LcStat
 __device__ void lc_norm(const float* x, float* xn, const float* scale, const int* list, int n,
                         int D, float* red) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    // a warp per sequence: sum of squares, then that sequence's row, so one
+    // CTA barrier closes the phase
     for (int i = warp; i < n; i += kWarps) {
         const float* xr = x + list[i] * D;
+        float* xo = xn + list[i] * D;
         float ss = 0.0f;
         for (int k = lane; k < D; k += 32) ss += xr[k] * xr[k];
         ss = warp_sum(ss);
-        if (lane == 0) red[i] = 1.0f / sqrtf(ss / (float)D + 1e-5f);
+        const float inv = 1.0f / sqrtf(ss / (float)D + 1e-5f);
+        for (int k = lane; k < D; k += 32) xo[k] = xr[k] * inv * scale[k];
     }
-    __syncthreads();
-    for (int i = 0; i < n; i++) {
-        const int b = list[i];
-        for (int k = threadIdx.x; k < D; k += blockDim.x) xn[b * D + k] = x[b * D + k] * red[i] * scale[k];
-    }
+    (void)red;
     __syncthreads();
 }
 
