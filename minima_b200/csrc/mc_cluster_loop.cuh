@@ -613,12 +613,14 @@ __device__ bool lc_layer(const ClusterParams& cp, const CSlice& sl, LcState& S,
     const float* rms1 = w + slice_floats(sl, D, F);
     const float* rms2 = rms1 + D;
 
-    // Attention units are (sequence, KV head, key split); keys are split
-    // when there are fewer (sequence, KV head) pairs than CTAs.  The first
-    // K/V tile of this CTA's first unit is requested now so that its
-    // transfer overlaps the QKV phase.
+    // Attention units are (sequence, KV head, key split).  A unit's warps
+    // take its keys 32 at a time, so keys are split over CTAs only past
+    // kWarps * 32 keys per unit (and only while there are idle CTAs): below
+    // that a split adds a merge after the cluster barrier and saves nothing.
+    // The first K/V tile of this CTA's first unit is requested now so that
+    // its transfer overlaps the QKV phase.
     const int nkeys = t + 1;
-    const int ns = min(nkeys, max(1, cs / (nf * K)));
+    const int ns = min(max(1, cs / (nf * K)), (nkeys + kWarps * 32 - 1) / (kWarps * 32));
     const int per = (nkeys + ns - 1) / ns;
     const int units = nf * K * ns;
     if (crank < units && threadIdx.x == 0) {
