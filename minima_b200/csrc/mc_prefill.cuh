@@ -290,6 +290,164 @@ __global__ void __launch_bounds__(256) pf_attention_kernel(PrefillArgs a, int la
     }
 }
 
+// The same causal attention with register tiles, for head_dim 16, 32 or 64
+// and G * QT <= 128 query rows per block.  256 threads as 16 x 16: thread
+// (tr, tc) holds rows tr + 16 i (i < 8) and, per 64-key tile, keys
+// tc + 16 j (j < 4) of the scores, and the same rows x dimensions
+// [HD/16 tc, HD/16 (tc + 1)) of the output, so a score costs one FMA per
+// dimension against float4 shared-memory reads shared by 4 x 8 products.
+// Row r is head r / QT of the block's KV head at position qt0 + r % QT.
+// Per key tile: scores, a per-row online softmax (the 16 threads of a row
+// reduce with shuffles), P through shared memory, then P.V.
+constexpr int PF_RT = 128;                    // rows per block
+constexpr int PF_PLD = PF_KT + 4;             // row stride of the probability tile
+
+template <int HD>
+__global__ void __launch_bounds__(256) pf_attention_tile_kernel(PrefillArgs a, int layer, int QT) {
+    constexpr int E = HD / 16;                // output dimensions per thread
+    constexpr int LD = HD + 4;                // padded row stride of the Q and K tiles
+    extern __shared__ __align__(16) float pfs[];
+    float* Qs = pfs;                          // [PF_RT][LD]
+    float* Ks = Qs + PF_RT * LD;              // [PF_KT][LD]
+    float* Vs = Ks + PF_KT * LD;              // [PF_KT][HD]
+    float* Ps = Vs + PF_KT * HD;              // [PF_RT][PF_PLD]
+    const int G = a.G, n = a.c1 - a.c0;
+    const int qt0 = a.c0 + blockIdx.x * QT;
+    const int g = blockIdx.y, b = blockIdx.z;
+    if (qt0 >= a.c1) return;
+    const int qt1 = min(a.c1, qt0 + QT);
+    const int rows = G * QT;
+    const int tr = threadIdx.x >> 4, tc = threadIdx.x & 15;
+    const float scale = 1.0f / sqrtf((float)HD);
+    // queries (zero rows past the block's)
+    for (int e = threadIdx.x; e < PF_RT * (HD / 4); e += blockDim.x) {
+        const int r = e / (HD / 4), c = e - r * (HD / 4);
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (r < rows) {
+            const int h = r / QT, t = qt0 + r % QT;
+            if (t < qt1)
+                v = *reinterpret_cast<const float4*>(a.QB + ((size_t)b * n + (t - a.c0)) * a.D +
+                                                     (g * G + h) * HD + 4 * c);
+        }
+        *reinterpret_cast<float4*>(Qs + r * LD + 4 * c) = v;
+    }
+    int pos[8];                               // position of each row, -1 past the block
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        const int r = tr + 16 * i;
+        const int t = qt0 + r % QT;
+        pos[i] = (r < rows && t < qt1) ? t : -1;
+    }
+    float m_run[8], l_run[8], o[8][E];
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        m_run[i] = -INFINITY;
+        l_run[i] = 0.0f;
+#pragma unroll
+        for (int e = 0; e < E; e++) o[i][e] = 0.0f;
+    }
+    const size_t cbase = (((size_t)layer * a.Bcap + b) * a.K + g) * a.cap;
+    const float* kg = a.kc + cbase * HD;
+    const float* vg = a.vc + cbase * HD;
+    for (int k0 = 0; k0 < qt1; k0 += PF_KT) {
+        const int kn = min(PF_KT, qt1 - k0);
+        __syncthreads();                      // the previous tile's readers are done
+        for (int e = threadIdx.x; e < PF_KT * (HD / 4); e += blockDim.x) {
+            const int j = e / (HD / 4), c = e - j * (HD / 4);
+            float4 kv4 = make_float4(0.f, 0.f, 0.f, 0.f), vv4 = kv4;
+            if (j < kn) {
+                kv4 = ldcg4(kg + (size_t)(k0 + j) * HD + 4 * c);
+                vv4 = ldcg4(vg + (size_t)(k0 + j) * HD + 4 * c);
+            }
+            *reinterpret_cast<float4*>(Ks + j * LD + 4 * c) = kv4;
+            *reinterpret_cast<float4*>(Vs + j * HD + 4 * c) = vv4;
+        }
+        __syncthreads();
+        // scores of rows tr + 16 i against keys tc + 16 j
+        float sacc[8][4];
+#pragma unroll
+        for (int i = 0; i < 8; i++)
+#pragma unroll
+            for (int j = 0; j < 4; j++) sacc[i][j] = 0.0f;
+#pragma unroll 4
+        for (int c = 0; c < HD / 4; c++) {
+            float4 kk[4];
+#pragma unroll
+            for (int j = 0; j < 4; j++) kk[j] = *reinterpret_cast<const float4*>(Ks + (tc + 16 * j) * LD + 4 * c);
+#pragma unroll
+            for (int i = 0; i < 8; i++) {
+                const float4 q = *reinterpret_cast<const float4*>(Qs + (tr + 16 * i) * LD + 4 * c);
+#pragma unroll
+                for (int j = 0; j < 4; j++)
+                    sacc[i][j] += q.x * kk[j].x + q.y * kk[j].y + q.z * kk[j].z + q.w * kk[j].w;
+            }
+        }
+        // causal mask, online softmax per row (the 16 threads of a row are
+        // lanes of one half-warp)
+#pragma unroll
+        for (int i = 0; i < 8; i++) {
+            float mx = -INFINITY;
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                const int key = k0 + tc + 16 * j;
+                const bool ok = tc + 16 * j < kn && pos[i] >= 0 && key <= pos[i];
+                sacc[i][j] = ok ? sacc[i][j] * scale : -INFINITY;
+                mx = fmaxf(mx, sacc[i][j]);
+            }
+#pragma unroll
+            for (int off = 8; off > 0; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+            const float mnew = fmaxf(m_run[i], mx);
+            const float corr = m_run[i] == -INFINITY ? 0.0f : expf(m_run[i] - mnew);
+            float ls = 0.0f;
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+                const float pj = sacc[i][j] == -INFINITY ? 0.0f : expf(sacc[i][j] - mnew);
+                Ps[(tr + 16 * i) * PF_PLD + tc + 16 * j] = pj;
+                ls += pj;
+            }
+#pragma unroll
+            for (int off = 8; off > 0; off >>= 1) ls += __shfl_xor_sync(0xffffffffu, ls, off);
+            l_run[i] = l_run[i] * corr + ls;
+            m_run[i] = mnew;
+#pragma unroll
+            for (int e = 0; e < E; e++) o[i][e] *= corr;
+        }
+        __syncthreads();
+        // P.V: rows tr + 16 i, dimensions E tc .. E tc + E - 1
+#pragma unroll 2
+        for (int j = 0; j < PF_KT; j += 4) {
+            float vv[4][E];
+#pragma unroll
+            for (int jj = 0; jj < 4; jj++)
+#pragma unroll
+                for (int e = 0; e < E; e++) vv[jj][e] = Vs[(j + jj) * HD + E * tc + e];
+#pragma unroll
+            for (int i = 0; i < 8; i++) {
+                const float4 p4 = *reinterpret_cast<const float4*>(Ps + (tr + 16 * i) * PF_PLD + j);
+#pragma unroll
+                for (int e = 0; e < E; e++)
+                    o[i][e] += p4.x * vv[0][e] + p4.y * vv[1][e] + p4.z * vv[2][e] + p4.w * vv[3][e];
+            }
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+        if (pos[i] < 0) continue;
+        const int r = tr + 16 * i, h = r / QT;
+        const size_t off = ((size_t)b * n + (pos[i] - a.c0)) * a.D + (g * G + h) * HD + E * tc;
+        const float inv = 1.0f / l_run[i];
+#pragma unroll
+        for (int e = 0; e < E; e++) {
+            a.ATT[off + e] = o[i][e] * inv;
+            if (a.ATT16) a.ATT16[off + e] = __float2bfloat16_rn(o[i][e] * inv);
+        }
+    }
+}
+
+__host__ inline size_t pf_attention_tile_smem(int hd) {
+    return ((size_t)PF_RT * (hd + 4) + (size_t)PF_KT * (hd + 4) + (size_t)PF_KT * hd + (size_t)PF_RT * PF_PLD) * 4;
+}
+
 __host__ inline size_t pf_attention_smem(int hd, int G, int QT) {
     return ((size_t)G * QT * hd + (size_t)PF_KT * (hd + 1) + (size_t)PF_KT * hd) * 4;
 }

@@ -942,10 +942,28 @@ mc_status run_prefill(mc_session* s, int batch, const uint16_t* prompts, int str
     const float* rms1 = m->norms;
     const float* rms2 = m->norms + (size_t)m->L * m->D;
     const int QT = std::max(1, 128 / a.G);
-    const size_t att_smem = mc::pf_attention_smem(m->hd, a.G, QT);
-    MC_CUDA(cudaFuncSetAttribute(mc::pf_attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 (int)att_smem));
+    // register-tiled attention for head_dim 16/32/64, else the row-per-warp kernel
+    const bool att_tile = m->hd == 16 || m->hd == 32 || m->hd == 64;
+    const size_t att_smem = att_tile ? mc::pf_attention_tile_smem(m->hd) : mc::pf_attention_smem(m->hd, a.G, QT);
+    if (att_tile)
+        MC_CUDA(cudaFuncSetAttribute(m->hd == 16 ? mc::pf_attention_tile_kernel<16>
+                                     : m->hd == 32 ? mc::pf_attention_tile_kernel<32>
+                                                   : mc::pf_attention_tile_kernel<64>,
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize, (int)att_smem));
+    else
+        MC_CUDA(cudaFuncSetAttribute(mc::pf_attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)att_smem));
     cudaStream_t st = s->stream;
+    const cudaStream_t st_ = st;
+    auto attention = [&](int l) {
+        const dim3 grid((a.chunk + QT - 1) / QT, m->K, batch);
+        switch (att_tile ? m->hd : 0) {
+        case 16: mc::pf_attention_tile_kernel<16><<<grid, 256, att_smem, st_>>>(a, l, QT); break;
+        case 32: mc::pf_attention_tile_kernel<32><<<grid, 256, att_smem, st_>>>(a, l, QT); break;
+        case 64: mc::pf_attention_tile_kernel<64><<<grid, 256, att_smem, st_>>>(a, l, QT); break;
+        default: mc::pf_attention_kernel<<<grid, 256, att_smem, st_>>>(a, l, QT); break;
+        }
+    };
     const size_t D = m->D, F = m->F, Q = m->Q;
     auto grid2 = [](int N, int M) { return dim3((N + mc::GBN - 1) / mc::GBN, (M + mc::GBM - 1) / mc::GBM); };
     for (int c0 = 0; c0 < Pf; c0 += kPrefillChunk) {
@@ -968,8 +986,7 @@ mc_status run_prefill(mc_session* s, int batch, const uint16_t* prompts, int str
                 g.N = m->Q; g.K = m->D; g.C = nullptr; g.ldc = 0;
                 e = tc_launch<KD, mc::EPI_QKV, 256>(mp[0], wm[0], wm[0], g, st);
                 if (e != cudaSuccess) return fail(MC_ERR_CUDA, "tcgen05 prefill: %s", cudaGetErrorString(e));
-                mc::pf_attention_kernel<<<dim3((a.chunk + QT - 1) / QT, m->K, batch), 256, att_smem, st>>>(
-                    a, l, QT);
+                attention(l);
                 g.N = m->D; g.K = m->D; g.C = a.X; g.ldc = m->D;
                 e = tc_launch<KD, mc::EPI_RESID, 256>(mp[1], wm[1], wm[1], g, st);
                 if (e != cudaSuccess) return fail(MC_ERR_CUDA, "tcgen05 prefill: %s", cudaGetErrorString(e));
@@ -985,8 +1002,7 @@ mc_status run_prefill(mc_session* s, int batch, const uint16_t* prompts, int str
             }
             mc::pf_gemm_kernel<WT, mc::EPI_QKV><<<grid2(m->Q, M), 256, 0, st>>>(
                 a, a.XN, M, m->Q, m->D, wqkv + l * Q * D, nullptr, nullptr, 0, l);
-            mc::pf_attention_kernel<<<dim3((a.chunk + QT - 1) / QT, m->K, batch), 256, att_smem, st>>>(
-                a, l, QT);
+            attention(l);
             mc::pf_gemm_kernel<WT, mc::EPI_RESID><<<grid2(m->D, M), 256, 0, st>>>(
                 a, a.ATT, M, m->D, m->D, wproj + l * D * D, nullptr, a.X, m->D, l);
             mc::pf_norm_kernel<WT><<<(M + 7) / 8, 256, 0, st>>>(a, emb, rms2 + l * D, 0);
