@@ -418,9 +418,19 @@ __global__ void __launch_bounds__(256) pf_attention_tile_kernel(PrefillArgs a, i
         for (int j = 0; j < PF_KT; j += 4) {
             float vv[4][E];
 #pragma unroll
-            for (int jj = 0; jj < 4; jj++)
+            for (int jj = 0; jj < 4; jj++) {
+                const float* vr = Vs + (j + jj) * HD + E * tc;
+                if constexpr (E == 4) {
+                    const float4 v4 = *reinterpret_cast<const float4*>(vr);
+                    vv[jj][0] = v4.x; vv[jj][1] = v4.y; vv[jj][2] = v4.z; vv[jj][3] = v4.w;
+                } else if constexpr (E == 2) {
+                    const float2 v2 = *reinterpret_cast<const float2*>(vr);
+                    vv[jj][0] = v2.x; vv[jj][1] = v2.y;
+                } else {
 #pragma unroll
-                for (int e = 0; e < E; e++) vv[jj][e] = Vs[(j + jj) * HD + E * tc + e];
+                    for (int e = 0; e < E; e++) vv[jj][e] = vr[e];
+                }
+            }
 #pragma unroll
             for (int i = 0; i < 8; i++) {
                 const float4 p4 = *reinterpret_cast<const float4*>(Ps + (tr + 16 * i) * PF_PLD + j);
