@@ -190,10 +190,10 @@ mc_status mc_session_stream(mc_session* session, void** stream);
  * mc_generate_static — mc_generate that allocates nothing.  No counterpart
  * in the reference (whose decode runs on the host stack).
  *
- * For callers that cannot call cudaMalloc: code running while a CUDA graph
- * is being captured, hosts that carve their device memory up front from
- * their own pool, plugins that must not grow the device footprint after
- * start-up.  The caller passes device buffers for everything it owns:
+ * For callers that cannot call cudaMalloc: real-time hosts that must not
+ * take its cost (or the device-wide wait of a later cudaFree) mid-session,
+ * hosts that carve their device memory up front from their own pool,
+ * plugins that must not grow the device footprint after start-up.  The caller passes device buffers for everything it owns:
  *   w            dims plus DEVICE pointers to the nine fp32 weight arrays
  *                (layout as in mc_model_desc)
  *   prompts, out_ids, rng_states, out_counts   device pointers, as with

@@ -1587,10 +1587,10 @@ mc_status mc_session_stream(mc_session* s, void** stream) {
 // ===========================================================================
 // mc_generate_static: the token loop with no device allocation at all.
 //
-// For callers that cannot call cudaMalloc: code running while a CUDA graph is
-// being captured, hosts whose device memory is carved up up front by their
-// own pool, and plugins that must not grow the process's device footprint
-// after start-up.  Weights, prompts and outputs are the caller's device
+// For callers that cannot call cudaMalloc: real-time hosts that must not take
+// its cost (or the device-wide wait of a later cudaFree) mid-session, hosts
+// whose device memory is carved up front by their own pool, and plugins that
+// must not grow the process's device footprint after start-up.  Weights, prompts and outputs are the caller's device
 // buffers; everything else the loop needs (KV cache, activations, split
 // partials, counters, RoPE table, sequence table) lives in one file-scope
 // __device__ array of MC_STATIC_SCRATCH_BYTES, which every GPU that loads

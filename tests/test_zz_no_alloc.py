@@ -1,9 +1,9 @@
 """GPU: mc_generate_static, the entry point that allocates no device memory.
 
-Some callers cannot call cudaMalloc at all — code running while a CUDA graph
-is being captured, hosts that hand out device memory only from their own
-pre-carved pool, plugins that must not grow the device footprint once the
-host application is up.  mc_generate_static serves them: they pass their
+Some callers cannot call cudaMalloc at all — real-time hosts that must not
+take its cost (or the device-wide wait of a later cudaFree) mid-session, hosts
+that hand out device memory only from their own pre-carved pool, plugins
+that must not grow the device footprint once the host application is up.  mc_generate_static serves them: they pass their
 own device buffers for weights, prompts and outputs, and the KV cache and
 work buffers come from a fixed static array inside the library.
 
