@@ -7,6 +7,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <atomic>
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
@@ -366,17 +367,27 @@ extern "C" {
 
 const char* mc_last_error(void) { return g_err; }
 
+// The drop-in calls mc_init on every generate call, so the device check is
+// made once per device and with single attribute queries: a full
+// cudaGetDeviceProperties takes about 2.5 ms on B200.
+static std::atomic<bool> g_device_checked[64];
+
 mc_status mc_init(int device) {
     int n = 0;
     MC_CUDA(cudaGetDeviceCount(&n));
     if (device < 0 || device >= n) return fail(MC_ERR_INVALID, "device %d of %d", device, n);
     MC_CUDA(cudaSetDevice(device));
-    cudaDeviceProp prop;
-    MC_CUDA(cudaGetDeviceProperties(&prop, device));
-    if (prop.major != 10)
+    const bool cache = device < 64;
+    if (cache && g_device_checked[device].load(std::memory_order_acquire)) return MC_OK;
+    int major = 0, minor = 0, coop = 0;
+    MC_CUDA(cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, device));
+    MC_CUDA(cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, device));
+    MC_CUDA(cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, device));
+    if (major != 10)
         return fail(MC_ERR_UNSUPPORTED, "device %d is sm_%d%d; this build targets sm_100a", device,
-                    prop.major, prop.minor);
-    if (!prop.cooperativeLaunch) return fail(MC_ERR_UNSUPPORTED, "no cooperative launch");
+                    major, minor);
+    if (!coop) return fail(MC_ERR_UNSUPPORTED, "no cooperative launch");
+    if (cache) g_device_checked[device].store(true, std::memory_order_release);
     return MC_OK;
 }
 
