@@ -82,19 +82,31 @@ __global__ void __launch_bounds__(256) pf_norm_kernel(PrefillArgs a, const WT* t
 enum PfEpi { EPI_QKV = 0, EPI_RESID = 1, EPI_SWIGLU = 2, EPI_STORE = 3 };
 
 constexpr int GBM = 64, GBN = 64, GBK = 32;
+constexpr int kPfMaxSplit = 8;   // K slices of one output tile (gridDim.z)
 
 // C[M][N] = A[M][K] . W[N][K]^T with a fused epilogue.  For EPI_SWIGLU, W2 is
 // the gate matrix and the output is silu(A.W2) * (A.W); EPI_STORE writes
 // C as is (the lm_head of model_forward).  K % 4 == 0.
+//
+// The next K tile is read from global memory into registers while the
+// current one is multiplied.  With gridDim.z = ks > 1 (small M, where the
+// tiles alone leave most SMs idle) the K blocks are split in ks contiguous
+// slices: each CTA stores its partial tile in `part`, and the last CTA of a
+// tile to arrive (counter `cnt`, left at zero again for the next launch)
+// sums the slices in slice order 0..ks-1, so the result does not depend on
+// the arrival order, and applies the epilogue.
 template <typename WT, int EPI>
 __global__ void __launch_bounds__(256, 1) pf_gemm_kernel(PrefillArgs a, const float* A, int M, int N,
                                                       int Kd, const WT* W, const WT* W2, float* C,
-                                                      int ldc, int layer) {
+                                                      int ldc, int layer, float* part, unsigned* cnt) {
     constexpr int DUAL = EPI == EPI_SWIGLU ? 2 : 1;
     __shared__ __align__(16) float As[GBK][GBM + 4];
     __shared__ __align__(16) float Ws[DUAL][GBK][GBN + 4];
+    __shared__ unsigned s_last;
     const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
     const int m0 = blockIdx.y * GBM, n0 = blockIdx.x * GBN;
+    const int nk = (Kd + GBK - 1) / GBK, ks = gridDim.z, z = blockIdx.z;
+    const int kb0 = (int)((long long)nk * z / ks), kb1 = (int)((long long)nk * (z + 1) / ks);
     float acc[DUAL][4][4];
 #pragma unroll
     for (int d = 0; d < DUAL; d++)
@@ -102,32 +114,45 @@ __global__ void __launch_bounds__(256, 1) pf_gemm_kernel(PrefillArgs a, const fl
         for (int i = 0; i < 4; i++)
 #pragma unroll
             for (int j = 0; j < 4; j++) acc[d][i][j] = 0.0f;
-    for (int k0 = 0; k0 < Kd; k0 += GBK) {
-        // tiles: 64 rows x 32 k = 512 float4, two per thread, stored k-major
-        for (int e = threadIdx.x; e < GBM * GBK / 4; e += 256) {
+    // tiles: 64 rows x 32 k = 512 float4, two per thread, stored k-major
+    float4 ra[2];
+    float rw[DUAL][2][4];
+    auto fetch = [&](int k0) {
+#pragma unroll
+        for (int u = 0; u < 2; u++) {
+            const int e = threadIdx.x + 256 * u;
             const int r = e / (GBK / 4), kq = (e % (GBK / 4)) * 4;
             const int gm = m0 + r, gk = k0 + kq;
-            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (gm < M && gk < Kd) v = *reinterpret_cast<const float4*>(A + (size_t)gm * Kd + gk);
-            As[kq + 0][r] = v.x; As[kq + 1][r] = v.y; As[kq + 2][r] = v.z; As[kq + 3][r] = v.w;
-        }
+            ra[u] = gm < M && gk < Kd ? *reinterpret_cast<const float4*>(A + (size_t)gm * Kd + gk)
+                                      : make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-        for (int d = 0; d < DUAL; d++) {
-            const WT* Wd = d == 0 ? W : W2;
-            for (int e = threadIdx.x; e < GBN * GBK / 4; e += 256) {
-                const int r = e / (GBK / 4), kq = (e % (GBK / 4)) * 4;
-                const int gn = n0 + r, gk = k0 + kq;
-                float w4[4] = {0.f, 0.f, 0.f, 0.f};
+            for (int d = 0; d < DUAL; d++) {
+                const WT* Wd = d == 0 ? W : W2;
+                const int gn = n0 + r;
+#pragma unroll
+                for (int q = 0; q < 4; q++) rw[d][u][q] = 0.0f;
                 if (gn < N && gk < Kd) {
                     const WT* src = Wd + (size_t)gn * Kd + gk;
 #pragma unroll
-                    for (int q = 0; q < 4; q++) w4[q] = wload1(src + q);
+                    for (int q = 0; q < 4; q++) rw[d][u][q] = wload1(src + q);
                 }
-#pragma unroll
-                for (int q = 0; q < 4; q++) Ws[d][kq + q][r] = w4[q];
             }
         }
+    };
+    if (kb0 < kb1) fetch(kb0 * GBK);
+    for (int kb = kb0; kb < kb1; kb++) {
+#pragma unroll
+        for (int u = 0; u < 2; u++) {
+            const int e = threadIdx.x + 256 * u;
+            const int r = e / (GBK / 4), kq = (e % (GBK / 4)) * 4;
+            As[kq + 0][r] = ra[u].x; As[kq + 1][r] = ra[u].y; As[kq + 2][r] = ra[u].z; As[kq + 3][r] = ra[u].w;
+#pragma unroll
+            for (int d = 0; d < DUAL; d++)
+#pragma unroll
+                for (int q = 0; q < 4; q++) Ws[d][kq + q][r] = rw[d][u][q];
+        }
         __syncthreads();
+        if (kb + 1 < kb1) fetch((kb + 1) * GBK);   // in flight during the FMAs below
 #pragma unroll 8
         for (int kk = 0; kk < GBK; kk++) {
             const float4 av = *reinterpret_cast<const float4*>(&As[kk][ty * 4]);
@@ -143,6 +168,41 @@ __global__ void __launch_bounds__(256, 1) pf_gemm_kernel(PrefillArgs a, const fl
             }
         }
         __syncthreads();
+    }
+    if (ks > 1) {
+        // partial tiles thread-major: each thread writes and later reads its own 16 * DUAL floats
+        const int tile = blockIdx.y * gridDim.x + blockIdx.x, ntiles = gridDim.x * gridDim.y;
+        float4* mine = reinterpret_cast<float4*>(part) +
+                       (((size_t)z * ntiles + tile) * 256 + threadIdx.x) * (4 * DUAL);
+#pragma unroll
+        for (int d = 0; d < DUAL; d++)
+#pragma unroll
+            for (int i = 0; i < 4; i++)
+                mine[d * 4 + i] = make_float4(acc[d][i][0], acc[d][i][1], acc[d][i][2], acc[d][i][3]);
+        __threadfence();
+        __syncthreads();
+        if (threadIdx.x == 0) s_last = atomicAdd(cnt + tile, 1u) == (unsigned)(ks - 1);
+        __syncthreads();
+        if (!s_last) return;
+        __threadfence();
+#pragma unroll
+        for (int d = 0; d < DUAL; d++)
+#pragma unroll
+            for (int i = 0; i < 4; i++)
+#pragma unroll
+                for (int j = 0; j < 4; j++) acc[d][i][j] = 0.0f;
+        for (int sl = 0; sl < ks; sl++) {
+            const float4* ps = reinterpret_cast<const float4*>(part) +
+                               (((size_t)sl * ntiles + tile) * 256 + threadIdx.x) * (4 * DUAL);
+#pragma unroll
+            for (int d = 0; d < DUAL; d++)
+#pragma unroll
+                for (int i = 0; i < 4; i++) {
+                    const float4 v = __ldcg(ps + d * 4 + i);
+                    acc[d][i][0] += v.x; acc[d][i][1] += v.y; acc[d][i][2] += v.z; acc[d][i][3] += v.w;
+                }
+        }
+        if (threadIdx.x == 0) cnt[tile] = 0u;
     }
 #pragma unroll
     for (int i = 0; i < 4; i++) {

@@ -131,6 +131,9 @@ struct mc_session {
     float* bd_part;               // K-slice partials of the decode GEMMs
     size_t bd_part_floats;
     float* pf_logits;             // [pf_rows][V] lm_head scratch of mc_model_forward
+    float* pf_part;               // K-slice partial tiles of the CUDA-core prefill GEMMs
+    size_t pf_part_floats;
+    unsigned* pf_cnt;             // per-tile arrival counters of those GEMMs (kept at zero)
     __nv_bfloat16 *pf_xn16, *pf_att16, *pf_f16;   // bf16 GEMM inputs (tensor cores, bf16 weights)
     cudaEvent_t ev_mid;           // end of prefill
     int last_prefill_pos;         // positions prefilled by the last call
@@ -491,7 +494,7 @@ mc_status mc_session_destroy(mc_session* s) {
                     s->status, s->seq, s->prompts, s->out, s->stop, s->trace, s->stamps,
                     s->xfin, s->hgen, s->hsync, s->hpv, s->hpi,
                     s->pf_x, s->pf_xn, s->pf_q, s->pf_att, s->pf_f, s->pf_logits,
-                    s->pf_xn16, s->pf_att16, s->pf_f16, s->bd_lists, s->bd_xn,
+                    s->pf_xn16, s->pf_att16, s->pf_f16, s->pf_part, s->pf_cnt, s->bd_lists, s->bd_xn,
                     s->bd_xn16, s->bd_att16, s->bd_f16, s->bd_part};
     for (void* b : bufs) cudaFree(b);
     if (s->ev_mid) cudaEventDestroy(s->ev_mid);
@@ -977,6 +980,36 @@ mc_status run_prefill(mc_session* s, int batch, const uint16_t* prompts, int str
     };
     const size_t D = m->D, F = m->F, Q = m->Q;
     auto grid2 = [](int N, int M) { return dim3((N + mc::GBN - 1) / mc::GBN, (M + mc::GBM - 1) / mc::GBM); };
+    // CUDA-core GEMMs whose tiles leave SMs idle (few prompt rows) split K
+    // into up to kPfMaxSplit slices of at least two K blocks each.
+    auto with_split = [&](dim3 g, int Kd) {
+        const int tiles = (int)(g.x * g.y), nk = (Kd + mc::GBK - 1) / mc::GBK;
+        g.z = (unsigned)std::max(1, std::min({mc::kPfMaxSplit, nk / 2, (s->grid + tiles - 1) / tiles}));
+        return g;
+    };
+    if (!tc) {
+        size_t need = 0;
+        for (int c0 = 0; c0 < Pf; c0 += kPrefillChunk) {
+            const int M = batch * (std::min(Pf, c0 + kPrefillChunk) - c0);
+            const struct { int N, Kd, dual; } gemms[4] = {
+                {m->Q, m->D, 1}, {m->D, m->D, 1}, {m->F, m->D, 2}, {m->D, m->F, 1}};
+            for (const auto& g : gemms) {
+                const dim3 gr = with_split(grid2(g.N, M), g.Kd);
+                if (gr.z > 1) need = std::max(need, (size_t)gr.z * gr.x * gr.y * 256 * 16 * g.dual);
+            }
+        }
+        if (need > s->pf_part_floats) {
+            cudaFree(s->pf_part);
+            s->pf_part = nullptr;
+            s->pf_part_floats = 0;
+            MC_CUDA(cudaMalloc(&s->pf_part, need * 4));
+            s->pf_part_floats = need;
+        }
+        if (need > 0 && !s->pf_cnt) {
+            MC_CUDA(cudaMalloc(&s->pf_cnt, 1024 * sizeof(unsigned)));
+            MC_CUDA(cudaMemsetAsync(s->pf_cnt, 0, 1024 * sizeof(unsigned), st));
+        }
+    }
     for (int c0 = 0; c0 < Pf; c0 += kPrefillChunk) {
         a.c0 = c0;
         a.c1 = std::min(Pf, c0 + kPrefillChunk);
@@ -1011,16 +1044,17 @@ mc_status run_prefill(mc_session* s, int batch, const uint16_t* prompts, int str
                 launches += 7;
                 continue;
             }
-            mc::pf_gemm_kernel<WT, mc::EPI_QKV><<<grid2(m->Q, M), 256, 0, st>>>(
-                a, a.XN, M, m->Q, m->D, wqkv + l * Q * D, nullptr, nullptr, 0, l);
+            mc::pf_gemm_kernel<WT, mc::EPI_QKV><<<with_split(grid2(m->Q, M), m->D), 256, 0, st>>>(
+                a, a.XN, M, m->Q, m->D, wqkv + l * Q * D, nullptr, nullptr, 0, l, s->pf_part, s->pf_cnt);
             attention(l);
-            mc::pf_gemm_kernel<WT, mc::EPI_RESID><<<grid2(m->D, M), 256, 0, st>>>(
-                a, a.ATT, M, m->D, m->D, wproj + l * D * D, nullptr, a.X, m->D, l);
+            mc::pf_gemm_kernel<WT, mc::EPI_RESID><<<with_split(grid2(m->D, M), m->D), 256, 0, st>>>(
+                a, a.ATT, M, m->D, m->D, wproj + l * D * D, nullptr, a.X, m->D, l, s->pf_part, s->pf_cnt);
             mc::pf_norm_kernel<WT><<<(M + 7) / 8, 256, 0, st>>>(a, emb, rms2 + l * D, 0);
-            mc::pf_gemm_kernel<WT, mc::EPI_SWIGLU><<<grid2(m->F, M), 256, 0, st>>>(
-                a, a.XN, M, m->F, m->D, wup + l * F * D, wgate + l * F * D, a.FH, m->F, l);
-            mc::pf_gemm_kernel<WT, mc::EPI_RESID><<<grid2(m->D, M), 256, 0, st>>>(
-                a, a.FH, M, m->D, m->F, wdown + l * D * F, nullptr, a.X, m->D, l);
+            mc::pf_gemm_kernel<WT, mc::EPI_SWIGLU><<<with_split(grid2(m->F, M), m->D), 256, 0, st>>>(
+                a, a.XN, M, m->F, m->D, wup + l * F * D, wgate + l * F * D, a.FH, m->F, l, s->pf_part,
+                s->pf_cnt);
+            mc::pf_gemm_kernel<WT, mc::EPI_RESID><<<with_split(grid2(m->D, M), m->F), 256, 0, st>>>(
+                a, a.FH, M, m->D, m->F, wdown + l * D * F, nullptr, a.X, m->D, l, s->pf_part, s->pf_cnt);
             launches += 7;
         }
         if (logits) {
@@ -1037,7 +1071,7 @@ mc_status run_prefill(mc_session* s, int batch, const uint16_t* prompts, int str
                 if (e != cudaSuccess) return fail(MC_ERR_CUDA, "tcgen05 lm_head: %s", cudaGetErrorString(e));
             } else {
                 mc::pf_gemm_kernel<WT, mc::EPI_STORE><<<grid2(m->V, M), 256, 0, st>>>(
-                    a, a.XN, M, m->V, m->D, emb, nullptr, s->pf_logits, m->V, 0);
+                    a, a.XN, M, m->V, m->D, emb, nullptr, s->pf_logits, m->V, 0, nullptr, nullptr);
             }
             launches += 2;
             // rows of sequence b are contiguous in the chunk and in the output
