@@ -207,13 +207,21 @@ mc_status mc_session_stream(mc_session* session, void** stream);
  * until the process exits; a model/batch/max_seq that needs more (the
  * reference's default 5.8M model fits at batch 4 and max_seq 512) is
  * rejected with MC_ERR_INVALID, as are batch > MC_STATIC_MAX_BATCH and
- * max_seq * head_dim/2 > MC_STATIC_MAX_ROPE.  Output equals mc_generate's.
+ * max_seq * head_dim/2 > MC_STATIC_MAX_ROPE; a shape whose shared-memory
+ * plan exceeds the device's per-block limit returns MC_ERR_UNSUPPORTED.
+ * It runs the grid-barrier token loop from position 0 (no batched
+ * prefill), so its ids equal mc_generate's within the token loop's fp32
+ * numerics (identical wherever no step is a near-tie).  The device-side
+ * waits honour MINIMA_CUDA_WAIT_NS / MINIMA_CUDA_TEST_STALL as the other
+ * loops do and end in MC_ERR_TIMEOUT.
  *
- * The first call on a device looks up the array's device address and sets
- * the kernel's shared-memory limit; make it before any stream capture.
- * Calls share the array (its contents persist between calls; what must
- * start at zero is cleared by each call), so calls that overlap on the GPU
- * race.  Not thread-safe.
+ * Every call looks up the array's device address and sets the kernel's
+ * shared-memory limit (nothing cached goes stale across a device reset);
+ * the first call on a device also loads the kernel: make it before any
+ * stream capture.  Calls share the array (its contents persist between
+ * calls; what must start at zero is cleared by each call), so calls that
+ * overlap on the GPU race.  The host-side staging (sequence table, RoPE
+ * table) is process-global too: not thread-safe.
  */
 #define MC_STATIC_SCRATCH_BYTES (16u << 20)
 #define MC_STATIC_MAX_BATCH     64

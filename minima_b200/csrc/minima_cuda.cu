@@ -160,6 +160,18 @@ bool vec_ok(const mc_model* m) {
     return m->D % n == 0 && m->F % n == 0;
 }
 
+// Every device-side wait gives up after this deadline (default 1 s) and
+// reports MC_ERR_TIMEOUT.  MINIMA_CUDA_WAIT_NS shortens it and
+// MINIMA_CUDA_TEST_STALL=1 makes each wait expect one arrival that never
+// comes: test hooks for the failure path, off unless set.
+template <typename WT>
+void wait_hooks(mc::LoopParams<WT>& p) {
+    const char* wait_ns = getenv("MINIMA_CUDA_WAIT_NS");
+    p.timeout_ns = wait_ns ? strtoull(wait_ns, nullptr, 10) : 1000ull * 1000ull * 1000ull;
+    const char* stall = getenv("MINIMA_CUDA_TEST_STALL");
+    p.extra_arrivals = (stall && stall[0] == '1') ? 1u : 0u;
+}
+
 template <typename WT>
 void fill_params(mc::LoopParams<WT>& p, const mc_session* s) {
     const mc_model* m = s->m;
@@ -184,14 +196,7 @@ void fill_params(mc::LoopParams<WT>& p, const mc_session* s) {
     p.counts = s->counts; p.banned = s->banned; p.max_split = s->max_split;
     p.seq = s->seq;
     p.bar = s->bar; p.status = s->status;
-    // Every device-side wait gives up after this deadline (default 1 s) and
-    // reports MC_ERR_TIMEOUT.  MINIMA_CUDA_WAIT_NS shortens it and
-    // MINIMA_CUDA_TEST_STALL=1 makes each wait expect one arrival that never
-    // comes: test hooks for the failure path, off unless set.
-    const char* wait_ns = getenv("MINIMA_CUDA_WAIT_NS");
-    p.timeout_ns = wait_ns ? strtoull(wait_ns, nullptr, 10) : 1000ull * 1000ull * 1000ull;
-    const char* stall = getenv("MINIMA_CUDA_TEST_STALL");
-    p.extra_arrivals = (stall && stall[0] == '1') ? 1u : 0u;
+    wait_hooks(p);
     p.bc = s->bc; p.xs_ld = s->xs_ld;
 }
 
@@ -1641,9 +1646,10 @@ mc_status mc_session_stream(mc_session* s, void** stream) {
 // __device__ array of MC_STATIC_SCRATCH_BYTES, which every GPU that loads
 // this library holds until the process exits.
 //
-// The first call on a device resolves the array's device address with
-// cudaGetSymbolAddress and sets the kernel's shared-memory limit; make that
-// first call before any stream capture.  All calls share the one array and
+// Every call resolves the array's device address with cudaGetSymbolAddress
+// (with the device current) and sets the kernel's shared-memory limit; the
+// first call on a device also reads its properties and loads the kernel, so
+// make that first call before any stream capture.  All calls share the one array and
 // it keeps the last call's contents, so the barrier counter, status word and
 // attention counters are cleared at the start of each call, and calls that
 // overlap on the GPU (on different streams, or from several host threads)
@@ -1656,7 +1662,6 @@ namespace {
 
 struct StaticDevice {
     bool ready;
-    unsigned char* scratch;   // device address of g_static_scratch on this device
     int sms;
     size_t smem_optin;
 };
@@ -1715,26 +1720,32 @@ StaticPlan static_plan(const mc_model_desc* d, int batch, int cap, int grid, siz
     return pl;
 }
 
-mc_status static_setup(int dev) {
+// Per-device set-up of the static path, with that device current.  The
+// device properties are cached; the array's device address and the
+// kernels' shared-memory limit are looked up on every call (both are cheap
+// after the first), so nothing cached goes stale if the host resets the
+// device between calls.
+mc_status static_setup(int dev, unsigned char** scratch) {
     StaticDevice& sd = g_static_dev[dev];
-    if (sd.ready) return MC_OK;
+    if (!sd.ready) {
+        cudaDeviceProp prop;
+        MC_CUDA(cudaGetDeviceProperties(&prop, dev));
+        if (prop.major != 10)
+            return fail(MC_ERR_UNSUPPORTED, "mc_generate_static: device %d is not sm_100", dev);
+        sd.sms = prop.multiProcessorCount;
+        sd.smem_optin = prop.sharedMemPerBlockOptin;
+        sd.ready = true;
+    }
     void* ptr = nullptr;
     cudaError_t e = cudaGetSymbolAddress(&ptr, g_static_scratch);
     if (e != cudaSuccess || !ptr)
         return fail(MC_ERR_CUDA, "mc_generate_static: cudaGetSymbolAddress: %s", cudaGetErrorString(e));
-    cudaDeviceProp prop;
-    MC_CUDA(cudaGetDeviceProperties(&prop, dev));
-    if (prop.major != 10)
-        return fail(MC_ERR_UNSUPPORTED, "mc_generate_static: device %d is not sm_100", dev);
-    const int optin = (int)prop.sharedMemPerBlockOptin;
+    const int optin = (int)sd.smem_optin;
     MC_CUDA(cudaFuncSetAttribute(mc::token_loop_kernel<float, true>,
                                  cudaFuncAttributeMaxDynamicSharedMemorySize, optin));
     MC_CUDA(cudaFuncSetAttribute(mc::token_loop_kernel<float, false>,
                                  cudaFuncAttributeMaxDynamicSharedMemorySize, optin));
-    sd.scratch = static_cast<unsigned char*>(ptr);
-    sd.sms = prop.multiProcessorCount;
-    sd.smem_optin = prop.sharedMemPerBlockOptin;
-    sd.ready = true;
+    *scratch = static_cast<unsigned char*>(ptr);
     return MC_OK;
 }
 
@@ -1764,7 +1775,8 @@ extern "C" mc_status mc_generate_static(const mc_model_desc* w, int batch,
     int dev = 0;
     MC_CUDA(cudaGetDevice(&dev));
     if (dev < 0 || dev >= 64) return fail(MC_ERR_UNSUPPORTED, "device index %d", dev);
-    st = static_setup(dev);
+    unsigned char* base = nullptr;
+    st = static_setup(dev, &base);
     if (st) return st;
     const StaticDevice& sd = g_static_dev[dev];
     const StaticPlan pl = static_plan(w, batch, max_seq, sd.sms, sd.smem_optin);
@@ -1776,7 +1788,6 @@ extern "C" mc_status mc_generate_static(const mc_model_desc* w, int batch,
     if (pl.smem > sd.smem_optin)
         return fail(MC_ERR_UNSUPPORTED, "mc_generate_static: shared memory plan %zu B", pl.smem);
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    unsigned char* base = sd.scratch;
 
     // Per-sequence bookkeeping exactly as generate.c:553-564.
     int T = 0;
@@ -1850,7 +1861,7 @@ extern "C" mc_status mc_generate_static(const mc_model_desc* w, int batch,
     p.s.pen_active = o->repetition_penalty > 1.0f || o->frequency_penalty != 0.0f ||
                      o->presence_penalty != 0.0f;
     p.T = T;
-    p.timeout_ns = 1000ull * 1000ull * 1000ull;
+    wait_hooks(p);
     p.bc = pl.bc; p.xs_ld = pl.xs_ld;
 
     // Clear what must start at zero; the array keeps the previous call's data.

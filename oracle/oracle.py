@@ -228,6 +228,16 @@ def random_prompt(n: int, vocab: int, seed: int) -> np.ndarray:
     return np.array([r.int(4, vocab - 1) for _ in range(n)], dtype=np.uint16)
 
 
+def ref_random_prompt(n: int, vocab: int, seed: int) -> np.ndarray:
+    """The same prompt drawn with the reference's own rng_seed/rng_int
+    (util.c:11-33) from oracle/_ref, for processes that must run nothing but
+    the reference (the benchmark's reference arm)."""
+    lib = _load_ref()
+    st = C.c_uint64(0)
+    lib.rng_seed(C.byref(st), seed)
+    return np.array([lib.rng_int(C.byref(st), 4, vocab - 1) for _ in range(n)], dtype=np.uint16)
+
+
 class _ModelBase:
     dims: Dims
 

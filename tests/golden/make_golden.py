@@ -8,7 +8,7 @@ machines without the reference sources.  Also records the C struct layouts
 of the reference's headers that the drop-in must match.
 
 Usage (needs the reference sources and a built oracle/_ref):
-    python tests/golden/make_golden.py [--ref /path/to/reference]
+    python tests/golden/make_golden.py --ref <directory of the Minima sources>
 """
 from __future__ import annotations
 
@@ -101,7 +101,7 @@ def struct_layout(include_dirs, headers, defines=()):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ref", required=True, help="directory of the Minima sources")
     args = ap.parse_args()
     if not O.ref_available():
         sys.exit("oracle/_ref/libminima_ref.so is not built (make -C oracle)")

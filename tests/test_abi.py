@@ -88,6 +88,11 @@ def test_host_init_matches_oracle_and_reference():
     for a, b in zip(hm.tensors(), orc.tensors()):
         assert np.array_equal(a, b)
     assert hm.param_count() == 5_808_256
+    if O.ref_available():
+        ref = O.RefModel(dims, 1)
+        for a, b in zip(hm.tensors(), ref.tensors()):
+            assert np.array_equal(a, b)
+        assert ref.param_count() == 5_808_256
 
 
 def test_host_init_bf16_rounding_matches_oracle():

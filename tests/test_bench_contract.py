@@ -78,7 +78,7 @@ def test_reference_arm_json_line():
     assert d["higher_is_better"] is True and d["scaling"] == "weak" and d["vs_baseline"] is None
     assert d["steps"] == 1 and d["warmup"] == 0 and d["n_gpus"] == 1
     assert d["value"] > 0 and d["ms_per_step"] > 0
-    assert d["config"]["workload"] == bench.WORKLOAD_NAME
+    assert d["config"] == bench.workload_config(1)
     cb = d["cpu_baseline"]
     assert cb["kind"] == ("reference" if O.ref_available() else "port")
     assert cb["cores"] >= 1 and cb["value"] == d["value"] and cb["unit"] == bench.UNIT
@@ -90,3 +90,28 @@ def test_reference_arm_other_ranks_do_no_work():
     r = _run_reference_arm({"RANK": "1", "LOCAL_RANK": "1", "WORLD_SIZE": "2"})
     assert r.returncode == 0, r.stderr[-2000:]
     assert not [l for l in r.stdout.splitlines() if l.startswith("{")]
+
+
+_MAPS_PROBE = r"""
+import argparse, sys
+sys.path.insert(0, sys.argv[1])
+import bench
+bench.reference_arm(argparse.Namespace(gpus=1, steps=1, warmup=0))
+with open("/proc/self/maps") as fh:
+    libs = sorted({l.split()[-1] for l in fh if ".so" in l})
+print("LIBS", " ".join(libs))
+"""
+
+
+@pytest.mark.skipif(not O.ref_available(), reason="oracle/_ref not built here")
+def test_reference_arm_loads_only_oracle_libraries():
+    """The reference arm's process maps the reference build (oracle/_ref) and
+    none of this repository's product libraries, so every function the
+    reference calls is its own."""
+    r = subprocess.run([sys.executable, "-c", _MAPS_PROBE, ROOT], cwd=ROOT, capture_output=True,
+                       text=True, timeout=300)
+    assert r.returncode == 0, r.stderr[-2000:]
+    libs = [l for l in r.stdout.splitlines() if l.startswith("LIBS ")][0].split()[1:]
+    ours = [l for l in libs if l.startswith(ROOT)]
+    assert any(l.endswith("oracle/_ref/libminima_ref.so") for l in ours)
+    assert not [l for l in ours if "/minima_b200/" in l], ours

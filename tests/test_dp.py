@@ -41,7 +41,7 @@ def _worker(rank, world, port, outdir, scenario):
     res = {"rank": rank}
     try:
         if scenario == "shard":
-            prompts, rng = bench.workload_prompts(rank)
+            prompts, rng = bench.workload_prompts(rank * bench.WL["batch"], bench.WL["batch"])
             res["prompts"] = prompts.tolist()
             res["rng"] = rng
             t = bench.max_over_ranks(dist, [10.0 + rank, 3.0 - rank], "cpu")

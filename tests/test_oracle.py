@@ -145,3 +145,44 @@ def test_sampler_tie_order_replay():
     opts = O.make_options(top_k=256)
     ids = {O.sample(logits, opts, np.zeros(0, np.uint16), s)[0] for s in range(1, 40)}
     assert all(i >= 4 for i in ids) and len(ids) > 5
+
+
+_ISOLATION_PROBE = r"""
+import ctypes as C, sys
+sys.path.insert(0, sys.argv[1])
+import minima_b200 as M
+M.libs()                       # the repo's host library, loaded RTLD_GLOBAL first
+from oracle import oracle as O
+lib = O._load_ref()
+# config.h:9-14 caps dim at 512: the reference's own model_config_validate
+# must reject dim 768 however the process was set up.
+h = lib.refsh_model_create(1000, 768, 1, 12, 1024, 64, 1)
+print("NULL" if not h else "ACCEPTED")
+"""
+
+
+def test_reference_library_is_not_interposed():
+    """The reference build keeps its own model_config_validate /
+    model_init_config / rng_* / arena_* even in a process that loaded this
+    repository's host library with RTLD_GLOBAL before it (the reference arm of
+    the benchmark and several tests run in such processes)."""
+    import subprocess
+    import sys
+    if not O.ref_available():
+        pytest.skip("oracle/_ref not built")
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    r = subprocess.run([sys.executable, "-c", _ISOLATION_PROBE, root], capture_output=True,
+                       text=True, timeout=120)
+    assert r.returncode == 0, r.stderr
+    assert r.stdout.strip().splitlines()[-1] == "NULL"
+
+
+def test_reference_prompts_equal_oracle_prompts():
+    """The reference's rng_int (util.c:29-33) and the restatement's give the
+    same prompt ids, so the reference arm can draw its prompts without the
+    product libraries."""
+    if not O.ref_available():
+        pytest.skip("oracle/_ref not built")
+    for seed in (1000, 1003, 7):
+        assert np.array_equal(O.ref_random_prompt(128, 30000, seed),
+                              O.random_prompt(128, 30000, seed))

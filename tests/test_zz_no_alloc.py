@@ -9,9 +9,14 @@ work buffers come from a fixed static array inside the library.
 
 This file is collected last on purpose (pytest orders files by name), so
 that a run stopping at the first failure has already run every other test.
-Each test checks the static entry point's output against mc_generate's,
-exactly (greedy and seeded sampling are deterministic), on two calls in a
-row; it passes alone in a fresh process and after the other tests.
+Each test checks the static entry point's output against mc_generate's on a
+session that runs the same grid-barrier token loop (MINIMA_CUDA_LOOP=grid),
+on two calls in a row: ids, counts and RNG states identical (greedy and
+seeded sampling are deterministic, and no step of these cases is a near-tie
+of the fp32 logits); it passes alone in a fresh process and after the other
+tests.  A last case makes the loop's grid barrier wait for an arrival that
+never comes (MINIMA_CUDA_TEST_STALL=1, 50 ms deadline): the call returns
+MC_ERR_TIMEOUT and the next call is correct again.
 """
 import ctypes as C
 
@@ -24,6 +29,7 @@ from oracle import oracle as O
 pytestmark = pytest.mark.gpu
 
 MC_ERR_INVALID = 1
+MC_ERR_TIMEOUT = 4
 
 
 def _lib():
@@ -51,9 +57,10 @@ def _device_weights(hm, torch):
     dict(temperature=0.8, top_k=40, top_p=0.95, repetition_penalty=1.2,
          frequency_penalty=0.3, no_repeat_ngram_size=2, max_new_tokens=48),
 ])
-def test_static_entry_point_matches_generate_twice(gpu, kw):
+def test_static_entry_point_matches_generate_twice(gpu, kw, monkeypatch):
     import torch
     cuda = _lib()
+    monkeypatch.setenv("MINIMA_CUDA_LOOP", "grid")
     # the reference's default model (config.h) at batch 4 and max_seq 512
     hm = M.HostModel(30000, 128, 8, 4, 512, 512, seed=1)
     B, P, cap, out_cap = 4, 32, 512, 128
@@ -64,6 +71,7 @@ def test_static_entry_point_matches_generate_twice(gpu, kw):
     # the existing entry point
     sess = M.Session(M.DeviceModel(hm), B, cap)
     ref_out, ref_counts, ref_rng, _ = sess.generate(prompts, [P] * B, out_cap, opts, rng0)
+    assert sess.last_kernel_name() == "mc::token_loop_kernel"
     sess.close()
 
     desc, keep = _device_weights(hm, torch)
@@ -112,3 +120,40 @@ def test_static_entry_point_rejects_oversize(gpu):
     assert st == MC_ERR_INVALID
     assert "scratch" in cuda.mc_last_error().decode()
     assert int(counts_d.sum()) == 0
+
+
+def test_static_entry_point_wait_deadline(gpu, monkeypatch):
+    """A grid barrier that can never complete ends the static call with
+    MC_ERR_TIMEOUT (no fault, no hang); the next call is correct."""
+    import torch
+    cuda = _lib()
+    hm = M.HostModel(4096, 128, 2, 4, 512, 128, seed=4)
+    orc = O.OrcModel(O.Dims(4096, 128, 2, 4, 512, 128), 4)
+    desc, keep = _device_weights(hm, torch)
+    B, P, out_cap = 2, 8, 32
+    prompts = np.stack([O.random_prompt(P, 4096, 10 + b) for b in range(B)])
+    prompts_d = torch.from_numpy(prompts.view(np.int16).copy()).cuda()
+    lens = (C.c_int * B)(*([P] * B))
+    opts = M.options(top_k=1, max_new_tokens=6)
+
+    def call():
+        out_d = torch.zeros((B, out_cap), dtype=torch.int16, device="cuda")
+        rng_d = torch.tensor([1, 2], dtype=torch.int64, device="cuda")
+        counts_d = torch.zeros(B, dtype=torch.int32, device="cuda")
+        st = cuda.mc_generate_static(C.byref(desc), B, prompts_d.data_ptr(), P, lens,
+                                     out_d.data_ptr(), out_cap, C.byref(opts), rng_d.data_ptr(),
+                                     counts_d.data_ptr(), 128, None)
+        torch.cuda.synchronize()
+        return st, out_d.cpu().numpy().view(np.uint16), counts_d.cpu().numpy()
+
+    monkeypatch.setenv("MINIMA_CUDA_TEST_STALL", "1")
+    monkeypatch.setenv("MINIMA_CUDA_WAIT_NS", str(50_000_000))   # 50 ms
+    st, _, _ = call()
+    assert st == MC_ERR_TIMEOUT, cuda.mc_last_error().decode()
+    monkeypatch.delenv("MINIMA_CUDA_TEST_STALL")
+    monkeypatch.delenv("MINIMA_CUDA_WAIT_NS")
+    st, out, counts = call()
+    assert st == 0, cuda.mc_last_error().decode()
+    for b in range(B):
+        ref, _, _ = orc.generate(prompts[b], out_cap, 128, O.make_options(top_k=1, max_new_tokens=6), b + 1)
+        assert np.array_equal(out[b, :counts[b]], ref)
