@@ -203,15 +203,15 @@ def measure_l2_read_gbs(dev, mib=24, reps=200):
     n = mib * (1 << 20) // 4
     a = torch.rand(n, device=dev)
     b = torch.empty_like(a)
-    out = torch.empty((), device=dev)
+    out = torch.empty(1, device=dev)
     best = 0.0
     for kind in ("sum", "copy"):
         for _ in range(10):
-            torch.sum(a, out=out) if kind == "sum" else b.copy_(a)
+            torch.sum(a, dim=0, keepdim=True, out=out) if kind == "sum" else b.copy_(a)
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record()
         for _ in range(reps):
-            torch.sum(a, out=out) if kind == "sum" else b.copy_(a)
+            torch.sum(a, dim=0, keepdim=True, out=out) if kind == "sum" else b.copy_(a)
         e1.record()
         torch.cuda.synchronize()
         s = e0.elapsed_time(e1) / 1e3

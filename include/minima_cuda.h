@@ -148,6 +148,32 @@ mc_status mc_generate(mc_session* session, int batch,
 mc_status mc_forward_logits(mc_session* session, int batch, const uint16_t* tokens,
     int n, float* logits_out);
 
+/*
+ * Next-token distribution after a prompt, computed on the device: the
+ * statistics generation_inspect_next_tokens prints (generate.c:291-388).
+ * tokens[0..n) are fed one position at a time (forward_one per prefix,
+ * generate.c:76-194); over the last position's logits with the reserved
+ * ids 0..3 excluded, the device computes the maximum, the softmax
+ * denominator and the entropy in bits (double precision) and the top_n
+ * (1..MC_STATS_MAX_TOP) ids by logit, ties to the lower id, with their
+ * probabilities and the cumulative top-1/5/10 masses.  The session's KV
+ * cache is overwritten.  out->status is 0, or 1 when a sampleable logit is
+ * not finite, or 2 when the denominator is not positive and finite (the
+ * reference's rejections); the call itself returns MC_OK in those cases.
+ */
+#define MC_STATS_MAX_TOP 20
+typedef struct {
+    int status;
+    int found;                               /* ids filled: min(top_n, vocab - 4) */
+    int ids[MC_STATS_MAX_TOP];
+    float logits[MC_STATS_MAX_TOP];
+    double probability[MC_STATS_MAX_TOP];
+    double max_logit, denominator, entropy_bits;
+    double top1_mass, top5_mass, top10_mass;  /* 0 where fewer ids were found */
+} mc_token_stats;
+mc_status mc_next_token_stats(mc_session* session, const uint16_t* tokens, int n, int top_n,
+    mc_token_stats* out);
+
 /* Batched causal forward of tokens[b*seq .. b*seq+seq) at every position —
    the logits of model_forward (forward.c:176-274), equal to forward_one per
    prefix (generate.c:76-194) within fp32 rounding: logits_out[(b*seq+t)*V].

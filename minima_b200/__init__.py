@@ -32,7 +32,7 @@ CUDA_SYMBOLS = ("mc_init", "mc_model_create", "mc_model_update", "mc_model_destr
                 "mc_last_kernel_ms", "mc_last_launch_count", "mc_last_step_times",
                 "mc_last_kernel_name", "mc_last_prefill", "mc_session_stream", "mc_last_error",
                 "mc_checkpoint_inspect", "mc_model_load_checkpoint", "mc_gemm",
-                "mc_model_forward")
+                "mc_model_forward", "mc_next_token_stats", "mc_generate_static")
 GENERATE_SYMBOLS = ("kvcache_init", "kvcache_reset", "generation_check_kv_cache",
                     "generation_inspect_next_tokens", "generate", "generate_with_options",
                     "generate_ex", "generate_batch_with_options", "minima_cuda_select_device",

@@ -22,6 +22,7 @@
 #include "mc_checkpoint.cuh"
 #include "mc_tcgen05.cuh"
 #include "mc_batched.cuh"
+#include "mc_stats.cuh"
 
 #include <cudaTypedefs.h>
 
@@ -136,6 +137,7 @@ struct mc_session {
     unsigned* pf_cnt;             // per-tile arrival counters of those GEMMs (kept at zero)
     __nv_bfloat16 *pf_xn16, *pf_att16, *pf_f16;   // bf16 GEMM inputs (tensor cores, bf16 weights)
     cudaEvent_t ev_mid;           // end of prefill
+    mc_token_stats* stats;   // result of mc_next_token_stats (allocated on first use)
     int last_prefill_pos;         // positions prefilled by the last call
     float last_prefill_ms;
 };
@@ -500,7 +502,7 @@ mc_status mc_session_destroy(mc_session* s) {
                     s->xfin, s->hgen, s->hsync, s->hpv, s->hpi,
                     s->pf_x, s->pf_xn, s->pf_q, s->pf_att, s->pf_f, s->pf_logits,
                     s->pf_xn16, s->pf_att16, s->pf_f16, s->pf_part, s->pf_cnt, s->bd_lists, s->bd_xn,
-                    s->bd_xn16, s->bd_att16, s->bd_f16, s->bd_part};
+                    s->bd_xn16, s->bd_att16, s->bd_f16, s->bd_part, s->stats};
     for (void* b : bufs) cudaFree(b);
     if (s->ev_mid) cudaEventDestroy(s->ev_mid);
     if (s->ev0) cudaEventDestroy(s->ev0);
@@ -1468,8 +1470,10 @@ mc_status generate_t(mc_session* s, int batch, const uint16_t* prompts, int prom
     return MC_OK;
 }
 
+// Teacher-forced forward of tokens[b*n .. b*n+n) (host ids), one position
+// at a time; leaves the logits of every position in s->trace on the device.
 template <typename WT>
-mc_status forward_logits_t(mc_session* s, int batch, const uint16_t* tokens, int n, float* out) {
+mc_status forward_logits_dev(mc_session* s, int batch, const uint16_t* tokens, int n) {
     const mc_model* m = s->m;
     for (size_t i = 0; i < (size_t)batch * n; i++)
         if (tokens[i] >= m->V) return fail(MC_ERR_INVALID, "token id %d >= vocab", (int)tokens[i]);
@@ -1503,7 +1507,14 @@ mc_status forward_logits_t(mc_session* s, int batch, const uint16_t* tokens, int
     if (st) return st;
     s->last_prefill_pos = 0;
     s->last_prefill_ms = 0.0f;
-    MC_CUDA(cudaMemcpy(out, s->trace, (size_t)batch * n * m->V * 4, cudaMemcpyDeviceToHost));
+    return MC_OK;
+}
+
+template <typename WT>
+mc_status forward_logits_t(mc_session* s, int batch, const uint16_t* tokens, int n, float* out) {
+    const mc_status st = forward_logits_dev<WT>(s, batch, tokens, n);
+    if (st) return st;
+    MC_CUDA(cudaMemcpy(out, s->trace, (size_t)batch * n * s->m->V * 4, cudaMemcpyDeviceToHost));
     return MC_OK;
 }
 
@@ -1590,6 +1601,27 @@ mc_status mc_forward_logits(mc_session* s, int batch, const uint16_t* tokens, in
     MC_CUDA(cudaSetDevice(s->m->device));
     if (s->m->dtype == MC_WEIGHTS_BF16) return forward_logits_t<__nv_bfloat16>(s, batch, tokens, n, out);
     return forward_logits_t<float>(s, batch, tokens, n, out);
+}
+
+mc_status mc_next_token_stats(mc_session* s, const uint16_t* tokens, int n, int top_n,
+                              mc_token_stats* out) {
+    if (!s || !tokens || !out) return fail(MC_ERR_INVALID, "null argument");
+    if (n <= 0 || n > s->cap || top_n <= 0 || top_n > MC_STATS_MAX_TOP)
+        return fail(MC_ERR_INVALID, "next_token_stats: n %d, top_n %d", n, top_n);
+    MC_CUDA(cudaSetDevice(s->m->device));
+    const mc_status st = s->m->dtype == MC_WEIGHTS_BF16
+                             ? forward_logits_dev<__nv_bfloat16>(s, 1, tokens, n)
+                             : forward_logits_dev<float>(s, 1, tokens, n);
+    if (st) return st;
+    if (!s->stats) MC_CUDA(cudaMalloc(&s->stats, sizeof(mc_token_stats)));
+    MC_CUDA(cudaMemsetAsync(s->stats, 0, sizeof(mc_token_stats), s->stream));
+    mc::next_token_stats_kernel<<<1, mc::kStatsThreads, 0, s->stream>>>(
+        s->trace + (size_t)(n - 1) * s->m->V, s->m->V, top_n, s->stats);
+    MC_CUDA(cudaGetLastError());
+    MC_CUDA(cudaMemcpyAsync(out, s->stats, sizeof(*out), cudaMemcpyDeviceToHost, s->stream));
+    MC_CUDA(cudaStreamSynchronize(s->stream));
+    s->last_launches += 1;
+    return MC_OK;
 }
 
 mc_status mc_last_kernel_ms(mc_session* s, float* ms) {

@@ -22,7 +22,6 @@
 #include <stdlib.h>
 #include <string.h>
 
-#define TOK_SPECIAL 4        /* tokenizer.h:14-18 */
 
 /* Host program symbols (generate.c's own dependencies). */
 bool model_validate(const Model* model);
@@ -503,30 +502,59 @@ bool generation_check_kv_cache(Model* model, KVCache* cache, Arena* temp_arena,
     return max_abs <= tolerance;
 }
 
-/* generate.c:268-287 */
-static void print_token_escaped(const Tokenizer* tok, int id) {
+/* The quoted, byte-safe form the reference prints for a token
+   (generate.c:267-287): printable ASCII as is, backslash, double quote,
+   newline, carriage return and tab as their C escapes, every other byte as
+   \xHH with upper-case hex digits; an id outside the tokenizer prints as
+   "<invalid>".  Formatted into a local buffer (flushed every 256 output
+   bytes) and written to stdout with fwrite. */
+static void write_quoted_token(const Tokenizer* tok, int id) {
     if (!tok || id < 0 || id >= tok->vocab_size) {
-        printf("\"<invalid>\"");
+        fputs("\"<invalid>\"", stdout);
         return;
     }
-    const unsigned char* s = (const unsigned char*)tok->token_str[id];
-    const int len = tok->token_len[id];
-    putchar('"');
-    for (int i = 0; i < len; i++) {
-        const unsigned char c = s[i];
-        if (c == '\\') printf("\\\\");
-        else if (c == '"') printf("\\\"");
-        else if (c == '\n') printf("\\n");
-        else if (c == '\r') printf("\\r");
-        else if (c == '\t') printf("\\t");
-        else if (c >= 32 && c <= 126) putchar((int)c);
-        else printf("\\x%02X", (unsigned int)c);
+    static const char kHex[] = "0123456789ABCDEF";
+    const unsigned char* bytes = (const unsigned char*)tok->token_str[id];
+    char buf[256 + 8];
+    size_t n = 0;
+    buf[n++] = '"';
+    for (int i = 0; i < tok->token_len[id]; i++) {
+        const unsigned char c = bytes[i];
+        char esc = 0;
+        switch (c) {
+        case '\\': esc = '\\'; break;
+        case '"': esc = '"'; break;
+        case '\n': esc = 'n'; break;
+        case '\r': esc = 'r'; break;
+        case '\t': esc = 't'; break;
+        default: break;
+        }
+        if (esc) {
+            buf[n++] = '\\';
+            buf[n++] = esc;
+        } else if (c >= 0x20 && c < 0x7F) {
+            buf[n++] = (char)c;
+        } else {
+            buf[n++] = '\\';
+            buf[n++] = 'x';
+            buf[n++] = kHex[c >> 4];
+            buf[n++] = kHex[c & 15];
+        }
+        if (n >= 256) {
+            fwrite(buf, 1, n, stdout);
+            n = 0;
+        }
     }
-    putchar('"');
+    buf[n++] = '"';
+    fwrite(buf, 1, n, stdout);
 }
 
-/* generate.c:291-388: logits from the device, statistics on the host in
-   double precision as the reference computes them. */
+/* generate.c:289-388.  The prompt runs through the device token loop
+   teacher-forced, and the statistics of the last position's logits
+   (maximum, softmax denominator and entropy in double precision, top-n by
+   logit with ties to the lower id, cumulative masses) are computed on the
+   device by mc_next_token_stats; this function validates like the
+   reference and prints the same report. */
 bool generation_inspect_next_tokens(Model* model, const Tokenizer* tok,
     KVCache* cache, const uint16_t* prompt_ids, int prompt_len, int top_n) {
     if (!model || !model_validate(model) || !tok || !cache || !prompt_ids || prompt_len <= 0 ||
@@ -534,69 +562,35 @@ bool generation_inspect_next_tokens(Model* model, const Tokenizer* tok,
         prompt_len > model->max_seq || prompt_len > cache->max_seq ||
         !cache_matches(cache, model))
         return false;
-    if (top_n > 20) top_n = 20;
+    if (top_n > MC_STATS_MAX_TOP) top_n = MC_STATS_MAX_TOP;
     kvcache_reset(cache);
+    /* the reference feeds ids until the first out-of-vocabulary one and
+       leaves cache->pos at that index */
     for (int i = 0; i < prompt_len; i++)
         if (prompt_ids[i] >= model->vocab_size) {
             cache->pos = i;
             return false;
         }
-    float* all = device_prefix_logits(model, cache, prompt_ids, prompt_len);
-    if (!all) return false;
-    const int V = model->vocab_size;
-    float* logits = all + (size_t)(prompt_len - 1) * V;
+    mc_model* dev = device_model(model, 0);
+    mc_session* sess = dev ? device_session(cache, dev, 1) : NULL;
+    if (!sess) return false;
+    mc_token_stats st;
+    if (mc_next_token_stats(sess, prompt_ids, prompt_len, top_n, &st) != MC_OK) {
+        set_err("mc_next_token_stats");
+        return false;
+    }
     cache->pos = prompt_len;
+    if (st.status != 0) return false;
 
-    float max_logit = -INFINITY;
-    for (int i = 0; i < V; i++) {
-        if (i < TOK_SPECIAL) { logits[i] = -INFINITY; continue; }
-        if (!isfinite(logits[i])) { free(all); return false; }
-        if (logits[i] > max_logit) max_logit = logits[i];
-    }
-    double denom = 0.0;
-    for (int i = TOK_SPECIAL; i < V; i++) denom += exp((double)logits[i] - (double)max_logit);
-    if (!(denom > 0.0) || !isfinite(denom)) { free(all); return false; }
-
-    int best_ids[20];
-    float best_logits[20];
-    int found = 0;
-    for (int id = TOK_SPECIAL; id < V; id++) {
-        int at = found;
-        if (at > top_n) at = top_n;
-        while (at > 0 && logits[id] > best_logits[at - 1]) {
-            if (at < top_n) {
-                best_logits[at] = best_logits[at - 1];
-                best_ids[at] = best_ids[at - 1];
-            }
-            at--;
-        }
-        if (at < top_n) {
-            best_logits[at] = logits[id];
-            best_ids[at] = id;
-            if (found < top_n) found++;
-        }
-    }
-    double entropy_bits = 0.0;
-    for (int i = TOK_SPECIAL; i < V; ++i) {
-        const double probability = exp((double)logits[i] - (double)max_logit) / denom;
-        if (probability > 0.0) entropy_bits -= probability * (log(probability) / log(2.0));
-    }
-    double top1 = 0.0, top5 = 0.0, top10 = 0.0, cumulative = 0.0;
-    for (int i = 0; i < found; ++i) {
-        cumulative += exp((double)best_logits[i] - (double)max_logit) / denom;
-        if (i == 0) top1 = cumulative;
-        if (i == 4) top5 = cumulative;
-        if (i == 9) top10 = cumulative;
-    }
-    printf("  Next-token distribution (top %d, sampleable-vocabulary probabilities):\n", found);
+    printf("  Next-token distribution (top %d, sampleable-vocabulary probabilities):\n",
+        st.found);
     printf("    entropy=%.4f bits, top-1=%.2f%%, top-5=%.2f%%, top-10=%.2f%%\n",
-        entropy_bits, top1 * 100.0, top5 * 100.0, top10 * 100.0);
-    for (int i = 0; i < found; i++) {
-        const double probability = exp((double)best_logits[i] - (double)max_logit) / denom;
-        printf("    %2d. id=%4d  p=%8.4f%%  token=", i + 1, best_ids[i], probability * 100.0);
-        print_token_escaped(tok, best_ids[i]);
-        putchar('\n');
+        st.entropy_bits, st.top1_mass * 100.0, st.top5_mass * 100.0, st.top10_mass * 100.0);
+    for (int rank = 0; rank < st.found; rank++) {
+        printf("    %2d. id=%4d  p=%8.4f%%  token=", rank + 1, st.ids[rank],
+            st.probability[rank] * 100.0);
+        write_quoted_token(tok, st.ids[rank]);
+        fputc('\n', stdout);
     }
-    free(all);
     return true;
 }

@@ -57,7 +57,7 @@ def compare(out, counts, trace, refs, lens, steps, atol, rtol, min_agree):
     divergence is allowed only at a step where the oracle's top-1/top-2
     margin is within twice the bound.  Returns (worst err/bound, agreed
     steps per sequence, smallest margin seen)."""
-    worst, agree, min_margin = 0.0, [], np.inf
+    worst, worst_at, agree, min_margin = 0.0, None, [], np.inf
     for b, (ids, _, _, rtr) in enumerate(refs):
         got = out[b, lens[b]:counts[b]]
         want = ids[lens[b]:]
@@ -70,8 +70,8 @@ def compare(out, counts, trace, refs, lens, steps, atol, rtol, min_agree):
             assert np.array_equal(np.isfinite(g), fin), f"seq {b} step {s}: mask differs"
             bound = atol + rtol * np.abs(w[fin])
             ratio = float((np.abs(g[fin] - w[fin]) / bound).max())
-            worst = max(worst, ratio)
-            assert ratio <= 1.0, f"seq {b} step {s}: err/bound {ratio:.3f}"
+            if ratio > worst:
+                worst, worst_at = ratio, (b, s)
             m = margin(rtr[s])
             min_margin = min(min_margin, m)
         if n < min(len(got), len(want)):
@@ -84,6 +84,8 @@ def compare(out, counts, trace, refs, lens, steps, atol, rtol, min_agree):
         else:
             assert len(got) == len(want)
         agree.append(n)
+    print(f"worst err/bound {worst:.3f} at (sequence, step) {worst_at}")
+    assert worst <= 1.0, f"err/bound {worst:.3f} at (sequence, step) {worst_at}"
     return worst, agree, min_margin
 
 
