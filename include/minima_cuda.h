@@ -185,6 +185,38 @@ mc_status mc_next_token_stats(mc_session* session, const uint16_t* tokens, int n
 mc_status mc_model_forward(mc_session* session, int batch, int seq, const uint16_t* tokens,
     float* logits_out, unsigned flags);
 
+/*
+ * model_forward (forward.c:176-274) with its caches: the batched causal
+ * forward of mc_model_forward on the fp32 CUDA-core GEMMs, also storing
+ * every per-layer activation that Minima's model_backward reads
+ * (backward.c:440-600), into host arrays laid out as the reference's
+ * Activations (forward.h:10-26): per-layer arrays [n_layers][batch*seq][w]
+ * with row b*seq + t, final arrays [batch*seq][w].  A NULL pointer is not
+ * written.  qkv holds Q and K after RoPE and V as projected
+ * (forward.c:224-227); x and x_norm are the final residual stream and the
+ * final RMSNorm output; logits [batch*seq][vocab].
+ */
+typedef struct {
+    float* x;
+    float* x_norm;
+    float* qkv;
+    float* attn_out;
+    float* ffn_buf;
+    float* up_buf;
+    float* gate_buf;
+    float* resid_attn;
+    float* resid_ffn;
+    float* logits;
+} mc_forward_caches;
+mc_status mc_model_forward_caches(mc_session* session, int batch, int seq, const uint16_t* tokens,
+    const mc_forward_caches* out);
+
+/* matmul of forward.h:49-50 (forward.c:24-40) on the device of the calling
+   thread: out[n][d_out] = x[n][d_in] . w[d_out][d_in]^T, fp32, k ascending
+   per output (FMA accumulation).  Host pointers; the operands are copied in
+   and the result out on every call. */
+mc_status mc_matmul(float* out, const float* x, const float* w, int n, int d_in, int d_out);
+
 /* Kernel time of the last mc_generate / mc_forward_logits on this session,
    measured with CUDA events on the launching stream (milliseconds). */
 mc_status mc_last_kernel_ms(mc_session* session, float* ms);

@@ -240,6 +240,12 @@ const char* minima_cuda_last_error(void);
 /* Device kernel time of the last generation call, milliseconds. */
 float minima_cuda_last_kernel_ms(void);
 
+/* The device session the drop-in model_forward (minima_forward.h) runs a
+   batch x seq forward of `model` on: one per model, grown as needed, with
+   the weights re-uploaded when they changed (the same side table as the
+   generation entry points).  NULL on failure (minima_cuda_last_error). */
+struct mc_session* minima_cuda_forward_session(const Model* model, int batch, int seq);
+
 #ifdef __cplusplus
 }
 #endif

@@ -24,6 +24,7 @@ PKG = os.path.dirname(os.path.abspath(__file__))
 LIB_CUDA = os.path.join(PKG, "libminima_cuda.so")
 LIB_GEN = os.path.join(PKG, "libminima_generate.so")
 LIB_HOST = os.path.join(PKG, "libminima_host.so")
+LIB_FWD = os.path.join(PKG, "libminima_forward.so")
 
 # Exported entry points, as declared in include/minima_cuda.h and
 # include/minima_generate.h.
@@ -39,6 +40,7 @@ GENERATE_SYMBOLS = ("kvcache_init", "kvcache_reset", "generation_check_kv_cache"
                     "minima_cuda_model_sync", "minima_cuda_release_model",
                     "minima_cuda_release_cache", "minima_cuda_last_error",
                     "minima_cuda_last_kernel_ms")
+FORWARD_SYMBOLS = ("activations_init", "rmsnorm", "matmul", "silu", "model_forward")
 HOST_SYMBOLS = ("rng_seed", "rng_u64", "rng_f32", "rng_int", "arena_init", "arena_free",
                 "arena_alloc", "arena_reset", "model_init_config", "model_config_validate",
                 "model_validate", "model_param_count", "minima_host_model_arena_bytes",
@@ -170,6 +172,22 @@ def libs():
         _declare(host, cuda, gen)
         _libs.update(host=host, cuda=cuda, gen=gen)
     return _libs["host"], _libs["cuda"], _libs["gen"]
+
+
+def forward_lib():
+    """ctypes handle of libminima_forward.so, the drop-in forward.h (loaded
+    after the libraries it depends on)."""
+    if "fwd" not in _libs:
+        libs()
+        if not os.path.exists(LIB_FWD):
+            raise MinimaCudaError("libminima_forward.so is not built: run python -m minima_b200.build")
+        fwd = C.CDLL(LIB_FWD)
+        fwd.activations_init.restype = C.c_bool
+        fwd.model_forward.restype = C.POINTER(C.c_float)
+        fwd.silu.restype = C.c_float
+        fwd.silu.argtypes = [C.c_float]
+        _libs["fwd"] = fwd
+    return _libs["fwd"]
 
 
 def _declare(host, cuda, gen):

@@ -3,6 +3,7 @@
 * libminima_cuda.so      CUDA token loop + C ABI (include/minima_cuda.h),
                          nvcc for sm_100a only.
 * libminima_generate.so  drop-in generate.h implementation (C) over it.
+* libminima_forward.so   drop-in forward.h implementation (C) over it.
 * libminima_host.so      model init / arena / RNG for standalone programs.
 
 Outputs stay next to the sources (not installed), so that the files a GPU
@@ -29,6 +30,7 @@ ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 LIB_CUDA = os.path.join(PKG, "libminima_cuda.so")
 LIB_GEN = os.path.join(PKG, "libminima_generate.so")
 LIB_HOST = os.path.join(PKG, "libminima_host.so")
+LIB_FWD = os.path.join(PKG, "libminima_forward.so")
 
 
 def _stale(target, deps):
@@ -59,6 +61,11 @@ def build(verbose: bool = False, force: bool = False) -> None:
         _run([GCC, "-std=c11", "-O2", "-fPIC", "-shared", "-Wall", "-Wextra", f"-I{INC}",
               "-o", LIB_GEN, gen_src, f"-L{PKG}", "-lminima_cuda", "-Wl,-rpath,$ORIGIN",
               "-lm"], verbose)
+    fwd_src = os.path.join(HOST, "forward_cuda.c")
+    if force or _stale(LIB_FWD, [fwd_src, LIB_GEN, LIB_CUDA] + _files(INC, (".h",))):
+        _run([GCC, "-std=c11", "-O2", "-fPIC", "-shared", "-Wall", "-Wextra", f"-I{INC}",
+              "-o", LIB_FWD, fwd_src, f"-L{PKG}", "-lminima_generate", "-lminima_cuda",
+              "-Wl,-rpath,$ORIGIN", "-lm"], verbose)
     host_src = os.path.join(HOST, "host_support.c")
     if force or _stale(LIB_HOST, [host_src] + _files(INC, (".h",))):
         _run([GCC, "-std=c11", "-O2", "-fPIC", "-shared", "-Wall", "-Wextra", f"-I{INC}",

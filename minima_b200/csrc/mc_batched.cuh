@@ -83,8 +83,20 @@ __global__ void __launch_bounds__(1024) bd_lists_kernel(const LoopParams<WT> p, 
 constexpr int kBdMaxParts = 16;              // K-slice partials of a decode GEMM
 constexpr int kBdNormCols = 4;               // float4 columns per norm thread (D <= 16 * kThreads)
 
+// The bf16 operands of the kind::f16 decode GEMMs carry each fp32
+// activation as two bf16 numbers, hi = bf16(v) and lo = bf16(v - hi), in
+// rows b and Bcap + b of the same buffer; the GEMM multiplies both by the
+// weight tile into one accumulator, so the activation keeps ~16 significant
+// bits instead of 8 (the error of a single bf16 copy, compounded over 24
+// layers, moved config 4's logits by ~3e-2).
+__device__ __forceinline__ void bf16_split_store(__nv_bfloat16* hi, size_t lo_off, float v) {
+    const __nv_bfloat16 h = __float2bfloat16_rn(v);
+    hi[0] = h;
+    hi[lo_off] = __float2bfloat16_rn(v - __bfloat162float(h));
+}
+
 // xn[b] = rmsnorm(x[b]) * scale (generate.c:57-63) for the listed sequences,
-// plus a bf16 copy when xn16 is set.  With embed, x[b] is first set to the
+// plus its bf16 hi/lo pair when xn16 is set.  With embed, x[b] is first set to the
 // embedding row of the id fed (generate.c:86-88); with nparts > 0, the
 // K-slice partials of the residual GEMM before it are first added to x[b]
 // in slice order (part + (s * B + b) * D).  One CTA per sequence; a thread
@@ -144,10 +156,11 @@ __global__ void __launch_bounds__(kThreads) bd_norm_kernel(const LoopParams<WT> 
         *reinterpret_cast<float4*>(xn + (size_t)b * p.D + 4 * c) = v;
         if (xn16) {
             __nv_bfloat16* o = xn16 + (size_t)b * p.D + 4 * c;
-            o[0] = __float2bfloat16_rn(v.x);
-            o[1] = __float2bfloat16_rn(v.y);
-            o[2] = __float2bfloat16_rn(v.z);
-            o[3] = __float2bfloat16_rn(v.w);
+            const size_t lo = (size_t)p.Bcap * p.D;
+            bf16_split_store(o, lo, v.x);
+            bf16_split_store(o + 1, lo, v.y);
+            bf16_split_store(o + 2, lo, v.z);
+            bf16_split_store(o + 3, lo, v.w);
         }
     }
 }
@@ -757,7 +770,7 @@ __global__ void __launch_bounds__(kBdWWarps * 32) bd_attw_kernel(const LoopParam
 // f[b] = SiLU(gate) * up (generate.c:165-179) of the running sequences, from
 // the nparts K-slice partials the up/gate GEMM left in part (slice r, row b
 // at part + (r * B + b) * 2F: up in [0, F), gate in [F, 2F)), summed in
-// slice order; plus a bf16 copy when f16 is set (the A operand of a
+// slice order; plus its bf16 hi/lo pair when f16 is set (the operand of a
 // kind::f16 down GEMM).
 template <typename WT>
 __global__ void __launch_bounds__(kThreads) bd_swiglu_kernel(const LoopParams<WT> p, BdLists L, const float* part,
@@ -785,12 +798,12 @@ __global__ void __launch_bounds__(kThreads) bd_swiglu_kernel(const LoopParams<WT
         *reinterpret_cast<float4*>(p.f + (size_t)b * p.F + c) = make_float4(v[0], v[1], v[2], v[3]);
         if (f16)
 #pragma unroll
-            for (int j = 0; j < 4; j++) f16[(size_t)b * p.F + c + j] = __float2bfloat16_rn(v[j]);
+            for (int j = 0; j < 4; j++) bf16_split_store(f16 + (size_t)b * p.F + c + j, (size_t)p.Bcap * p.F, v[j]);
     }
 }
 
-// bf16 copy of the attention output of the listed sequences (the A operand
-// of a kind::f16 proj GEMM).
+// bf16 hi/lo pair of the attention output of the listed sequences (the
+// operand of a kind::f16 proj GEMM).
 template <typename WT>
 __global__ void __launch_bounds__(kThreads) bd_cvt_kernel(const LoopParams<WT> p, BdLists L, __nv_bfloat16* dst) {
     pdl_wait();
@@ -798,7 +811,7 @@ __global__ void __launch_bounds__(kThreads) bd_cvt_kernel(const LoopParams<WT> p
     const int b = blockIdx.x;
     if (b >= p.B || !L.act_fwd()[b]) return;
     for (int k = threadIdx.x; k < p.D; k += blockDim.x)
-        dst[(size_t)b * p.D + k] = __float2bfloat16_rn(p.att[(size_t)b * p.D + k]);
+        bf16_split_store(dst + (size_t)b * p.D + k, (size_t)p.Bcap * p.D, p.att[(size_t)b * p.D + k]);
 }
 
 // Sampling and bookkeeping of the head sequences (the token loop's phase).

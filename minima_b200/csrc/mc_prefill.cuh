@@ -37,6 +37,10 @@ struct PrefillArgs {
     __nv_bfloat16* XN16;
     __nv_bfloat16* ATT16;
     __nv_bfloat16* FH16;
+    // model_forward's per-layer caches (forward.h:17-23): when set, the
+    // SwiGLU epilogue also stores the up and gate projections [B*chunk][F]
+    float* UP;
+    float* GATE;
     int* status;
 };
 
@@ -246,9 +250,36 @@ __global__ void __launch_bounds__(256, 1) pf_gemm_kernel(PrefillArgs a, const fl
                 } else {
                     const float up = acc[0][i][j], g = acc[DUAL - 1][i][j];
                     C[(size_t)m * ldc + n] = (g / (1.0f + expf(-g))) * up;
+                    if (a.UP) {
+                        a.UP[(size_t)m * ldc + n] = up;
+                        a.GATE[(size_t)m * ldc + n] = g;
+                    }
                 }
             }
         }
+    }
+}
+
+// The rows of model_forward's qkv cache (forward.c:224-227: the QKV
+// projection after RoPE) for the chunk: Q from QB, K and V from the KV
+// cache, laid out [row][Q heads | K heads | V heads].  One CTA per row.
+__global__ void __launch_bounds__(256) pf_gather_qkv_kernel(PrefillArgs a, int layer, float* out) {
+    const int m = blockIdx.x;
+    if (m >= pf_rows(a)) return;
+    int b, t;
+    pf_row(a, m, b, t);
+    float* row = out + (size_t)m * a.Q;
+    for (int n = threadIdx.x; n < a.Q; n += blockDim.x) {
+        float v;
+        if (n < a.D) {
+            v = a.QB[(size_t)m * a.D + n];
+        } else {
+            const bool isk = n < a.D + a.kvd;
+            const int c = isk ? n - a.D : n - a.D - a.kvd;
+            const int g = c / a.hd, dd = c % a.hd;
+            v = (isk ? a.kc : a.vc)[((((size_t)layer * a.Bcap + b) * a.K + g) * a.cap + t) * a.hd + dd];
+        }
+        row[n] = v;
     }
 }
 

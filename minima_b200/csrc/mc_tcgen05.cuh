@@ -61,6 +61,7 @@ struct TcArgs {
     int* status;
     unsigned long long timeout_ns;
     int ksplit;                // CTAs splitting K per tile (<= 1: no split; EPI_PART only)
+    int x_lo_row;              // decode, bf16: first row of the lo halves in the X map
     // decode lm_head (tc_dec_kernel with TCE_STORE and head != 0): ids 0..3
     // are stored as -inf (generate.c:580-581) and, for greedy sampling, each
     // (sequence, 128-id tile)'s best transformed value and its id
@@ -442,7 +443,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
     constexpr int ES = KIND == TC_TF32 ? 4 : 2;
     constexpr int BKE = TC_BKB / ES;                       // K elements per stage
     constexpr uint32_t XTILE = (uint32_t)BN * TC_BKB;      // bytes of the sequence tile
-    constexpr uint32_t STAGE = DUAL * TC_TILE + XTILE;
+    // bf16: the activations come as hi and lo tiles (rows s0 and
+    // g.x_lo_row + s0 of X), both multiplied into the same accumulator
+    constexpr int XS = KIND == TC_BF16 ? 2 : 1;
+    constexpr uint32_t STAGE = DUAL * TC_TILE + XS * XTILE;
     constexpr int TLD = DUAL * TC_BM + 4;                  // epilogue tile row stride (floats)
     static_assert(BN % 16 == 0 && BN >= 16 && BN <= 256, "N of an M = 128 MMA");
     static_assert(DUAL * BN <= 512 && (DUAL * BN & (DUAL * BN - 1)) == 0 && DUAL * BN >= 32,
@@ -546,6 +550,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
                 if constexpr (DUAL == 2) tc_tma_3d(sa + TC_TILE, &tmW2, kx, f0, g.layer, fb);
             }
             tc_tma_2d(sa + DUAL * TC_TILE, &tmX, kx, s0, fb);
+            if constexpr (XS == 2) tc_tma_2d(sa + DUAL * TC_TILE + XTILE, &tmX, kx, g.x_lo_row + s0, fb);
             issued++;
         }
         ctl[2] = issued;
@@ -565,11 +570,14 @@ __global__ void __launch_bounds__(TC_THREADS, 1)
             const uint32_t sa = smem_addr(base + (size_t)st * STAGE);
 #pragma unroll
             for (int k = 0; k < TC_BKB / 32; k++) {
-                const uint64_t xd = tc_sw128_desc(sa + DUAL * TC_TILE + 32 * k);
-                const uint32_t acc = (kb | k) != 0;
-                tc_mma<KIND>(tmem, tc_sw128_desc(sa + 32 * k), xd, idesc, acc);
-                if constexpr (DUAL == 2)
-                    tc_mma<KIND>(tmem + BN, tc_sw128_desc(sa + TC_TILE + 32 * k), xd, idesc, acc);
+#pragma unroll
+                for (int x = 0; x < XS; x++) {
+                    const uint64_t xd = tc_sw128_desc(sa + DUAL * TC_TILE + x * XTILE + 32 * k);
+                    const uint32_t acc = (kb | k | x) != 0;
+                    tc_mma<KIND>(tmem, tc_sw128_desc(sa + 32 * k), xd, idesc, acc);
+                    if constexpr (DUAL == 2)
+                        tc_mma<KIND>(tmem + BN, tc_sw128_desc(sa + TC_TILE + 32 * k), xd, idesc, acc);
+                }
             }
             tc_commit(smem_addr(&empty[st]));
         }

@@ -23,6 +23,7 @@
 #include "mc_tcgen05.cuh"
 #include "mc_batched.cuh"
 #include "mc_stats.cuh"
+#include "mc_matmul.cuh"
 
 #include <cudaTypedefs.h>
 
@@ -138,6 +139,8 @@ struct mc_session {
     __nv_bfloat16 *pf_xn16, *pf_att16, *pf_f16;   // bf16 GEMM inputs (tensor cores, bf16 weights)
     cudaEvent_t ev_mid;           // end of prefill
     mc_token_stats* stats;   // result of mc_next_token_stats (allocated on first use)
+    float *pf_cap_qkv, *pf_cap_up, *pf_cap_gate;   // model_forward cache staging (on first use)
+    size_t pf_cap_rows;
     int last_prefill_pos;         // positions prefilled by the last call
     float last_prefill_ms;
 };
@@ -502,7 +505,8 @@ mc_status mc_session_destroy(mc_session* s) {
                     s->xfin, s->hgen, s->hsync, s->hpv, s->hpi,
                     s->pf_x, s->pf_xn, s->pf_q, s->pf_att, s->pf_f, s->pf_logits,
                     s->pf_xn16, s->pf_att16, s->pf_f16, s->pf_part, s->pf_cnt, s->bd_lists, s->bd_xn,
-                    s->bd_xn16, s->bd_att16, s->bd_f16, s->bd_part, s->stats};
+                    s->bd_xn16, s->bd_att16, s->bd_f16, s->bd_part, s->stats,
+                    s->pf_cap_qkv, s->pf_cap_up, s->pf_cap_gate};
     for (void* b : bufs) cudaFree(b);
     if (s->ev_mid) cudaEventDestroy(s->ev_mid);
     if (s->ev0) cudaEventDestroy(s->ev0);
@@ -824,7 +828,8 @@ template <int KIND, int EPI, int BN, int STAGES>
 cudaError_t tc_dec_launch(const CUtensorMap& x, const CUtensorMap& w, const CUtensorMap& w2,
                           const mc::TcArgs& g, cudaStream_t st) {
     constexpr int DUAL = EPI == mc::EPI_PART2 ? 2 : 1;
-    const size_t smem = 1024 + (size_t)STAGES * (DUAL * mc::TC_TILE + (size_t)BN * mc::TC_BKB) + 256;
+    constexpr int XS = KIND == mc::TC_BF16 ? 2 : 1;      // bf16: hi and lo activation tiles
+    const size_t smem = 1024 + (size_t)STAGES * (DUAL * mc::TC_TILE + (size_t)XS * BN * mc::TC_BKB) + 256;
     static unsigned long long attr_set = 0;    // one bit per device
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
@@ -894,7 +899,8 @@ mc_status pf_tc_maps(mc_session* s) {
 // to logits[b][t][V] (sequence length S, host or device memory).
 template <typename WT>
 mc_status run_prefill(mc_session* s, int batch, const uint16_t* prompts, int stride, int Pf,
-                      int& launches, float* logits = nullptr, bool logits_dev = false, int S = 0) {
+                      int& launches, float* logits = nullptr, bool logits_dev = false, int S = 0,
+                      const mc_forward_caches* caps = nullptr) {
     const mc_model* m = s->m;
     const size_t rows = (size_t)s->Bcap * std::min(kPrefillChunk, s->cap);
     if (s->pf_rows < rows) {
@@ -919,7 +925,23 @@ mc_status run_prefill(mc_session* s, int batch, const uint16_t* prompts, int str
     constexpr bool kB16 = std::is_same<WT, __nv_bfloat16>::value;
     constexpr int KD = kB16 ? mc::TC_BF16 : mc::TC_TF32;
     // bf16 operands need rows of a multiple of 8 elements (16-byte strides)
-    const bool tc = s->pf_tc && (!kB16 || (m->D % 8 == 0 && m->F % 8 == 0));
+    // (the cache capture of model_forward runs the fp32 CUDA-core GEMMs)
+    const bool tc = s->pf_tc && !caps && (!kB16 || (m->D % 8 == 0 && m->F % 8 == 0));
+    if (caps && (!s->pf_cap_qkv || s->pf_cap_rows < s->pf_rows)) {
+        for (float** b : {&s->pf_cap_qkv, &s->pf_cap_up, &s->pf_cap_gate}) {
+            cudaFree(*b);
+            *b = nullptr;
+        }
+        const size_t R = s->pf_rows;
+        if (cudaMalloc(&s->pf_cap_qkv, R * m->Q * 4) != cudaSuccess ||
+            cudaMalloc(&s->pf_cap_up, R * m->F * 4) != cudaSuccess ||
+            cudaMalloc(&s->pf_cap_gate, R * m->F * 4) != cudaSuccess) {
+            cudaGetLastError();
+            s->pf_cap_rows = 0;
+            return fail(MC_ERR_NOMEM, "model_forward: cache staging buffers");
+        }
+        s->pf_cap_rows = R;
+    }
     if (tc && kB16 && !s->pf_xn16) {
         const size_t D = m->D, F = m->F, R = s->pf_rows;
         if (cudaMalloc(&s->pf_xn16, R * D * 2) != cudaSuccess || cudaMalloc(&s->pf_att16, R * D * 2) != cudaSuccess ||
@@ -953,6 +975,10 @@ mc_status run_prefill(mc_session* s, int batch, const uint16_t* prompts, int str
         a.FH16 = s->pf_f16;
     }
     a.status = s->status;
+    if (caps) {
+        a.UP = s->pf_cap_up;
+        a.GATE = s->pf_cap_gate;
+    }
     const char* wb = static_cast<const char*>(m->wblock);
     const WT* emb = reinterpret_cast<const WT*>(wb + m->off[0]);
     const WT* wqkv = reinterpret_cast<const WT*>(wb + m->off[1]);
@@ -976,6 +1002,16 @@ mc_status run_prefill(mc_session* s, int batch, const uint16_t* prompts, int str
                                      (int)att_smem));
     cudaStream_t st = s->stream;
     const cudaStream_t st_ = st;
+    // Copy `width` floats per chunk row from the device buffer src to the
+    // host array dst laid out as model_forward's caches: [layers][batch*S]
+    // rows, row b*S + t (the chunk's rows of sequence b are contiguous).
+    auto capture = [&](float* dst, int layer, const float* src, int width) -> cudaError_t {
+        if (!dst) return cudaSuccess;
+        const size_t w = (size_t)width, n = (size_t)a.chunk;
+        float* d0 = dst + ((size_t)layer * batch * S + a.c0) * w;
+        return cudaMemcpy2DAsync(d0, (size_t)S * w * 4, src, n * w * 4, n * w * 4, batch,
+                                 cudaMemcpyDeviceToHost, st);
+    };
     auto attention = [&](int l) {
         const dim3 grid((a.chunk + QT - 1) / QT, m->K, batch);
         switch (att_tile ? m->hd : 0) {
@@ -1051,19 +1087,39 @@ mc_status run_prefill(mc_session* s, int batch, const uint16_t* prompts, int str
                 launches += 7;
                 continue;
             }
+            if (caps) MC_CUDA(capture(caps->resid_attn, l, a.X, m->D));
             mc::pf_gemm_kernel<WT, mc::EPI_QKV><<<with_split(grid2(m->Q, M), m->D), 256, 0, st>>>(
                 a, a.XN, M, m->Q, m->D, wqkv + l * Q * D, nullptr, nullptr, 0, l, s->pf_part, s->pf_cnt);
+            if (caps && caps->qkv) {
+                mc::pf_gather_qkv_kernel<<<M, 256, 0, st>>>(a, l, s->pf_cap_qkv);
+                MC_CUDA(capture(caps->qkv, l, s->pf_cap_qkv, m->Q));
+                launches++;
+            }
             attention(l);
+            if (caps) MC_CUDA(capture(caps->attn_out, l, a.ATT, m->D));
             mc::pf_gemm_kernel<WT, mc::EPI_RESID><<<with_split(grid2(m->D, M), m->D), 256, 0, st>>>(
                 a, a.ATT, M, m->D, m->D, wproj + l * D * D, nullptr, a.X, m->D, l, s->pf_part, s->pf_cnt);
+            if (caps) MC_CUDA(capture(caps->resid_ffn, l, a.X, m->D));
             mc::pf_norm_kernel<WT><<<(M + 7) / 8, 256, 0, st>>>(a, emb, rms2 + l * D, 0);
             mc::pf_gemm_kernel<WT, mc::EPI_SWIGLU><<<with_split(grid2(m->F, M), m->D), 256, 0, st>>>(
                 a, a.XN, M, m->F, m->D, wup + l * F * D, wgate + l * F * D, a.FH, m->F, l, s->pf_part,
                 s->pf_cnt);
+            if (caps) {
+                MC_CUDA(capture(caps->up_buf, l, a.UP, m->F));
+                MC_CUDA(capture(caps->gate_buf, l, a.GATE, m->F));
+                MC_CUDA(capture(caps->ffn_buf, l, a.FH, m->F));
+            }
             mc::pf_gemm_kernel<WT, mc::EPI_RESID><<<with_split(grid2(m->D, M), m->F), 256, 0, st>>>(
                 a, a.FH, M, m->D, m->F, wdown + l * D * F, nullptr, a.X, m->D, l, s->pf_part, s->pf_cnt);
             launches += 7;
         }
+        if (caps && !logits && (caps->x || caps->x_norm)) {
+            const float* rmsf = m->norms + 2 * (size_t)m->L * m->D;
+            mc::pf_norm_kernel<WT><<<(M + 7) / 8, 256, 0, st>>>(a, emb, rmsf, 0);
+            launches++;
+        }
+        if (caps) MC_CUDA(capture(caps->x, 0, a.X, m->D));
+        if (caps && !logits) MC_CUDA(capture(caps->x_norm, 0, a.XN, m->D));
         if (logits) {
             const float* rmsf = m->norms + 2 * (size_t)m->L * m->D;
             mc::pf_norm_kernel<WT><<<(M + 7) / 8, 256, 0, st>>>(a, emb, rmsf, 0);
@@ -1081,6 +1137,7 @@ mc_status run_prefill(mc_session* s, int batch, const uint16_t* prompts, int str
                     a, a.XN, M, m->V, m->D, emb, nullptr, s->pf_logits, m->V, 0, nullptr, nullptr);
             }
             launches += 2;
+            if (caps) MC_CUDA(capture(caps->x_norm, 0, a.XN, m->D));
             // rows of sequence b are contiguous in the chunk and in the output
             const size_t n = a.chunk, V = m->V;
             for (int b = 0; b < batch; b++)
@@ -1111,6 +1168,8 @@ mc_status run_batched(mc_session* s, mc::LoopParams<WT>& p) {
     constexpr bool kB16 = std::is_same<WT, __nv_bfloat16>::value;
     constexpr int KD = kB16 ? mc::TC_BF16 : mc::TC_TF32;
     constexpr int BN = 64;                       // sequences per decode GEMM tile
+    // ring stages: the bf16 stages carry two activation tiles
+    constexpr int ST1 = kB16 ? 6 : 8, ST2 = kB16 ? 4 : 5;
     fill_params(p, s);
     p.stamps = s->stamps;
     s->last_T = p.T;
@@ -1133,10 +1192,11 @@ mc_status run_batched(mc_session* s, mc::LoopParams<WT>& p) {
     if (!s->bd_lists) {
         bool ok = cudaMalloc(&s->bd_lists, mc::bd_lists_ints(s->Bcap) * 4) == cudaSuccess &&
                   cudaMalloc(&s->bd_xn, Bc * D * 4) == cudaSuccess;
+        // bf16 operands: rows [0, Bc) hi halves, rows [Bc, 2 Bc) lo halves
         if (ok && kB16)
-            ok = cudaMalloc(&s->bd_xn16, Bc * D * 2) == cudaSuccess &&
-                 cudaMalloc(&s->bd_att16, Bc * D * 2) == cudaSuccess &&
-                 cudaMalloc(&s->bd_f16, Bc * F * 2) == cudaSuccess;
+            ok = cudaMalloc(&s->bd_xn16, 2 * Bc * D * 2) == cudaSuccess &&
+                 cudaMalloc(&s->bd_att16, 2 * Bc * D * 2) == cudaSuccess &&
+                 cudaMalloc(&s->bd_f16, 2 * Bc * F * 2) == cudaSuccess;
         if (!ok) {
             cudaGetLastError();
             return fail(MC_ERR_NOMEM, "batched decode buffers");
@@ -1156,9 +1216,10 @@ mc_status run_batched(mc_session* s, mc::LoopParams<WT>& p) {
     if (!s->bd_maps_ok) {
         const int es = kB16 ? 2 : 4;
         mc_status st = MC_OK;
-        if (!st) st = tc_map(&s->bd_xmap[0], kB16 ? (const void*)s->bd_xn16 : (const void*)s->bd_xn, es, D, Bc, 0, BN);
-        if (!st) st = tc_map(&s->bd_xmap[1], kB16 ? (const void*)s->bd_att16 : (const void*)s->att, es, D, Bc, 0, BN);
-        if (!st) st = tc_map(&s->bd_xmap[2], kB16 ? (const void*)s->bd_f16 : (const void*)s->f, es, F, Bc, 0, BN);
+        const uint64_t xrows = kB16 ? 2 * Bc : Bc;
+        if (!st) st = tc_map(&s->bd_xmap[0], kB16 ? (const void*)s->bd_xn16 : (const void*)s->bd_xn, es, D, xrows, 0, BN);
+        if (!st) st = tc_map(&s->bd_xmap[1], kB16 ? (const void*)s->bd_att16 : (const void*)s->att, es, D, xrows, 0, BN);
+        if (!st) st = tc_map(&s->bd_xmap[2], kB16 ? (const void*)s->bd_f16 : (const void*)s->f, es, F, xrows, 0, BN);
         const char* wb = static_cast<const char*>(m->wblock);
         const uint64_t L = m->L;
         if (!st) st = tc_map(&s->bd_wmap[0], wb + m->off[1], es, D, Q, L, mc::TC_BM);
@@ -1194,6 +1255,7 @@ mc_status run_batched(mc_session* s, mc::LoopParams<WT>& p) {
     const mc::BdLists L{s->bd_lists, s->Bcap};
     mc::TcArgs g{};
     g.M = p.B;
+    g.x_lo_row = kB16 ? (int)Bc : 0;
     g.act = L.base + 4 + 2 * (size_t)s->Bcap;      // act_fwd
     g.tpos = L.base + 2;
     g.status = s->status;
@@ -1233,7 +1295,7 @@ mc_status run_batched(mc_session* s, mc::LoopParams<WT>& p) {
                 break;
             g.layer = l;
             g.N = m->Q; g.K = m->D; g.ldc = m->Q; g.ksplit = ks_qkv;
-            if ((e = tc_dec_launch<KD, mc::EPI_PART, BN, 8>(xm[0], wm[0], wm[0], g, st)) != cudaSuccess) break;
+            if ((e = tc_dec_launch<KD, mc::EPI_PART, BN, ST1>(xm[0], wm[0], wm[0], g, st)) != cudaSuccess) break;
             if (att_lane)
                 e = launch_pdl(m->hd == 32 ? mc::bd_attw_kernel<WT, 32> : mc::bd_attw_kernel<WT, 64>,
                                dim3(att_units), dim3(mc::kBdWWarps * 32), att_smem, st, p, L, l, t, klen,
@@ -1246,18 +1308,18 @@ mc_status run_batched(mc_session* s, mc::LoopParams<WT>& p) {
                                         s->bd_att16)) != cudaSuccess)
                 break;
             g.N = m->D; g.K = m->D; g.ldc = m->D; g.ksplit = ks_proj;
-            if ((e = tc_dec_launch<KD, mc::EPI_PART, BN, 8>(xm[1], wm[1], wm[1], g, st)) != cudaSuccess) break;
+            if ((e = tc_dec_launch<KD, mc::EPI_PART, BN, ST1>(xm[1], wm[1], wm[1], g, st)) != cudaSuccess) break;
             if ((e = launch_pdl(mc::bd_norm_kernel<WT>, dim3(p.B), dim3(mc::kThreads), 0, st, p, L, 0,
                                 m->norms + ((size_t)m->L + l) * D, 0, s->bd_xn, xn16, s->bd_part, ks_proj)) !=
                 cudaSuccess)
                 break;
             g.N = m->F; g.K = m->D; g.ldc = 2 * m->F; g.ksplit = ks_up;
-            if ((e = tc_dec_launch<KD, mc::EPI_PART2, BN, 5>(xm[0], wm[2], wm[3], g, st)) != cudaSuccess) break;
+            if ((e = tc_dec_launch<KD, mc::EPI_PART2, BN, ST2>(xm[0], wm[2], wm[3], g, st)) != cudaSuccess) break;
             if ((e = launch_pdl(mc::bd_swiglu_kernel<WT>, dim3(swiglu_blocks), dim3(mc::kThreads), 0, st, p, L,
                                 (const float*)s->bd_part, ks_up, f16)) != cudaSuccess)
                 break;
             g.N = m->D; g.K = m->F; g.ldc = m->D; g.ksplit = ks_down;
-            if ((e = tc_dec_launch<KD, mc::EPI_PART, BN, 8>(xm[2], wm[4], wm[4], g, st)) != cudaSuccess) break;
+            if ((e = tc_dec_launch<KD, mc::EPI_PART, BN, ST1>(xm[2], wm[4], wm[4], g, st)) != cudaSuccess) break;
             launches += kB16 ? 9 : 8;
         }
         if (e != cudaSuccess) break;
@@ -1271,7 +1333,7 @@ mc_status run_batched(mc_session* s, mc::LoopParams<WT>& p) {
         gh.N = m->V; gh.K = m->D; gh.C = s->logits; gh.ldc = m->V; gh.layer = 0; gh.ksplit = 1;
         gh.head = 1; gh.sa = p.s; gh.counts = s->counts; gh.banned = s->banned;
         gh.amax_v = s->amax_v; gh.amax_i = s->amax_i;
-        if ((e = tc_dec_launch<KD, mc::TCE_STORE, BN, 8>(xm[0], wm[5], wm[5], gh, st)) != cudaSuccess) break;
+        if ((e = tc_dec_launch<KD, mc::TCE_STORE, BN, ST1>(xm[0], wm[5], wm[5], gh, st)) != cudaSuccess) break;
         if ((e = launch_pdl(mc::bd_sample_kernel<WT>, dim3(s->grid), dim3(mc::kThreads), s->smem, st, p, L,
                             (int)((m->V + mc::TC_BM - 1) / mc::TC_BM))) != cudaSuccess)
             break;
@@ -1550,7 +1612,7 @@ namespace {
 
 template <typename WT>
 mc_status model_forward_t(mc_session* s, int batch, int seq, const uint16_t* tokens, float* logits,
-                          bool dev) {
+                          bool dev, const mc_forward_caches* caps = nullptr) {
     const mc_model* m = s->m;
     const uint16_t* dtok = tokens;
     if (!dev) {
@@ -1562,7 +1624,7 @@ mc_status model_forward_t(mc_session* s, int batch, int seq, const uint16_t* tok
     MC_CUDA(cudaMemsetAsync(s->status, 0, 256, s->stream));
     MC_CUDA(cudaEventRecord(s->ev0, s->stream));
     int launches = 0;
-    const mc_status st = run_prefill<WT>(s, batch, dtok, seq, seq, launches, logits, dev, seq);
+    const mc_status st = run_prefill<WT>(s, batch, dtok, seq, seq, launches, logits, dev, seq, caps);
     if (st) return st;
     MC_CUDA(cudaEventRecord(s->ev1, s->stream));
     int status = 0;
@@ -1594,6 +1656,19 @@ mc_status mc_model_forward(mc_session* s, int batch, int seq, const uint16_t* to
     return model_forward_t<float>(s, batch, seq, tokens, logits_out, dev);
 }
 
+mc_status mc_model_forward_caches(mc_session* s, int batch, int seq, const uint16_t* tokens,
+                                  const mc_forward_caches* caps) {
+    if (!s || !tokens || !caps) return fail(MC_ERR_INVALID, "null argument");
+    if (batch <= 0 || batch > s->Bcap || seq <= 0 || seq > s->cap)
+        return fail(MC_ERR_INVALID, "model_forward: batch %d, seq %d outside [1, %d] x [1, %d]", batch, seq,
+                    s->Bcap, s->cap);
+    if (!prefill_ok(s->m)) return fail(MC_ERR_UNSUPPORTED, "model_forward: no batched kernels for this shape");
+    MC_CUDA(cudaSetDevice(s->m->device));
+    if (s->m->dtype == MC_WEIGHTS_BF16)
+        return model_forward_t<__nv_bfloat16>(s, batch, seq, tokens, caps->logits, false, caps);
+    return model_forward_t<float>(s, batch, seq, tokens, caps->logits, false, caps);
+}
+
 mc_status mc_forward_logits(mc_session* s, int batch, const uint16_t* tokens, int n, float* out) {
     if (!s) return fail(MC_ERR_INVALID, "null session");
     if (batch <= 0 || batch > s->Bcap || n <= 0 || n > s->cap || !tokens || !out)
@@ -1621,6 +1696,42 @@ mc_status mc_next_token_stats(mc_session* s, const uint16_t* tokens, int n, int 
     MC_CUDA(cudaMemcpyAsync(out, s->stats, sizeof(*out), cudaMemcpyDeviceToHost, s->stream));
     MC_CUDA(cudaStreamSynchronize(s->stream));
     s->last_launches += 1;
+    return MC_OK;
+}
+
+// Device buffers of mc_matmul, per device, grown on demand and kept.
+namespace {
+struct MatmulScratch {
+    float* buf;
+    size_t floats;
+};
+MatmulScratch g_mm[64];
+}  // namespace
+
+mc_status mc_matmul(float* out, const float* x, const float* w, int n, int d_in, int d_out) {
+    if (!out || !x || !w || n <= 0 || d_in <= 0 || d_out <= 0)
+        return fail(MC_ERR_INVALID, "matmul: null operand or empty shape");
+    int dev = 0;
+    MC_CUDA(cudaGetDevice(&dev));
+    if (dev < 0 || dev >= 64) return fail(MC_ERR_UNSUPPORTED, "device index %d", dev);
+    const size_t nx = (size_t)n * d_in, nw = (size_t)d_out * d_in, no = (size_t)n * d_out;
+    MatmulScratch& sc = g_mm[dev];
+    if (sc.floats < nx + nw + no) {
+        cudaFree(sc.buf);
+        sc.buf = nullptr;
+        sc.floats = 0;
+        MC_CUDA(cudaMalloc(&sc.buf, (nx + nw + no) * 4));
+        sc.floats = nx + nw + no;
+    }
+    float* dx = sc.buf;
+    float* dw = dx + nx;
+    float* dout = dw + nw;
+    MC_CUDA(cudaMemcpy(dx, x, nx * 4, cudaMemcpyHostToDevice));
+    MC_CUDA(cudaMemcpy(dw, w, nw * 4, cudaMemcpyHostToDevice));
+    const dim3 grid((d_out + mc::kMmTile - 1) / mc::kMmTile, (n + mc::kMmTile - 1) / mc::kMmTile);
+    mc::matmul_f32_kernel<<<grid, 256>>>(dx, dw, dout, n, d_in, d_out);
+    MC_CUDA(cudaGetLastError());
+    MC_CUDA(cudaMemcpy(out, dout, no * 4, cudaMemcpyDeviceToHost));
     return MC_OK;
 }
 

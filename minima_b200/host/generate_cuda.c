@@ -4,11 +4,12 @@
  *
  * Same entry points, signatures, validation order and return values as
  * generate.c (cited per function).  Host-side dependencies are the ones
- * generate.c has on the rest of the program: model_validate (model.c:55-89),
- * arena_alloc / arena_reset (arena.c:127-177) and, for
- * generation_check_kv_cache only, activations_init / model_forward
- * (forward.c:124-274).  Inside Minima those come from its own files; a
- * standalone program links libminima_host.so instead.
+ * generate.c has on the rest of the program: model_validate (model.c:55-89)
+ * and arena_alloc / arena_reset (arena.c:127-177).  Inside Minima those
+ * come from its own files; a standalone program links libminima_host.so
+ * instead.  generation_check_kv_cache compares two device paths, as the
+ * reference compares its two CPU paths: the token loop position by position
+ * and the batched causal forward (the drop-in model_forward's kernels).
  *
  * Device state (uploaded weights, device KV caches) is kept in small side
  * tables keyed by the caller's Model* / KVCache*, so the reference structs
@@ -27,11 +28,6 @@
 bool model_validate(const Model* model);
 void* arena_alloc(Arena* a, size_t n);
 void arena_reset(Arena* a);
-/* Optional: only generation_check_kv_cache needs the CPU full forward. */
-bool activations_init(Activations* act, Arena* temp_arena, int batch, int seq,
-    const Model* model) __attribute__((weak));
-float* model_forward(Model* model, Activations* act, const uint16_t* tokens,
-    int batch, int seq) __attribute__((weak));
 
 /* ------------------------------------------------------------ side tables */
 
@@ -131,7 +127,10 @@ static mc_model_desc describe(const Model* m) {
     return d;
 }
 
+static void drop_forward_sessions_of(mc_model* dev);
+
 static void drop_sessions_of(mc_model* dev) {
+    drop_forward_sessions_of(dev);
     for (int i = 0; i < MAX_CACHES; i++)
         if (g_caches[i].key && g_caches[i].dev == dev) {
             mc_session_destroy(g_caches[i].sess);
@@ -204,6 +203,62 @@ static mc_session* device_session(const KVCache* cache, mc_model* dev, int batch
     e->cap = cache->max_seq;
     e->bcap = batch;
     return s;
+}
+
+/* Forward sessions, one per model (the drop-in model_forward's device
+   state), grown to the largest batch and sequence length asked for. */
+typedef struct {
+    const Model* key;
+    mc_session* sess;
+    mc_model* dev;
+    int bcap, cap;
+} ForwardEntry;
+static ForwardEntry g_forward[MAX_MODELS];
+
+struct mc_session* minima_cuda_forward_session(const Model* model, int batch, int seq) {
+    if (!model || batch <= 0 || seq <= 0 || batch > MC_MAX_BATCH || seq > model->max_seq) return NULL;
+    mc_model* dev = device_model(model, 0);
+    if (!dev) return NULL;
+    ForwardEntry* e = NULL;
+    for (int i = 0; i < MAX_MODELS && !e; i++)
+        if (g_forward[i].key == model) e = &g_forward[i];
+    if (e && e->dev == dev && e->bcap >= batch && e->cap >= seq) return e->sess;
+    int bcap = batch, cap = seq;
+    if (e) {
+        if (e->dev == dev) {
+            bcap = e->bcap > bcap ? e->bcap : bcap;
+            cap = e->cap > cap ? e->cap : cap;
+        }
+        mc_session_destroy(e->sess);
+        memset(e, 0, sizeof(*e));
+    } else {
+        for (int i = 0; i < MAX_MODELS && !e; i++)
+            if (!g_forward[i].key) e = &g_forward[i];
+        if (!e) {
+            e = &g_forward[0];
+            mc_session_destroy(e->sess);
+            memset(e, 0, sizeof(*e));
+        }
+    }
+    mc_session* s = NULL;
+    if (mc_session_create(dev, bcap, cap, &s) != MC_OK) {
+        set_err("mc_session_create");
+        return NULL;
+    }
+    e->key = model;
+    e->sess = s;
+    e->dev = dev;
+    e->bcap = bcap;
+    e->cap = cap;
+    return s;
+}
+
+static void drop_forward_sessions_of(mc_model* dev) {
+    for (int i = 0; i < MAX_MODELS; i++)
+        if (g_forward[i].key && g_forward[i].dev == dev) {
+            mc_session_destroy(g_forward[i].sess);
+            memset(&g_forward[i], 0, sizeof(g_forward[i]));
+        }
 }
 
 int minima_cuda_model_sync(const Model* model) {
@@ -458,8 +513,10 @@ static float* device_prefix_logits(Model* model, KVCache* cache, const uint16_t*
     return out;
 }
 
-/* generate.c:202-265: the device incremental path against the host
-   program's full causal forward. */
+/* generate.c:202-265: the device token loop (forward_one per position)
+   against the device batched causal forward (model_forward's arithmetic),
+   with the full-forward logits kept in the caller's temp arena as the
+   reference keeps its activations there. */
 bool generation_check_kv_cache(Model* model, KVCache* cache, Arena* temp_arena,
     const uint16_t* tokens, int seq, float tolerance) {
     if (!model || !model_validate(model) || !cache || !temp_arena || !tokens || seq <= 0 ||
@@ -469,16 +526,16 @@ bool generation_check_kv_cache(Model* model, KVCache* cache, Arena* temp_arena,
         return false;
     for (int i = 0; i < seq; i++)
         if (tokens[i] >= model->vocab_size) return false;
-    if (!activations_init || !model_forward) {
-        snprintf(g_err, sizeof(g_err),
-            "generation_check_kv_cache: the host program provides no model_forward");
+    arena_reset(temp_arena);
+    float* full_logits = (float*)arena_alloc(temp_arena,
+        (size_t)seq * (size_t)model->vocab_size * sizeof(float));
+    if (!full_logits) return false;
+    struct mc_session* fs = minima_cuda_forward_session(model, 1, seq);
+    if (!fs) return false;
+    if (mc_model_forward(fs, 1, seq, tokens, full_logits, 0u) != MC_OK) {
+        set_err("mc_model_forward");
         return false;
     }
-    arena_reset(temp_arena);
-    Activations act;
-    if (!activations_init(&act, temp_arena, 1, seq, model)) return false;
-    const float* full_logits = model_forward(model, &act, tokens, 1, seq);
-    if (!full_logits) return false;
     kvcache_reset(cache);
     float* cached = device_prefix_logits(model, cache, tokens, seq);
     if (!cached) return false;

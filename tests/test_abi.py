@@ -52,6 +52,24 @@ def test_libraries_export_every_declared_symbol():
         assert hasattr(gen, name), name
     assert set(M.CUDA_SYMBOLS) <= cuda_decl
     assert set(M.GENERATE_SYMBOLS) <= gen_decl
+    fwd = M.forward_lib()
+    fwd_decl = declared_functions("minima_forward.h")
+    assert fwd_decl == set(M.FORWARD_SYMBOLS)
+    for name in fwd_decl:
+        assert hasattr(fwd, name), name
+
+
+def test_forward_drop_in_exports_match_reference_forward_h():
+    """libminima_forward.so defines every function of the reference's
+    forward.h:43-57, and the scalar helpers compute what forward.c does."""
+    out = subprocess.run(["nm", "-D", "--defined-only", M.LIB_FWD], capture_output=True, text=True,
+                         check=True).stdout
+    for name in M.FORWARD_SYMBOLS:
+        assert re.search(rf"\bT {name}\b", out), name
+    fwd = M.forward_lib()
+    for v in (-3.5, -0.25, 0.0, 0.7, 12.0):
+        want = np.float32(v) / (np.float32(1) + np.exp(np.float64(-v)).astype(np.float32))
+        assert abs(np.float32(fwd.silu(v)) - want) <= 2 * np.spacing(np.float32(abs(want)))
 
 
 def test_exports_match_reference_generate_h():
