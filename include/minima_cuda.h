@@ -115,6 +115,23 @@ mc_status mc_model_destroy(mc_model* model);
    max_seq tokens each (max_seq <= the model's max_seq). */
 mc_status mc_session_create(mc_model* model, int max_batch, int max_seq,
     mc_session** out);
+
+/*
+ * A session whose KV cache is paged: a pool of n_pages pages, each holding
+ * page_len consecutive positions of one sequence for every layer and KV
+ * head (page_len a power of two >= MC_MIN_PAGE_LEN), and a per-sequence
+ * page table.  The reference's KVCache (generate.h:11-24; kvcache_init,
+ * generate.c:13-47) reserves max_seq positions per sequence; here each
+ * mc_generate call gives every sequence ceil((prompt + new ids - 1) /
+ * page_len) pages (mc_forward_logits / mc_model_forward: the positions
+ * they feed), so a batch of mixed lengths needs only the pages it fills.
+ * A call whose sequences need more pages than the pool holds returns
+ * MC_ERR_NOMEM.  mc_session_create is the same with an identity table of
+ * max_batch * ceil(max_seq / MC_MIN_PAGE_LEN) pages.
+ */
+#define MC_MIN_PAGE_LEN 64
+mc_status mc_session_create_paged(mc_model* model, int max_batch, int max_seq, int page_len,
+    int n_pages, mc_session** out);
 mc_status mc_session_destroy(mc_session* session);
 
 /*

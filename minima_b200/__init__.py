@@ -33,7 +33,8 @@ CUDA_SYMBOLS = ("mc_init", "mc_model_create", "mc_model_update", "mc_model_destr
                 "mc_last_kernel_ms", "mc_last_launch_count", "mc_last_step_times",
                 "mc_last_kernel_name", "mc_last_prefill", "mc_session_stream", "mc_last_error",
                 "mc_checkpoint_inspect", "mc_model_load_checkpoint", "mc_gemm",
-                "mc_model_forward", "mc_next_token_stats", "mc_generate_static")
+                "mc_model_forward", "mc_next_token_stats", "mc_generate_static",
+                "mc_session_create_paged", "mc_model_forward_caches", "mc_matmul")
 GENERATE_SYMBOLS = ("kvcache_init", "kvcache_reset", "generation_check_kv_cache",
                     "generation_inspect_next_tokens", "generate", "generate_with_options",
                     "generate_ex", "generate_batch_with_options", "minima_cuda_select_device",
@@ -215,6 +216,7 @@ def _declare(host, cuda, gen):
     cuda.mc_model_update.argtypes = [vp, C.POINTER(ModelDesc)]
     cuda.mc_model_destroy.argtypes = [vp]
     cuda.mc_session_create.argtypes = [vp, C.c_int, C.c_int, C.POINTER(vp)]
+    cuda.mc_session_create_paged.argtypes = [vp, C.c_int, C.c_int, C.c_int, C.c_int, C.POINTER(vp)]
     cuda.mc_session_destroy.argtypes = [vp]
     cuda.mc_generate.argtypes = [vp, C.c_int, vp, C.c_int, i32p, vp, C.c_int,
                                  C.POINTER(GenerationOptions), vp, vp, vp, C.c_uint, _f32p, C.c_int]
@@ -509,12 +511,20 @@ class DeviceModel:
 class Session:
     """mc_session: device KV cache and work buffers for up to max_batch sequences."""
 
-    def __init__(self, dm: DeviceModel, max_batch: int, max_seq: int):
+    def __init__(self, dm: DeviceModel, max_batch: int, max_seq: int, page_len: int = 0,
+                 n_pages: int = 0):
+        """page_len > 0: a paged KV cache of n_pages pages of page_len
+        positions (mc_session_create_paged); else every sequence owns
+        max_seq positions."""
         _, cuda, _ = libs()
         self.dm = dm
         self.h = C.c_void_p()
-        _check(cuda.mc_session_create(dm.h, max_batch, max_seq, C.byref(self.h)),
-               "mc_session_create")
+        if page_len:
+            _check(cuda.mc_session_create_paged(dm.h, max_batch, max_seq, page_len, n_pages,
+                                                C.byref(self.h)), "mc_session_create_paged")
+        else:
+            _check(cuda.mc_session_create(dm.h, max_batch, max_seq, C.byref(self.h)),
+                   "mc_session_create")
 
     def generate(self, prompts, prompt_lens, out_cap, opts, rng_states, trace_steps=0):
         """mc_generate with host buffers; returns (out, counts, rng_states, final_pos[, trace])."""

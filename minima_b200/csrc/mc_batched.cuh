@@ -225,9 +225,10 @@ __global__ void __launch_bounds__(kBdAttThreads) bd_att_kernel(const LoopParams<
     if (b >= p.B) return;
     const int j0 = s * klen, j1 = min(nkeys, j0 + klen);
     const int ntiles = (j1 - j0 + kBdTile - 1) / kBdTile;
-    const size_t cache_off = (((size_t)l * p.Bcap + b) * p.K + g) * p.cap;
-    const float* kb = p.kc + (cache_off + j0) * hd;
-    const float* vb = p.vc + (cache_off + j0) * hd;
+    // tiles of kBdTile (64) keys from j0 (a multiple of 64): each in one page
+    auto krow_of = [&](int j) { return kv_row(p.pg, p.L, p.K, l, b, g, j); };
+    const float* kb = p.kc + krow_of(j0) * hd;
+    const float* vb = p.vc + krow_of(j0) * hd;
     int* flag = reinterpret_cast<int*>(smem_f);
     float* kt = smem_f + 4;                  // [kBdRing][kBdTile][hd], 16-byte aligned
     float* vt = kt + kBdRing * kBdTile * hd;
@@ -274,15 +275,18 @@ __global__ void __launch_bounds__(kBdAttThreads) bd_att_kernel(const LoopParams<
         const int nt = i < ntiles ? min(kBdTile, j1 - j0 - k0) - (has_t && i == ntiles - 1 ? 1 : 0) : 0;
         float* kd = kt + (i % kBdRing) * kBdTile * hd;
         float* vd = vt + (i % kBdRing) * kBdTile * hd;
+        const size_t r0 = nt > 0 ? krow_of(j0 + k0) : 0;
+        const float* ks = p.kc + r0 * hd;
+        const float* vs = p.vc + r0 * hd;
         if (vec) {
             for (int e = threadIdx.x; e < nt * q4; e += blockDim.x) {
-                cp_async16(kd + 4 * e, kb + (size_t)k0 * hd + 4 * e);
-                cp_async16(vd + 4 * e, vb + (size_t)k0 * hd + 4 * e);
+                cp_async16(kd + 4 * e, ks + 4 * e);
+                cp_async16(vd + 4 * e, vs + 4 * e);
             }
         } else {
             for (int e = threadIdx.x; e < nt * hd; e += blockDim.x) {
-                kd[e] = ldcg(kb + (size_t)k0 * hd + e);
-                vd[e] = ldcg(vb + (size_t)k0 * hd + e);
+                kd[e] = ldcg(ks + e);
+                vd[e] = ldcg(vs + e);
             }
         }
         cp_async_commit();
@@ -357,7 +361,7 @@ __global__ void __launch_bounds__(kBdAttThreads) bd_att_kernel(const LoopParams<
             const int k = i - G * hp;
             const bool isk = k < hp;
             const int d = 2 * (isk ? k : k - hp);
-            float* dst = (isk ? p.kc : p.vc) + (cache_off + t) * hd + d;
+            float* dst = (isk ? p.kc : p.vc) + krow_of(t) * hd + d;
             const float* row = isk ? krow : vrow;
             dst[0] = row[d];
             dst[1] = row[d + 1];
@@ -528,9 +532,6 @@ __global__ void __launch_bounds__(kBdWWarps * 32) bd_attw_kernel(const LoopParam
     const int b = u / (nsplit * p.K);
     if (b >= p.B) return;
     const int j0 = s * klen, j1 = min(nkeys, j0 + klen);
-    const size_t cache_off = (((size_t)l * p.Bcap + b) * p.K + g) * p.cap;
-    const float* kbase = p.kc + cache_off * HD;
-    const float* vbase = p.vc + cache_off * HD;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     constexpr int KLD = HD + 4;                           // K tile row stride
     float* qs = smem_f;                                   // [G][HD]
@@ -557,9 +558,15 @@ __global__ void __launch_bounds__(kBdWWarps * 32) bd_attw_kernel(const LoopParam
     const bool has_t = nq > 0 && s == nsplit - 1;
     const int nchunks = (j1 - j0 + 31) / 32;
     // K and V rows [r0, r1) of chunk c -> this warp's tiles (16-byte pieces, coalesced)
+    // chunk c holds keys j0 + 32 c ... (32-aligned, so in one page)
     auto issue = [&](int c, int r0, int r1) {
-        const float* ksrc = kbase + (size_t)(j0 + 32 * c) * HD;
-        const float* vsrc = vbase + (size_t)(j0 + 32 * c) * HD;
+        if (r1 <= r0) {
+            cp_async_commit();
+            return;
+        }
+        const size_t row = kv_row(p.pg, p.L, p.K, l, b, g, j0 + 32 * c);
+        const float* ksrc = p.kc + row * HD;
+        const float* vsrc = p.vc + row * HD;
         for (int e = r0 * Q4 + lane; e < r1 * Q4; e += 32) {
             const int r = e / Q4, c4 = e - r * Q4;
             cp_async16(wk + r * KLD + 4 * c4, ksrc + 4 * e);
@@ -601,7 +608,7 @@ __global__ void __launch_bounds__(kBdWWarps * 32) bd_attw_kernel(const LoopParam
                 const bool isk = k < HP;
                 const int pr = isk ? k : k - HP;
                 col = (isk ? p.H + g : p.H + p.K + g) * HD + 2 * pr;
-                dst = (isk ? p.kc : p.vc) + (cache_off + t) * HD + 2 * pr;
+                dst = (isk ? p.kc : p.vc) + kv_row(p.pg, p.L, p.K, l, b, g, t) * HD + 2 * pr;
                 rope = isk;
             }
             float x0 = 0.0f, x1 = 0.0f;

@@ -227,15 +227,25 @@ __device__ void lc_norm(const float* x, float* xn, const float* scale, const int
 // t is produced in this step and is read from the qkv buffer instead, so the
 // copies stop below it.  Thread 0 only; after a failed wait no further
 // copies are issued (the cluster leaves at its next barrier).
-__device__ __forceinline__ void att_issue_tile(const ClusterParams& cp, LcState& S, const float* kg,
-                                               const float* vg, int a0, int n, int t, int hd) {
+// Keys [a0, a0 + rows) of (layer l, sequence b, KV head g) are contiguous
+// within a page only, so the tile arrives as one K and one V copy per page
+// it touches (row t, written in this step, is never copied).
+__device__ __forceinline__ void att_issue_tile(const ClusterParams& cp, LcState& S, int l, int b, int g,
+                                               int a0, int n, int t, int hd) {
     if (S.ints[39]) return;
+    const LoopParams<float>& p = cp.lp;
     const int rows = min(n, t - a0);
     const unsigned bytes = rows > 0 ? (unsigned)(rows * hd * 4) : 0u;
     mbar_expect_tx(S.kvbar, 2 * bytes);
-    if (bytes) {
-        bulk_g2s(S.kv, kg + (size_t)a0 * hd, bytes, S.kvbar);
-        bulk_g2s(S.kv + (size_t)cp.kv_tile * hd, vg + (size_t)a0 * hd, bytes, S.kvbar);
+    const int plen = 1 << p.pg.shift;
+    for (int r = 0; r < rows;) {
+        const int j = a0 + r;
+        const int seg = min(rows - r, plen - (j & (plen - 1)));
+        const size_t row = kv_row(p.pg, p.L, p.K, l, b, g, j);
+        const unsigned sb = (unsigned)(seg * hd * 4);
+        bulk_g2s(S.kv + (size_t)r * hd, p.kc + row * hd, sb, S.kvbar);
+        bulk_g2s(S.kv + (size_t)(cp.kv_tile + r) * hd, p.vc + row * hd, sb, S.kvbar);
+        r += seg;
     }
     S.kvpend = 1;
 }
@@ -474,9 +484,6 @@ __device__ bool lc_attention(const ClusterParams& cp, LcState& S, cg::cluster_gr
     float* vs = S.kv + (size_t)cp.kv_tile * hd;
     for (int u = crank; u < units; u += cs) {
         const AttUnit a = att_unit(u, K, ns, per, nkeys, fl);
-        const size_t cbase = (((size_t)l * p.Bcap + a.b) * K + a.g) * p.cap;
-        const float* kg = p.kc + cbase * hd;
-        const float* vg = p.vc + cbase * hd;
         const float* q = S.qkv + a.b * Q + a.g * ghd;
         const float* kq = S.qkv + a.b * Q + D + a.g * hd;          // row t of K
         const float* vq = kq + p.kvd;                              // row t of V
@@ -493,7 +500,7 @@ __device__ bool lc_attention(const ClusterParams& cp, LcState& S, cg::cluster_gr
             // every warp is past the previous tile (the barrier closing it,
             // or the merge of the previous unit): the tile buffer is free
             if (threadIdx.x == 0 && (u != crank || a0 != a.j0))
-                att_issue_tile(cp, S, kg, vg, a0, n, t, hd);
+                att_issue_tile(cp, S, l, a.b, a.g, a0, n, t, hd);
             // Row t is produced in this step: the copies stop below it and its
             // slot is filled from the qkv buffer.  V rows from n up to the next
             // multiple of 32 are cleared for the unmasked P.V.  The copies
@@ -625,10 +632,7 @@ __device__ bool lc_layer(const ClusterParams& cp, const CSlice& sl, LcState& S,
     const int units = nf * K * ns;
     if (crank < units && threadIdx.x == 0) {
         const AttUnit a = att_unit(crank, K, ns, per, nkeys, fl);
-        const size_t cbase = (((size_t)l * p.Bcap + a.b) * K + a.g) * p.cap;
-        if (a.j1 > a.j0)
-            att_issue_tile(cp, S, p.kc + cbase * hd, p.vc + cbase * hd, a.j0,
-                           min(cp.kv_tile, a.j1 - a.j0), t, hd);
+        if (a.j1 > a.j0) att_issue_tile(cp, S, l, a.b, a.g, a.j0, min(cp.kv_tile, a.j1 - a.j0), t, hd);
     }
 
     // ---- QKV + RoPE + K/V append (generate.c:99-119)
@@ -654,7 +658,7 @@ __device__ bool lc_layer(const ClusterParams& cp, const CSlice& sl, LcState& S,
             if (slot >= H) {
                 const bool isk = slot < H + K;
                 const int g = isk ? slot - H : slot - H - K;
-                (isk ? p.kc : p.vc)[((((size_t)l * p.Bcap + b) * K + g) * p.cap + t) * hd + d] = out;
+                (isk ? p.kc : p.vc)[kv_row(p.pg, p.L, K, l, b, g, t) * hd + d] = out;
                 wrote_kv = true;
             }
         }

@@ -15,6 +15,29 @@ namespace mc {
 // Device status word values (mirrors MC_* in minima_cuda.h).
 enum : int { ST_OK = 0, ST_TIMEOUT = 4, ST_DEVICE = 5 };
 
+// Paged KV cache (the reference's KVCache, generate.h:11-24, holds
+// [layer][max_seq][kv_dim] per sequence).  Here the K and V pools are
+// [n_pages][L][K][page_len][hd] fp32: a page holds page_len consecutive
+// positions of one sequence for every layer and KV head, and a sequence's
+// positions [i * page_len, (i + 1) * page_len) live in page table[b][i].
+// page_len is a power of two and a multiple of 64, so every key run the
+// attention kernels read (32 or 64 keys from a 64-aligned start) lies in
+// one page; the cluster loop's bulk copies are split at page boundaries.
+// A session without a page pool has the identity table (b * pps + i).
+struct KvPages {
+    const int* table;   // [Bcap][pps]
+    int pps;            // table entries per sequence
+    int shift;          // log2(page_len)
+};
+constexpr int kKvMinPageShift = 6;
+
+// Row index (times head_dim: the element offset) of position t of
+// (layer l, sequence b, KV head g).  t < pps << shift.
+__device__ __forceinline__ size_t kv_row(const KvPages& pg, int L, int K, int l, int b, int g, int t) {
+    const int page = __ldg(pg.table + (size_t)b * pg.pps + (t >> pg.shift));
+    return ((((size_t)page * L + l) * K + g) << pg.shift) + (size_t)(t & ((1 << pg.shift) - 1));
+}
+
 // Programmatic dependent launch (kernels launched with the programmatic
 // stream serialization attribute): pdl_wait returns once the previous kernel
 // in the stream has completed and its memory operations are visible (at

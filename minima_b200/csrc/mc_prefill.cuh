@@ -25,8 +25,9 @@ struct PrefillArgs {
     const uint16_t* prompts;
     int prompt_stride;
     const float2* rope;
-    float* kc;
+    float* kc;                 // K / V pages (KvPages)
     float* vc;
+    KvPages pg;
     float* X;                  // [B*chunk][D] residual
     float* XN;                 // [B*chunk][D]
     float* QB;                 // [B*chunk][D] rotated queries
@@ -232,8 +233,7 @@ __global__ void __launch_bounds__(256, 1) pf_gemm_kernel(PrefillArgs a, const fl
                 } else {
                     const bool isk = slot < a.H + a.K;
                     const int g = isk ? slot - a.H : slot - a.H - a.K;
-                    float* dst = (isk ? a.kc : a.vc) +
-                                 ((((size_t)layer * a.Bcap + b) * a.K + g) * a.cap + t) * a.hd + dd;
+                    float* dst = (isk ? a.kc : a.vc) + kv_row(a.pg, a.L, a.K, layer, b, g, t) * a.hd + dd;
                     dst[0] = v0;
                     dst[1] = v1;
                 }
@@ -277,7 +277,7 @@ __global__ void __launch_bounds__(256) pf_gather_qkv_kernel(PrefillArgs a, int l
             const bool isk = n < a.D + a.kvd;
             const int c = isk ? n - a.D : n - a.D - a.kvd;
             const int g = c / a.hd, dd = c % a.hd;
-            v = (isk ? a.kc : a.vc)[((((size_t)layer * a.Bcap + b) * a.K + g) * a.cap + t) * a.hd + dd];
+            v = (isk ? a.kc : a.vc)[kv_row(a.pg, a.L, a.K, layer, b, g, t) * a.hd + dd];
         }
         row[n] = v;
     }
@@ -312,16 +312,17 @@ __global__ void __launch_bounds__(256) pf_attention_kernel(PrefillArgs a, int la
     float m_run[RPW], l_run[RPW], o_acc[RPW][2];
 #pragma unroll
     for (int k = 0; k < RPW; k++) { m_run[k] = -INFINITY; l_run[k] = 0.0f; o_acc[k][0] = o_acc[k][1] = 0.0f; }
-    const size_t cbase = (((size_t)layer * a.Bcap + b) * a.K + g) * a.cap;
-    const float* kg = a.kc + cbase * hd;
-    const float* vg = a.vc + cbase * hd;
     for (int k0 = 0; k0 < qt1; k0 += PF_KT) {
         const int kn = min(PF_KT, qt1 - k0);
+        // PF_KT (64) keys from a multiple of 64: one page
+        const size_t row0 = kv_row(a.pg, a.L, a.K, layer, b, g, k0);
+        const float* kg = a.kc + row0 * hd;
+        const float* vg = a.vc + row0 * hd;
         __syncthreads();
         for (int e = threadIdx.x; e < kn * hd; e += blockDim.x) {
             const int j = e / hd, d = e % hd;
-            Ks[j * (hd + 1) + d] = ldcg(kg + (size_t)(k0 + j) * hd + d);
-            Vs[j * hd + d] = ldcg(vg + (size_t)(k0 + j) * hd + d);
+            Ks[j * (hd + 1) + d] = ldcg(kg + (size_t)j * hd + d);
+            Vs[j * hd + d] = ldcg(vg + (size_t)j * hd + d);
         }
         __syncthreads();
 #pragma unroll
@@ -437,18 +438,19 @@ __global__ void __launch_bounds__(256) pf_attention_tile_kernel(PrefillArgs a, i
 #pragma unroll
         for (int e = 0; e < E; e++) o[i][e] = 0.0f;
     }
-    const size_t cbase = (((size_t)layer * a.Bcap + b) * a.K + g) * a.cap;
-    const float* kg = a.kc + cbase * HD;
-    const float* vg = a.vc + cbase * HD;
     for (int k0 = 0; k0 < qt1; k0 += PF_KT) {
         const int kn = min(PF_KT, qt1 - k0);
+        // PF_KT (64) keys from a multiple of 64: one page
+        const size_t row0 = kv_row(a.pg, a.L, a.K, layer, b, g, k0);
+        const float* kg = a.kc + row0 * HD;
+        const float* vg = a.vc + row0 * HD;
         __syncthreads();                      // the previous tile's readers are done
         for (int e = threadIdx.x; e < PF_KT * (HD / 4); e += blockDim.x) {
             const int j = e / (HD / 4), c = e - j * (HD / 4);
             float4 kv4 = make_float4(0.f, 0.f, 0.f, 0.f), vv4 = kv4;
             if (j < kn) {
-                kv4 = ldcg4(kg + (size_t)(k0 + j) * HD + 4 * c);
-                vv4 = ldcg4(vg + (size_t)(k0 + j) * HD + 4 * c);
+                kv4 = ldcg4(kg + (size_t)j * HD + 4 * c);
+                vv4 = ldcg4(vg + (size_t)j * HD + 4 * c);
             }
             *reinterpret_cast<float4*>(Ks + j * LD + 4 * c) = kv4;
             *reinterpret_cast<float4*>(Vs + j * HD + 4 * c) = vv4;

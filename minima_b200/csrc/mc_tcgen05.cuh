@@ -197,8 +197,7 @@ __device__ __forceinline__ void tc_epilogue(const TcArgs& g, int m, int n, const
             } else {
                 const bool isk = slot < a.H + a.K;
                 const int gk = isk ? slot - a.H : slot - a.H - a.K;
-                float* dst = (isk ? a.kc : a.vc) +
-                             ((((size_t)g.layer * a.Bcap + b) * a.K + gk) * a.cap + t) * a.hd + dd;
+                float* dst = (isk ? a.kc : a.vc) + kv_row(a.pg, a.L, a.K, g.layer, b, gk, t) * a.hd + dd;
                 dst[0] = v0;
                 dst[1] = v1;
             }

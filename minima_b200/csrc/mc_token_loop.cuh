@@ -60,8 +60,9 @@ struct LoopParams {
     const float* rmsf;
     const float2* rope;   // [rope_len][hd/2] (cos, sin) computed on the host
     int rope_len;
-    float* kc;            // [L][Bcap][K][cap][hd]
-    float* vc;
+    float* kc;            // K pages [n_pages][L][K][page_len][hd] (KvPages)
+    float* vc;            // V pages, same layout
+    KvPages pg;           // page table of the sequences
     int cap;
     int Bcap;
     float* x;             // [Bcap][D] residual stream
@@ -265,8 +266,7 @@ __device__ void phase_qkv(const LoopParams<WT>& p, int l, int t, LoopSmem& sm, i
                     } else {
                         const bool isk = slot < p.H + p.K;
                         const int g = isk ? slot - p.H : slot - p.H - p.K;
-                        float* base = (isk ? p.kc : p.vc) +
-                            ((((size_t)l * p.Bcap + b) * p.K + g) * p.cap + t) * p.hd + d;
+                        float* base = (isk ? p.kc : p.vc) + kv_row(p.pg, p.L, p.K, l, b, g, t) * p.hd + d;
                         base[0] = a;
                         if (has1) base[1] = z;
                     }
@@ -301,9 +301,10 @@ __device__ void phase_att(const LoopParams<WT>& p, int l, int t, LoopSmem& sm, i
         const int g = (u / nsplit) % p.K;
         const int b = sm.fwd[u / (nsplit * p.K)];
         const int j0 = s * kSplitLen, j1 = min(nkeys, j0 + kSplitLen), n = j1 - j0;
-        const size_t cache_off = (((size_t)l * p.Bcap + b) * p.K + g) * p.cap;
-        const float* kb = p.kc + (cache_off + j0) * hd;
-        const float* vb = p.vc + (cache_off + j0) * hd;
+        // the split's kSplitLen (64) keys start 64-aligned: one page
+        const size_t row0 = kv_row(p.pg, p.L, p.K, l, b, g, j0);
+        const float* kb = p.kc + row0 * hd;
+        const float* vb = p.vc + row0 * hd;
         // stage q, and the split's K and V rows, with coalesced L2 reads
         // (rows written by other CTAs earlier in this launch)
         for (int i = threadIdx.x; i < G * hd; i += blockDim.x)

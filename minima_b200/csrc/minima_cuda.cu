@@ -88,6 +88,14 @@ struct mc_session {
     int bc, xs_ld, max_split;
     // device buffers
     float *kc, *vc, *x, *q, *att, *f, *logits, *part_o, *part_m, *part_l, *amax_v;
+    // paged KV cache (mc::KvPages): pools kc / vc of kv_pages pages of
+    // 2^kv_shift positions, table [Bcap][kv_pps] on the device and its host
+    // copy; a paged session (kv_paged) hands out pages per call from
+    // kv_order, other sessions keep the identity table
+    int* kv_table;
+    int kv_pps, kv_shift, kv_pages;
+    bool kv_paged;
+    std::vector<int> kv_host, kv_order;
     int* amax_i;
     unsigned *att_cnt, *counts, *banned;
     unsigned* bar;
@@ -195,6 +203,7 @@ void fill_params(mc::LoopParams<WT>& p, const mc_session* s) {
     p.rope = m->rope;
     p.rope_len = m->max_seq;
     p.kc = s->kc; p.vc = s->vc; p.cap = s->cap; p.Bcap = s->Bcap;
+    p.pg = mc::KvPages{s->kv_table, s->kv_pps, s->kv_shift};
     p.x = s->x; p.q = s->q; p.att = s->att; p.f = s->f; p.logits = s->logits;
     p.part_o = s->part_o; p.part_m = s->part_m; p.part_l = s->part_l;
     p.att_cnt = s->att_cnt; p.amax_v = s->amax_v; p.amax_i = s->amax_i;
@@ -499,7 +508,7 @@ mc_status mc_model_destroy(mc_model* m) {
 
 mc_status mc_session_destroy(mc_session* s) {
     if (!s) return MC_OK;
-    void* bufs[] = {s->kc, s->vc, s->x, s->q, s->att, s->f, s->logits, s->part_o, s->part_m,
+    void* bufs[] = {s->kv_table, s->kc, s->vc, s->x, s->q, s->att, s->f, s->logits, s->part_o, s->part_m,
                     s->part_l, s->amax_v, s->amax_i, s->att_cnt, s->counts, s->banned, s->bar,
                     s->status, s->seq, s->prompts, s->out, s->stop, s->trace, s->stamps,
                     s->xfin, s->hgen, s->hsync, s->hpv, s->hpi,
@@ -516,14 +525,45 @@ mc_status mc_session_destroy(mc_session* s) {
     return MC_OK;
 }
 
-mc_status mc_session_create(mc_model* m, int max_batch, int max_seq, mc_session** out) {
+}  // extern "C"
+
+namespace {
+
+// page_len 0: the identity table over max_batch * ceil(max_seq / 64) pages
+// of 64 positions (every sequence owns max_seq positions, as kvcache_init
+// reserves them); otherwise a pool of n_pages pages of page_len positions
+// handed out per call.
+mc_status session_create(mc_model* m, int max_batch, int max_seq, int page_len, int n_pages,
+                         mc_session** out) {
     if (!out) return fail(MC_ERR_INVALID, "null output handle");
     *out = nullptr;
     if (!m) return fail(MC_ERR_INVALID, "null model");
     if (max_batch <= 0 || max_batch > MC_MAX_BATCH || max_seq <= 0 || max_seq > m->max_seq)
         return fail(MC_ERR_INVALID, "session batch %d / max_seq %d outside [1,%d] / [1,%d]",
                     max_batch, max_seq, MC_MAX_BATCH, m->max_seq);
+    const bool paged = page_len != 0;
+    if (paged && (page_len < MC_MIN_PAGE_LEN || (page_len & (page_len - 1)) || page_len > MC_MAX_SEQ ||
+                  n_pages <= 0))
+        return fail(MC_ERR_INVALID, "page_len %d (a power of two >= %d) / n_pages %d", page_len,
+                    MC_MIN_PAGE_LEN, n_pages);
+    if (!paged) page_len = MC_MIN_PAGE_LEN;
+    int shift = 0;
+    while ((1 << shift) < page_len) shift++;
+    const int pps = (max_seq + page_len - 1) / page_len;
+    if (!paged) n_pages = max_batch * pps;
     mc_session* s = new mc_session();
+    s->kv_paged = paged;
+    s->kv_shift = shift;
+    s->kv_pps = pps;
+    s->kv_pages = n_pages;
+    s->kv_host.assign((size_t)max_batch * pps, 0);
+    if (paged) {
+        // handed out from the top of the pool down, so that consecutive
+        // positions of a sequence never sit in consecutive pages
+        for (int i = n_pages - 1; i >= 0; i--) s->kv_order.push_back(i);
+    } else {
+        for (size_t i = 0; i < s->kv_host.size(); i++) s->kv_host[i] = (int)i;
+    }
     {
         const char* pe = getenv("MINIMA_CUDA_PREFILL");
         s->pf_tc = pe && std::strcmp(pe, "tcgen05") == 0;
@@ -589,9 +629,11 @@ mc_status mc_session_create(mc_model* m, int max_batch, int max_seq, mc_session*
 
     const size_t B = max_batch, L = m->L, K = m->K, hd = m->hd, D = m->D, F = m->F, V = m->V;
     const size_t H = m->H, cap = max_seq, ms = s->max_split;
+    const size_t page_floats = L * K * ((size_t)1 << shift) * hd;
     struct Alloc { void** p; size_t bytes; } allocs[] = {
-        {(void**)&s->kc, L * B * K * cap * hd * 4},
-        {(void**)&s->vc, L * B * K * cap * hd * 4},
+        {(void**)&s->kc, (size_t)n_pages * page_floats * 4},
+        {(void**)&s->vc, (size_t)n_pages * page_floats * 4},
+        {(void**)&s->kv_table, s->kv_host.size() * 4},
         {(void**)&s->x, B * D * 4},
         {(void**)&s->q, B * D * 4},
         {(void**)&s->att, B * D * 4},
@@ -643,6 +685,8 @@ mc_status mc_session_create(mc_model* m, int max_batch, int max_seq, mc_session*
         }
     }
     e = cudaMemset(s->att_cnt, 0, B * K * 4);
+    if (e == cudaSuccess)
+        e = cudaMemcpy(s->kv_table, s->kv_host.data(), s->kv_host.size() * 4, cudaMemcpyHostToDevice);
     if (e == cudaSuccess) e = cudaStreamCreateWithFlags(&s->stream, cudaStreamNonBlocking);
     if (e == cudaSuccess) e = cudaEventCreate(&s->ev0);
     if (e == cudaSuccess) e = cudaEventCreate(&s->ev_mid);
@@ -655,9 +699,47 @@ mc_status mc_session_create(mc_model* m, int max_batch, int max_seq, mc_session*
     return MC_OK;
 }
 
+}  // namespace
+
+extern "C" {
+
+mc_status mc_session_create(mc_model* m, int max_batch, int max_seq, mc_session** out) {
+    return session_create(m, max_batch, max_seq, 0, 0, out);
+}
+
+mc_status mc_session_create_paged(mc_model* m, int max_batch, int max_seq, int page_len, int n_pages,
+                                  mc_session** out) {
+    if (page_len == 0) return fail(MC_ERR_INVALID, "page_len 0");
+    return session_create(m, max_batch, max_seq, page_len, n_pages, out);
+}
+
 }  // extern "C"
 
 namespace {
+
+// Pages for positions [0, positions[b]) of sequences b < batch of a paged
+// session, from the pool in kv_order (a call starts every sequence at
+// position 0, so the whole pool is free at each call).  Unassigned table
+// entries repeat the sequence's last page.  Identity sessions: nothing to do.
+mc_status assign_pages(mc_session* s, int batch, const int* positions) {
+    if (!s->kv_paged) return MC_OK;
+    const int plen = 1 << s->kv_shift;
+    size_t next = 0;
+    for (int b = 0; b < batch; b++) {
+        const int need = std::max(1, (positions[b] + plen - 1) / plen);
+        if (need > s->kv_pps || next + need > s->kv_order.size())
+            return fail(MC_ERR_NOMEM, "paged KV cache: %d sequences need more than the pool's %d pages of %d "
+                        "positions", batch, s->kv_pages, plen);
+        int* row = s->kv_host.data() + (size_t)b * s->kv_pps;
+        for (int i = 0; i < s->kv_pps; i++) row[i] = s->kv_order[next + std::min(i, need - 1)];
+        next += need;
+    }
+    MC_CUDA(cudaMemcpyAsync(s->kv_table, s->kv_host.data(), (size_t)batch * s->kv_pps * 4,
+                            cudaMemcpyHostToDevice, s->stream));
+    // the host copy is reused by the next call: wait until this one is read
+    MC_CUDA(cudaStreamSynchronize(s->stream));
+    return MC_OK;
+}
 
 mc_status ensure_trace(mc_session* s, size_t bytes) {
     if (bytes <= s->trace_bytes) return MC_OK;
@@ -968,6 +1050,7 @@ mc_status run_prefill(mc_session* s, int batch, const uint16_t* prompts, int str
     a.B = batch; a.Bcap = s->Bcap; a.cap = s->cap;
     a.prompts = prompts; a.prompt_stride = stride;
     a.rope = m->rope; a.kc = s->kc; a.vc = s->vc;
+    a.pg = mc::KvPages{s->kv_table, s->kv_pps, s->kv_shift};
     a.X = s->pf_x; a.XN = s->pf_xn; a.QB = s->pf_q; a.ATT = s->pf_att; a.FH = s->pf_f;
     if (tc && kB16) {
         a.XN16 = s->pf_xn16;
@@ -1408,6 +1491,13 @@ mc_status generate_t(mc_session* s, int batch, const uint16_t* prompts, int prom
     }
     for (int i = 0; i < o->stop_sequence_len; i++)
         if (o->stop_sequence_ids[i] >= m->V) return fail(MC_ERR_INVALID, "stop id >= vocab");
+    if (s->kv_paged) {
+        // positions a sequence feeds: its prompt and all but its last new id
+        std::vector<int> need(batch);
+        for (int b = 0; b < batch; b++) need[b] = seq[b].nnew > 0 ? seq[b].P + seq[b].nnew - 1 : 0;
+        const mc_status st = assign_pages(s, batch, need.data());
+        if (st) return st;
+    }
 
     mc::LoopParams<WT> p{};
     p.B = batch;
@@ -1547,6 +1637,11 @@ mc_status forward_logits_dev(mc_session* s, int batch, const uint16_t* tokens, i
     }
     mc_status st = ensure_trace(s, (size_t)batch * n * m->V * 4);
     if (st) return st;
+    if (s->kv_paged) {
+        std::vector<int> need(batch, n);
+        st = assign_pages(s, batch, need.data());
+        if (st) return st;
+    }
     mc::LoopParams<WT> p{};
     p.B = batch;
     p.prompts = s->prompts;
@@ -1615,6 +1710,11 @@ mc_status model_forward_t(mc_session* s, int batch, int seq, const uint16_t* tok
                           bool dev, const mc_forward_caches* caps = nullptr) {
     const mc_model* m = s->m;
     const uint16_t* dtok = tokens;
+    if (s->kv_paged) {
+        std::vector<int> need(batch, seq);
+        const mc_status st = assign_pages(s, batch, need.data());
+        if (st) return st;
+    }
     if (!dev) {
         for (size_t i = 0; i < (size_t)batch * seq; i++)   // forward.c:179-186
             if (tokens[i] >= m->V) return fail(MC_ERR_INVALID, "model_forward: token id %d >= vocab", tokens[i]);
@@ -1814,13 +1914,14 @@ StaticDevice g_static_dev[64];
 // host memory either.
 mc::SeqState g_static_seq[MC_STATIC_MAX_BATCH];
 float2 g_static_rope[MC_STATIC_MAX_ROPE];
+int g_static_pages[MC_STATIC_MAX_BATCH * (MC_MAX_SEQ / MC_MIN_PAGE_LEN)];
 int g_static_status;
 
 struct StaticPlan {
     size_t off[22];
     size_t total;
     size_t smem;
-    int bc, xs_ld, max_split;
+    int bc, xs_ld, max_split, pps;
 };
 
 // Carve the scratch array the same way mc_session_create sizes its buffers.
@@ -1830,8 +1931,11 @@ StaticPlan static_plan(const mc_model_desc* d, int batch, int cap, int grid, siz
     const size_t F = d->ffn_dim, V = d->vocab_size, H = d->n_heads;
     pl.max_split = (cap + mc::kSplitLen - 1) / mc::kSplitLen;
     const size_t ms = pl.max_split;
+    // KV pages of MC_MIN_PAGE_LEN positions, identity table
+    pl.pps = (cap + MC_MIN_PAGE_LEN - 1) / MC_MIN_PAGE_LEN;
+    const size_t kv_bytes = B * pl.pps * L * K * (size_t)MC_MIN_PAGE_LEN * hd * 4;
     const size_t sizes[22] = {
-        L * B * K * cap * hd * 4, L * B * K * cap * hd * 4,   // kc, vc
+        kv_bytes, kv_bytes,                                   // kc, vc
         B * D * 4, B * D * 4, B * D * 4, B * F * 4,           // x, q, att, f
         B * V * 4,                                            // logits
         B * H * ms * hd * 4, B * H * ms * 4, B * H * ms * 4,  // part_o, part_m, part_l
@@ -1840,7 +1944,8 @@ StaticPlan static_plan(const mc_model_desc* d, int batch, int cap, int grid, siz
         256, 256,                                             // bar, status
         B * sizeof(mc::SeqState), (size_t)MC_MAX_STOP * 2,    // seq, stop ids
         (size_t)cap * (hd / 2 > 0 ? hd / 2 : 1) * sizeof(float2),  // rope
-        0, 0};
+        B * (size_t)pl.pps * 4,                               // page table
+        0};
     size_t off = 0;
     for (int i = 0; i < 22; i++) {
         pl.off[i] = off;
@@ -1991,6 +2096,9 @@ extern "C" mc_status mc_generate_static(const mc_model_desc* w, int batch,
     mc::SeqState* dseq = reinterpret_cast<mc::SeqState*>(base + pl.off[17]);
     uint16_t* dstop = reinterpret_cast<uint16_t*>(base + pl.off[18]);
     float2* drope = reinterpret_cast<float2*>(base + pl.off[19]);
+    int* dpages = reinterpret_cast<int*>(base + pl.off[20]);
+    p.pg = mc::KvPages{dpages, pl.pps, 6};
+    static_assert(MC_MIN_PAGE_LEN == 64, "the static path's pages are 2^6 positions");
     p.rope = drope; p.rope_len = max_seq;
     p.cap = max_seq; p.Bcap = batch; p.max_split = pl.max_split;
     p.seq = dseq; p.B = batch;
@@ -2017,6 +2125,8 @@ extern "C" mc_status mc_generate_static(const mc_model_desc* w, int batch,
     if (o->stop_sequence_len > 0)
         MC_CUDA(cudaMemcpyAsync(dstop, o->stop_sequence_ids, o->stop_sequence_len * 2,
                                 cudaMemcpyHostToDevice, s));
+    for (int i = 0; i < batch * pl.pps; i++) g_static_pages[i] = i;
+    MC_CUDA(cudaMemcpyAsync(dpages, g_static_pages, (size_t)batch * pl.pps * 4, cudaMemcpyHostToDevice, s));
     MC_CUDA(cudaMemcpyAsync(dseq, g_static_seq, batch * sizeof(mc::SeqState),
                             cudaMemcpyHostToDevice, s));
     for (int b = 0; b < batch; b++)
