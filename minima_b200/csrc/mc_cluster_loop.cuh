@@ -87,6 +87,13 @@ struct ClusterParams {
     int hc_rows;                // tok_emb rows per head CTA
     unsigned hc_ld;             // padded row stride (floats) of the resident slice
     unsigned off_hc_x;          // byte offset of the normalised-x copy
+    // two-phase layer loop (mc_cluster_loop2.cuh)
+    int v2;
+    unsigned off_wb;            // phase B weight buffer (off_stage: phase A buffer)
+    int fpc;                    // up/gate rows (ffn_down columns) per CTA, padded
+    int dp_b;                   // sequence stride of the ffn_down partials
+    const float* proj_h;        // [L][K][D][G hd] attn_proj column blocks per KV head
+    const float* down_s;        // [L][cs][D][fpc] ffn_down column blocks per CTA
     float* xfin;                // [Bcap][D] rmsnorm(x, rms_final), layer -> head
     int* hgen;                  // [Bcap] sampler step of each sequence in this head phase, -1 = none
     unsigned* go;               // head phases issued (or kExit)
@@ -151,7 +158,9 @@ struct LcState {
     float* f;      // [B][F]
     float* sc;     // [kWarps][G * hd + 2 G] per-warp attention states, [kWarps][kAttMaxG][32] probabilities
     float* kv;     // [K, V][kv_tile][hd]
-    float* stage;  // [kStages][stage_floats]
+    float* stage;  // [kStages][stage_floats] (two-phase loop: the phase A buffer)
+    float* wb;     // two-phase loop: the phase B weight buffer
+    float* dp;     // two-phase loop: ffn_down partials [cs][kBCMax][D] (shares kv's bytes)
     float* rmsf;   // [D] final RMSNorm scale
     float2* rope;  // [hd/2] (cos, sin) at the current position
     unsigned long long* bar;  // [kStages]
@@ -1180,17 +1189,6 @@ __device__ void hc_main(const ClusterParams& cp, unsigned char* smem, int hc) {
         __threadfence();
         __syncthreads();
         if (threadIdx.x == 0) red_release_add_u32(cp.hdone, 1u);
-    }
-}
-
-__global__ void __launch_bounds__(kThreads, 1) cluster_loop_kernel(const ClusterParams cp) {
-    extern __shared__ __align__(128) unsigned char smem_c[];
-    cg::cluster_group cl = cg::this_cluster();
-    const int cid = blockIdx.x / cp.cs;
-    if (cid == 0) {
-        lc_main(cp, smem_c, cl, (int)cl.block_rank());
-    } else {
-        hc_main(cp, smem_c, blockIdx.x - cp.cs);
     }
 }
 

@@ -1,0 +1,543 @@
+// mc_cluster_loop2.cuh — the two-phase layer loop of the cluster-resident
+// token loop (used when every (sequence, KV head) pair of the batch gets a
+// CTA of the layer cluster; the five-phase loop of mc_cluster_loop.cuh
+// serves the other shapes).  Head CTAs, the hand-off and the sampler are
+// those of mc_cluster_loop.cuh.
+//
+// One layer of forward_one (generate.c:97-185) for the sequences fed at
+// position t, in two phases separated by cluster barriers:
+//
+//  A. unit phase: CTA u < nf K owns sequence fl[u / K] and KV head u % K.
+//     It normalises that sequence's residual (rms1), computes the Q rows of
+//     the head group's G query heads and the K and V rows of its KV head
+//     (+RoPE, K/V appended to the paged cache), attends over keys 0..t for
+//     the G heads, and multiplies the G heads' outputs by their columns of
+//     attn_proj: a D-long partial of x += W_proj . attn, pushed to every CTA.
+//  B. FFN phase: every CTA adds the K partials of each sequence to its
+//     residual (KV head order), normalises (rms2), computes its slice of
+//     up/gate rows and the SwiGLU product, and multiplies that slice by its
+//     columns of ffn_down: a D-long partial per sequence, pushed to every
+//     CTA.  The next layer (or the final norm) starts by adding the cs
+//     partials in CTA order.
+//
+// Every CTA therefore keeps the whole residual stream of every sequence,
+// updated by the same additions in the same order (identical everywhere).
+// The column blocks of attn_proj per KV head and of ffn_down per CTA are
+// contiguous copies made by cl2_relayout_kernel when the weights change.
+// Each phase's weights (A: Q/K/V rows of the CTA's KV head, its attn_proj
+// block, rms1; B: its up/gate rows, its ffn_down block, rms2) stream into a
+// single buffer per phase by bulk copies issued as soon as the phase is
+// done with the previous layer's, so a copy has the other phase's duration
+// to land.  The down partials share their shared memory with the K/V tile:
+// they are summed before the tile's first copy is issued and written by
+// other CTAs only after the barrier that ends the attention.
+#pragma once
+
+#include "mc_cluster_loop.cuh"
+
+namespace mc {
+
+// proj_h[l][g][i][c] = W_proj[l][i][g G hd + c]; down_s[l][c][i][j] =
+// W_down[l][i][c fpc + j] (0 past F).
+__global__ void cl2_relayout_kernel(const float* __restrict__ w_proj, const float* __restrict__ w_down,
+                                    float* __restrict__ proj_h, float* __restrict__ down_s, int L, int D,
+                                    int F, int K, int ghd, int cs, int fpc) {
+    const size_t n1 = (size_t)L * K * D * ghd, n2 = (size_t)L * cs * D * fpc;
+    for (size_t e = blockIdx.x * (size_t)blockDim.x + threadIdx.x; e < n1 + n2;
+         e += (size_t)gridDim.x * blockDim.x) {
+        if (e < n1) {
+            const size_t c = e % ghd, i = (e / ghd) % D, g = (e / ((size_t)ghd * D)) % K, l = e / ((size_t)ghd * D * K);
+            proj_h[e] = w_proj[(l * D + i) * D + g * ghd + c];
+        } else {
+            const size_t f = e - n1;
+            const size_t j = f % fpc, i = (f / fpc) % D, c = (f / ((size_t)fpc * D)) % cs, l = f / ((size_t)fpc * D * cs);
+            const size_t col = c * fpc + j;
+            down_s[f] = col < (size_t)F ? w_down[(l * D + i) * F + col] : 0.0f;
+        }
+    }
+}
+
+// Phase A weights of layer l for KV head g: Q rows of heads g G .. g G +
+// G - 1, the K and V rows of KV head g, the attn_proj block of g, rms1.
+__device__ void cl2_issue_a(const ClusterParams& cp, LcState& S, int l, int g) {
+    const LoopParams<float>& p = cp.lp;
+    const size_t D = p.D;
+    const int G = p.G, hd = p.hd, ghd = G * hd;
+    float* dst = S.stage;
+    const unsigned qb = (unsigned)(ghd * D * 4), kb = (unsigned)(hd * D * 4), pb = (unsigned)(D * ghd * 4);
+    mbar_expect_tx(&S.bar[0], qb + 2 * kb + pb + (unsigned)(D * 4));
+    const float* wl = p.w_qkv + (size_t)l * p.Q * D;
+    bulk_g2s(dst, wl + (size_t)g * ghd * D, qb, &S.bar[0]);
+    bulk_g2s(dst + (size_t)ghd * D, wl + (D + (size_t)g * hd) * D, kb, &S.bar[0]);
+    bulk_g2s(dst + (size_t)(ghd + hd) * D, wl + (D + (size_t)p.kvd + (size_t)g * hd) * D, kb, &S.bar[0]);
+    bulk_g2s(dst + (size_t)(ghd + 2 * hd) * D, cp.proj_h + ((size_t)l * p.K + g) * D * ghd, pb, &S.bar[0]);
+    bulk_g2s(dst + (size_t)(ghd + 2 * hd) * D + D * ghd, p.rms1 + (size_t)l * D, (unsigned)(D * 4), &S.bar[0]);
+}
+
+// Phase B weights of layer l for this CTA: up and gate rows [f0, f1), its
+// ffn_down block [D][fpc], rms2.
+__device__ void cl2_issue_b(const ClusterParams& cp, const CSlice& sl, LcState& S, int l, int crank) {
+    const LoopParams<float>& p = cp.lp;
+    const size_t D = p.D, fpc = cp.fpc;
+    const unsigned nfr = (unsigned)(sl.f1 - sl.f0);
+    float* dst = S.wb;
+    const unsigned ub = (unsigned)(nfr * D * 4), db = (unsigned)(D * fpc * 4);
+    mbar_expect_tx(&S.bar[1], 2 * ub + db + (unsigned)(D * 4));
+    if (nfr) {
+        bulk_g2s(dst, p.w_up + ((size_t)l * p.F + sl.f0) * D, ub, &S.bar[1]);
+        bulk_g2s(dst + fpc * D, p.w_gate + ((size_t)l * p.F + sl.f0) * D, ub, &S.bar[1]);
+    }
+    bulk_g2s(dst + 2 * fpc * D, cp.down_s + ((size_t)l * cp.cs + crank) * D * fpc, db, &S.bar[1]);
+    bulk_g2s(dst + 2 * fpc * D + D * fpc, p.rms2 + (size_t)l * D, (unsigned)(D * 4), &S.bar[1]);
+}
+
+// 32 rows of length len (row stride ld) against one vector: lane j returns
+// the dot product of row r0 + j (0 past nrows).  Lanes read 16-byte chunks
+// of each row (a warp reads 512 contiguous bytes), then a transposed
+// reduction.  len % 4 == 0.
+__device__ __forceinline__ float cl2_dot32(const float* rows, int ld, int r0, int nrows, int len,
+                                           const float* xv) {
+    const int lane = threadIdx.x & 31;
+    float acc[32];
+#pragma unroll
+    for (int j = 0; j < 32; j++) acc[j] = 0.0f;
+    for (int k = 4 * lane; k < len; k += 128) {
+        const float4 x = *reinterpret_cast<const float4*>(xv + k);
+#pragma unroll
+        for (int j = 0; j < 32; j++) {
+            if (r0 + j < nrows) {
+                const float4 w = *reinterpret_cast<const float4*>(rows + (size_t)(r0 + j) * ld + k);
+                acc[j] += w.x * x.x + w.y * x.y + w.z * x.z + w.w * x.w;
+            }
+        }
+    }
+    return transpose_reduce32(acc);
+}
+
+// x[b] += sum over the cs CTAs' ffn_down partials (CTA order) for the
+// sequences in fl.  All threads; ends with a CTA barrier.
+__device__ __forceinline__ void cl2_add_down(const ClusterParams& cp, LcState& S, const int* fl, int nf) {
+    const int D = cp.lp.D, cs = cp.cs;
+    for (int e = threadIdx.x; e < nf * D; e += blockDim.x) {
+        const int b = fl[e / D], k = e % D;
+        float s = 0.0f;
+        for (int c = 0; c < cs; c++) s += S.dp[((size_t)c * cp.dp_b + b) * D + k];
+        S.x[b * D + k] += s;
+    }
+    __syncthreads();
+}
+
+// One layer (two phases, two cluster barriers).  pa / pb: parities of the
+// phase buffers' next copies; `first`: the residual is the embedding.
+template <int HD>
+__device__ bool cl2_layer(const ClusterParams& cp, const CSlice& sl, LcState& S, cg::cluster_group& cl,
+                          int crank, int l, int t, const int* fl, int nf, bool first, unsigned& pa,
+                          unsigned& pbp) {
+    const LoopParams<float>& p = cp.lp;
+    const int D = p.D, K = p.K, G = p.G, hd = HD > 0 ? HD : p.hd, cs = cp.cs;
+    const int ghd = G * hd, rows_a = ghd + 2 * hd, fpc = cp.fpc;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int nd = (hd + 31) / 32;
+    if (!first) cl2_add_down(cp, S, fl, nf);
+
+    // ------------------------------------------------ phase A: unit crank
+    if (!mbar_wait(&S.bar[0], pa, p.timeout_ns)) lc_fail(S, p.status, ST_TIMEOUT);
+    pa ^= 1u;
+    const bool unit = crank < nf * K;
+    const int g = crank % K;
+    const int b = unit ? fl[crank / K] : 0;
+    const int nkeys = t + 1;
+    bool wrote_kv = false;
+    if (unit) {
+        if (threadIdx.x == 0) att_issue_tile(cp, S, l, b, g, 0, min(cp.kv_tile, nkeys), t, hd);
+        const float* wa = S.stage;
+        const float* rms1 = wa + (size_t)(rows_a + ghd) * D;
+        // rmsnorm of sequence b (generate.c:57-63): one warp sums, the CTA scales
+        if (warp == 0) {
+            float ss = 0.0f;
+            for (int k = lane; k < D; k += 32) ss += S.x[b * D + k] * S.x[b * D + k];
+            ss = warp_sum(ss);
+            if (lane == 0) S.red[0] = 1.0f / sqrtf(ss / (float)D + 1e-5f);
+        }
+        __syncthreads();
+        const float inv = S.red[0];
+        float* xn = S.xn + b * D;
+        for (int k = threadIdx.x; k < D; k += blockDim.x) xn[k] = S.x[b * D + k] * inv * rms1[k];
+        __syncthreads();
+        // Q rows of the G heads, K and V rows of KV head g (generate.c:99-119)
+        for (int r0 = 32 * warp; r0 < rows_a; r0 += 32 * kWarps) {
+            const float val = cl2_dot32(wa, D, r0, rows_a, D, xn);
+            const float other = __shfl_xor_sync(0xffffffffu, val, 1);    // RoPE partner (2p <-> 2p+1)
+            const int r = r0 + lane;
+            if (r < rows_a) {
+                const bool isq = r < ghd, isk = !isq && r < ghd + hd;
+                const int d = isq ? r % hd : isk ? r - ghd : r - ghd - hd;
+                float out = val;
+                if (isq || isk) {
+                    const float2 rr = S.rope[d / 2];
+                    out = (d & 1) ? other * rr.y + val * rr.x : val * rr.x - other * rr.y;
+                }
+                S.qkv[r] = out;
+                if (!isq) {
+                    (isk ? p.kc : p.vc)[kv_row(p.pg, p.L, K, l, b, g, t) * hd + d] = out;
+                    wrote_kv = true;
+                }
+            }
+        }
+        __syncthreads();
+        // attention of the G heads over keys 0..t (generate.c:121-156)
+        const float scale = 1.0f / sqrtf((float)hd);
+        const int pw = ghd + 2 * G;
+        float* part = S.sc;                                       // [kWarps][pw]
+        float* pbuf = S.sc + kWarps * pw + warp * 32 * kAttMaxG;   // this warp's probabilities
+        float* ks = S.kv;
+        float* vs = S.kv + (size_t)cp.kv_tile * hd;
+        const float* q = S.qkv;
+        const float* kq = S.qkv + ghd;
+        const float* vq = kq + hd;
+        float mrun[kAttMaxG], lrun[kAttMaxG], o[kAttMaxG][kAttMaxND];
+#pragma unroll
+        for (int h = 0; h < kAttMaxG; h++) {
+            mrun[h] = -INFINITY;
+            lrun[h] = 0.0f;
+#pragma unroll
+            for (int i = 0; i < kAttMaxND; i++) o[h][i] = 0.0f;
+        }
+        for (int a0 = 0; a0 < nkeys; a0 += cp.kv_tile) {
+            const int n = min(cp.kv_tile, nkeys - a0);
+            if (threadIdx.x == 0 && a0 != 0) att_issue_tile(cp, S, l, b, g, a0, n, t, hd);
+            if (t >= a0 && t < a0 + n)
+                for (int c = threadIdx.x; c < 2 * hd; c += blockDim.x) {
+                    if (c < hd) ks[(t - a0) * hd + c] = kq[c];
+                    else vs[(t - a0) * hd + c - hd] = vq[c - hd];
+                }
+            const int pad = ((n + 31) & ~31) - n;
+            for (int c = threadIdx.x; c < pad * hd; c += blockDim.x) vs[n * hd + c] = 0.0f;
+            if (threadIdx.x == 0) att_wait_tile(p, S);
+            __syncthreads();
+            for (int rr = warp; rr * 32 < n; rr += kWarps)
+                att_run<HD>(ks + (size_t)rr * 32 * hd, vs + (size_t)rr * 32 * hd, q, pbuf, min(32, n - rr * 32),
+                            hd, G, scale, mrun, lrun, o);
+            __syncthreads();
+        }
+#pragma unroll
+        for (int h = 0; h < kAttMaxG; h++)
+            if (h < G) {
+                if (lane == 0) {
+                    part[warp * pw + ghd + 2 * h] = mrun[h];
+                    part[warp * pw + ghd + 2 * h + 1] = lrun[h];
+                }
+#pragma unroll
+                for (int i = 0; i < kAttMaxND; i++) {
+                    const int d = lane + 32 * i;
+                    if (i < nd && d < hd) part[warp * pw + h * hd + d] = o[h][i];
+                }
+            }
+        __syncthreads();
+        for (int i = threadIdx.x; i < ghd; i += blockDim.x) {
+            const int h = i / hd;
+            float M = -INFINITY;
+#pragma unroll
+            for (int w = 0; w < kWarps; w++) M = fmaxf(M, part[w * pw + ghd + 2 * h]);
+            float num = 0.0f, den = 0.0f;
+#pragma unroll
+            for (int w = 0; w < kWarps; w++) {
+                const float mw = part[w * pw + ghd + 2 * h];
+                const float c = mw == -INFINITY ? 0.0f : expf(mw - M);   // a warp may see no keys
+                den += c * part[w * pw + ghd + 2 * h + 1];
+                num += c * part[w * pw + i];
+            }
+            S.att[i] = num / den;
+        }
+        __syncthreads();
+        // this head group's share of attn_proj (generate.c:158-163)
+        const float* wp = wa + (size_t)rows_a * D;
+        for (int r0 = 32 * warp; r0 < D; r0 += 32 * kWarps) {
+            const float val = cl2_dot32(wp, ghd, r0, D, ghd, S.att);
+            if (r0 + lane < D) S.attp[crank * D + r0 + lane] = val;
+        }
+        __syncthreads();
+        push_block(cl, S.attp, crank * D, D, cs, crank);
+    }
+    // K/V rows written in this step are read by later steps' bulk copies
+    // (async proxy) in other CTAs: order them before the cluster barrier
+    if (wrote_kv) asm volatile("fence.proxy.async.global;" ::: "memory");
+    __syncthreads();
+    if (threadIdx.x == 0) cl2_issue_a(cp, S, (l + 1) % p.L, g);
+    if (!lc_sync(cl, S, cs)) return false;
+
+    // ------------------------------------------------ phase B: FFN slice
+    for (int e = threadIdx.x; e < nf * D; e += blockDim.x) {
+        const int i = e / D, k = e % D;
+        float s = 0.0f;
+        for (int gg = 0; gg < K; gg++) s += S.attp[(i * K + gg) * D + k];
+        S.x[fl[i] * D + k] += s;
+    }
+    if (!mbar_wait(&S.bar[1], pbp, p.timeout_ns)) lc_fail(S, p.status, ST_TIMEOUT);
+    pbp ^= 1u;
+    __syncthreads();
+    const float* wu = S.wb;
+    const float* wg = S.wb + (size_t)fpc * D;
+    const float* wd = S.wb + 2 * (size_t)fpc * D;
+    const float* rms2 = wd + (size_t)D * fpc;
+    lc_norm(S.x, S.xn, rms2, fl, nf, D, S.red);
+    // up/gate rows [f0, f1) and SwiGLU (generate.c:165-179)
+    for (int j = sl.f0 + 2 * warp; j < sl.f1; j += 2 * kWarps) {
+        // rows: up j, up j+1, gate j, gate j+1 -> the gate of lane's up row is in lane ^ 16
+        const float* u0 = wu + (size_t)(j - sl.f0) * D;
+        const float* g0 = wg + (size_t)(j - sl.f0) * D;
+        const float val = lc_gemv4(u0, u0 + D, g0, g0 + D, D, S.xn, D, fl, nf);
+        const float gate = __shfl_xor_sync(0xffffffffu, val, 16);
+        const int i = lane & 7;
+        if (lane < 16 && i < nf) {
+            const float sv = gate / (1.0f + expf(-gate));
+            S.f[fl[i] * fpc + (j - sl.f0) + (lane >> 3)] = sv * val;
+        }
+    }
+    __syncthreads();
+    // this slice's share of ffn_down (generate.c:181-184), into this CTA's
+    // slot of the partials
+    const int nfr = sl.f1 - sl.f0;
+    float* mine = S.dp + (size_t)crank * cp.dp_b * D;
+    if (nfr > 0) {
+        for (int i0 = 4 * warp; i0 < D; i0 += 4 * kWarps) {
+            const float* w0 = wd + (size_t)i0 * fpc;
+            const float val = lc_gemv4(w0, w0 + fpc, w0 + 2 * fpc, w0 + 3 * fpc, nfr, S.f, fpc, fl, nf);
+            const int i = lane & 7;
+            if (i < nf) mine[fl[i] * D + i0 + (lane >> 3)] = val;
+        }
+    } else {
+        for (int e = threadIdx.x; e < nf * D; e += blockDim.x) mine[fl[e / D] * D + e % D] = 0.0f;
+    }
+    __syncthreads();
+    {
+        const int n4 = D >> 2, per_rank = nf * n4;
+        for (int e = threadIdx.x; e < per_rank * cs; e += blockDim.x) {
+            const int r = e / per_rank;
+            if (r == crank) continue;
+            const int w = e - r * per_rank, i = w / n4, c = w - i * n4;
+            const int off = fl[i] * D + 4 * c;
+            const float4 v = *reinterpret_cast<const float4*>(mine + off);
+            *reinterpret_cast<float4*>(cl.map_shared_rank(mine, r) + off) = v;
+        }
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) cl2_issue_b(cp, sl, S, (l + 1) % p.L, crank);
+    return lc_sync(cl, S, cs);
+}
+
+__device__ void cl2_main(const ClusterParams& cp, unsigned char* smem, cg::cluster_group& cl, int crank) {
+    const LoopParams<float>& p = cp.lp;
+    LcState S;
+    S.bar = reinterpret_cast<unsigned long long*>(smem);   // [0] phase A, [1] phase B
+    S.kvbar = S.bar + 2;
+    S.ints = reinterpret_cast<int*>(smem + 64);
+    S.red = reinterpret_cast<float*>(smem + 64 + 64 * 4);
+    S.x = reinterpret_cast<float*>(smem + cp.off_x);
+    S.xn = reinterpret_cast<float*>(smem + cp.off_xn);
+    S.qkv = reinterpret_cast<float*>(smem + cp.off_qkv);
+    S.att = reinterpret_cast<float*>(smem + cp.off_att);
+    S.attp = reinterpret_cast<float*>(smem + cp.off_attp);
+    S.f = reinterpret_cast<float*>(smem + cp.off_f);
+    S.sc = reinterpret_cast<float*>(smem + cp.off_sc);
+    S.kv = reinterpret_cast<float*>(smem + cp.off_kv);
+    S.dp = S.kv;                                           // shared with the K/V tile
+    S.stage = reinterpret_cast<float*>(smem + cp.off_stage);
+    S.wb = reinterpret_cast<float*>(smem + cp.off_wb);
+    S.rmsf = reinterpret_cast<float*>(smem + cp.off_rmsf);
+    S.rope = reinterpret_cast<float2*>(smem + cp.off_rope);
+    S.seq = reinterpret_cast<SeqMirror*>(smem + 576);
+    const CSlice sl = cluster_slice(crank, cp.cs, p.Q, p.D, p.F);
+    const int nhc = (cp.n_clusters - 1) * cp.cs;
+    int* fl = S.ints;        // [16]
+    int* hl = S.ints + 16;   // [16]
+    int* toks = S.ints + 40; // [8] ids fed at this step
+    const int warp = threadIdx.x >> 5;
+
+    if (threadIdx.x == 0) {
+        mbar_init(&S.bar[0], 1);
+        mbar_init(&S.bar[1], 1);
+        mbar_init(S.kvbar, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        S.ints[38] = 0;
+        S.ints[39] = 0;
+    }
+    S.kvph = 0u;
+    S.kvpend = 0;
+    for (int b = threadIdx.x; b < p.B; b += blockDim.x) {
+        const SeqState& g = p.seq[b];
+        SeqMirror& m = S.seq[b];
+        m.P = g.P; m.nnew = g.nnew; m.gen = g.gen; m.done = g.done; m.tok = g.tok;
+        m.result = g.result; m.final_pos = g.final_pos; m.rng = g.rng;
+    }
+    for (int k = threadIdx.x; k < p.D; k += blockDim.x) S.rmsf[k] = __ldg(p.rmsf + k);
+    // the SwiGLU slice is read past f1 - f0 by nobody, but keep it finite
+    for (int e = threadIdx.x; e < cp.dp_b * cp.fpc; e += blockDim.x) S.f[e] = 0.0f;
+    __syncthreads();
+    // prologue: prompts into the history, penalty counts, first bans (CTA b)
+    for (int b = crank; b < p.B; b += cp.cs) {
+        const SeqState* st = p.seq + b;
+        if (st->done) continue;
+        const int P = st->P;
+        uint16_t* out = p.out_ids + (size_t)b * p.out_cap;
+        for (int i = threadIdx.x; i < P; i += blockDim.x) out[i] = p.prompts[(size_t)b * p.prompt_stride + i];
+        if (p.s.pen_active) {
+            unsigned* cnt = p.counts + (size_t)b * p.V;
+            for (int v = threadIdx.x; v < p.V; v += blockDim.x) cnt[v] = 0u;
+            __syncthreads();
+            for (int i = threadIdx.x; i < P; i += blockDim.x) {
+                const int id = p.prompts[(size_t)b * p.prompt_stride + i];
+                if (id < p.V) atomicAdd(&cnt[id], 1u);
+            }
+        }
+        __syncthreads();
+        if (p.s.ngram > 0) compute_bans(p, b, P);
+    }
+    __threadfence();
+    unsigned pa = 0u, pbp = 0u;
+    if (threadIdx.x == 0) {
+        cl2_issue_a(cp, S, 0, crank % p.K);
+        cl2_issue_b(cp, sl, S, 0, crank);
+    }
+    unsigned heads = 0;
+    S.epoch = 0;
+    if (threadIdx.x == 0) { S.ints[36] = 0; S.ints[37] = 0; }
+    cl.sync();   // error slots are zero everywhere before anyone can set one
+    bool ok = lc_sync(cl, S, cp.cs);
+
+    for (int t = p.t0; ok && t < p.T; t++) {
+        if (threadIdx.x == 0) {
+            int nf = 0, nh = 0;
+            for (int b = 0; b < p.B; b++) {
+                const SeqMirror& m = S.seq[b];
+                if (m.done || t >= m.P + m.nnew - 1) continue;
+                fl[nf++] = b;
+                if (t >= m.P - 1) hl[nh++] = b;
+            }
+            S.ints[32] = nf;
+            S.ints[33] = nh;
+            if (crank == 0 && p.stamps) p.stamps[t] = globaltimer_ns();
+        }
+        __syncthreads();
+        const int nf = S.ints[32], nh = S.ints[33];
+        if (nf == 0) break;
+        // ids fed at position t and this position's RoPE row, in one round trip
+        if (threadIdx.x < nf) {
+            const int b = fl[threadIdx.x];
+            const SeqMirror& m = S.seq[b];
+            int tok = t < m.P ? (int)p.prompts[(size_t)b * p.prompt_stride + t] : m.tok;
+            if (tok < 0 || tok >= p.V) {
+                lc_fail(S, p.status, ST_DEVICE);
+                tok = 0;
+            }
+            toks[threadIdx.x] = tok;
+        }
+        for (int j = threadIdx.x; j < p.hd / 2; j += blockDim.x)
+            S.rope[j] = p.rope[(size_t)t * (p.hd / 2) + j];
+        __syncthreads();
+        // embedding of the token at position t (generate.c:86-88)
+        for (int e = threadIdx.x; e < nf * p.D; e += blockDim.x) {
+            const int i = e / p.D, k = e % p.D;
+            S.x[fl[i] * p.D + k] = __ldg(p.tok_emb + (size_t)toks[i] * p.D + k);
+        }
+        __syncthreads();
+        for (int l = 0; ok && l < p.L; l++) {
+            switch (p.hd) {
+            case 16: ok = cl2_layer<16>(cp, sl, S, cl, crank, l, t, fl, nf, l == 0, pa, pbp); break;
+            case 32: ok = cl2_layer<32>(cp, sl, S, cl, crank, l, t, fl, nf, l == 0, pa, pbp); break;
+            case 64: ok = cl2_layer<64>(cp, sl, S, cl, crank, l, t, fl, nf, l == 0, pa, pbp); break;
+            default: ok = cl2_layer<0>(cp, sl, S, cl, crank, l, t, fl, nf, l == 0, pa, pbp); break;
+            }
+        }
+        if (!ok) break;
+        if (nh == 0) continue;
+        cl2_add_down(cp, S, fl, nf);
+
+        // ---- hand the final norm to the head CTAs (generate.c:187-191)
+        lc_norm(S.x, S.xn, S.rmsf, hl, nh, p.D, S.red);
+        {
+            const int cols = (p.D + cp.cs - 1) / cp.cs, c0 = crank * cols, c1 = min(p.D, c0 + cols);
+            for (int e = threadIdx.x; e < nh * (c1 - c0); e += blockDim.x) {
+                const int b = hl[e / (c1 - c0)], k = c0 + e % (c1 - c0);
+                cp.xfin[(size_t)b * p.D + k] = S.xn[b * p.D + k];
+            }
+            if (crank == 0)
+                for (int b = threadIdx.x; b < p.B; b += blockDim.x) {
+                    int g = -1;
+                    for (int i = 0; i < nh; i++)
+                        if (hl[i] == b) g = S.seq[b].gen;
+                    cp.hgen[b] = g;
+                }
+        }
+        __threadfence();
+        ok = lc_sync(cl, S, cp.cs);
+        if (!ok) break;
+        heads++;
+        if (crank == 0) {
+            // ---- release the head CTAs, wait for all of them, choose the next ids
+            if (threadIdx.x == 0) {
+                st_release_u32(cp.go, heads);
+                const unsigned target = heads * ((unsigned)nhc + p.extra_arrivals);
+                const unsigned long long t0 = globaltimer_ns();
+                while ((int)(ld_acquire_u32(cp.hdone) - target) < 0) {
+                    if (globaltimer_ns() - t0 > p.timeout_ns) {
+                        lc_fail(S, p.status, ST_TIMEOUT);
+                        break;
+                    }
+                }
+            }
+            __syncthreads();
+            if (warp < nh) lc_choose(cp, S.seq[hl[warp]], hl[warp], nhc, warp, S.ints);
+            __syncthreads();
+            if (p.s.ngram > 0)
+                for (int i = 0; i < nh; i++)
+                    if (!S.ints[40 + i]) compute_bans(p, hl[i], S.seq[hl[i]].P + S.ints[48 + i]);
+            __syncthreads();
+            const int words = p.B * (int)(sizeof(SeqMirror) / 4);
+            for (int e = threadIdx.x; e < words * cp.cs; e += blockDim.x) {
+                const int r = e / words, w = e % words;
+                if (r == 0) continue;
+                int* dst = reinterpret_cast<int*>(cl.map_shared_rank(S.seq, r));
+                dst[w] = reinterpret_cast<const int*>(S.seq)[w];
+            }
+            __threadfence();
+        }
+        ok = lc_sync(cl, S, cp.cs);
+    }
+    // release the head CTAs, publish the sequence table, drain bulk copies
+    if (crank == 0) {
+        for (int b = threadIdx.x; b < p.B; b += blockDim.x) {
+            const SeqMirror& m = S.seq[b];
+            SeqState& g = p.seq[b];
+            g.gen = m.gen; g.done = m.done; g.tok = m.tok; g.result = m.result;
+            g.final_pos = m.final_pos; g.rng = m.rng;
+        }
+        __threadfence();
+        __syncthreads();
+        if (threadIdx.x == 0) st_release_u32(cp.go, kExit);
+    }
+    if (threadIdx.x == 0 && crank == 0 && p.stamps) p.stamps[p.T] = globaltimer_ns();
+    // one copy per phase buffer is always in flight (issued for the next
+    // layer), and possibly a K/V tile after a failed wait
+    if (threadIdx.x == 0) {
+        if (!mbar_wait(&S.bar[0], pa, p.timeout_ns)) atomicMax(p.status, (int)ST_TIMEOUT);
+        if (!mbar_wait(&S.bar[1], pbp, p.timeout_ns)) atomicMax(p.status, (int)ST_TIMEOUT);
+        if (S.kvpend && !mbar_wait(S.kvbar, S.kvph, p.timeout_ns)) atomicMax(p.status, (int)ST_TIMEOUT);
+    }
+    __syncthreads();
+    cl.sync();   // no CTA leaves while others may still write its shared memory
+}
+
+__global__ void __launch_bounds__(kThreads, 1) cluster_loop_kernel(const ClusterParams cp) {
+    extern __shared__ __align__(128) unsigned char smem_c[];
+    cg::cluster_group cl = cg::this_cluster();
+    const int cid = blockIdx.x / cp.cs;
+    if (cid == 0) {
+        if (cp.v2) cl2_main(cp, smem_c, cl, (int)cl.block_rank());
+        else lc_main(cp, smem_c, cl, (int)cl.block_rank());
+    } else {
+        hc_main(cp, smem_c, blockIdx.x - cp.cs);
+    }
+}
+
+}  // namespace mc

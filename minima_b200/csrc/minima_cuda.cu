@@ -17,7 +17,7 @@
 #include <vector>
 
 #include "mc_token_loop.cuh"
-#include "mc_cluster_loop.cuh"
+#include "mc_cluster_loop2.cuh"
 #include "mc_prefill.cuh"
 #include "mc_checkpoint.cuh"
 #include "mc_tcgen05.cuh"
@@ -76,6 +76,7 @@ struct mc_model {
     float2* rope;              // [max_seq][hd/2]
     size_t off[6];             // byte offsets of the six matrices in wblock
     size_t weight_bytes;
+    unsigned version;          // bumped whenever the weights are (re)written
 };
 
 struct mc_session {
@@ -115,6 +116,8 @@ struct mc_session {
     int cl_cs, cl_nc;             // CTAs per cluster, clusters
     size_t cl_smem;
     mc::ClusterParams cl_plan;    // shared-memory offsets and geometry
+    float *cl_proj_h, *cl_down_s; // two-phase loop: column blocks of attn_proj / ffn_down
+    unsigned cl2_version;         // model version those blocks were made from
     float* xfin;
     int* hgen;
     unsigned* hsync;              // [0] go, [32] hdone (separate lines)
@@ -233,10 +236,14 @@ cudaError_t launch_cluster(const mc::ClusterParams& cp, int cs, int nc, size_t s
     return cudaLaunchKernelEx(&cfg, mc::cluster_loop_kernel, cp);
 }
 
-// Plan of the cluster-resident loop (mc_cluster_loop.cuh) for this model on
-// this device: shared-memory offsets, cluster size and count such that every
-// cluster is co-resident.  Returns false when the loop does not apply; the
-// grid-barrier loop then serves every call.
+// Plan of the cluster-resident loop (mc_cluster_loop.cuh, and its
+// two-phase layer loop in mc_cluster_loop2.cuh) for this model on this
+// device: shared-memory offsets, cluster size and count such that every
+// cluster is co-resident.  The two-phase loop is chosen when every
+// (sequence, KV head) pair of the session's batch gets a CTA of the layer
+// cluster and its buffers fit (MINIMA_CUDA_LOOP=cluster1 keeps the
+// five-phase loop).  Returns false when neither applies; the grid-barrier
+// loop then serves every call.
 bool plan_cluster(mc_session* s, const cudaDeviceProp& prop) {
     const mc_model* m = s->m;
     if (m->dtype != MC_WEIGHTS_F32) return false;
@@ -247,6 +254,7 @@ bool plan_cluster(mc_session* s, const cudaDeviceProp& prop) {
         return false;
     const char* env = getenv("MINIMA_CUDA_LOOP");
     if (env && strcmp(env, "grid") == 0) return false;
+    const bool allow_v2 = !(env && strcmp(env, "cluster1") == 0);
     const size_t optin = prop.sharedMemPerBlockOptin;
     if (cudaFuncSetAttribute(mc::cluster_loop_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)optin) != cudaSuccess ||
@@ -256,81 +264,111 @@ bool plan_cluster(mc_session* s, const cudaDeviceProp& prop) {
         return false;
     }
     const int B8 = std::min(s->Bcap, mc::kBCMax);    // activation rows held per CTA
-    for (int cs : {16, 8}) {
-        mc::ClusterParams cp{};
-        cp.cs = cs;
-        const mc::CSlice s0 = mc::cluster_slice(0, cs, m->Q, m->D, m->F);
-        // weight slice plus this layer's rms1 / rms2 scales
-        const size_t stage_f = align_up(mc::slice_floats(s0, m->D, m->F) + 2 * (size_t)m->D, 32);
-        if (stage_f * 4 >= (1u << 20)) continue;           // mbarrier tx-count limit
-        size_t off = mc::kLcHeader;
-        auto take = [&](size_t floats, size_t align) {
-            off = align_up(off, align);
-            const size_t o = off;
-            off += floats * 4;
-            return (unsigned)o;
-        };
-        cp.off_x = take((size_t)B8 * m->D, 16);
-        cp.off_xn = take((size_t)B8 * m->D, 16);
-        cp.off_qkv = take((size_t)B8 * m->Q, 16);
-        cp.off_att = take((size_t)B8 * m->D, 16);
-        // merged states of split attention units: at most max(cs, B K) units
-        cp.off_attp = take((size_t)std::max(cs, B8 * m->K) * ((G * m->hd + 2 * G + 3) & ~3), 16);
-        cp.off_f = take((size_t)B8 * m->F, 16);
-        cp.off_rmsf = take((size_t)m->D, 16);
-        cp.off_rope = take((size_t)std::max(m->hd, 2), 16);
-        const size_t fixed = off;
-        // per-warp attention states and probabilities, then the K/V tile
-        const size_t sc_f = (size_t)mc::kWarps * (G * m->hd + 2 * G + 32 * mc::kAttMaxG);
-        int tile = mc::kAttMaxTile;
-        for (; tile >= 32; tile /= 2) {
-            size_t o2 = align_up(fixed, 16) + sc_f * 4;
-            o2 = align_up(o2, 16) + 2 * (size_t)tile * m->hd * 4;
-            o2 = align_up(o2, 128) + mc::kStages * stage_f * 4;
-            if (o2 <= optin) break;
-        }
-        if (tile < 32) continue;
-        cp.kv_tile = tile;
-        cp.off_sc = take(sc_f, 16);
-        cp.off_kv = take(2 * (size_t)tile * m->hd, 16);
-        cp.off_stage = take(mc::kStages * stage_f, 128);
-        cp.stage_floats = (unsigned)stage_f;
-        const size_t lc_bytes = off;
-        for (int nc = prop.multiProcessorCount / cs; nc >= 2; nc--) {
-            const int nhc = (nc - 1) * cs;
-            const int rows = (m->V + nhc - 1) / nhc;
-            const size_t ld = (size_t)m->D + 4;
-            if ((size_t)rows * m->D * 4 >= (1u << 20)) break;
-            const size_t hc_x = align_up(mc::kHcEmbOffset + (size_t)rows * ld * 4, 16);
-            const size_t hc_bytes = hc_x + (size_t)B8 * m->D * 4;
-            const size_t smem = align_up(std::max(lc_bytes, hc_bytes), 128);
-            if (smem > optin) break;
-            cudaLaunchConfig_t cfg = {};
-            cfg.gridDim = dim3(nc * cs);
-            cfg.blockDim = dim3(mc::kThreads);
-            cfg.dynamicSmemBytes = smem;
-            cudaLaunchAttribute attr[1];
-            attr[0].id = cudaLaunchAttributeClusterDimension;
-            attr[0].val.clusterDim.x = cs;
-            attr[0].val.clusterDim.y = 1;
-            attr[0].val.clusterDim.z = 1;
-            cfg.attrs = attr;
-            cfg.numAttrs = 1;
-            int maxc = 0;
-            if (cudaOccupancyMaxActiveClusters(&maxc, (void*)mc::cluster_loop_kernel, &cfg) != cudaSuccess) {
-                cudaGetLastError();
-                break;
+    const int hd = m->hd, ghd = G * hd, D = m->D, F = m->F;
+    for (int v2 = allow_v2 ? 1 : 0; v2 >= 0; v2--) {
+        for (int cs : {16, 8}) {
+            if (v2 && B8 * m->K > cs) continue;
+            mc::ClusterParams cp{};
+            cp.cs = cs;
+            cp.v2 = v2;
+            size_t off = mc::kLcHeader;
+            auto take = [&](size_t floats, size_t align) {
+                off = align_up(off, align);
+                const size_t o = off;
+                off += floats * 4;
+                return (unsigned)o;
+            };
+            size_t stage_f = 0, wb_f = 0, sc_f = 0, union_min = 0;
+            if (v2) {
+                const mc::CSlice s0 = mc::cluster_slice(0, cs, m->Q, D, F);
+                cp.fpc = s0.f1 - s0.f0;
+                cp.dp_b = B8;
+                stage_f = (size_t)(ghd + 2 * hd) * D + (size_t)D * ghd + D;
+                wb_f = 2 * (size_t)cp.fpc * D + (size_t)D * cp.fpc + D;
+                if (stage_f * 4 >= (1u << 20) || wb_f * 4 >= (1u << 20)) continue;   // mbarrier tx-count limit
+                cp.off_x = take((size_t)B8 * D, 16);
+                cp.off_xn = take((size_t)B8 * D, 16);
+                cp.off_qkv = take((size_t)ghd + 2 * hd, 16);
+                cp.off_att = take((size_t)ghd, 16);
+                cp.off_attp = take((size_t)B8 * m->K * D, 16);
+                cp.off_f = take((size_t)B8 * cp.fpc, 16);
+                cp.off_rmsf = take((size_t)D, 16);
+                cp.off_rope = take((size_t)std::max(hd, 2), 16);
+                sc_f = (size_t)mc::kWarps * (ghd + 2 * G + 32 * mc::kAttMaxG);
+                cp.off_sc = take(sc_f, 16);
+                cp.off_stage = take(stage_f, 128);
+                cp.off_wb = take(wb_f, 128);
+                union_min = (size_t)cs * B8 * D;          // ffn_down partials
+            } else {
+                const mc::CSlice s0 = mc::cluster_slice(0, cs, m->Q, D, F);
+                // weight slice plus this layer's rms1 / rms2 scales
+                stage_f = align_up(mc::slice_floats(s0, D, F) + 2 * (size_t)D, 32);
+                if (stage_f * 4 >= (1u << 20)) continue;           // mbarrier tx-count limit
+                cp.off_x = take((size_t)B8 * D, 16);
+                cp.off_xn = take((size_t)B8 * D, 16);
+                cp.off_qkv = take((size_t)B8 * m->Q, 16);
+                cp.off_att = take((size_t)B8 * D, 16);
+                // merged states of split attention units: at most max(cs, B K) units
+                cp.off_attp = take((size_t)std::max(cs, B8 * m->K) * ((ghd + 2 * G + 3) & ~3), 16);
+                cp.off_f = take((size_t)B8 * F, 16);
+                cp.off_rmsf = take((size_t)D, 16);
+                cp.off_rope = take((size_t)std::max(hd, 2), 16);
+                sc_f = (size_t)mc::kWarps * (ghd + 2 * G + 32 * mc::kAttMaxG);
             }
-            if (maxc >= nc) {
-                cp.n_clusters = nc;
-                cp.hc_rows = rows;
-                cp.hc_ld = (unsigned)ld;
-                cp.off_hc_x = (unsigned)hc_x;
-                s->cl_cs = cs;
-                s->cl_nc = nc;
-                s->cl_smem = smem;
-                s->cl_plan = cp;
-                return true;
+            const size_t fixed = off;
+            // the K/V tile (v2: sharing its bytes with the ffn_down partials),
+            // then, for the five-phase loop, the weight stages
+            int tile = mc::kAttMaxTile;
+            for (; tile >= 32; tile /= 2) {
+                size_t o2 = align_up(fixed, 16);
+                if (!v2) o2 += sc_f * 4;
+                o2 = align_up(o2, 16) + std::max(2 * (size_t)tile * hd, union_min) * 4;
+                if (!v2) o2 = align_up(o2, 128) + mc::kStages * stage_f * 4;
+                if (o2 <= optin) break;
+            }
+            if (tile < 32) continue;
+            cp.kv_tile = tile;
+            if (!v2) cp.off_sc = take(sc_f, 16);
+            cp.off_kv = take(std::max(2 * (size_t)tile * hd, union_min), 16);
+            if (!v2) cp.off_stage = take(mc::kStages * stage_f, 128);
+            cp.stage_floats = (unsigned)stage_f;
+            const size_t lc_bytes = off;
+            for (int nc = prop.multiProcessorCount / cs; nc >= 2; nc--) {
+                const int nhc = (nc - 1) * cs;
+                const int rows = (m->V + nhc - 1) / nhc;
+                const size_t ld = (size_t)D + 4;
+                if ((size_t)rows * D * 4 >= (1u << 20)) break;
+                const size_t hc_x = align_up(mc::kHcEmbOffset + (size_t)rows * ld * 4, 16);
+                const size_t hc_bytes = hc_x + (size_t)B8 * D * 4;
+                const size_t smem = align_up(std::max(lc_bytes, hc_bytes), 128);
+                if (smem > optin) break;
+                cudaLaunchConfig_t cfg = {};
+                cfg.gridDim = dim3(nc * cs);
+                cfg.blockDim = dim3(mc::kThreads);
+                cfg.dynamicSmemBytes = smem;
+                cudaLaunchAttribute attr[1];
+                attr[0].id = cudaLaunchAttributeClusterDimension;
+                attr[0].val.clusterDim.x = cs;
+                attr[0].val.clusterDim.y = 1;
+                attr[0].val.clusterDim.z = 1;
+                cfg.attrs = attr;
+                cfg.numAttrs = 1;
+                int maxc = 0;
+                if (cudaOccupancyMaxActiveClusters(&maxc, (void*)mc::cluster_loop_kernel, &cfg) != cudaSuccess) {
+                    cudaGetLastError();
+                    break;
+                }
+                if (maxc >= nc) {
+                    cp.n_clusters = nc;
+                    cp.hc_rows = rows;
+                    cp.hc_ld = (unsigned)ld;
+                    cp.off_hc_x = (unsigned)hc_x;
+                    s->cl_cs = cs;
+                    s->cl_nc = nc;
+                    s->cl_smem = smem;
+                    s->cl_plan = cp;
+                    return true;
+                }
             }
         }
     }
@@ -380,6 +418,7 @@ mc_status upload_weights(mc_model* m, const mc_model_desc* d) {
     MC_CUDA(cudaMemcpy(m->norms, d->rms1_scale, L * D * 4, cudaMemcpyHostToDevice));
     MC_CUDA(cudaMemcpy(m->norms + L * D, d->rms2_scale, L * D * 4, cudaMemcpyHostToDevice));
     MC_CUDA(cudaMemcpy(m->norms + 2 * L * D, d->rms_final_scale, D * 4, cudaMemcpyHostToDevice));
+    m->version++;
     return MC_OK;
 }
 
@@ -515,7 +554,7 @@ mc_status mc_session_destroy(mc_session* s) {
                     s->pf_x, s->pf_xn, s->pf_q, s->pf_att, s->pf_f, s->pf_logits,
                     s->pf_xn16, s->pf_att16, s->pf_f16, s->pf_part, s->pf_cnt, s->bd_lists, s->bd_xn,
                     s->bd_xn16, s->bd_att16, s->bd_f16, s->bd_part, s->stats,
-                    s->pf_cap_qkv, s->pf_cap_up, s->pf_cap_gate};
+                    s->pf_cap_qkv, s->pf_cap_up, s->pf_cap_gate, s->cl_proj_h, s->cl_down_s};
     for (void* b : bufs) cudaFree(b);
     if (s->ev_mid) cudaEventDestroy(s->ev_mid);
     if (s->ev0) cudaEventDestroy(s->ev0);
@@ -668,14 +707,20 @@ mc_status session_create(mc_model* m, int max_batch, int max_seq, int page_len, 
     s->cl_ok = plan_cluster(s, prop);
     if (s->cl_ok) {
         const size_t nhc = (size_t)(s->cl_nc - 1) * s->cl_cs;
+        const mc::ClusterParams& cpl = s->cl_plan;
+        const size_t G = m->H / m->K;
         struct Alloc cl_allocs[] = {
+            {(void**)&s->cl_proj_h, cpl.v2 ? L * K * D * G * hd * 4 : 0},
+            {(void**)&s->cl_down_s, cpl.v2 ? L * (size_t)s->cl_cs * D * cpl.fpc * 4 : 0},
             {(void**)&s->xfin, B * D * 4},
             {(void**)&s->hgen, B * 4},
             {(void**)&s->hsync, 64 * 4},
             {(void**)&s->hpv, B * nhc * 2 * 4},
             {(void**)&s->hpi, B * nhc * 2 * 4},
         };
+        s->cl2_version = ~0u;
         for (auto& a : cl_allocs) {
+            if (!a.bytes) continue;
             e = cudaMalloc(a.p, a.bytes);
             if (e != cudaSuccess) {
                 mc_session_destroy(s);
@@ -790,6 +835,20 @@ mc_status run_cluster(mc_session* s, mc::LoopParams<float>& p) {
     cp.hdone = s->hsync + 32;
     cp.hpv = s->hpv;
     cp.hpi = s->hpi;
+    cp.proj_h = s->cl_proj_h;
+    cp.down_s = s->cl_down_s;
+    int relayouts = 0;
+    if (cp.v2 && s->cl2_version != s->m->version) {
+        // the column blocks of attn_proj / ffn_down, from the current weights
+        const mc_model* m = s->m;
+        const char* wb = static_cast<const char*>(m->wblock);
+        mc::cl2_relayout_kernel<<<4 * 148, 256, 0, s->stream>>>(
+            reinterpret_cast<const float*>(wb + m->off[2]), reinterpret_cast<const float*>(wb + m->off[5]),
+            s->cl_proj_h, s->cl_down_s, m->L, m->D, m->F, m->K, (m->H / m->K) * m->hd, s->cl_cs, cp.fpc);
+        MC_CUDA(cudaGetLastError());
+        s->cl2_version = m->version;
+        relayouts = 1;
+    }
     MC_CUDA(cudaMemsetAsync(s->stamps, 0, ((size_t)p.T + 1) * 8, s->stream));
     MC_CUDA(cudaMemsetAsync(s->status, 0, 256, s->stream));
     MC_CUDA(cudaMemsetAsync(s->hsync, 0, 64 * 4, s->stream));
@@ -806,7 +865,7 @@ mc_status run_cluster(mc_session* s, mc::LoopParams<float>& p) {
     }
     if (e != cudaSuccess) return fail(MC_ERR_CUDA, "cluster loop launch: %s", cudaGetErrorString(e));
     MC_CUDA(cudaEventRecord(s->ev1, s->stream));
-    s->last_launches = 1;
+    s->last_launches = 1 + relayouts;
     s->last_path = 1;
     int status = 0;
     MC_CUDA(cudaMemcpyAsync(&status, s->status, 4, cudaMemcpyDeviceToHost, s->stream));

@@ -19,10 +19,10 @@ pytestmark = pytest.mark.gpu
 DIMS = O.Dims(4096, 128, 2, 4, 512, 128)
 
 
-@pytest.mark.parametrize("loop", ["grid", "cluster"])
+@pytest.mark.parametrize("loop", ["grid", "cluster", "cluster1"])
 def test_wait_deadline_reports_timeout_and_recovers(gpu, loop, monkeypatch):
-    if loop == "grid":
-        monkeypatch.setenv("MINIMA_CUDA_LOOP", "grid")
+    if loop in ("grid", "cluster1"):
+        monkeypatch.setenv("MINIMA_CUDA_LOOP", loop)
     else:
         monkeypatch.delenv("MINIMA_CUDA_LOOP", raising=False)
     hm = M.HostModel(DIMS.vocab, DIMS.dim, DIMS.n_layers, DIMS.n_heads, DIMS.ffn_dim, DIMS.max_seq,
@@ -42,5 +42,5 @@ def test_wait_deadline_reports_timeout_and_recovers(gpu, loop, monkeypatch):
     for b in range(2):
         ref, _, _ = orc.generate(prompts[b], 32, 128, O.make_options(top_k=1, max_new_tokens=6), b + 1)
         assert np.array_equal(out[b, :counts[b]], ref)
-    expected = "mc::cluster_loop_kernel" if loop == "cluster" else "mc::token_loop_kernel"
+    expected = "mc::token_loop_kernel" if loop == "grid" else "mc::cluster_loop_kernel"
     assert sess.last_kernel_name() == expected

@@ -100,13 +100,14 @@ def test_c2_batch_greedy(gpu):
     assert [c.pos for c in caches.caches] == [384] * B
 
 
-@pytest.mark.parametrize("loop", ["cluster", "grid"])
+@pytest.mark.parametrize("loop", ["cluster", "cluster1", "grid"])
 def test_c2_shape_both_loops(gpu, loop, monkeypatch):
     """The config-2 shape (4 x prompt 128, greedy) on the cluster-resident loop
-    and on the grid-barrier loop: same ids as the oracle, and each session
-    reports the loop it ran."""
-    if loop == "grid":
-        monkeypatch.setenv("MINIMA_CUDA_LOOP", "grid")
+    (its two-phase layer loop, and the five-phase one with
+    MINIMA_CUDA_LOOP=cluster1) and on the grid-barrier loop: same ids as the
+    oracle, and each session reports the loop it ran."""
+    if loop in ("grid", "cluster1"):
+        monkeypatch.setenv("MINIMA_CUDA_LOOP", loop)
     else:
         monkeypatch.delenv("MINIMA_CUDA_LOOP", raising=False)
     hm = M.HostModel(C1.vocab, C1.dim, C1.n_layers, C1.n_heads, C1.ffn_dim, C1.max_seq, seed=1)
@@ -116,8 +117,8 @@ def test_c2_shape_both_loops(gpu, loop, monkeypatch):
     sess = M.Session(M.DeviceModel(hm), B, 512)
     opts = M.options(top_k=1, max_new_tokens=96, repetition_penalty=1.05)
     out, counts, st, fpos = sess.generate(prompts, [128] * B, 512, opts, [5, 6, 7, 8])
-    assert sess.last_kernel_name() == ("mc::cluster_loop_kernel" if loop == "cluster"
-                                       else "mc::token_loop_kernel")
+    assert sess.last_kernel_name() == ("mc::token_loop_kernel" if loop == "grid"
+                                       else "mc::cluster_loop_kernel")
     ok, outr, countsr, str_ = orc.generate_batch(
         prompts, [128] * B, 512, 512, O.make_options(top_k=1, max_new_tokens=96,
                                                       repetition_penalty=1.05), [5, 6, 7, 8])
