@@ -95,6 +95,14 @@ __device__ __forceinline__ void bf16_split_store(__nv_bfloat16* hi, size_t lo_of
     hi[lo_off] = __float2bfloat16_rn(v - __bfloat162float(h));
 }
 
+// An attention output element: fp32 for the next kernels, and its bf16
+// hi/lo pair when the proj GEMM takes bf16 operands (att16 set).
+template <typename WT>
+__device__ __forceinline__ void att_store(const LoopParams<WT>& p, __nv_bfloat16* att16, size_t i, float v) {
+    p.att[i] = v;
+    if (att16) bf16_split_store(att16 + i, (size_t)p.Bcap * p.D, v);
+}
+
 // xn[b] = rmsnorm(x[b]) * scale (generate.c:57-63) for the listed sequences,
 // plus its bf16 hi/lo pair when xn16 is set.  With embed, x[b] is first set to the
 // embedding row of the id fed (generate.c:86-88); with nparts > 0, the
@@ -213,7 +221,8 @@ __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_gr
 
 template <typename WT>
 __global__ void __launch_bounds__(kBdAttThreads) bd_att_kernel(const LoopParams<WT> p, BdLists L, int l, int t,
-                                                               int klen, const float* qkvp, int nq) {
+                                                               int klen, const float* qkvp, int nq,
+                                                               __nv_bfloat16* att16) {
     extern __shared__ __align__(16) float smem_f[];
     const int nkeys = t + 1;
     const int nsplit = (nkeys + klen - 1) / klen;
@@ -456,7 +465,7 @@ __global__ void __launch_bounds__(kBdAttThreads) bd_att_kernel(const LoopParams<
         const int i = threadIdx.x + k * kBdAttThreads;
         if (i < G * hd) {
             const int h = i / hd, d = i - h * hd;
-            if (!combine) p.att[(size_t)b * p.D + (g * G + h) * hd + d] = o[k] / rl[h];
+            if (!combine) att_store(p, att16, (size_t)b * p.D + (g * G + h) * hd + d, o[k] / rl[h]);
             else p.part_o[(((size_t)b * p.H + g * G + h) * p.max_split + s) * hd + d] = o[k];
         }
     }
@@ -487,7 +496,7 @@ __global__ void __launch_bounds__(kBdAttThreads) bd_att_kernel(const LoopParams<
             den += w * ldcg(p.part_l + pb + s2);
             num += w * ldcg(p.part_o + (pb + s2) * hd + d);
         }
-        p.att[(size_t)b * p.D + (g * G + h) * hd + d] = num / den;
+        att_store(p, att16, (size_t)b * p.D + (g * G + h) * hd + d, num / den);
     }
     if (threadIdx.x == 0) p.att_cnt[b * p.K + g] = 0u;
 }
@@ -518,7 +527,8 @@ __host__ __device__ inline size_t bd_attw_smem(int G, int hd) {
 
 template <typename WT, int HD>
 __global__ void __launch_bounds__(kBdWWarps * 32) bd_attw_kernel(const LoopParams<WT> p, BdLists L, int l, int t,
-                                                                 int klen, const float* qkvp, int nq) {
+                                                                 int klen, const float* qkvp, int nq,
+                                                                 __nv_bfloat16* att16) {
     static_assert(HD == 32 || HD == 64, "a lane holds HD/32 output dimensions");
     constexpr int E = HD / 32;
     constexpr int Q4 = HD / 4;
@@ -737,7 +747,7 @@ __global__ void __launch_bounds__(kBdWWarps * 32) bd_attw_kernel(const LoopParam
             num += wgt * os[(w * G + h) * HD + d];
         }
         if (!combine) {
-            p.att[(size_t)b * p.D + (g * G + h) * HD + d] = num / den;
+            att_store(p, att16, (size_t)b * p.D + (g * G + h) * HD + d, num / den);
         } else {
             const size_t pi = ((size_t)b * p.H + g * G + h) * p.max_split + s;
             p.part_o[pi * HD + d] = num;
@@ -769,7 +779,7 @@ __global__ void __launch_bounds__(kBdWWarps * 32) bd_attw_kernel(const LoopParam
             den += w * ldcg(p.part_l + pb2 + s2);
             num += w * ldcg(p.part_o + (pb2 + s2) * HD + d);
         }
-        p.att[(size_t)b * p.D + (g * G + h) * HD + d] = num / den;
+        att_store(p, att16, (size_t)b * p.D + (g * G + h) * HD + d, num / den);
     }
     if (threadIdx.x == 0) p.att_cnt[b * p.K + g] = 0u;
 }
@@ -807,18 +817,6 @@ __global__ void __launch_bounds__(kThreads) bd_swiglu_kernel(const LoopParams<WT
 #pragma unroll
             for (int j = 0; j < 4; j++) bf16_split_store(f16 + (size_t)b * p.F + c + j, (size_t)p.Bcap * p.F, v[j]);
     }
-}
-
-// bf16 hi/lo pair of the attention output of the listed sequences (the
-// operand of a kind::f16 proj GEMM).
-template <typename WT>
-__global__ void __launch_bounds__(kThreads) bd_cvt_kernel(const LoopParams<WT> p, BdLists L, __nv_bfloat16* dst) {
-    pdl_wait();
-    pdl_trigger();
-    const int b = blockIdx.x;
-    if (b >= p.B || !L.act_fwd()[b]) return;
-    for (int k = threadIdx.x; k < p.D; k += blockDim.x)
-        bf16_split_store(dst + (size_t)b * p.D + k, (size_t)p.Bcap * p.D, p.att[(size_t)b * p.D + k]);
 }
 
 // Sampling and bookkeeping of the head sequences (the token loop's phase).

@@ -80,7 +80,7 @@ struct ClusterParams {
     int n_clusters;
     // layer-cluster shared-memory plan (byte offsets)
     unsigned off_x, off_xn, off_qkv, off_att, off_attp, off_f, off_sc, off_kv, off_stage;
-    unsigned off_rmsf, off_rope;
+    unsigned off_rmsf, off_rope, off_pages;
     unsigned stage_floats;      // floats per weight stage (slice + rms1 + rms2)
     int kv_tile;                // keys staged per attention tile
     // head clusters
@@ -165,6 +165,7 @@ struct LcState {
     float2* rope;  // [hd/2] (cos, sin) at the current position
     unsigned long long* bar;  // [kStages]
     unsigned long long* kvbar;  // K/V tile copies
+    int* pages;    // [kBCMax][pps] the sequences' page tables, copied at launch
     int* ints;     // [64]: 0..15 fwd list, 16..31 head list, 32.. scalars,
                    //       36/37 cluster error slots, 38 this CTA saw an error,
                    //       39 a K/V tile wait failed (thread 0)
@@ -213,8 +214,8 @@ __device__ void lc_issue_layer(const ClusterParams& cp, const CSlice& sl, LcStat
 }
 
 // x_b * inv_rms * scale for the sequences in `list` (generate.c:57-63).
-__device__ void lc_norm(const float* x, float* xn, const float* scale, const int* list, int n,
-                        int D, float* red) {
+__device__ __forceinline__ void lc_norm(const float* x, float* xn, const float* scale, const int* list, int n,
+                                        int D, float* red) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     // a warp per sequence: sum of squares, then that sequence's row, so one
     // CTA barrier closes the phase
@@ -250,7 +251,8 @@ __device__ __forceinline__ void att_issue_tile(const ClusterParams& cp, LcState&
     for (int r = 0; r < rows;) {
         const int j = a0 + r;
         const int seg = min(rows - r, plen - (j & (plen - 1)));
-        const size_t row = kv_row(p.pg, p.L, p.K, l, b, g, j);
+        const size_t row =
+            kv_row_at(S.pages[b * p.pg.pps + (j >> p.pg.shift)], p.pg.shift, p.L, p.K, l, g, j);
         const unsigned sb = (unsigned)(seg * hd * 4);
         bulk_g2s(S.kv + (size_t)r * hd, p.kc + row * hd, sb, S.kvbar);
         bulk_g2s(S.kv + (size_t)(cp.kv_tile + r) * hd, p.vc + row * hd, sb, S.kvbar);
@@ -667,7 +669,8 @@ __device__ bool lc_layer(const ClusterParams& cp, const CSlice& sl, LcState& S,
             if (slot >= H) {
                 const bool isk = slot < H + K;
                 const int g = isk ? slot - H : slot - H - K;
-                (isk ? p.kc : p.vc)[kv_row(p.pg, p.L, K, l, b, g, t) * hd + d] = out;
+                (isk ? p.kc : p.vc)[kv_row_at(S.pages[b * p.pg.pps + (t >> p.pg.shift)], p.pg.shift, p.L, K,
+                                              l, g, t) * hd + d] = out;
                 wrote_kv = true;
             }
         }
@@ -829,6 +832,7 @@ __device__ void lc_main(const ClusterParams& cp, unsigned char* smem, cg::cluste
     S.stage = reinterpret_cast<float*>(smem + cp.off_stage);
     S.rmsf = reinterpret_cast<float*>(smem + cp.off_rmsf);
     S.rope = reinterpret_cast<float2*>(smem + cp.off_rope);
+    S.pages = reinterpret_cast<int*>(smem + cp.off_pages);
     S.seq = reinterpret_cast<SeqMirror*>(smem + 576);
     const CSlice sl = cluster_slice(crank, cp.cs, p.Q, p.D, p.F);
     const int nhc = (cp.n_clusters - 1) * cp.cs;
@@ -836,6 +840,7 @@ __device__ void lc_main(const ClusterParams& cp, unsigned char* smem, cg::cluste
     int* hl = S.ints + 16;   // [16]
     int* toks = S.ints + 40; // [8] ids fed at this step
     const int warp = threadIdx.x >> 5;
+    for (int e = threadIdx.x; e < p.B * p.pg.pps; e += blockDim.x) S.pages[e] = __ldg(p.pg.table + e);
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kStages; s++) mbar_init(&S.bar[s], 1);

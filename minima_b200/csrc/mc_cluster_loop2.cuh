@@ -23,7 +23,9 @@
 // Every CTA therefore keeps the whole residual stream of every sequence,
 // updated by the same additions in the same order (identical everywhere).
 // The column blocks of attn_proj per KV head and of ffn_down per CTA are
-// contiguous copies made by cl2_relayout_kernel when the weights change.
+// contiguous, transposed copies made by cl2_relayout_kernel when the
+// weights change ([input][output]: a thread per output reads consecutive
+// addresses across the warp).
 // Each phase's weights (A: Q/K/V rows of the CTA's KV head, its attn_proj
 // block, rms1; B: its up/gate rows, its ffn_down block, rms2) stream into a
 // single buffer per phase by bulk copies issued as soon as the phase is
@@ -37,8 +39,13 @@
 
 namespace mc {
 
-// proj_h[l][g][i][c] = W_proj[l][i][g G hd + c]; down_s[l][c][i][j] =
-// W_down[l][i][c fpc + j] (0 past F).
+// The thread that issues and awaits the K/V tile copies (its LcState holds
+// the tile's mbarrier phase): lane 0 of the last warp, so that warp 0 is
+// free for the RMSNorm that follows the first request.
+constexpr int kTileThread = kThreads - 32;
+
+// proj_h[l][g][c][i] = W_proj[l][i][g G hd + c]; down_s[l][s][j][i] =
+// W_down[l][i][s fpc + j] (0 past F).
 __global__ void cl2_relayout_kernel(const float* __restrict__ w_proj, const float* __restrict__ w_down,
                                     float* __restrict__ proj_h, float* __restrict__ down_s, int L, int D,
                                     int F, int K, int ghd, int cs, int fpc) {
@@ -46,11 +53,11 @@ __global__ void cl2_relayout_kernel(const float* __restrict__ w_proj, const floa
     for (size_t e = blockIdx.x * (size_t)blockDim.x + threadIdx.x; e < n1 + n2;
          e += (size_t)gridDim.x * blockDim.x) {
         if (e < n1) {
-            const size_t c = e % ghd, i = (e / ghd) % D, g = (e / ((size_t)ghd * D)) % K, l = e / ((size_t)ghd * D * K);
+            const size_t i = e % D, c = (e / D) % ghd, g = (e / ((size_t)D * ghd)) % K, l = e / ((size_t)D * ghd * K);
             proj_h[e] = w_proj[(l * D + i) * D + g * ghd + c];
         } else {
             const size_t f = e - n1;
-            const size_t j = f % fpc, i = (f / fpc) % D, c = (f / ((size_t)fpc * D)) % cs, l = f / ((size_t)fpc * D * cs);
+            const size_t i = f % D, j = (f / D) % fpc, c = (f / ((size_t)D * fpc)) % cs, l = f / ((size_t)D * fpc * cs);
             const size_t col = c * fpc + j;
             down_s[f] = col < (size_t)F ? w_down[(l * D + i) * F + col] : 0.0f;
         }
@@ -75,7 +82,7 @@ __device__ void cl2_issue_a(const ClusterParams& cp, LcState& S, int l, int g) {
 }
 
 // Phase B weights of layer l for this CTA: up and gate rows [f0, f1), its
-// ffn_down block [D][fpc], rms2.
+// ffn_down block [fpc][D], rms2.
 __device__ void cl2_issue_b(const ClusterParams& cp, const CSlice& sl, LcState& S, int l, int crank) {
     const LoopParams<float>& p = cp.lp;
     const size_t D = p.D, fpc = cp.fpc;
@@ -115,13 +122,20 @@ __device__ __forceinline__ float cl2_dot32(const float* rows, int ld, int r0, in
 }
 
 // x[b] += sum over the cs CTAs' ffn_down partials (CTA order) for the
-// sequences in fl.  All threads; ends with a CTA barrier.
+// sequences in fl: a thread per element, all cs loads issued before the
+// additions.  All threads; ends with a CTA barrier.
 __device__ __forceinline__ void cl2_add_down(const ClusterParams& cp, LcState& S, const int* fl, int nf) {
     const int D = cp.lp.D, cs = cp.cs;
+    const size_t cstride = (size_t)cp.dp_b * D;
     for (int e = threadIdx.x; e < nf * D; e += blockDim.x) {
         const int b = fl[e / D], k = e % D;
+        const float* src = S.dp + (size_t)b * D + k;
+        float v[16];
+#pragma unroll
+        for (int c = 0; c < 16; c++) v[c] = c < cs ? src[c * cstride] : 0.0f;
         float s = 0.0f;
-        for (int c = 0; c < cs; c++) s += S.dp[((size_t)c * cp.dp_b + b) * D + k];
+#pragma unroll
+        for (int c = 0; c < 16; c++) s += v[c];
         S.x[b * D + k] += s;
     }
     __syncthreads();
@@ -129,13 +143,16 @@ __device__ __forceinline__ void cl2_add_down(const ClusterParams& cp, LcState& S
 
 // One layer (two phases, two cluster barriers).  pa / pb: parities of the
 // phase buffers' next copies; `first`: the residual is the embedding.
-template <int HD>
+// HD / DC / FC > 0 fix head_dim, dim and the F slice at compile time (the
+// default model's 32 / 128 / 32), so that the short loops of every phase
+// have constant trip counts; 0 = read them from the parameters.
+template <int HD, int DC, int FC>
 __device__ bool cl2_layer(const ClusterParams& cp, const CSlice& sl, LcState& S, cg::cluster_group& cl,
                           int crank, int l, int t, const int* fl, int nf, bool first, unsigned& pa,
                           unsigned& pbp) {
     const LoopParams<float>& p = cp.lp;
-    const int D = p.D, K = p.K, G = p.G, hd = HD > 0 ? HD : p.hd, cs = cp.cs;
-    const int ghd = G * hd, rows_a = ghd + 2 * hd, fpc = cp.fpc;
+    const int D = DC > 0 ? DC : p.D, K = p.K, G = p.G, hd = HD > 0 ? HD : p.hd, cs = cp.cs;
+    const int ghd = G * hd, rows_a = ghd + 2 * hd, fpc = FC > 0 ? FC : cp.fpc;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int nd = (hd + 31) / 32;
     if (!first) cl2_add_down(cp, S, fl, nf);
@@ -149,7 +166,8 @@ __device__ bool cl2_layer(const ClusterParams& cp, const CSlice& sl, LcState& S,
     const int nkeys = t + 1;
     bool wrote_kv = false;
     if (unit) {
-        if (threadIdx.x == 0) att_issue_tile(cp, S, l, b, g, 0, min(cp.kv_tile, nkeys), t, hd);
+        // the first K/V tile is requested by the last warp (warp 0 normalises)
+        if (threadIdx.x == kTileThread) att_issue_tile(cp, S, l, b, g, 0, min(cp.kv_tile, nkeys), t, hd);
         const float* wa = S.stage;
         const float* rms1 = wa + (size_t)(rows_a + ghd) * D;
         // rmsnorm of sequence b (generate.c:57-63): one warp sums, the CTA scales
@@ -179,7 +197,8 @@ __device__ bool cl2_layer(const ClusterParams& cp, const CSlice& sl, LcState& S,
                 }
                 S.qkv[r] = out;
                 if (!isq) {
-                    (isk ? p.kc : p.vc)[kv_row(p.pg, p.L, K, l, b, g, t) * hd + d] = out;
+                    const int page = S.pages[b * p.pg.pps + (t >> p.pg.shift)];
+                    (isk ? p.kc : p.vc)[kv_row_at(page, p.pg.shift, p.L, K, l, g, t) * hd + d] = out;
                     wrote_kv = true;
                 }
             }
@@ -205,7 +224,7 @@ __device__ bool cl2_layer(const ClusterParams& cp, const CSlice& sl, LcState& S,
         }
         for (int a0 = 0; a0 < nkeys; a0 += cp.kv_tile) {
             const int n = min(cp.kv_tile, nkeys - a0);
-            if (threadIdx.x == 0 && a0 != 0) att_issue_tile(cp, S, l, b, g, a0, n, t, hd);
+            if (threadIdx.x == kTileThread && a0 != 0) att_issue_tile(cp, S, l, b, g, a0, n, t, hd);
             if (t >= a0 && t < a0 + n)
                 for (int c = threadIdx.x; c < 2 * hd; c += blockDim.x) {
                     if (c < hd) ks[(t - a0) * hd + c] = kq[c];
@@ -213,7 +232,7 @@ __device__ bool cl2_layer(const ClusterParams& cp, const CSlice& sl, LcState& S,
                 }
             const int pad = ((n + 31) & ~31) - n;
             for (int c = threadIdx.x; c < pad * hd; c += blockDim.x) vs[n * hd + c] = 0.0f;
-            if (threadIdx.x == 0) att_wait_tile(p, S);
+            if (threadIdx.x == kTileThread) att_wait_tile(p, S);
             __syncthreads();
             for (int rr = warp; rr * 32 < n; rr += kWarps)
                 att_run<HD>(ks + (size_t)rr * 32 * hd, vs + (size_t)rr * 32 * hd, q, pbuf, min(32, n - rr * 32),
@@ -250,11 +269,18 @@ __device__ bool cl2_layer(const ClusterParams& cp, const CSlice& sl, LcState& S,
             S.att[i] = num / den;
         }
         __syncthreads();
-        // this head group's share of attn_proj (generate.c:158-163)
+        // this head group's share of attn_proj (generate.c:158-163): a thread
+        // per output over the block's [G hd][D] (transposed) columns
         const float* wp = wa + (size_t)rows_a * D;
-        for (int r0 = 32 * warp; r0 < D; r0 += 32 * kWarps) {
-            const float val = cl2_dot32(wp, ghd, r0, D, ghd, S.att);
-            if (r0 + lane < D) S.attp[crank * D + r0 + lane] = val;
+        for (int i = threadIdx.x; i < D; i += blockDim.x) {
+            float a0 = 0.0f, a1 = 0.0f;
+            int c = 0;
+            for (; c + 1 < ghd; c += 2) {
+                a0 = fmaf(wp[(size_t)c * D + i], S.att[c], a0);
+                a1 = fmaf(wp[(size_t)(c + 1) * D + i], S.att[c + 1], a1);
+            }
+            if (c < ghd) a0 = fmaf(wp[(size_t)c * D + i], S.att[c], a0);
+            S.attp[crank * D + i] = a0 + a1;
         }
         __syncthreads();
         push_block(cl, S.attp, crank * D, D, cs, crank);
@@ -297,17 +323,21 @@ __device__ bool cl2_layer(const ClusterParams& cp, const CSlice& sl, LcState& S,
     __syncthreads();
     // this slice's share of ffn_down (generate.c:181-184), into this CTA's
     // slot of the partials
+    // a thread per (output, sequence) over the block's [fpc][D] (transposed)
+    // columns; the SwiGLU values are broadcast reads
     const int nfr = sl.f1 - sl.f0;
     float* mine = S.dp + (size_t)crank * cp.dp_b * D;
-    if (nfr > 0) {
-        for (int i0 = 4 * warp; i0 < D; i0 += 4 * kWarps) {
-            const float* w0 = wd + (size_t)i0 * fpc;
-            const float val = lc_gemv4(w0, w0 + fpc, w0 + 2 * fpc, w0 + 3 * fpc, nfr, S.f, fpc, fl, nf);
-            const int i = lane & 7;
-            if (i < nf) mine[fl[i] * D + i0 + (lane >> 3)] = val;
+    for (int e = threadIdx.x; e < D * nf; e += blockDim.x) {
+        const int i = e % D, b = fl[e / D];
+        const float* fr = S.f + b * fpc;
+        float a0 = 0.0f, a1 = 0.0f;
+        int j = 0;
+        for (; j + 1 < nfr; j += 2) {
+            a0 = fmaf(wd[(size_t)j * D + i], fr[j], a0);
+            a1 = fmaf(wd[(size_t)(j + 1) * D + i], fr[j + 1], a1);
         }
-    } else {
-        for (int e = threadIdx.x; e < nf * D; e += blockDim.x) mine[fl[e / D] * D + e % D] = 0.0f;
+        if (j < nfr) a0 = fmaf(wd[(size_t)j * D + i], fr[j], a0);
+        mine[b * D + i] = a0 + a1;
     }
     __syncthreads();
     {
@@ -346,6 +376,7 @@ __device__ void cl2_main(const ClusterParams& cp, unsigned char* smem, cg::clust
     S.wb = reinterpret_cast<float*>(smem + cp.off_wb);
     S.rmsf = reinterpret_cast<float*>(smem + cp.off_rmsf);
     S.rope = reinterpret_cast<float2*>(smem + cp.off_rope);
+    S.pages = reinterpret_cast<int*>(smem + cp.off_pages);
     S.seq = reinterpret_cast<SeqMirror*>(smem + 576);
     const CSlice sl = cluster_slice(crank, cp.cs, p.Q, p.D, p.F);
     const int nhc = (cp.n_clusters - 1) * cp.cs;
@@ -371,6 +402,7 @@ __device__ void cl2_main(const ClusterParams& cp, unsigned char* smem, cg::clust
         m.result = g.result; m.final_pos = g.final_pos; m.rng = g.rng;
     }
     for (int k = threadIdx.x; k < p.D; k += blockDim.x) S.rmsf[k] = __ldg(p.rmsf + k);
+    for (int e = threadIdx.x; e < p.B * p.pg.pps; e += blockDim.x) S.pages[e] = __ldg(p.pg.table + e);
     // the SwiGLU slice is read past f1 - f0 by nobody, but keep it finite
     for (int e = threadIdx.x; e < cp.dp_b * cp.fpc; e += blockDim.x) S.f[e] = 0.0f;
     __syncthreads();
@@ -442,11 +474,15 @@ __device__ void cl2_main(const ClusterParams& cp, unsigned char* smem, cg::clust
         }
         __syncthreads();
         for (int l = 0; ok && l < p.L; l++) {
-            switch (p.hd) {
-            case 16: ok = cl2_layer<16>(cp, sl, S, cl, crank, l, t, fl, nf, l == 0, pa, pbp); break;
-            case 32: ok = cl2_layer<32>(cp, sl, S, cl, crank, l, t, fl, nf, l == 0, pa, pbp); break;
-            case 64: ok = cl2_layer<64>(cp, sl, S, cl, crank, l, t, fl, nf, l == 0, pa, pbp); break;
-            default: ok = cl2_layer<0>(cp, sl, S, cl, crank, l, t, fl, nf, l == 0, pa, pbp); break;
+            if (p.hd == 32 && p.D == 128 && cp.fpc == 32) {    // the default model (config.h)
+                ok = cl2_layer<32, 128, 32>(cp, sl, S, cl, crank, l, t, fl, nf, l == 0, pa, pbp);
+            } else {
+                switch (p.hd) {
+                case 16: ok = cl2_layer<16, 0, 0>(cp, sl, S, cl, crank, l, t, fl, nf, l == 0, pa, pbp); break;
+                case 32: ok = cl2_layer<32, 0, 0>(cp, sl, S, cl, crank, l, t, fl, nf, l == 0, pa, pbp); break;
+                case 64: ok = cl2_layer<64, 0, 0>(cp, sl, S, cl, crank, l, t, fl, nf, l == 0, pa, pbp); break;
+                default: ok = cl2_layer<0, 0, 0>(cp, sl, S, cl, crank, l, t, fl, nf, l == 0, pa, pbp); break;
+                }
             }
         }
         if (!ok) break;
@@ -522,8 +558,9 @@ __device__ void cl2_main(const ClusterParams& cp, unsigned char* smem, cg::clust
     if (threadIdx.x == 0) {
         if (!mbar_wait(&S.bar[0], pa, p.timeout_ns)) atomicMax(p.status, (int)ST_TIMEOUT);
         if (!mbar_wait(&S.bar[1], pbp, p.timeout_ns)) atomicMax(p.status, (int)ST_TIMEOUT);
-        if (S.kvpend && !mbar_wait(S.kvbar, S.kvph, p.timeout_ns)) atomicMax(p.status, (int)ST_TIMEOUT);
     }
+    if (threadIdx.x == kTileThread && S.kvpend && !mbar_wait(S.kvbar, S.kvph, p.timeout_ns))
+        atomicMax(p.status, (int)ST_TIMEOUT);
     __syncthreads();
     cl.sync();   // no CTA leaves while others may still write its shared memory
 }

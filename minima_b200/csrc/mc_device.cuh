@@ -33,9 +33,12 @@ constexpr int kKvMinPageShift = 6;
 
 // Row index (times head_dim: the element offset) of position t of
 // (layer l, sequence b, KV head g).  t < pps << shift.
+__device__ __forceinline__ size_t kv_row_at(int page, int shift, int L, int K, int l, int g, int t) {
+    return ((((size_t)page * L + l) * K + g) << shift) + (size_t)(t & ((1 << shift) - 1));
+}
 __device__ __forceinline__ size_t kv_row(const KvPages& pg, int L, int K, int l, int b, int g, int t) {
     const int page = __ldg(pg.table + (size_t)b * pg.pps + (t >> pg.shift));
-    return ((((size_t)page * L + l) * K + g) << pg.shift) + (size_t)(t & ((1 << pg.shift) - 1));
+    return kv_row_at(page, pg.shift, L, K, l, g, t);
 }
 
 // Programmatic dependent launch (kernels launched with the programmatic

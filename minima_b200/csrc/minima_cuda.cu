@@ -294,6 +294,7 @@ bool plan_cluster(mc_session* s, const cudaDeviceProp& prop) {
                 cp.off_f = take((size_t)B8 * cp.fpc, 16);
                 cp.off_rmsf = take((size_t)D, 16);
                 cp.off_rope = take((size_t)std::max(hd, 2), 16);
+                cp.off_pages = take((size_t)B8 * s->kv_pps, 16);
                 sc_f = (size_t)mc::kWarps * (ghd + 2 * G + 32 * mc::kAttMaxG);
                 cp.off_sc = take(sc_f, 16);
                 cp.off_stage = take(stage_f, 128);
@@ -313,6 +314,7 @@ bool plan_cluster(mc_session* s, const cudaDeviceProp& prop) {
                 cp.off_f = take((size_t)B8 * F, 16);
                 cp.off_rmsf = take((size_t)D, 16);
                 cp.off_rope = take((size_t)std::max(hd, 2), 16);
+                cp.off_pages = take((size_t)B8 * s->kv_pps, 16);
                 sc_f = (size_t)mc::kWarps * (ghd + 2 * G + 32 * mc::kAttMaxG);
             }
             const size_t fixed = off;
@@ -1438,17 +1440,16 @@ mc_status run_batched(mc_session* s, mc::LoopParams<WT>& p) {
             g.layer = l;
             g.N = m->Q; g.K = m->D; g.ldc = m->Q; g.ksplit = ks_qkv;
             if ((e = tc_dec_launch<KD, mc::EPI_PART, BN, ST1>(xm[0], wm[0], wm[0], g, st)) != cudaSuccess) break;
+            // (bf16: the attention also writes the hi/lo operand of the proj GEMM)
+            __nv_bfloat16* att16 = kB16 ? s->bd_att16 : nullptr;
             if (att_lane)
                 e = launch_pdl(m->hd == 32 ? mc::bd_attw_kernel<WT, 32> : mc::bd_attw_kernel<WT, 64>,
                                dim3(att_units), dim3(mc::kBdWWarps * 32), att_smem, st, p, L, l, t, klen,
-                               (const float*)s->bd_part, ks_qkv);
+                               (const float*)s->bd_part, ks_qkv, att16);
             else
                 e = launch_pdl(mc::bd_att_kernel<WT>, dim3(att_units), dim3(mc::kBdAttThreads), att_smem, st, p,
-                               L, l, t, klen, (const float*)s->bd_part, ks_qkv);
+                               L, l, t, klen, (const float*)s->bd_part, ks_qkv, att16);
             if (e != cudaSuccess) break;
-            if (kB16 && (e = launch_pdl(mc::bd_cvt_kernel<WT>, dim3(p.B), dim3(mc::kThreads), 0, st, p, L,
-                                        s->bd_att16)) != cudaSuccess)
-                break;
             g.N = m->D; g.K = m->D; g.ldc = m->D; g.ksplit = ks_proj;
             if ((e = tc_dec_launch<KD, mc::EPI_PART, BN, ST1>(xm[1], wm[1], wm[1], g, st)) != cudaSuccess) break;
             if ((e = launch_pdl(mc::bd_norm_kernel<WT>, dim3(p.B), dim3(mc::kThreads), 0, st, p, L, 0,
@@ -1462,7 +1463,7 @@ mc_status run_batched(mc_session* s, mc::LoopParams<WT>& p) {
                 break;
             g.N = m->D; g.K = m->F; g.ldc = m->D; g.ksplit = ks_down;
             if ((e = tc_dec_launch<KD, mc::EPI_PART, BN, ST1>(xm[2], wm[4], wm[4], g, st)) != cudaSuccess) break;
-            launches += kB16 ? 9 : 8;
+            launches += 8;
         }
         if (e != cudaSuccess) break;
         if ((e = launch_pdl(mc::bd_norm_kernel<WT>, dim3(p.B), dim3(mc::kThreads), 0, st, p, L, 1, rmsf, 0,
