@@ -1380,6 +1380,7 @@ mc_status run_batched(mc_session* s, mc::LoopParams<WT>& p) {
     const int G = m->H / m->K;
     const bool att_lane = (m->hd == 32 || m->hd == 64) && G <= mc::kBdWMaxG;
     const size_t att_smem = att_lane ? mc::bd_attw_smem(G, m->hd) : mc::bd_att_smem(G, m->hd);
+    const int att_warps = mc::kBdWWarps;
     if (att_smem > (size_t)optin)
         return fail(MC_ERR_UNSUPPORTED, "batched attention needs %zu B of shared memory", att_smem);
     cudaStream_t st = s->stream;
@@ -1409,6 +1410,17 @@ mc_status run_batched(mc_session* s, mc::LoopParams<WT>& p) {
     const CUtensorMap* wm = s->bd_wmap;
     const float* rmsf = m->norms + 2 * (size_t)m->L * m->D;
     const unsigned swiglu_blocks = (unsigned)std::max(1, std::min(4 * sms, (int)((p.B * F / 4 + 255) / 256)));
+    // resident attention CTAs per SM (lane-per-key kernel), for the split choice below
+    int att_per_sm = 1;
+    if (att_lane) {
+        const cudaError_t oe = cudaOccupancyMaxActiveBlocksPerMultiprocessor(
+            &att_per_sm, m->hd == 32 ? mc::bd_attw_kernel<WT, 32> : mc::bd_attw_kernel<WT, 64>, att_warps * 32,
+            att_smem);
+        if (oe != cudaSuccess || att_per_sm < 1) {
+            cudaGetLastError();
+            att_per_sm = 1;
+        }
+    }
     __nv_bfloat16* xn16 = kB16 ? s->bd_xn16 : nullptr;
     __nv_bfloat16* f16 = kB16 ? s->bd_f16 : nullptr;
     int launches = 0;
@@ -1424,10 +1436,31 @@ mc_status run_batched(mc_session* s, mc::LoopParams<WT>& p) {
         // klen-key pieces only when the pairs alone would not fill the GPU
         // twice over (the device's position is t too)
         const int pairs = p.B * m->K, nkeys = t + 1;
-        const int want = std::max(1, (2 * sms + pairs - 1) / pairs);
         // (a multiple of the tile, and at least kSplitLen keys so that the
         // splits fit the max_split partial slots)
-        const int klen = std::max(mc::kSplitLen, ((nkeys + want - 1) / want + mc::kBdTile - 1) / mc::kBdTile * mc::kBdTile);
+        auto klen_of = [&](int want) {
+            return std::max(mc::kSplitLen, ((nkeys + want - 1) / want + mc::kBdTile - 1) / mc::kBdTile * mc::kBdTile);
+        };
+        int klen = klen_of(std::max(1, (2 * sms + pairs - 1) / pairs));
+        if (att_lane) {
+            // lane-per-key kernel: the split count with the fewest (waves of
+            // resident CTAs) x (32-key chunks per warp), one chunk's worth
+            // added for the merge of split units
+            const long slots = (long)att_per_sm * sms;
+            long best = -1;
+            for (int want = 1; want <= p.max_split; want++) {
+                const int kl = klen_of(want), ns = (nkeys + kl - 1) / kl;
+                if (want > 1 && ns == (nkeys + klen_of(want - 1) - 1) / klen_of(want - 1)) continue;
+                const long waves = ((long)pairs * ns + slots - 1) / slots;
+                const long per_warp = ((kl + 31) / 32 + att_warps - 1) / att_warps;
+                const long cost = waves * per_warp + (ns > 1 ? 1 : 0);
+                if (best < 0 || cost < best) {
+                    best = cost;
+                    klen = kl;
+                }
+                if (ns >= nkeys / mc::kSplitLen) break;
+            }
+        }
         const unsigned att_units = (unsigned)pairs * (unsigned)((nkeys + klen - 1) / klen);
         // every GEMM leaves K-slice partials in bd_part; the kernel after it
         // sums them in slice order (norm: residual; attention: q and the
