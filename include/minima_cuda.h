@@ -257,6 +257,13 @@ mc_status mc_last_step_times(mc_session* session, unsigned long long* ns, int ca
    loop) or "mc::cluster_loop_kernel" (cluster-resident greedy loop). */
 const char* mc_last_kernel_name(mc_session* session);
 
+/* Layer loop of this session's cluster-resident plan: -1 none (the
+   grid-barrier loop serves every call), 0 five phases per layer, 1 two
+   phases closed by cluster barriers, 2 two phases whose partials move by
+   bulk copies onto the receivers' mbarriers.  MINIMA_CUDA_LOOP=grid,
+   cluster1 or cluster2 (read at mc_session_create) caps the choice. */
+mc_status mc_session_cluster_variant(mc_session* session, int* variant);
+
 /* The CUDA stream (cudaStream_t) every call on this session is issued on,
    so that callers can time or order their own work against it. */
 mc_status mc_session_stream(mc_session* session, void** stream);

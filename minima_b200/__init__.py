@@ -32,6 +32,7 @@ CUDA_SYMBOLS = ("mc_init", "mc_model_create", "mc_model_update", "mc_model_destr
                 "mc_session_create", "mc_session_destroy", "mc_generate", "mc_forward_logits",
                 "mc_last_kernel_ms", "mc_last_launch_count", "mc_last_step_times",
                 "mc_last_kernel_name", "mc_last_prefill", "mc_session_stream", "mc_last_error",
+                "mc_session_cluster_variant",
                 "mc_checkpoint_inspect", "mc_model_load_checkpoint", "mc_gemm",
                 "mc_model_forward", "mc_next_token_stats", "mc_generate_static",
                 "mc_session_create_paged", "mc_model_forward_caches", "mc_matmul")
@@ -228,6 +229,7 @@ def _declare(host, cuda, gen):
     cuda.mc_last_prefill.argtypes = [vp, i32p, _f32p]
     cuda.mc_last_kernel_name.restype = C.c_char_p
     cuda.mc_last_kernel_name.argtypes = [vp]
+    cuda.mc_session_cluster_variant.argtypes = [vp, C.POINTER(C.c_int)]
     cuda.mc_last_error.restype = C.c_char_p
     cuda.mc_model_forward.argtypes = [vp, C.c_int, C.c_int, u16p, _f32p, C.c_uint]
     cuda.mc_gemm.argtypes = [C.c_int, vp, vp, _f32p, C.c_int, C.c_int, C.c_int, C.c_uint, _f32p]
@@ -606,6 +608,13 @@ class Session:
 
     def last_kernel_name(self) -> str:
         return libs()[1].mc_last_kernel_name(self.h).decode()
+
+    def cluster_variant(self) -> int:
+        """Layer loop of the cluster-resident plan (-1 none, 0 five phases,
+        1 two phases with cluster barriers, 2 two phases, dataflow)."""
+        v = C.c_int()
+        _check(libs()[1].mc_session_cluster_variant(self.h, C.byref(v)), "mc_session_cluster_variant")
+        return v.value
 
     def stream_handle(self) -> int:
         """cudaStream_t of this session, as an integer handle."""

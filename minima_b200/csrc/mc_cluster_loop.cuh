@@ -88,7 +88,9 @@ struct ClusterParams {
     unsigned hc_ld;             // padded row stride (floats) of the resident slice
     unsigned off_hc_x;          // byte offset of the normalised-x copy
     // two-phase layer loop (mc_cluster_loop2.cuh)
-    int v2;
+    int v2;                     // 0: five-phase loop; 1: two-phase loop, cluster barriers
+                                // between phases; 2: two-phase loop, partials exchanged by
+                                // bulk copies onto the receivers' mbarriers (dataflow)
     unsigned off_wb;            // phase B weight buffer (off_stage: phase A buffer)
     int fpc;                    // up/gate rows (ffn_down columns) per CTA, padded
     int dp_b;                   // sequence stride of the ffn_down partials
@@ -134,6 +136,21 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, unsigned by
         : "memory");
 }
 
+// 1-D bulk copy of `bytes` (a multiple of 16, 16-byte aligned) from this
+// CTA's shared memory to the same offset in CTA `rank` of the cluster; the
+// bytes complete on that CTA's mbarrier at `bar`'s offset.
+__device__ __forceinline__ void bulk_s2peer(const void* src, unsigned bytes, unsigned long long* bar,
+                                            unsigned rank) {
+    unsigned dst, rbar;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(dst) : "r"(smem_addr(src)), "r"(rank));
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(rbar) : "r"(smem_addr(bar)), "r"(rank));
+    asm volatile(
+        "cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::
+            "r"(dst),
+        "r"(smem_addr(src)), "r"(bytes), "r"(rbar)
+        : "memory");
+}
+
 // Wait for phase `parity` of `bar`, bounded by the deadline; false on expiry.
 __device__ __forceinline__ bool mbar_wait(unsigned long long* bar, unsigned parity,
                                           unsigned long long timeout_ns) {
@@ -167,6 +184,7 @@ struct LcState {
     unsigned long long* kvbar;  // K/V tile copies
     int* pages;    // [kBCMax][pps] the sequences' page tables, copied at launch
     int* ints;     // [64]: 0..15 fwd list, 16..31 head list, 32.. scalars,
+                   //       34 dataflow exchange stopped after a failed wait,
                    //       36/37 cluster error slots, 38 this CTA saw an error,
                    //       39 a K/V tile wait failed (thread 0)
     float* red;    // [64]
@@ -174,6 +192,12 @@ struct LcState {
     int epoch;     // cluster barriers passed (identical in every CTA of the cluster)
     unsigned kvph;      // thread 0: phase of kvbar awaited next
     int kvpend;         // thread 0: a copy into the K/V tile is outstanding
+    // dataflow exchange of the two-phase loop (all threads hold the same values)
+    unsigned long long* atbar;   // attn_proj partials of every unit have landed
+    unsigned long long* dpbar;   // [2] ffn_down partials of every CTA have landed (layer parity)
+    unsigned atph;               // phase of atbar awaited next
+    unsigned dpph;               // bit p: phase of dpbar[p] awaited next
+    int nlayer;                  // layers run in this launch (selects the dpbar / partial buffer)
 };
 
 // The sequence table in shared memory: the layer cluster reads it every

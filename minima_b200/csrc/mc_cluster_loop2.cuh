@@ -33,6 +33,33 @@
 // to land.  The down partials share their shared memory with the K/V tile:
 // they are summed before the tile's first copy is issued and written by
 // other CTAs only after the barrier that ends the attention.
+//
+// Dataflow exchange (plan v2 == 2): instead of remote stores closed by a
+// cluster barrier, each CTA sends its partial with one bulk copy per peer
+// (shared::cta -> shared::cluster) that completes on the receiver's
+// mbarrier, and a receiver waits only for the bytes it sums:
+//  * atbar: the nf K units' attn_proj partials (single buffer).  A unit
+//    writes layer n+1's partial only after it summed every CTA's layer-n
+//    down partials, each sent after that CTA had summed layer n's attn_proj
+//    partials, so no copy lands on a buffer still being read, and the
+//    sender's own slot has been read by every receiver.
+//  * dpbar[n & 1]: the cs CTAs' ffn_down partials of layer n, in two
+//    buffers by layer parity (a CTA that is not a unit may still be summing
+//    layer n's while a fast peer already sends layer n+1's; layer n+2's
+//    needs its layer n+1 partial first).  Both buffers share the K/V
+//    tile's bytes: layer n's is summed before the tile of layer n+1 is
+//    requested, and no layer n+1 partial exists before every unit has
+//    finished that layer's attention.
+// Arrivals may precede the receiver's expect_tx (tx-count goes negative in
+// between, as the mbarrier allows); the chains above keep every phase
+// complete before bytes of the next one of the same barrier are sent.  The
+// step's own cluster barrier (the head hand-off, or one added when no
+// sequence samples) keeps ordering the K/V rows written in the step before
+// later steps' bulk reads and makes failures cluster-wide.  After a failed
+// wait a CTA stops arming, waiting and sending for the rest of the launch
+// (its peers' waits then expire too) and every CTA leaves at that step's
+// barrier; a launch that failed this way lets in-flight copies land before
+// its CTAs exit.
 #pragma once
 
 #include "mc_cluster_loop.cuh"
@@ -121,15 +148,17 @@ __device__ __forceinline__ float cl2_dot32(const float* rows, int ld, int r0, in
     return transpose_reduce32(acc);
 }
 
-// x[b] += sum over the cs CTAs' ffn_down partials (CTA order) for the
-// sequences in fl: a thread per element, all cs loads issued before the
-// additions.  All threads; ends with a CTA barrier.
-__device__ __forceinline__ void cl2_add_down(const ClusterParams& cp, LcState& S, const int* fl, int nf) {
+// x[fl[i]] += sum over the cs CTAs' ffn_down partials (CTA order; partial
+// of CTA c for the i-th fed sequence at dp[(c dp_b + i) D]): a thread per
+// element, all cs loads issued before the additions.  All threads; ends
+// with a CTA barrier.
+__device__ __forceinline__ void cl2_add_down(const ClusterParams& cp, LcState& S, const float* dp,
+                                             const int* fl, int nf) {
     const int D = cp.lp.D, cs = cp.cs;
     const size_t cstride = (size_t)cp.dp_b * D;
     for (int e = threadIdx.x; e < nf * D; e += blockDim.x) {
-        const int b = fl[e / D], k = e % D;
-        const float* src = S.dp + (size_t)b * D + k;
+        const int i = e / D, k = e % D, b = fl[i];
+        const float* src = dp + (size_t)i * D + k;
         float v[16];
 #pragma unroll
         for (int c = 0; c < 16; c++) v[c] = c < cs ? src[c * cstride] : 0.0f;
@@ -141,13 +170,26 @@ __device__ __forceinline__ void cl2_add_down(const ClusterParams& cp, LcState& S
     __syncthreads();
 }
 
-// One layer (two phases, two cluster barriers).  pa / pb: parities of the
-// phase buffers' next copies; `first`: the residual is the embedding.
+// Thread 0: wait (bounded) for the phase `ph` of a dataflow mbarrier.  A
+// failure stops the exchange for the rest of the launch (ints[34]).
+__device__ __forceinline__ void df_wait(const LoopParams<float>& p, LcState& S, unsigned long long* bar,
+                                        unsigned ph) {
+    if (!S.ints[34] && !mbar_wait(bar, ph, p.timeout_ns)) {
+        S.ints[34] = 1;
+        lc_fail(S, p.status, ST_TIMEOUT);
+    }
+}
+
+// One layer (two phases).  pa / pb: parities of the phase buffers' next
+// copies; `first`: the residual is the embedding.  DF: partials move by
+// bulk copies onto the receivers' mbarriers and the layer ends with the
+// ffn_down partials summed; otherwise by remote stores, each phase closed
+// by a cluster barrier, and the next layer starts with that sum.
 // HD / DC / FC > 0 fix head_dim, dim and the F slice at compile time (the
 // default model's 32 / 128 / 32), so that the short loops of every phase
 // have constant trip counts; 0 = read them from the parameters.
-template <int HD, int DC, int FC>
-__device__ bool cl2_layer(const ClusterParams& cp, const CSlice& sl, LcState& S, cg::cluster_group& cl,
+template <int HD, int DC, int FC, bool DF>
+__device__ __forceinline__ bool cl2_layer(const ClusterParams& cp, const CSlice& sl, LcState& S, cg::cluster_group& cl,
                           int crank, int l, int t, const int* fl, int nf, bool first, unsigned& pa,
                           unsigned& pbp) {
     const LoopParams<float>& p = cp.lp;
@@ -155,12 +197,16 @@ __device__ bool cl2_layer(const ClusterParams& cp, const CSlice& sl, LcState& S,
     const int ghd = G * hd, rows_a = ghd + 2 * hd, fpc = FC > 0 ? FC : cp.fpc;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int nd = (hd + 31) / 32;
-    if (!first) cl2_add_down(cp, S, fl, nf);
+    if (!DF && !first) cl2_add_down(cp, S, S.dp, fl, nf);
+    const int nu = nf * K;
+    const bool unit = crank < nu;
+    // this layer's attn_proj partials: one from each unit but this CTA
+    if (DF && threadIdx.x == 0 && !S.ints[34])
+        mbar_expect_tx(S.atbar, (unsigned)(nu - (unit ? 1 : 0)) * (unsigned)(D * 4));
 
     // ------------------------------------------------ phase A: unit crank
     if (!mbar_wait(&S.bar[0], pa, p.timeout_ns)) lc_fail(S, p.status, ST_TIMEOUT);
     pa ^= 1u;
-    const bool unit = crank < nf * K;
     const int g = crank % K;
     const int b = unit ? fl[crank / K] : 0;
     const int nkeys = t + 1;
@@ -282,17 +328,33 @@ __device__ bool cl2_layer(const ClusterParams& cp, const CSlice& sl, LcState& S,
             if (c < ghd) a0 = fmaf(wp[(size_t)c * D + i], S.att[c], a0);
             S.attp[crank * D + i] = a0 + a1;
         }
+        // DF: this thread's shared-memory writes (the partial, and the K/V
+        // tile that later partials overwrite) before the async proxy's copies
+        if (DF) asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
         __syncthreads();
-        push_block(cl, S.attp, crank * D, D, cs, crank);
+        if (!DF) push_block(cl, S.attp, crank * D, D, cs, crank);
+        else if (warp == 0 && lane < cs && lane != crank && !S.ints[34])
+            bulk_s2peer(S.attp + (size_t)crank * D, (unsigned)(D * 4), S.atbar, (unsigned)lane);
     }
     // K/V rows written in this step are read by later steps' bulk copies
     // (async proxy) in other CTAs: order them before the cluster barrier
     if (wrote_kv) asm volatile("fence.proxy.async.global;" ::: "memory");
     __syncthreads();
     if (threadIdx.x == 0) cl2_issue_a(cp, S, (l + 1) % p.L, g);
-    if (!lc_sync(cl, S, cs)) return false;
+    if (DF) {
+        if (threadIdx.x == 0) df_wait(p, S, S.atbar, S.atph);
+        S.atph ^= 1u;
+        __syncthreads();
+    } else if (!lc_sync(cl, S, cs)) {
+        return false;
+    }
 
     // ------------------------------------------------ phase B: FFN slice
+    const int par = DF ? (S.nlayer & 1) : 0;
+    float* dpb = S.dp + (size_t)par * cs * cp.dp_b * D;
+    // this layer's ffn_down partials: one from every other CTA
+    if (DF && threadIdx.x == 0 && !S.ints[34])
+        mbar_expect_tx(&S.dpbar[par], (unsigned)((cs - 1) * nf * D * 4));
     for (int e = threadIdx.x; e < nf * D; e += blockDim.x) {
         const int i = e / D, k = e % D;
         float s = 0.0f;
@@ -326,10 +388,10 @@ __device__ bool cl2_layer(const ClusterParams& cp, const CSlice& sl, LcState& S,
     // a thread per (output, sequence) over the block's [fpc][D] (transposed)
     // columns; the SwiGLU values are broadcast reads
     const int nfr = sl.f1 - sl.f0;
-    float* mine = S.dp + (size_t)crank * cp.dp_b * D;
+    float* mine = dpb + (size_t)crank * cp.dp_b * D;
     for (int e = threadIdx.x; e < D * nf; e += blockDim.x) {
-        const int i = e % D, b = fl[e / D];
-        const float* fr = S.f + b * fpc;
+        const int i = e % D, s = e / D;
+        const float* fr = S.f + fl[s] * fpc;
         float a0 = 0.0f, a1 = 0.0f;
         int j = 0;
         for (; j + 1 < nfr; j += 2) {
@@ -337,30 +399,60 @@ __device__ bool cl2_layer(const ClusterParams& cp, const CSlice& sl, LcState& S,
             a1 = fmaf(wd[(size_t)(j + 1) * D + i], fr[j + 1], a1);
         }
         if (j < nfr) a0 = fmaf(wd[(size_t)j * D + i], fr[j], a0);
-        mine[b * D + i] = a0 + a1;
+        mine[s * D + i] = a0 + a1;
     }
+    if (DF) asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
     __syncthreads();
-    {
+    if (DF) {
+        if (warp == 0 && lane < cs && lane != crank && !S.ints[34])
+            bulk_s2peer(mine, (unsigned)(nf * D * 4), &S.dpbar[par], (unsigned)lane);
+    } else {
         const int n4 = D >> 2, per_rank = nf * n4;
         for (int e = threadIdx.x; e < per_rank * cs; e += blockDim.x) {
             const int r = e / per_rank;
             if (r == crank) continue;
-            const int w = e - r * per_rank, i = w / n4, c = w - i * n4;
-            const int off = fl[i] * D + 4 * c;
+            const int off = 4 * (e - r * per_rank);
             const float4 v = *reinterpret_cast<const float4*>(mine + off);
             *reinterpret_cast<float4*>(cl.map_shared_rank(mine, r) + off) = v;
         }
+        __syncthreads();
     }
-    __syncthreads();
     if (threadIdx.x == 0) cl2_issue_b(cp, sl, S, (l + 1) % p.L, crank);
-    return lc_sync(cl, S, cs);
+    if (!DF) return lc_sync(cl, S, cs);
+    if (threadIdx.x == 0) df_wait(p, S, &S.dpbar[par], (S.dpph >> par) & 1u);
+    S.dpph ^= 1u << par;
+    S.nlayer++;
+    __syncthreads();
+    cl2_add_down(cp, S, dpb, fl, nf);
+    return true;
 }
 
+// Layer l through the specialisation for this model's dims.
+template <bool DF>
+__device__ __forceinline__ bool cl2_layer_any(const ClusterParams& cp, const CSlice& sl, LcState& S,
+                                              cg::cluster_group& cl, int crank, int l, int t, const int* fl,
+                                              int nf, unsigned& pa, unsigned& pbp) {
+    const LoopParams<float>& p = cp.lp;
+    const bool first = l == 0;
+    if (p.hd == 32 && p.D == 128 && cp.fpc == 32)    // the default model (config.h)
+        return cl2_layer<32, 128, 32, DF>(cp, sl, S, cl, crank, l, t, fl, nf, first, pa, pbp);
+    switch (p.hd) {
+    case 16: return cl2_layer<16, 0, 0, DF>(cp, sl, S, cl, crank, l, t, fl, nf, first, pa, pbp);
+    case 32: return cl2_layer<32, 0, 0, DF>(cp, sl, S, cl, crank, l, t, fl, nf, first, pa, pbp);
+    case 64: return cl2_layer<64, 0, 0, DF>(cp, sl, S, cl, crank, l, t, fl, nf, first, pa, pbp);
+    default: return cl2_layer<0, 0, 0, DF>(cp, sl, S, cl, crank, l, t, fl, nf, first, pa, pbp);
+    }
+}
+
+template <bool DF>
 __device__ void cl2_main(const ClusterParams& cp, unsigned char* smem, cg::cluster_group& cl, int crank) {
     const LoopParams<float>& p = cp.lp;
     LcState S;
     S.bar = reinterpret_cast<unsigned long long*>(smem);   // [0] phase A, [1] phase B
     S.kvbar = S.bar + 2;
+    S.atbar = S.bar + 3;
+    S.dpbar = S.bar + 4;                                   // [2]
+    constexpr bool df = DF;
     S.ints = reinterpret_cast<int*>(smem + 64);
     S.red = reinterpret_cast<float*>(smem + 64 + 64 * 4);
     S.x = reinterpret_cast<float*>(smem + cp.off_x);
@@ -389,12 +481,19 @@ __device__ void cl2_main(const ClusterParams& cp, unsigned char* smem, cg::clust
         mbar_init(&S.bar[0], 1);
         mbar_init(&S.bar[1], 1);
         mbar_init(S.kvbar, 1);
+        mbar_init(S.atbar, 1);
+        mbar_init(&S.dpbar[0], 1);
+        mbar_init(&S.dpbar[1], 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        S.ints[34] = 0;
         S.ints[38] = 0;
         S.ints[39] = 0;
     }
     S.kvph = 0u;
     S.kvpend = 0;
+    S.atph = 0u;
+    S.dpph = 0u;
+    S.nlayer = 0;
     for (int b = threadIdx.x; b < p.B; b += blockDim.x) {
         const SeqState& g = p.seq[b];
         SeqMirror& m = S.seq[b];
@@ -473,21 +572,17 @@ __device__ void cl2_main(const ClusterParams& cp, unsigned char* smem, cg::clust
             S.x[fl[i] * p.D + k] = __ldg(p.tok_emb + (size_t)toks[i] * p.D + k);
         }
         __syncthreads();
-        for (int l = 0; ok && l < p.L; l++) {
-            if (p.hd == 32 && p.D == 128 && cp.fpc == 32) {    // the default model (config.h)
-                ok = cl2_layer<32, 128, 32>(cp, sl, S, cl, crank, l, t, fl, nf, l == 0, pa, pbp);
-            } else {
-                switch (p.hd) {
-                case 16: ok = cl2_layer<16, 0, 0>(cp, sl, S, cl, crank, l, t, fl, nf, l == 0, pa, pbp); break;
-                case 32: ok = cl2_layer<32, 0, 0>(cp, sl, S, cl, crank, l, t, fl, nf, l == 0, pa, pbp); break;
-                case 64: ok = cl2_layer<64, 0, 0>(cp, sl, S, cl, crank, l, t, fl, nf, l == 0, pa, pbp); break;
-                default: ok = cl2_layer<0, 0, 0>(cp, sl, S, cl, crank, l, t, fl, nf, l == 0, pa, pbp); break;
-                }
-            }
-        }
+        for (int l = 0; ok && l < p.L; l++)
+            ok = cl2_layer_any<DF>(cp, sl, S, cl, crank, l, t, fl, nf, pa, pbp);
         if (!ok) break;
-        if (nh == 0) continue;
-        cl2_add_down(cp, S, fl, nf);
+        if (nh == 0) {
+            // the dataflow layers have no cluster barrier of their own: one
+            // per step orders this step's K/V rows before later bulk reads
+            // and makes a failure cluster-wide
+            if (df) ok = lc_sync(cl, S, cp.cs);
+            continue;
+        }
+        if (!df) cl2_add_down(cp, S, S.dp, fl, nf);
 
         // ---- hand the final norm to the head CTAs (generate.c:187-191)
         lc_norm(S.x, S.xn, S.rmsf, hl, nh, p.D, S.red);
@@ -563,18 +658,32 @@ __device__ void cl2_main(const ClusterParams& cp, unsigned char* smem, cg::clust
         atomicMax(p.status, (int)ST_TIMEOUT);
     __syncthreads();
     cl.sync();   // no CTA leaves while others may still write its shared memory
+    if (df && !ok) {
+        // after a failed dataflow wait, copies already issued to a CTA that
+        // stopped waiting may still be in flight: let them land first
+        const unsigned long long t0 = globaltimer_ns();
+        while (globaltimer_ns() - t0 < 50000ull) {
+        }
+        cl.sync();
+    }
 }
 
+// One instantiation per layer loop (V2 == cp.v2), so that each is
+// register-allocated on its own.
+template <int V2>
 __global__ void __launch_bounds__(kThreads, 1) cluster_loop_kernel(const ClusterParams cp) {
     extern __shared__ __align__(128) unsigned char smem_c[];
     cg::cluster_group cl = cg::this_cluster();
     const int cid = blockIdx.x / cp.cs;
     if (cid == 0) {
-        if (cp.v2) cl2_main(cp, smem_c, cl, (int)cl.block_rank());
-        else lc_main(cp, smem_c, cl, (int)cl.block_rank());
+        if constexpr (V2 == 0) lc_main(cp, smem_c, cl, (int)cl.block_rank());
+        else cl2_main<V2 == 2>(cp, smem_c, cl, (int)cl.block_rank());
     } else {
         hc_main(cp, smem_c, blockIdx.x - cp.cs);
     }
 }
+template __global__ void cluster_loop_kernel<0>(const ClusterParams);
+template __global__ void cluster_loop_kernel<1>(const ClusterParams);
+template __global__ void cluster_loop_kernel<2>(const ClusterParams);
 
 }  // namespace mc

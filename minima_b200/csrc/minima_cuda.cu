@@ -217,6 +217,12 @@ void fill_params(mc::LoopParams<WT>& p, const mc_session* s) {
     p.bc = s->bc; p.xs_ld = s->xs_ld;
 }
 
+// The cluster loop's instantiation for a plan's layer loop (ClusterParams::v2).
+using ClusterKernel = void (*)(const mc::ClusterParams);
+ClusterKernel cluster_kernel(int v2) {
+    return v2 == 2 ? mc::cluster_loop_kernel<2> : v2 == 1 ? mc::cluster_loop_kernel<1> : mc::cluster_loop_kernel<0>;
+}
+
 cudaError_t launch_cluster(const mc::ClusterParams& cp, int cs, int nc, size_t smem,
                            cudaStream_t st, bool cooperative) {
     cudaLaunchConfig_t cfg = {};
@@ -233,7 +239,7 @@ cudaError_t launch_cluster(const mc::ClusterParams& cp, int cs, int nc, size_t s
     attr[1].val.cooperative = 1;
     cfg.attrs = attr;
     cfg.numAttrs = cooperative ? 2 : 1;
-    return cudaLaunchKernelEx(&cfg, mc::cluster_loop_kernel, cp);
+    return cudaLaunchKernelEx(&cfg, cluster_kernel(cp.v2), cp);
 }
 
 // Plan of the cluster-resident loop (mc_cluster_loop.cuh, and its
@@ -241,9 +247,10 @@ cudaError_t launch_cluster(const mc::ClusterParams& cp, int cs, int nc, size_t s
 // device: shared-memory offsets, cluster size and count such that every
 // cluster is co-resident.  The two-phase loop is chosen when every
 // (sequence, KV head) pair of the session's batch gets a CTA of the layer
-// cluster and its buffers fit (MINIMA_CUDA_LOOP=cluster1 keeps the
-// five-phase loop).  Returns false when neither applies; the grid-barrier
-// loop then serves every call.
+// cluster and its buffers fit, with its dataflow exchange when the two
+// buffers of ffn_down partials fit too (MINIMA_CUDA_LOOP=cluster2 keeps
+// the cluster barriers, cluster1 the five-phase loop).  Returns false when
+// none applies; the grid-barrier loop then serves every call.
 bool plan_cluster(mc_session* s, const cudaDeviceProp& prop) {
     const mc_model* m = s->m;
     if (m->dtype != MC_WEIGHTS_F32) return false;
@@ -254,18 +261,19 @@ bool plan_cluster(mc_session* s, const cudaDeviceProp& prop) {
         return false;
     const char* env = getenv("MINIMA_CUDA_LOOP");
     if (env && strcmp(env, "grid") == 0) return false;
-    const bool allow_v2 = !(env && strcmp(env, "cluster1") == 0);
+    const int max_v2 = env && strcmp(env, "cluster1") == 0 ? 0 : env && strcmp(env, "cluster2") == 0 ? 1 : 2;
     const size_t optin = prop.sharedMemPerBlockOptin;
-    if (cudaFuncSetAttribute(mc::cluster_loop_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)optin) != cudaSuccess ||
-        cudaFuncSetAttribute(mc::cluster_loop_kernel,
-                             cudaFuncAttributeNonPortableClusterSizeAllowed, 1) != cudaSuccess) {
-        cudaGetLastError();
-        return false;
-    }
+    for (int v = 0; v <= 2; v++)
+        if (cudaFuncSetAttribute(cluster_kernel(v), cudaFuncAttributeMaxDynamicSharedMemorySize, (int)optin) !=
+                cudaSuccess ||
+            cudaFuncSetAttribute(cluster_kernel(v), cudaFuncAttributeNonPortableClusterSizeAllowed, 1) !=
+                cudaSuccess) {
+            cudaGetLastError();
+            return false;
+        }
     const int B8 = std::min(s->Bcap, mc::kBCMax);    // activation rows held per CTA
     const int hd = m->hd, ghd = G * hd, D = m->D, F = m->F;
-    for (int v2 = allow_v2 ? 1 : 0; v2 >= 0; v2--) {
+    for (int v2 = max_v2; v2 >= 0; v2--) {
         for (int cs : {16, 8}) {
             if (v2 && B8 * m->K > cs) continue;
             mc::ClusterParams cp{};
@@ -299,7 +307,11 @@ bool plan_cluster(mc_session* s, const cudaDeviceProp& prop) {
                 cp.off_sc = take(sc_f, 16);
                 cp.off_stage = take(stage_f, 128);
                 cp.off_wb = take(wb_f, 128);
-                union_min = (size_t)cs * B8 * D;          // ffn_down partials
+                // ffn_down partials (two buffers for the dataflow exchange,
+                // whose per-phase byte count must stay well inside the
+                // mbarrier's tx-count range)
+                union_min = (size_t)(v2 == 2 ? 2 : 1) * cs * B8 * D;
+                if (v2 == 2 && (size_t)(cs - 1) * B8 * D * 4 * 2 >= (1u << 20)) continue;
             } else {
                 const mc::CSlice s0 = mc::cluster_slice(0, cs, m->Q, D, F);
                 // weight slice plus this layer's rms1 / rms2 scales
@@ -356,7 +368,7 @@ bool plan_cluster(mc_session* s, const cudaDeviceProp& prop) {
                 cfg.attrs = attr;
                 cfg.numAttrs = 1;
                 int maxc = 0;
-                if (cudaOccupancyMaxActiveClusters(&maxc, (void*)mc::cluster_loop_kernel, &cfg) != cudaSuccess) {
+                if (cudaOccupancyMaxActiveClusters(&maxc, (void*)cluster_kernel(v2), &cfg) != cudaSuccess) {
                     cudaGetLastError();
                     break;
                 }
@@ -1960,6 +1972,12 @@ mc_status mc_last_step_times(mc_session* s, unsigned long long* ns, int cap, int
 const char* mc_last_kernel_name(mc_session* s) {
     if (!s || s->last_launches == 0) return "";
     return s->last_path == 2 ? "mc::tc_gemm_kernel" : s->last_path == 1 ? "mc::cluster_loop_kernel" : "mc::token_loop_kernel";
+}
+
+mc_status mc_session_cluster_variant(mc_session* s, int* variant) {
+    if (!s || !variant) return fail(MC_ERR_INVALID, "null argument");
+    *variant = s->cl_ok ? s->cl_plan.v2 : -1;
+    return MC_OK;
 }
 
 mc_status mc_session_stream(mc_session* s, void** stream) {

@@ -105,6 +105,7 @@ def test_cluster_loop_logits_at_bench_config(gpu, monkeypatch, cfg):
     out, counts, st, fpos, trace = sess.generate(prompts, [P] * B, 512, M.options(top_k=1, max_new_tokens=N),
                                                  rng, trace_steps=steps)
     assert sess.last_kernel_name() == "mc::cluster_loop_kernel"
+    assert sess.cluster_variant() == 2               # two-phase layers, dataflow exchange
     refs = oracle_runs(orc, prompts, [P] * B, 512, dict(top_k=1, max_new_tokens=N), rng, steps)
     worst, agree, mm = compare(out, counts, trace, refs, [P] * B, steps, ATOL, RTOL, 64)
     print(f"{cfg}: worst err/bound {worst:.3f}, ids agree {agree} of {N}, "

@@ -19,9 +19,9 @@ pytestmark = pytest.mark.gpu
 DIMS = O.Dims(4096, 128, 2, 4, 512, 128)
 
 
-@pytest.mark.parametrize("loop", ["grid", "cluster", "cluster1"])
+@pytest.mark.parametrize("loop", ["grid", "cluster", "cluster2", "cluster1"])
 def test_wait_deadline_reports_timeout_and_recovers(gpu, loop, monkeypatch):
-    if loop in ("grid", "cluster1"):
+    if loop in ("grid", "cluster1", "cluster2"):
         monkeypatch.setenv("MINIMA_CUDA_LOOP", loop)
     else:
         monkeypatch.delenv("MINIMA_CUDA_LOOP", raising=False)
@@ -44,3 +44,4 @@ def test_wait_deadline_reports_timeout_and_recovers(gpu, loop, monkeypatch):
         assert np.array_equal(out[b, :counts[b]], ref)
     expected = "mc::token_loop_kernel" if loop == "grid" else "mc::cluster_loop_kernel"
     assert sess.last_kernel_name() == expected
+    assert sess.cluster_variant() == {"cluster": 2, "cluster2": 1, "cluster1": 0, "grid": -1}[loop]

@@ -55,12 +55,12 @@ def check(out, counts, trace, orc, prompts, lens, cap, kw, rng, steps, atol, rto
     return worst
 
 
-@pytest.mark.parametrize("loop,page_len", [("cluster", 64), ("cluster1", 64), ("grid", 64),
-                                           ("grid", 128), ("tcgen05", 64)])
+@pytest.mark.parametrize("loop,page_len", [("cluster", 64), ("cluster2", 64), ("cluster1", 64),
+                                           ("grid", 64), ("grid", 128), ("tcgen05", 64)])
 def test_paged_sessions_match_oracle(gpu, monkeypatch, loop, page_len):
     monkeypatch.delenv("MINIMA_CUDA_LOOP", raising=False)
     monkeypatch.delenv("MINIMA_CUDA_DECODE", raising=False)
-    if loop in ("grid", "cluster1"):
+    if loop in ("grid", "cluster1", "cluster2"):
         monkeypatch.setenv("MINIMA_CUDA_LOOP", loop)
     if loop == "tcgen05":
         monkeypatch.setenv("MINIMA_CUDA_DECODE", "tcgen05")
@@ -78,8 +78,9 @@ def test_paged_sessions_match_oracle(gpu, monkeypatch, loop, page_len):
     for _ in range(2):                            # the pool is reused call after call
         out, counts, st, fpos, trace = sess.generate(prompts, lens, cap, M.options(**kw), rng,
                                                      trace_steps=new)
-    expected = {"cluster": "mc::cluster_loop_kernel", "cluster1": "mc::cluster_loop_kernel",
-                "grid": "mc::token_loop_kernel", "tcgen05": "mc::tc_gemm_kernel"}[loop]
+    expected = {"cluster": "mc::cluster_loop_kernel", "cluster2": "mc::cluster_loop_kernel",
+                "cluster1": "mc::cluster_loop_kernel", "grid": "mc::token_loop_kernel",
+                "tcgen05": "mc::tc_gemm_kernel"}[loop]
     assert sess.last_kernel_name() == expected
     atol, rtol = (1e-2, 1e-2) if loop == "tcgen05" else (1e-3, 1e-4)
     worst = check(out, counts, trace, orc, prompts, lens, cap, kw, rng, new, atol, rtol,

@@ -100,13 +100,14 @@ def test_c2_batch_greedy(gpu):
     assert [c.pos for c in caches.caches] == [384] * B
 
 
-@pytest.mark.parametrize("loop", ["cluster", "cluster1", "grid"])
+@pytest.mark.parametrize("loop", ["cluster", "cluster2", "cluster1", "grid"])
 def test_c2_shape_both_loops(gpu, loop, monkeypatch):
     """The config-2 shape (4 x prompt 128, greedy) on the cluster-resident loop
-    (its two-phase layer loop, and the five-phase one with
-    MINIMA_CUDA_LOOP=cluster1) and on the grid-barrier loop: same ids as the
-    oracle, and each session reports the loop it ran."""
-    if loop in ("grid", "cluster1"):
+    (its two-phase layer loop with the dataflow exchange, the same loop with
+    cluster barriers under MINIMA_CUDA_LOOP=cluster2, and the five-phase one
+    with MINIMA_CUDA_LOOP=cluster1) and on the grid-barrier loop: same ids as
+    the oracle, and each session reports the loop it ran."""
+    if loop in ("grid", "cluster1", "cluster2"):
         monkeypatch.setenv("MINIMA_CUDA_LOOP", loop)
     else:
         monkeypatch.delenv("MINIMA_CUDA_LOOP", raising=False)
@@ -119,6 +120,7 @@ def test_c2_shape_both_loops(gpu, loop, monkeypatch):
     out, counts, st, fpos = sess.generate(prompts, [128] * B, 512, opts, [5, 6, 7, 8])
     assert sess.last_kernel_name() == ("mc::token_loop_kernel" if loop == "grid"
                                        else "mc::cluster_loop_kernel")
+    assert sess.cluster_variant() == {"cluster": 2, "cluster2": 1, "cluster1": 0, "grid": -1}[loop]
     ok, outr, countsr, str_ = orc.generate_batch(
         prompts, [128] * B, 512, 512, O.make_options(top_k=1, max_new_tokens=96,
                                                       repetition_penalty=1.05), [5, 6, 7, 8])
