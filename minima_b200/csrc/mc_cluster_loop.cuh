@@ -80,7 +80,7 @@ struct ClusterParams {
     int n_clusters;
     // layer-cluster shared-memory plan (byte offsets)
     unsigned off_x, off_xn, off_qkv, off_att, off_attp, off_f, off_sc, off_kv, off_stage;
-    unsigned off_rmsf, off_rope, off_pages;
+    unsigned off_rope, off_pages;
     unsigned stage_floats;      // floats per weight stage (slice + rms1 + rms2)
     int kv_tile;                // keys staged per attention tile
     // head clusters
@@ -178,7 +178,6 @@ struct LcState {
     float* stage;  // [kStages][stage_floats] (two-phase loop: the phase A buffer)
     float* wb;     // two-phase loop: the phase B weight buffer
     float* dp;     // two-phase loop: ffn_down partials [cs][kBCMax][D] (shares kv's bytes)
-    float* rmsf;   // [D] final RMSNorm scale
     float2* rope;  // [hd/2] (cos, sin) at the current position
     unsigned long long* bar;  // [kStages]
     unsigned long long* kvbar;  // K/V tile copies
@@ -781,6 +780,24 @@ __device__ bool lc_layer(const ClusterParams& cp, const CSlice& sl, LcState& S,
 // bookkeeping (generate.c:560-595): history, penalty counts, stop sequence,
 // length.  One warp; lane 0 updates the mirrored table entry m and leaves
 // done / generated in ints[40 + slot] / ints[48 + slot].
+// Layer CTA 0: the residual rows of the sequences in hl (nh of them) and
+// each sequence's sampler step (-1 = no logits this phase) for the head
+// CTAs; ends with a CTA barrier (the caller's release of `go` follows).
+__device__ __forceinline__ void lc_publish_rows(const ClusterParams& cp, const LcState& S, const int* hl, int nh) {
+    const LoopParams<float>& p = cp.lp;
+    for (int e = threadIdx.x; e < nh * p.D; e += blockDim.x) {
+        const int b = hl[e / p.D], k = e % p.D;
+        cp.xfin[(size_t)b * p.D + k] = S.x[b * p.D + k];
+    }
+    for (int b = threadIdx.x; b < p.B; b += blockDim.x) {
+        int g = -1;
+        for (int i = 0; i < nh; i++)
+            if (hl[i] == b) g = S.seq[b].gen;
+        cp.hgen[b] = g;
+    }
+    __syncthreads();
+}
+
 __device__ void lc_choose(const ClusterParams& cp, SeqMirror& m, int b, int nhc, int slot, int* ints) {
     const LoopParams<float>& p = cp.lp;
     const int lane = threadIdx.x & 31;
@@ -854,7 +871,6 @@ __device__ void lc_main(const ClusterParams& cp, unsigned char* smem, cg::cluste
     S.sc = reinterpret_cast<float*>(smem + cp.off_sc);
     S.kv = reinterpret_cast<float*>(smem + cp.off_kv);
     S.stage = reinterpret_cast<float*>(smem + cp.off_stage);
-    S.rmsf = reinterpret_cast<float*>(smem + cp.off_rmsf);
     S.rope = reinterpret_cast<float2*>(smem + cp.off_rope);
     S.pages = reinterpret_cast<int*>(smem + cp.off_pages);
     S.seq = reinterpret_cast<SeqMirror*>(smem + 576);
@@ -881,7 +897,6 @@ __device__ void lc_main(const ClusterParams& cp, unsigned char* smem, cg::cluste
         m.P = g.P; m.nnew = g.nnew; m.gen = g.gen; m.done = g.done; m.tok = g.tok;
         m.result = g.result; m.final_pos = g.final_pos; m.rng = g.rng;
     }
-    for (int k = threadIdx.x; k < p.D; k += blockDim.x) S.rmsf[k] = __ldg(p.rmsf + k);
     __syncthreads();
     // prologue: prompts into the history, penalty counts, first bans (CTA b)
     for (int b = crank; b < p.B; b += cp.cs) {
@@ -968,29 +983,14 @@ __device__ void lc_main(const ClusterParams& cp, unsigned char* smem, cg::cluste
         if (!ok) break;
         if (nh == 0) continue;
 
-        // ---- hand the final norm to the head CTAs (generate.c:187-191)
-        lc_norm(S.x, S.xn, S.rmsf, hl, nh, p.D, S.red);
-        {
-            const int cols = (p.D + cp.cs - 1) / cp.cs, c0 = crank * cols, c1 = min(p.D, c0 + cols);
-            for (int e = threadIdx.x; e < nh * (c1 - c0); e += blockDim.x) {
-                const int b = hl[e / (c1 - c0)], k = c0 + e % (c1 - c0);
-                cp.xfin[(size_t)b * p.D + k] = S.xn[b * p.D + k];
-            }
-            if (crank == 0)
-                for (int b = threadIdx.x; b < p.B; b += blockDim.x) {
-                    int g = -1;
-                    for (int i = 0; i < nh; i++)
-                        if (hl[i] == b) g = S.seq[b].gen;
-                    cp.hgen[b] = g;
-                }
-        }
-        __threadfence();
-        ok = lc_sync(cl, S, cp.cs);
-        if (!ok) break;
         heads++;
         if (crank == 0) {
-            // ---- release the head CTAs, wait for all of them, choose the next ids
+            // ---- hand the sampling sequences' residual rows to the head CTAs
+            // (which apply the final rmsnorm, generate.c:187-191), release
+            // them, wait for all of them, choose the next ids
+            lc_publish_rows(cp, S, hl, nh);
             if (threadIdx.x == 0) {
+                __threadfence();
                 st_release_u32(cp.go, heads);
                 const unsigned target = heads * ((unsigned)nhc + p.extra_arrivals);
                 const unsigned long long t0 = globaltimer_ns();
@@ -1017,7 +1017,7 @@ __device__ void lc_main(const ClusterParams& cp, unsigned char* smem, cg::cluste
                 int* dst = reinterpret_cast<int*>(cl.map_shared_rank(S.seq, r));
                 dst[w] = reinterpret_cast<const int*>(S.seq)[w];
             }
-            __threadfence();
+            // (the cluster barrier's release / acquire orders these stores)
         }
         ok = lc_sync(cl, S, cp.cs);
     }
@@ -1193,6 +1193,20 @@ __device__ void hc_main(const ClusterParams& cp, unsigned char* smem, int hc) {
             for (int b = 0; b < p.B; b++)
                 if (hg[b] >= 0) ints[8 + nh++] = b;
             ints[1] = nh;
+        }
+        // the final rmsnorm of each sampling sequence (generate.c:187-189),
+        // in place: warp b normalises row b (B <= kBCMax <= kWarps)
+        static_assert(kBCMax <= kWarps, "a warp per sequence");
+        {
+            const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+            if (w < p.B && hg[w] >= 0) {
+                float* xr = xs + w * D;
+                float ss = 0.0f;
+                for (int k = lane; k < D; k += 32) ss += xr[k] * xr[k];
+                ss = warp_sum(ss);
+                const float inv = 1.0f / sqrtf(ss / (float)D + 1e-5f);
+                for (int k = lane; k < D; k += 32) xr[k] = xr[k] * inv * __ldg(p.rmsf + k);
+            }
         }
         __syncthreads();
         const int nh = ints[1];

@@ -17,8 +17,11 @@
 //     residual (KV head order), normalises (rms2), computes its slice of
 //     up/gate rows and the SwiGLU product, and multiplies that slice by its
 //     columns of ffn_down: a D-long partial per sequence, pushed to every
-//     CTA.  The next layer (or the final norm) starts by adding the cs
-//     partials in CTA order.
+//     CTA.  The next layer (or the hand-off to the head CTAs, which apply
+//     the final norm) starts by adding the cs partials in CTA order.
+// At D = 128 the RMSNorms of both phases run in the registers of each warp
+// that computes rows (lane j: elements 4j .. 4j + 3), without a phase of
+// their own.
 //
 // Every CTA therefore keeps the whole residual stream of every sequence,
 // updated by the same additions in the same order (identical everywhere).
@@ -53,9 +56,9 @@
 // Arrivals may precede the receiver's expect_tx (tx-count goes negative in
 // between, as the mbarrier allows); the chains above keep every phase
 // complete before bytes of the next one of the same barrier are sent.  The
-// step's own cluster barrier (the head hand-off, or one added when no
-// sequence samples) keeps ordering the K/V rows written in the step before
-// later steps' bulk reads and makes failures cluster-wide.  After a failed
+// step's own cluster barrier (after CTA 0 broadcasts the sampled ids, or
+// one added when no sequence samples) keeps ordering the K/V rows written in
+// the step before later steps' bulk reads and makes failures cluster-wide.  After a failed
 // wait a CTA stops arming, waiting and sending for the rest of the launch
 // (its peers' waits then expire too) and every CTA leaves at that step's
 // barrier; a launch that failed this way lets in-flight copies land before
@@ -148,6 +151,63 @@ __device__ __forceinline__ float cl2_dot32(const float* rows, int ld, int r0, in
     return transpose_reduce32(acc);
 }
 
+// RMSNorm (generate.c:57-63) of one D = 128 row, in registers: lane j of
+// the calling warp returns elements 4j .. 4j + 3 of x * inv_rms * scale.
+__device__ __forceinline__ float4 cl2_norm128(const float* x, const float* scale) {
+    const int lane = threadIdx.x & 31;
+    const float4 v = *reinterpret_cast<const float4*>(x + 4 * lane);
+    float ss = v.x * v.x;
+    ss += v.y * v.y;
+    ss += v.z * v.z;
+    ss += v.w * v.w;
+    ss = warp_sum(ss);
+    const float inv = 1.0f / sqrtf(ss / 128.0f + 1e-5f);
+    const float4 sc = *reinterpret_cast<const float4*>(scale + 4 * lane);
+    return make_float4(v.x * inv * sc.x, v.y * inv * sc.y, v.z * inv * sc.z, v.w * inv * sc.w);
+}
+
+// cl2_dot32 for rows of length 128 against a vector held in registers as
+// cl2_norm128 returns it.
+__device__ __forceinline__ float cl2_dot32_r(const float* rows, int ld, int r0, int nrows, float4 x) {
+    const int lane = threadIdx.x & 31;
+    float acc[32];
+#pragma unroll
+    for (int j = 0; j < 32; j++) {
+        acc[j] = 0.0f;
+        if (r0 + j < nrows) {
+            const float4 w = *reinterpret_cast<const float4*>(rows + (size_t)(r0 + j) * ld + 4 * lane);
+            acc[j] = w.x * x.x + w.y * x.y + w.z * x.z + w.w * x.w;
+        }
+    }
+    return transpose_reduce32(acc);
+}
+
+// lc_gemv4 for rows of length 128 against the normalised rows of up to
+// kBCMax sequences held in registers (xr[i]: sequence list[i], as
+// cl2_norm128 returns it); lane l returns row (l >> 3) . xr[l & 7].
+__device__ __forceinline__ float cl2_gemv4_r(const float* r0, const float* r1, const float* r2,
+                                             const float* r3, const float4 (&xr)[kBCMax], int n) {
+    const int k = 4 * (threadIdx.x & 31);
+    const float4 w0 = *reinterpret_cast<const float4*>(r0 + k);
+    const float4 w1 = *reinterpret_cast<const float4*>(r1 + k);
+    const float4 w2 = *reinterpret_cast<const float4*>(r2 + k);
+    const float4 w3 = *reinterpret_cast<const float4*>(r3 + k);
+    float acc[32];
+#pragma unroll
+    for (int i = 0; i < 32; i++) acc[i] = 0.0f;
+#pragma unroll
+    for (int i = 0; i < kBCMax; i++) {
+        if (i < n) {
+            const float4 x = xr[i];
+            acc[0 * 8 + i] = w0.x * x.x + w0.y * x.y + w0.z * x.z + w0.w * x.w;
+            acc[1 * 8 + i] = w1.x * x.x + w1.y * x.y + w1.z * x.z + w1.w * x.w;
+            acc[2 * 8 + i] = w2.x * x.x + w2.y * x.y + w2.z * x.z + w2.w * x.w;
+            acc[3 * 8 + i] = w3.x * x.x + w3.y * x.y + w3.z * x.z + w3.w * x.w;
+        }
+    }
+    return transpose_reduce32(acc);
+}
+
 // x[fl[i]] += sum over the cs CTAs' ffn_down partials (CTA order; partial
 // of CTA c for the i-th fed sequence at dp[(c dp_b + i) D]): a thread per
 // element, all cs loads issued before the additions.  All threads; ends
@@ -185,15 +245,16 @@ __device__ __forceinline__ void df_wait(const LoopParams<float>& p, LcState& S, 
 // bulk copies onto the receivers' mbarriers and the layer ends with the
 // ffn_down partials summed; otherwise by remote stores, each phase closed
 // by a cluster barrier, and the next layer starts with that sum.
-// HD / DC / FC > 0 fix head_dim, dim and the F slice at compile time (the
-// default model's 32 / 128 / 32), so that the short loops of every phase
-// have constant trip counts; 0 = read them from the parameters.
-template <int HD, int DC, int FC, bool DF>
+// HD / DC / FC / GC > 0 fix head_dim, dim, the F slice and the query heads
+// per KV head at compile time (the default model's 32 / 128 / 32 / 2), so
+// that the short loops of every phase have constant trip counts and their
+// loads issue ahead of the arithmetic; 0 = read them from the parameters.
+template <int HD, int DC, int FC, int GC, bool DF>
 __device__ __forceinline__ bool cl2_layer(const ClusterParams& cp, const CSlice& sl, LcState& S, cg::cluster_group& cl,
                           int crank, int l, int t, const int* fl, int nf, bool first, unsigned& pa,
                           unsigned& pbp) {
     const LoopParams<float>& p = cp.lp;
-    const int D = DC > 0 ? DC : p.D, K = p.K, G = p.G, hd = HD > 0 ? HD : p.hd, cs = cp.cs;
+    const int D = DC > 0 ? DC : p.D, K = p.K, G = GC > 0 ? GC : p.G, hd = HD > 0 ? HD : p.hd, cs = cp.cs;
     const int ghd = G * hd, rows_a = ghd + 2 * hd, fpc = FC > 0 ? FC : cp.fpc;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int nd = (hd + 31) / 32;
@@ -211,26 +272,41 @@ __device__ __forceinline__ bool cl2_layer(const ClusterParams& cp, const CSlice&
     const int b = unit ? fl[crank / K] : 0;
     const int nkeys = t + 1;
     bool wrote_kv = false;
+    // DF: this layer's FFN weights are requested here, behind the first K/V
+    // tile, which the unit phase waits on first (the barrier variant
+    // requests them at the end of the previous layer)
+    if (DF && !unit && threadIdx.x == kTileThread) cl2_issue_b(cp, sl, S, l, crank);
     if (unit) {
         // the first K/V tile is requested by the last warp (warp 0 normalises)
-        if (threadIdx.x == kTileThread) att_issue_tile(cp, S, l, b, g, 0, min(cp.kv_tile, nkeys), t, hd);
+        if (threadIdx.x == kTileThread) {
+            att_issue_tile(cp, S, l, b, g, 0, min(cp.kv_tile, nkeys), t, hd);
+            if (DF) cl2_issue_b(cp, sl, S, l, crank);
+        }
         const float* wa = S.stage;
         const float* rms1 = wa + (size_t)(rows_a + ghd) * D;
-        // rmsnorm of sequence b (generate.c:57-63): one warp sums, the CTA scales
-        if (warp == 0) {
-            float ss = 0.0f;
-            for (int k = lane; k < D; k += 32) ss += S.x[b * D + k] * S.x[b * D + k];
-            ss = warp_sum(ss);
-            if (lane == 0) S.red[0] = 1.0f / sqrtf(ss / (float)D + 1e-5f);
-        }
-        __syncthreads();
-        const float inv = S.red[0];
+        // rmsnorm of sequence b (generate.c:57-63): at D = 128 each warp that
+        // computes rows normalises in registers; otherwise one warp sums and
+        // the CTA scales
+        float4 xn4 = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
         float* xn = S.xn + b * D;
-        for (int k = threadIdx.x; k < D; k += blockDim.x) xn[k] = S.x[b * D + k] * inv * rms1[k];
-        __syncthreads();
+        if constexpr (DC == 128) {
+            if (32 * warp < rows_a) xn4 = cl2_norm128(S.x + b * D, rms1);
+        } else {
+            if (warp == 0) {
+                float ss = 0.0f;
+                for (int k = lane; k < D; k += 32) ss += S.x[b * D + k] * S.x[b * D + k];
+                ss = warp_sum(ss);
+                if (lane == 0) S.red[0] = 1.0f / sqrtf(ss / (float)D + 1e-5f);
+            }
+            __syncthreads();
+            const float inv = S.red[0];
+            for (int k = threadIdx.x; k < D; k += blockDim.x) xn[k] = S.x[b * D + k] * inv * rms1[k];
+            __syncthreads();
+        }
         // Q rows of the G heads, K and V rows of KV head g (generate.c:99-119)
         for (int r0 = 32 * warp; r0 < rows_a; r0 += 32 * kWarps) {
-            const float val = cl2_dot32(wa, D, r0, rows_a, D, xn);
+            const float val =
+                DC == 128 ? cl2_dot32_r(wa, D, r0, rows_a, xn4) : cl2_dot32(wa, D, r0, rows_a, D, xn);
             const float other = __shfl_xor_sync(0xffffffffu, val, 1);    // RoPE partner (2p <-> 2p+1)
             const int r = r0 + lane;
             if (r < rows_a) {
@@ -321,6 +397,7 @@ __device__ __forceinline__ bool cl2_layer(const ClusterParams& cp, const CSlice&
         for (int i = threadIdx.x; i < D; i += blockDim.x) {
             float a0 = 0.0f, a1 = 0.0f;
             int c = 0;
+#pragma unroll
             for (; c + 1 < ghd; c += 2) {
                 a0 = fmaf(wp[(size_t)c * D + i], S.att[c], a0);
                 a1 = fmaf(wp[(size_t)(c + 1) * D + i], S.att[c + 1], a1);
@@ -368,13 +445,25 @@ __device__ __forceinline__ bool cl2_layer(const ClusterParams& cp, const CSlice&
     const float* wg = S.wb + (size_t)fpc * D;
     const float* wd = S.wb + 2 * (size_t)fpc * D;
     const float* rms2 = wd + (size_t)D * fpc;
-    lc_norm(S.x, S.xn, rms2, fl, nf, D, S.red);
+    // rmsnorm of every fed sequence (generate.c:57-63): at D = 128 in the
+    // registers of each warp that computes rows, otherwise a warp per sequence
+    float4 xr[kBCMax];
+    if constexpr (DC == 128) {
+        if (sl.f0 + 2 * warp < sl.f1) {
+#pragma unroll
+            for (int i = 0; i < kBCMax; i++)
+                xr[i] = i < nf ? cl2_norm128(S.x + fl[i] * D, rms2) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        }
+    } else {
+        lc_norm(S.x, S.xn, rms2, fl, nf, D, S.red);
+    }
     // up/gate rows [f0, f1) and SwiGLU (generate.c:165-179)
     for (int j = sl.f0 + 2 * warp; j < sl.f1; j += 2 * kWarps) {
         // rows: up j, up j+1, gate j, gate j+1 -> the gate of lane's up row is in lane ^ 16
         const float* u0 = wu + (size_t)(j - sl.f0) * D;
         const float* g0 = wg + (size_t)(j - sl.f0) * D;
-        const float val = lc_gemv4(u0, u0 + D, g0, g0 + D, D, S.xn, D, fl, nf);
+        const float val = DC == 128 ? cl2_gemv4_r(u0, u0 + D, g0, g0 + D, xr, nf)
+                                    : lc_gemv4(u0, u0 + D, g0, g0 + D, D, S.xn, D, fl, nf);
         const float gate = __shfl_xor_sync(0xffffffffu, val, 16);
         const int i = lane & 7;
         if (lane < 16 && i < nf) {
@@ -387,18 +476,20 @@ __device__ __forceinline__ bool cl2_layer(const ClusterParams& cp, const CSlice&
     // slot of the partials
     // a thread per (output, sequence) over the block's [fpc][D] (transposed)
     // columns; the SwiGLU values are broadcast reads
-    const int nfr = sl.f1 - sl.f0;
+    // all fpc columns: past this CTA's rows the SwiGLU values and the block
+    // are zero, so the extra terms add exact zeros
     float* mine = dpb + (size_t)crank * cp.dp_b * D;
     for (int e = threadIdx.x; e < D * nf; e += blockDim.x) {
         const int i = e % D, s = e / D;
         const float* fr = S.f + fl[s] * fpc;
         float a0 = 0.0f, a1 = 0.0f;
         int j = 0;
-        for (; j + 1 < nfr; j += 2) {
+#pragma unroll
+        for (; j + 1 < fpc; j += 2) {
             a0 = fmaf(wd[(size_t)j * D + i], fr[j], a0);
             a1 = fmaf(wd[(size_t)(j + 1) * D + i], fr[j + 1], a1);
         }
-        if (j < nfr) a0 = fmaf(wd[(size_t)j * D + i], fr[j], a0);
+        if (j < fpc) a0 = fmaf(wd[(size_t)j * D + i], fr[j], a0);
         mine[s * D + i] = a0 + a1;
     }
     if (DF) asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
@@ -417,7 +508,7 @@ __device__ __forceinline__ bool cl2_layer(const ClusterParams& cp, const CSlice&
         }
         __syncthreads();
     }
-    if (threadIdx.x == 0) cl2_issue_b(cp, sl, S, (l + 1) % p.L, crank);
+    if (!DF && threadIdx.x == 0) cl2_issue_b(cp, sl, S, (l + 1) % p.L, crank);
     if (!DF) return lc_sync(cl, S, cs);
     if (threadIdx.x == 0) df_wait(p, S, &S.dpbar[par], (S.dpph >> par) & 1u);
     S.dpph ^= 1u << par;
@@ -434,13 +525,13 @@ __device__ __forceinline__ bool cl2_layer_any(const ClusterParams& cp, const CSl
                                               int nf, unsigned& pa, unsigned& pbp) {
     const LoopParams<float>& p = cp.lp;
     const bool first = l == 0;
-    if (p.hd == 32 && p.D == 128 && cp.fpc == 32)    // the default model (config.h)
-        return cl2_layer<32, 128, 32, DF>(cp, sl, S, cl, crank, l, t, fl, nf, first, pa, pbp);
+    if (p.hd == 32 && p.D == 128 && cp.fpc == 32 && p.G == 2)    // the default model (config.h)
+        return cl2_layer<32, 128, 32, 2, DF>(cp, sl, S, cl, crank, l, t, fl, nf, first, pa, pbp);
     switch (p.hd) {
-    case 16: return cl2_layer<16, 0, 0, DF>(cp, sl, S, cl, crank, l, t, fl, nf, first, pa, pbp);
-    case 32: return cl2_layer<32, 0, 0, DF>(cp, sl, S, cl, crank, l, t, fl, nf, first, pa, pbp);
-    case 64: return cl2_layer<64, 0, 0, DF>(cp, sl, S, cl, crank, l, t, fl, nf, first, pa, pbp);
-    default: return cl2_layer<0, 0, 0, DF>(cp, sl, S, cl, crank, l, t, fl, nf, first, pa, pbp);
+    case 16: return cl2_layer<16, 0, 0, 0, DF>(cp, sl, S, cl, crank, l, t, fl, nf, first, pa, pbp);
+    case 32: return cl2_layer<32, 0, 0, 0, DF>(cp, sl, S, cl, crank, l, t, fl, nf, first, pa, pbp);
+    case 64: return cl2_layer<64, 0, 0, 0, DF>(cp, sl, S, cl, crank, l, t, fl, nf, first, pa, pbp);
+    default: return cl2_layer<0, 0, 0, 0, DF>(cp, sl, S, cl, crank, l, t, fl, nf, first, pa, pbp);
     }
 }
 
@@ -466,7 +557,6 @@ __device__ void cl2_main(const ClusterParams& cp, unsigned char* smem, cg::clust
     S.dp = S.kv;                                           // shared with the K/V tile
     S.stage = reinterpret_cast<float*>(smem + cp.off_stage);
     S.wb = reinterpret_cast<float*>(smem + cp.off_wb);
-    S.rmsf = reinterpret_cast<float*>(smem + cp.off_rmsf);
     S.rope = reinterpret_cast<float2*>(smem + cp.off_rope);
     S.pages = reinterpret_cast<int*>(smem + cp.off_pages);
     S.seq = reinterpret_cast<SeqMirror*>(smem + 576);
@@ -500,7 +590,6 @@ __device__ void cl2_main(const ClusterParams& cp, unsigned char* smem, cg::clust
         m.P = g.P; m.nnew = g.nnew; m.gen = g.gen; m.done = g.done; m.tok = g.tok;
         m.result = g.result; m.final_pos = g.final_pos; m.rng = g.rng;
     }
-    for (int k = threadIdx.x; k < p.D; k += blockDim.x) S.rmsf[k] = __ldg(p.rmsf + k);
     for (int e = threadIdx.x; e < p.B * p.pg.pps; e += blockDim.x) S.pages[e] = __ldg(p.pg.table + e);
     // the SwiGLU slice is read past f1 - f0 by nobody, but keep it finite
     for (int e = threadIdx.x; e < cp.dp_b * cp.fpc; e += blockDim.x) S.f[e] = 0.0f;
@@ -528,7 +617,7 @@ __device__ void cl2_main(const ClusterParams& cp, unsigned char* smem, cg::clust
     unsigned pa = 0u, pbp = 0u;
     if (threadIdx.x == 0) {
         cl2_issue_a(cp, S, 0, crank % p.K);
-        cl2_issue_b(cp, sl, S, 0, crank);
+        if (!DF) cl2_issue_b(cp, sl, S, 0, crank);
     }
     unsigned heads = 0;
     S.epoch = 0;
@@ -584,29 +673,14 @@ __device__ void cl2_main(const ClusterParams& cp, unsigned char* smem, cg::clust
         }
         if (!df) cl2_add_down(cp, S, S.dp, fl, nf);
 
-        // ---- hand the final norm to the head CTAs (generate.c:187-191)
-        lc_norm(S.x, S.xn, S.rmsf, hl, nh, p.D, S.red);
-        {
-            const int cols = (p.D + cp.cs - 1) / cp.cs, c0 = crank * cols, c1 = min(p.D, c0 + cols);
-            for (int e = threadIdx.x; e < nh * (c1 - c0); e += blockDim.x) {
-                const int b = hl[e / (c1 - c0)], k = c0 + e % (c1 - c0);
-                cp.xfin[(size_t)b * p.D + k] = S.xn[b * p.D + k];
-            }
-            if (crank == 0)
-                for (int b = threadIdx.x; b < p.B; b += blockDim.x) {
-                    int g = -1;
-                    for (int i = 0; i < nh; i++)
-                        if (hl[i] == b) g = S.seq[b].gen;
-                    cp.hgen[b] = g;
-                }
-        }
-        __threadfence();
-        ok = lc_sync(cl, S, cp.cs);
-        if (!ok) break;
         heads++;
         if (crank == 0) {
-            // ---- release the head CTAs, wait for all of them, choose the next ids
+            // ---- hand the sampling sequences' residual rows to the head CTAs
+            // (which apply the final rmsnorm, generate.c:187-191), release
+            // them, wait for all of them, choose the next ids
+            lc_publish_rows(cp, S, hl, nh);
             if (threadIdx.x == 0) {
+                __threadfence();
                 st_release_u32(cp.go, heads);
                 const unsigned target = heads * ((unsigned)nhc + p.extra_arrivals);
                 const unsigned long long t0 = globaltimer_ns();
@@ -631,7 +705,7 @@ __device__ void cl2_main(const ClusterParams& cp, unsigned char* smem, cg::clust
                 int* dst = reinterpret_cast<int*>(cl.map_shared_rank(S.seq, r));
                 dst[w] = reinterpret_cast<const int*>(S.seq)[w];
             }
-            __threadfence();
+            // (the cluster barrier's release / acquire orders these stores)
         }
         ok = lc_sync(cl, S, cp.cs);
     }
@@ -649,10 +723,11 @@ __device__ void cl2_main(const ClusterParams& cp, unsigned char* smem, cg::clust
     }
     if (threadIdx.x == 0 && crank == 0 && p.stamps) p.stamps[p.T] = globaltimer_ns();
     // one copy per phase buffer is always in flight (issued for the next
-    // layer), and possibly a K/V tile after a failed wait
+    // layer; DF: only the unit phase's, the FFN weights being requested in
+    // their own layer), and possibly a K/V tile after a failed wait
     if (threadIdx.x == 0) {
         if (!mbar_wait(&S.bar[0], pa, p.timeout_ns)) atomicMax(p.status, (int)ST_TIMEOUT);
-        if (!mbar_wait(&S.bar[1], pbp, p.timeout_ns)) atomicMax(p.status, (int)ST_TIMEOUT);
+        if (!DF && !mbar_wait(&S.bar[1], pbp, p.timeout_ns)) atomicMax(p.status, (int)ST_TIMEOUT);
     }
     if (threadIdx.x == kTileThread && S.kvpend && !mbar_wait(S.kvbar, S.kvph, p.timeout_ns))
         atomicMax(p.status, (int)ST_TIMEOUT);

@@ -300,7 +300,6 @@ bool plan_cluster(mc_session* s, const cudaDeviceProp& prop) {
                 cp.off_att = take((size_t)ghd, 16);
                 cp.off_attp = take((size_t)B8 * m->K * D, 16);
                 cp.off_f = take((size_t)B8 * cp.fpc, 16);
-                cp.off_rmsf = take((size_t)D, 16);
                 cp.off_rope = take((size_t)std::max(hd, 2), 16);
                 cp.off_pages = take((size_t)B8 * s->kv_pps, 16);
                 sc_f = (size_t)mc::kWarps * (ghd + 2 * G + 32 * mc::kAttMaxG);
@@ -324,7 +323,6 @@ bool plan_cluster(mc_session* s, const cudaDeviceProp& prop) {
                 // merged states of split attention units: at most max(cs, B K) units
                 cp.off_attp = take((size_t)std::max(cs, B8 * m->K) * ((ghd + 2 * G + 3) & ~3), 16);
                 cp.off_f = take((size_t)B8 * F, 16);
-                cp.off_rmsf = take((size_t)D, 16);
                 cp.off_rope = take((size_t)std::max(hd, 2), 16);
                 cp.off_pages = take((size_t)B8 * s->kv_pps, 16);
                 sc_f = (size_t)mc::kWarps * (ghd + 2 * G + 32 * mc::kAttMaxG);
