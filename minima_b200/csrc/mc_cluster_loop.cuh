@@ -100,8 +100,8 @@ struct ClusterParams {
     int* hgen;                  // [Bcap] sampler step of each sequence in this head phase, -1 = none
     unsigned* go;               // head phases issued (or kExit)
     unsigned* hdone;            // head CTA arrivals
-    float* hpv;                 // [Bcap][n_head_ctas][2] best transformed value (bans, no bans)
-    int* hpi;                   // [Bcap][n_head_ctas][2] its id
+    unsigned long long* hkey;   // [Bcap][2] best (bans, no bans) over the head CTAs as
+                                // hc_key(value, id), 0 = none; CTA 0 zeroes them once read
 };
 
 // ---------------------------------------------------------------- mbarrier
@@ -798,26 +798,35 @@ __device__ __forceinline__ void lc_publish_rows(const ClusterParams& cp, const L
     __syncthreads();
 }
 
-__device__ void lc_choose(const ClusterParams& cp, SeqMirror& m, int b, int nhc, int slot, int* ints) {
+// Greedy selection key: for values that are not NaN, a > b between keys is
+// better() between (value, id) pairs (larger value; equal values, +0 and
+// -0 included, keep the lower id), and every key is nonzero.
+__device__ __forceinline__ unsigned long long hc_key(float v, int id) {
+    return ((unsigned long long)order_key(v) << 32) | (unsigned)~(unsigned)id;
+}
+// (value, id) of a key; 0 (no candidate) gives (-inf, 0x7fffffff).
+__device__ __forceinline__ void hc_unkey(unsigned long long k, float& v, int& id) {
+    if (k == 0ull) {
+        v = -INFINITY;
+        id = 0x7fffffff;
+        return;
+    }
+    const unsigned o = (unsigned)(k >> 32);
+    v = __uint_as_float((o & 0x80000000u) ? (o & 0x7fffffffu) : ~o);
+    id = (int)~(unsigned)k;
+}
+
+__device__ void lc_choose(const ClusterParams& cp, SeqMirror& m, int b, int slot, int* ints) {
     const LoopParams<float>& p = cp.lp;
     const int lane = threadIdx.x & 31;
     const bool twok = p.s.ngram > 0;
-    float bv0 = -INFINITY, bv1 = -INFINITY;
-    int bi0 = 0x7fffffff, bi1 = 0x7fffffff;
-    for (int c = lane; c < nhc; c += 32) {
-        const size_t at = ((size_t)b * nhc + c) * 2;
-        const float v = ldcg(cp.hpv + at);
-        const int i = __ldcg(cp.hpi + at);
-        if (better(v, i, bv0, bi0)) { bv0 = v; bi0 = i; }
-        if (twok) {
-            const float v1 = ldcg(cp.hpv + at + 1);
-            const int i1 = __ldcg(cp.hpi + at + 1);
-            if (better(v1, i1, bv1, bi1)) { bv1 = v1; bi1 = i1; }
-        }
-    }
-    warp_argmax(bv0, bi0);
-    if (twok) warp_argmax(bv1, bi1);
     if (lane != 0) return;
+    float bv0, bv1 = -INFINITY;
+    int bi0, bi1 = 0x7fffffff;
+    hc_unkey(__ldcg(cp.hkey + 2 * b), bv0, bi0);
+    if (twok) hc_unkey(__ldcg(cp.hkey + 2 * b + 1), bv1, bi1);
+    cp.hkey[2 * b] = 0ull;      // ready for the next head phase (released with `go`)
+    cp.hkey[2 * b + 1] = 0ull;
     if (bi0 == 0x7fffffff) bi0 = 0;
     if (bi1 == 0x7fffffff) bi1 = 0;
     int id;
@@ -1003,7 +1012,7 @@ __device__ void lc_main(const ClusterParams& cp, unsigned char* smem, cg::cluste
             }
             __syncthreads();
             // one warp per head sequence; bans need the whole CTA afterwards
-            if (warp < nh) lc_choose(cp, S.seq[hl[warp]], hl[warp], nhc, warp, S.ints);
+            if (warp < nh) lc_choose(cp, S.seq[hl[warp]], hl[warp], warp, S.ints);
             __syncthreads();
             if (p.s.ngram > 0)
                 for (int i = 0; i < nh; i++)
@@ -1049,93 +1058,102 @@ __device__ void lc_main(const ClusterParams& cp, unsigned char* smem, cg::cluste
 }
 
 // Logits of this head CTA's rows for the head sequences (generate.c:187-191)
-// and the sampler's greedy choice among them.  NHP is nh rounded up to a
-// power of two: a warp takes groups of 32 / NHP rows; lanes split each row
-// in float4 chunks (the sequences' chunks stay in registers) and a
-// transposed reduction leaves lane l with row l / NHP of the group for
-// sequence slot l % NHP.  Each lane keeps the best transformed value of its
-// slot; the warp's best per slot lands in red / ints (k = 0: with bans,
-// k = 1: without, only when bans are active).
+// and the sampler's greedy choice among them.  A lane owns one row per
+// round (a warp: 32 consecutive rows, conflict-free float4 reads when
+// D % 32 == 0 since rows are padded to hc_ld = D + 4 floats) and runs its
+// whole dot products with the nh <= NHP normalised rows (broadcast reads).
+// Each lane keeps the best transformed value per slot; the warp's best per
+// slot lands in red / ints (k = 0: with bans, k = 1: without, only when bans
+// are active).
 template <int NHP>
 __device__ __forceinline__ void hc_rows(const ClusterParams& cp, const float* emb, const float* xs,
                                         const int* hl, const int* hg, int nh, int r0, int nr,
                                         float* red, int* ints) {
+    constexpr int HR = 1;    // rows per lane and round (more measured slower)
     const LoopParams<float>& p = cp.lp;
     const int D = p.D;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    constexpr int R = 32 / NHP;
-    const int s = lane % NHP;
     const int nwords = (p.V + 31) >> 5;
     const bool twok = p.s.ngram > 0;
-    float bv0 = -INFINITY, bv1 = -INFINITY;
-    int bi0 = 0x7fffffff, bi1 = 0x7fffffff;
-    const int ngroups = (nr + R - 1) / R;
-    for (int gq = warp; gq < ngroups; gq += kWarps) {
-        float v[32];
+    float bv0[NHP], bv1[NHP];
+    int bi0[NHP], bi1[NHP];
+    const float* xq[NHP];
 #pragma unroll
-        for (int j = 0; j < 32; j++) v[j] = 0.0f;
-        for (int k0 = 0; k0 < D; k0 += 128) {
-            const int k = k0 + 4 * lane;
-            const bool kin = k < D;
-            float4 xv[NHP];
+    for (int q = 0; q < NHP; q++) {
+        bv0[q] = bv1[q] = -INFINITY;
+        bi0[q] = bi1[q] = 0x7fffffff;
+        xq[q] = xs + (q < nh ? hl[q] : hl[0]) * D;
+    }
+    for (int blk = 32 * HR * warp; blk < nr; blk += 32 * HR * kWarps) {
+        const float* er[HR];
 #pragma unroll
-            for (int ss = 0; ss < NHP; ss++)
-                xv[ss] = kin && ss < nh ? *reinterpret_cast<const float4*>(xs + hl[ss] * D + k)
-                                        : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        for (int j = 0; j < HR; j++) {
+            const int row = blk + lane + 32 * j;
+            er[j] = emb + (size_t)(row < nr ? row : 0) * cp.hc_ld;
+        }
+        float acc[HR][NHP];
 #pragma unroll
-            for (int rr = 0; rr < R; rr++) {
-                const int row = gq * R + rr;
-                const float4 w = kin && row < nr
-                                     ? *reinterpret_cast<const float4*>(emb + (size_t)row * cp.hc_ld + k)
-                                     : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        for (int j = 0; j < HR; j++)
 #pragma unroll
-                for (int ss = 0; ss < NHP; ss++) {
-                    float& a = v[rr * NHP + ss];
-                    a = fmaf(w.x, xv[ss].x, a);
-                    a = fmaf(w.y, xv[ss].y, a);
-                    a = fmaf(w.z, xv[ss].z, a);
-                    a = fmaf(w.w, xv[ss].w, a);
+            for (int q = 0; q < NHP; q++) acc[j][q] = 0.0f;
+#pragma unroll 4
+        for (int k = 0; k < D; k += 4) {
+            float4 w[HR];
+#pragma unroll
+            for (int j = 0; j < HR; j++) w[j] = *reinterpret_cast<const float4*>(er[j] + k);
+#pragma unroll
+            for (int q = 0; q < NHP; q++) {
+                if (q < nh) {
+                    const float4 x = *reinterpret_cast<const float4*>(xq[q] + k);
+#pragma unroll
+                    for (int j = 0; j < HR; j++) {
+                        acc[j][q] = fmaf(w[j].x, x.x, acc[j][q]);
+                        acc[j][q] = fmaf(w[j].y, x.y, acc[j][q]);
+                        acc[j][q] = fmaf(w[j].z, x.z, acc[j][q]);
+                        acc[j][q] = fmaf(w[j].w, x.w, acc[j][q]);
+                    }
                 }
             }
         }
-        const float dot = transpose_reduce32(v);
-        const int row = gq * R + lane / NHP, vid = r0 + row;
-        if (row < nr && s < nh) {
-            const int b = hl[s];
-            const float lg = vid < 4 ? -INFINITY : dot;
-            if (p.trace) {
-                const int gi = hg[b];
-                if (gi < p.trace_steps) p.trace[((size_t)b * p.trace_steps + gi) * p.V + vid] = lg;
-            }
-            const unsigned cnt = p.s.pen_active ? __ldcg(p.counts + (size_t)b * p.V + vid) : 0u;
-            const bool ban =
-                twok && ((__ldcg(p.banned + (size_t)b * nwords + (vid >> 5)) >> (vid & 31)) & 1u);
-            const float tv = transform_value(lg, cnt, ban, p.s);
-            if (better(tv, vid, bv0, bi0)) { bv0 = tv; bi0 = vid; }
-            if (twok) {
-                const float tn = transform_value(lg, cnt, false, p.s);
-                if (better(tn, vid, bv1, bi1)) { bv1 = tn; bi1 = vid; }
-            }
-        }
-    }
-    // the warp's best per slot: lanes of one slot are NHP apart
 #pragma unroll
-    for (int o = NHP; o < 32; o <<= 1) {
-        const float ov = __shfl_xor_sync(0xffffffffu, bv0, o);
-        const int oi = __shfl_xor_sync(0xffffffffu, bi0, o);
-        if (better(ov, oi, bv0, bi0)) { bv0 = ov; bi0 = oi; }
-        if (twok) {
-            const float ov1 = __shfl_xor_sync(0xffffffffu, bv1, o);
-            const int oi1 = __shfl_xor_sync(0xffffffffu, bi1, o);
-            if (better(ov1, oi1, bv1, bi1)) { bv1 = ov1; bi1 = oi1; }
+        for (int j = 0; j < HR; j++) {
+            const int row = blk + lane + 32 * j;
+            if (row >= nr) continue;
+            const int vid = r0 + row;
+#pragma unroll
+            for (int q = 0; q < NHP; q++) {
+                if (q >= nh) continue;
+                const int b = hl[q];
+                const float lg = vid < 4 ? -INFINITY : acc[j][q];
+                if (p.trace) {
+                    const int gi = hg[b];
+                    if (gi < p.trace_steps) p.trace[((size_t)b * p.trace_steps + gi) * p.V + vid] = lg;
+                }
+                const unsigned cnt = p.s.pen_active ? __ldcg(p.counts + (size_t)b * p.V + vid) : 0u;
+                const bool ban =
+                    twok && ((__ldcg(p.banned + (size_t)b * nwords + (vid >> 5)) >> (vid & 31)) & 1u);
+                const float tv = transform_value(lg, cnt, ban, p.s);
+                if (better(tv, vid, bv0[q], bi0[q])) { bv0[q] = tv; bi0[q] = vid; }
+                if (twok) {
+                    const float tn = transform_value(lg, cnt, false, p.s);
+                    if (better(tn, vid, bv1[q], bi1[q])) { bv1[q] = tn; bi1[q] = vid; }
+                }
+            }
         }
     }
-    if (lane < nh && lane < NHP) {
-        red[lane * kWarps + warp] = bv0;
-        ints[64 + lane * kWarps + warp] = bi0;
-        if (twok) {
-            red[(kBCMax + lane) * kWarps + warp] = bv1;
-            ints[64 + (kBCMax + lane) * kWarps + warp] = bi1;
+    // the warp's best per slot
+#pragma unroll
+    for (int q = 0; q < NHP; q++) {
+        if (q >= nh) continue;
+        warp_argmax(bv0[q], bi0[q]);
+        if (twok) warp_argmax(bv1[q], bi1[q]);
+        if (lane == 0) {
+            red[q * kWarps + warp] = bv0[q];
+            ints[64 + q * kWarps + warp] = bi0[q];
+            if (twok) {
+                red[(kBCMax + q) * kWarps + warp] = bv1[q];
+                ints[64 + (kBCMax + q) * kWarps + warp] = bi1[q];
+            }
         }
     }
 }
@@ -1151,7 +1169,6 @@ __device__ void hc_main(const ClusterParams& cp, unsigned char* smem, int hc) {
     float* red = reinterpret_cast<float*>(smem + 1088);
     float* emb = reinterpret_cast<float*>(smem + kHcEmbOffset);
     float* xs = reinterpret_cast<float*>(smem + cp.off_hc_x);
-    const int nhc = (cp.n_clusters - 1) * cp.cs;
     if (threadIdx.x == 0) {
         mbar_init(bar, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
@@ -1225,9 +1242,9 @@ __device__ void hc_main(const ClusterParams& cp, unsigned char* smem, int hc) {
             int id = ints[64 + base];
             for (int w = 1; w < kWarps; w++)
                 if (better(red[base + w], ints[64 + base + w], v, id)) { v = red[base + w]; id = ints[64 + base + w]; }
-            const size_t at = ((size_t)hl[i] * nhc + hc) * 2 + k;
-            cp.hpv[at] = v;
-            cp.hpi[at] = id;
+            // this CTA's best into the sequence's maximum over all head CTAs
+            // (no candidate: every value was NaN, nothing to publish)
+            if (id != 0x7fffffff) atomicMax(cp.hkey + 2 * (size_t)hl[i] + k, hc_key(v, id));
         }
         __threadfence();
         __syncthreads();

@@ -58,11 +58,11 @@
 // complete before bytes of the next one of the same barrier are sent.  The
 // step's own cluster barrier (after CTA 0 broadcasts the sampled ids, or
 // one added when no sequence samples) keeps ordering the K/V rows written in
-// the step before later steps' bulk reads and makes failures cluster-wide.  After a failed
-// wait a CTA stops arming, waiting and sending for the rest of the launch
-// (its peers' waits then expire too) and every CTA leaves at that step's
-// barrier; a launch that failed this way lets in-flight copies land before
-// its CTAs exit.
+// the step before later steps' bulk reads and makes failures cluster-wide.
+// After a failed wait a CTA stops arming, waiting and sending for the rest
+// of the launch (its peers' waits then expire too) and every CTA leaves at
+// that step's barrier; a launch that failed this way lets in-flight copies
+// land before its CTAs exit.
 #pragma once
 
 #include "mc_cluster_loop.cuh"
@@ -182,30 +182,39 @@ __device__ __forceinline__ float cl2_dot32_r(const float* rows, int ld, int r0, 
     return transpose_reduce32(acc);
 }
 
-// lc_gemv4 for rows of length 128 against the normalised rows of up to
-// kBCMax sequences held in registers (xr[i]: sequence list[i], as
-// cl2_norm128 returns it); lane l returns row (l >> 3) . xr[l & 7].
-__device__ __forceinline__ float cl2_gemv4_r(const float* r0, const float* r1, const float* r2,
-                                             const float* r3, const float4 (&xr)[kBCMax], int n) {
-    const int k = 4 * (threadIdx.x & 31);
-    const float4 w0 = *reinterpret_cast<const float4*>(r0 + k);
-    const float4 w1 = *reinterpret_cast<const float4*>(r1 + k);
-    const float4 w2 = *reinterpret_cast<const float4*>(r2 + k);
-    const float4 w3 = *reinterpret_cast<const float4*>(r3 + k);
-    float acc[32];
+// Up/gate rows [f0, f1) of this CTA's slice and their SwiGLU
+// (generate.c:165-179) at D = 128, for nf <= NFP sequences normalised in
+// registers (xr[q]: sequence fl[q], as cl2_norm128 returns it).  A warp
+// takes H = 16 / NFP F indices per round: rows up j .. j + H - 1, then gate
+// j .. j + H - 1, lane r NFP + q holding row r against sequence q after the
+// transposed reduction, so the gate of an up value sits in lane ^ 16.  Rows
+// are read up to the next multiple of H past f1 (inside the weight buffer
+// when the slice is a multiple of 16 rows; those results are not stored).
+template <int NFP>
+__device__ __forceinline__ void cl2_upgate(const float* wu, const float* wg, const float4 (&xr)[kBCMax],
+                                           const int* fl, int nf, int f0, int f1, int fpc, float* f) {
+    constexpr int R = 32 / NFP, H = R / 2;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    for (int j = f0 + H * warp; j < f1; j += H * kWarps) {
+        float acc[32];
 #pragma unroll
-    for (int i = 0; i < 32; i++) acc[i] = 0.0f;
+        for (int r = 0; r < R; r++) {
+            const float* row = r < H ? wu + (size_t)(j - f0 + r) * 128 : wg + (size_t)(j - f0 + r - H) * 128;
+            const float4 w = *reinterpret_cast<const float4*>(row + 4 * lane);
 #pragma unroll
-    for (int i = 0; i < kBCMax; i++) {
-        if (i < n) {
-            const float4 x = xr[i];
-            acc[0 * 8 + i] = w0.x * x.x + w0.y * x.y + w0.z * x.z + w0.w * x.w;
-            acc[1 * 8 + i] = w1.x * x.x + w1.y * x.y + w1.z * x.z + w1.w * x.w;
-            acc[2 * 8 + i] = w2.x * x.x + w2.y * x.y + w2.z * x.z + w2.w * x.w;
-            acc[3 * 8 + i] = w3.x * x.x + w3.y * x.y + w3.z * x.z + w3.w * x.w;
+            for (int q = 0; q < NFP; q++) {
+                const float4 x = xr[q];
+                acc[r * NFP + q] = q < nf ? w.x * x.x + w.y * x.y + w.z * x.z + w.w * x.w : 0.0f;
+            }
+        }
+        const float val = transpose_reduce32(acc);
+        const float gate = __shfl_xor_sync(0xffffffffu, val, 16);
+        const int q = lane % NFP, r = lane / NFP;
+        if (lane < 16 && q < nf && j + r < f1) {
+            const float sv = gate / (1.0f + expf(-gate));
+            f[fl[q] * fpc + (j - f0) + r] = sv * val;
         }
     }
-    return transpose_reduce32(acc);
 }
 
 // x[fl[i]] += sum over the cs CTAs' ffn_down partials (CTA order; partial
@@ -447,28 +456,30 @@ __device__ __forceinline__ bool cl2_layer(const ClusterParams& cp, const CSlice&
     const float* rms2 = wd + (size_t)D * fpc;
     // rmsnorm of every fed sequence (generate.c:57-63): at D = 128 in the
     // registers of each warp that computes rows, otherwise a warp per sequence
-    float4 xr[kBCMax];
-    if constexpr (DC == 128) {
-        if (sl.f0 + 2 * warp < sl.f1) {
+    if constexpr (DC == 128 && FC % 16 == 0) {
+        // FC % 16 == 0: every round's rows stay inside the up/gate buffer
+        float4 xr[kBCMax];
 #pragma unroll
-            for (int i = 0; i < kBCMax; i++)
-                xr[i] = i < nf ? cl2_norm128(S.x + fl[i] * D, rms2) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
-        }
+        for (int i = 0; i < kBCMax; i++)
+            xr[i] = i < nf ? cl2_norm128(S.x + fl[i] * D, rms2) : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+        // four sequence slots per round at nf <= 4 (a 32-row slice is one
+        // round of the 8 warps; fewer slots would leave warps idle), else eight
+        if (nf <= 4) cl2_upgate<4>(wu, wg, xr, fl, nf, sl.f0, sl.f1, fpc, S.f);
+        else cl2_upgate<8>(wu, wg, xr, fl, nf, sl.f0, sl.f1, fpc, S.f);
     } else {
         lc_norm(S.x, S.xn, rms2, fl, nf, D, S.red);
-    }
-    // up/gate rows [f0, f1) and SwiGLU (generate.c:165-179)
-    for (int j = sl.f0 + 2 * warp; j < sl.f1; j += 2 * kWarps) {
-        // rows: up j, up j+1, gate j, gate j+1 -> the gate of lane's up row is in lane ^ 16
-        const float* u0 = wu + (size_t)(j - sl.f0) * D;
-        const float* g0 = wg + (size_t)(j - sl.f0) * D;
-        const float val = DC == 128 ? cl2_gemv4_r(u0, u0 + D, g0, g0 + D, xr, nf)
-                                    : lc_gemv4(u0, u0 + D, g0, g0 + D, D, S.xn, D, fl, nf);
-        const float gate = __shfl_xor_sync(0xffffffffu, val, 16);
-        const int i = lane & 7;
-        if (lane < 16 && i < nf) {
-            const float sv = gate / (1.0f + expf(-gate));
-            S.f[fl[i] * fpc + (j - sl.f0) + (lane >> 3)] = sv * val;
+        // up/gate rows [f0, f1) and SwiGLU (generate.c:165-179)
+        for (int j = sl.f0 + 2 * warp; j < sl.f1; j += 2 * kWarps) {
+            // rows: up j, up j+1, gate j, gate j+1 -> the gate of lane's up row is in lane ^ 16
+            const float* u0 = wu + (size_t)(j - sl.f0) * D;
+            const float* g0 = wg + (size_t)(j - sl.f0) * D;
+            const float val = lc_gemv4(u0, u0 + D, g0, g0 + D, D, S.xn, D, fl, nf);
+            const float gate = __shfl_xor_sync(0xffffffffu, val, 16);
+            const int i = lane & 7;
+            if (lane < 16 && i < nf) {
+                const float sv = gate / (1.0f + expf(-gate));
+                S.f[fl[i] * fpc + (j - sl.f0) + (lane >> 3)] = sv * val;
+            }
         }
     }
     __syncthreads();
@@ -692,7 +703,7 @@ __device__ void cl2_main(const ClusterParams& cp, unsigned char* smem, cg::clust
                 }
             }
             __syncthreads();
-            if (warp < nh) lc_choose(cp, S.seq[hl[warp]], hl[warp], nhc, warp, S.ints);
+            if (warp < nh) lc_choose(cp, S.seq[hl[warp]], hl[warp], warp, S.ints);
             __syncthreads();
             if (p.s.ngram > 0)
                 for (int i = 0; i < nh; i++)

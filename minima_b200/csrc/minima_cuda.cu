@@ -121,8 +121,7 @@ struct mc_session {
     float* xfin;
     int* hgen;
     unsigned* hsync;              // [0] go, [32] hdone (separate lines)
-    float* hpv;
-    int* hpi;
+    unsigned long long* hkey;     // [Bcap][2] head CTAs' greedy maxima
     int last_path;                // 0 grid loop, 1 cluster loop
     // batched prefill work buffers (allocated on first use)
     float *pf_x, *pf_xn, *pf_q, *pf_att, *pf_f;
@@ -562,7 +561,7 @@ mc_status mc_session_destroy(mc_session* s) {
     void* bufs[] = {s->kv_table, s->kc, s->vc, s->x, s->q, s->att, s->f, s->logits, s->part_o, s->part_m,
                     s->part_l, s->amax_v, s->amax_i, s->att_cnt, s->counts, s->banned, s->bar,
                     s->status, s->seq, s->prompts, s->out, s->stop, s->trace, s->stamps,
-                    s->xfin, s->hgen, s->hsync, s->hpv, s->hpi,
+                    s->xfin, s->hgen, s->hsync, s->hkey,
                     s->pf_x, s->pf_xn, s->pf_q, s->pf_att, s->pf_f, s->pf_logits,
                     s->pf_xn16, s->pf_att16, s->pf_f16, s->pf_part, s->pf_cnt, s->bd_lists, s->bd_xn,
                     s->bd_xn16, s->bd_att16, s->bd_f16, s->bd_part, s->stats,
@@ -718,7 +717,6 @@ mc_status session_create(mc_model* m, int max_batch, int max_seq, int page_len, 
     }
     s->cl_ok = plan_cluster(s, prop);
     if (s->cl_ok) {
-        const size_t nhc = (size_t)(s->cl_nc - 1) * s->cl_cs;
         const mc::ClusterParams& cpl = s->cl_plan;
         const size_t G = m->H / m->K;
         struct Alloc cl_allocs[] = {
@@ -727,8 +725,7 @@ mc_status session_create(mc_model* m, int max_batch, int max_seq, int page_len, 
             {(void**)&s->xfin, B * D * 4},
             {(void**)&s->hgen, B * 4},
             {(void**)&s->hsync, 64 * 4},
-            {(void**)&s->hpv, B * nhc * 2 * 4},
-            {(void**)&s->hpi, B * nhc * 2 * 4},
+            {(void**)&s->hkey, B * 2 * 8},
         };
         s->cl2_version = ~0u;
         for (auto& a : cl_allocs) {
@@ -845,8 +842,7 @@ mc_status run_cluster(mc_session* s, mc::LoopParams<float>& p) {
     cp.hgen = s->hgen;
     cp.go = s->hsync;
     cp.hdone = s->hsync + 32;
-    cp.hpv = s->hpv;
-    cp.hpi = s->hpi;
+    cp.hkey = s->hkey;
     cp.proj_h = s->cl_proj_h;
     cp.down_s = s->cl_down_s;
     int relayouts = 0;
@@ -864,6 +860,7 @@ mc_status run_cluster(mc_session* s, mc::LoopParams<float>& p) {
     MC_CUDA(cudaMemsetAsync(s->stamps, 0, ((size_t)p.T + 1) * 8, s->stream));
     MC_CUDA(cudaMemsetAsync(s->status, 0, 256, s->stream));
     MC_CUDA(cudaMemsetAsync(s->hsync, 0, 64 * 4, s->stream));
+    MC_CUDA(cudaMemsetAsync(s->hkey, 0, (size_t)s->Bcap * 2 * 8, s->stream));
     // MINIMA_CUDA_CLUSTER_NONCOOP=1 skips the cooperative attribute (kernel
     // profilers that cannot instrument cooperative cluster launches)
     const char* noncoop = getenv("MINIMA_CUDA_CLUSTER_NONCOOP");
