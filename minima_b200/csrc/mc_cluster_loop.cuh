@@ -92,6 +92,7 @@ struct ClusterParams {
                                 // between phases; 2: two-phase loop, partials exchanged by
                                 // bulk copies onto the receivers' mbarriers (dataflow)
     unsigned off_wb;            // phase B weight buffer (off_stage: phase A buffer)
+    unsigned off_pair;          // a unit's second key range: merged attention state
     int fpc;                    // up/gate rows (ffn_down columns) per CTA, padded
     int dp_b;                   // sequence stride of the ffn_down partials
     const float* proj_h;        // [L][K][D][G hd] attn_proj column blocks per KV head
@@ -197,6 +198,9 @@ struct LcState {
     unsigned atph;               // phase of atbar awaited next
     unsigned dpph;               // bit p: phase of dpbar[p] awaited next
     int nlayer;                  // layers run in this launch (selects the dpbar / partial buffer)
+    unsigned long long* pairbar; // a unit's second key range: its merged state has landed
+    float* pair;                 // [G hd + 2 G, padded to 4] that state (sent / received)
+    unsigned prph;               // phase of pairbar awaited next
 };
 
 // The sequence table in shared memory: the layer cluster reads it every

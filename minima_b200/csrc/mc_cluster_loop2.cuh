@@ -277,18 +277,32 @@ __device__ __forceinline__ bool cl2_layer(const ClusterParams& cp, const CSlice&
     // ------------------------------------------------ phase A: unit crank
     if (!mbar_wait(&S.bar[0], pa, p.timeout_ns)) lc_fail(S, p.status, ST_TIMEOUT);
     pa ^= 1u;
-    const int g = crank % K;
-    const int b = unit ? fl[crank / K] : 0;
     const int nkeys = t + 1;
+    // DF, when a unit's keys need more than one tile and the cluster has a
+    // CTA to spare for every unit: CTA nu + u (the second of unit u: same
+    // sequence and KV head, since nu is a multiple of K) attends over keys
+    // [kv_tile, t] and sends its merged state to u, which covers
+    // [0, kv_tile) and merges the two (the same online-softmax merge as its
+    // warps').  The second computes the Q/K/V rows itself (row t is in its
+    // range) but leaves the cache append to the unit.
+    const bool split = DF && 2 * nu <= cs && nkeys > cp.kv_tile;
+    const bool second = split && crank >= nu && crank < 2 * nu;
+    const bool attends = unit || second;
+    const int key0 = second ? cp.kv_tile : 0;
+    const int key1 = unit && split ? cp.kv_tile : nkeys;
+    const unsigned pair_bytes = (unsigned)(((ghd + 2 * G + 3) & ~3) * 4);
+    if (split && unit && threadIdx.x == 0 && !S.ints[34]) mbar_expect_tx(S.pairbar, pair_bytes);
+    const int g = crank % K;
+    const int b = attends ? fl[(second ? crank - nu : crank) / K] : 0;
     bool wrote_kv = false;
     // DF: this layer's FFN weights are requested here, behind the first K/V
     // tile, which the unit phase waits on first (the barrier variant
     // requests them at the end of the previous layer)
-    if (DF && !unit && threadIdx.x == kTileThread) cl2_issue_b(cp, sl, S, l, crank);
-    if (unit) {
+    if (DF && !attends && threadIdx.x == kTileThread) cl2_issue_b(cp, sl, S, l, crank);
+    if (attends) {
         // the first K/V tile is requested by the last warp (warp 0 normalises)
         if (threadIdx.x == kTileThread) {
-            att_issue_tile(cp, S, l, b, g, 0, min(cp.kv_tile, nkeys), t, hd);
+            att_issue_tile(cp, S, l, b, g, key0, min(cp.kv_tile, key1 - key0), t, hd);
             if (DF) cl2_issue_b(cp, sl, S, l, crank);
         }
         const float* wa = S.stage;
@@ -327,7 +341,7 @@ __device__ __forceinline__ bool cl2_layer(const ClusterParams& cp, const CSlice&
                     out = (d & 1) ? other * rr.y + val * rr.x : val * rr.x - other * rr.y;
                 }
                 S.qkv[r] = out;
-                if (!isq) {
+                if (!isq && unit) {
                     const int page = S.pages[b * p.pg.pps + (t >> p.pg.shift)];
                     (isk ? p.kc : p.vc)[kv_row_at(page, p.pg.shift, p.L, K, l, g, t) * hd + d] = out;
                     wrote_kv = true;
@@ -353,9 +367,9 @@ __device__ __forceinline__ bool cl2_layer(const ClusterParams& cp, const CSlice&
 #pragma unroll
             for (int i = 0; i < kAttMaxND; i++) o[h][i] = 0.0f;
         }
-        for (int a0 = 0; a0 < nkeys; a0 += cp.kv_tile) {
-            const int n = min(cp.kv_tile, nkeys - a0);
-            if (threadIdx.x == kTileThread && a0 != 0) att_issue_tile(cp, S, l, b, g, a0, n, t, hd);
+        for (int a0 = key0; a0 < key1; a0 += cp.kv_tile) {
+            const int n = min(cp.kv_tile, key1 - a0);
+            if (threadIdx.x == kTileThread && a0 != key0) att_issue_tile(cp, S, l, b, g, a0, n, t, hd);
             if (t >= a0 && t < a0 + n)
                 for (int c = threadIdx.x; c < 2 * hd; c += blockDim.x) {
                     if (c < hd) ks[(t - a0) * hd + c] = kq[c];
@@ -384,43 +398,78 @@ __device__ __forceinline__ bool cl2_layer(const ClusterParams& cp, const CSlice&
                 }
             }
         __syncthreads();
-        for (int i = threadIdx.x; i < ghd; i += blockDim.x) {
-            const int h = i / hd;
-            float M = -INFINITY;
+        if (second) {
+            // this range's state merged over the warps, unnormalised:
+            // pair[i < G hd] = sum_w c_w o_w, pair[G hd + 2h] = max_w m_w,
+            // pair[G hd + 2h + 1] = sum_w c_w l_w (c_w = exp(m_w - max))
+            for (int i = threadIdx.x; i < ghd + 2 * G; i += blockDim.x) {
+                const int h = i < ghd ? i / hd : (i - ghd) / 2;
+                float M = -INFINITY;
 #pragma unroll
-            for (int w = 0; w < kWarps; w++) M = fmaxf(M, part[w * pw + ghd + 2 * h]);
-            float num = 0.0f, den = 0.0f;
+                for (int w = 0; w < kWarps; w++) M = fmaxf(M, part[w * pw + ghd + 2 * h]);
+                float acc = 0.0f;
+                const int src = i < ghd ? i : ghd + 2 * h + 1;
 #pragma unroll
-            for (int w = 0; w < kWarps; w++) {
-                const float mw = part[w * pw + ghd + 2 * h];
-                const float c = mw == -INFINITY ? 0.0f : expf(mw - M);   // a warp may see no keys
-                den += c * part[w * pw + ghd + 2 * h + 1];
-                num += c * part[w * pw + i];
+                for (int w = 0; w < kWarps; w++) {
+                    const float mw = part[w * pw + ghd + 2 * h];
+                    const float c = mw == -INFINITY ? 0.0f : expf(mw - M);
+                    acc += c * part[w * pw + src];
+                }
+                S.pair[i] = (i >= ghd && ((i - ghd) & 1) == 0) ? M : acc;
             }
-            S.att[i] = num / den;
-        }
-        __syncthreads();
-        // this head group's share of attn_proj (generate.c:158-163): a thread
-        // per output over the block's [G hd][D] (transposed) columns
-        const float* wp = wa + (size_t)rows_a * D;
-        for (int i = threadIdx.x; i < D; i += blockDim.x) {
-            float a0 = 0.0f, a1 = 0.0f;
-            int c = 0;
-#pragma unroll
-            for (; c + 1 < ghd; c += 2) {
-                a0 = fmaf(wp[(size_t)c * D + i], S.att[c], a0);
-                a1 = fmaf(wp[(size_t)(c + 1) * D + i], S.att[c + 1], a1);
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            __syncthreads();
+            if (threadIdx.x == 0 && !S.ints[34]) bulk_s2peer(S.pair, pair_bytes, S.pairbar, (unsigned)(crank - nu));
+        } else {
+            if (split) {
+                if (threadIdx.x == 0) df_wait(p, S, S.pairbar, S.prph);
+                S.prph ^= 1u;
+                __syncthreads();
             }
-            if (c < ghd) a0 = fmaf(wp[(size_t)c * D + i], S.att[c], a0);
-            S.attp[crank * D + i] = a0 + a1;
+            for (int i = threadIdx.x; i < ghd; i += blockDim.x) {
+                const int h = i / hd;
+                float M = -INFINITY;
+#pragma unroll
+                for (int w = 0; w < kWarps; w++) M = fmaxf(M, part[w * pw + ghd + 2 * h]);
+                if (split) M = fmaxf(M, S.pair[ghd + 2 * h]);
+                float num = 0.0f, den = 0.0f;
+#pragma unroll
+                for (int w = 0; w < kWarps; w++) {
+                    const float mw = part[w * pw + ghd + 2 * h];
+                    const float c = mw == -INFINITY ? 0.0f : expf(mw - M);   // a warp may see no keys
+                    den += c * part[w * pw + ghd + 2 * h + 1];
+                    num += c * part[w * pw + i];
+                }
+                if (split) {   // the second range always holds key t: its maximum is finite
+                    const float c = expf(S.pair[ghd + 2 * h] - M);
+                    den += c * S.pair[ghd + 2 * h + 1];
+                    num += c * S.pair[i];
+                }
+                S.att[i] = num / den;
+            }
+            __syncthreads();
+            // this head group's share of attn_proj (generate.c:158-163): a thread
+            // per output over the block's [G hd][D] (transposed) columns
+            const float* wp = wa + (size_t)rows_a * D;
+            for (int i = threadIdx.x; i < D; i += blockDim.x) {
+                float a0 = 0.0f, a1 = 0.0f;
+                int c = 0;
+#pragma unroll
+                for (; c + 1 < ghd; c += 2) {
+                    a0 = fmaf(wp[(size_t)c * D + i], S.att[c], a0);
+                    a1 = fmaf(wp[(size_t)(c + 1) * D + i], S.att[c + 1], a1);
+                }
+                if (c < ghd) a0 = fmaf(wp[(size_t)c * D + i], S.att[c], a0);
+                S.attp[crank * D + i] = a0 + a1;
+            }
+            // DF: this thread's shared-memory writes (the partial, and the K/V
+            // tile that later partials overwrite) before the async proxy's copies
+            if (DF) asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            __syncthreads();
+            if (!DF) push_block(cl, S.attp, crank * D, D, cs, crank);
+            else if (warp == 0 && lane < cs && lane != crank && !S.ints[34])
+                bulk_s2peer(S.attp + (size_t)crank * D, (unsigned)(D * 4), S.atbar, (unsigned)lane);
         }
-        // DF: this thread's shared-memory writes (the partial, and the K/V
-        // tile that later partials overwrite) before the async proxy's copies
-        if (DF) asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-        __syncthreads();
-        if (!DF) push_block(cl, S.attp, crank * D, D, cs, crank);
-        else if (warp == 0 && lane < cs && lane != crank && !S.ints[34])
-            bulk_s2peer(S.attp + (size_t)crank * D, (unsigned)(D * 4), S.atbar, (unsigned)lane);
     }
     // K/V rows written in this step are read by later steps' bulk copies
     // (async proxy) in other CTAs: order them before the cluster barrier
@@ -554,6 +603,8 @@ __device__ void cl2_main(const ClusterParams& cp, unsigned char* smem, cg::clust
     S.kvbar = S.bar + 2;
     S.atbar = S.bar + 3;
     S.dpbar = S.bar + 4;                                   // [2]
+    S.pairbar = S.bar + 6;
+    S.pair = reinterpret_cast<float*>(smem + cp.off_pair);
     constexpr bool df = DF;
     S.ints = reinterpret_cast<int*>(smem + 64);
     S.red = reinterpret_cast<float*>(smem + 64 + 64 * 4);
@@ -585,6 +636,7 @@ __device__ void cl2_main(const ClusterParams& cp, unsigned char* smem, cg::clust
         mbar_init(S.atbar, 1);
         mbar_init(&S.dpbar[0], 1);
         mbar_init(&S.dpbar[1], 1);
+        mbar_init(S.pairbar, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         S.ints[34] = 0;
         S.ints[38] = 0;
@@ -594,6 +646,7 @@ __device__ void cl2_main(const ClusterParams& cp, unsigned char* smem, cg::clust
     S.kvpend = 0;
     S.atph = 0u;
     S.dpph = 0u;
+    S.prph = 0u;
     S.nlayer = 0;
     for (int b = threadIdx.x; b < p.B; b += blockDim.x) {
         const SeqState& g = p.seq[b];

@@ -301,6 +301,7 @@ bool plan_cluster(mc_session* s, const cudaDeviceProp& prop) {
                 cp.off_f = take((size_t)B8 * cp.fpc, 16);
                 cp.off_rope = take((size_t)std::max(hd, 2), 16);
                 cp.off_pages = take((size_t)B8 * s->kv_pps, 16);
+                cp.off_pair = take((size_t)((ghd + 2 * G + 3) & ~3), 16);
                 sc_f = (size_t)mc::kWarps * (ghd + 2 * G + 32 * mc::kAttMaxG);
                 cp.off_sc = take(sc_f, 16);
                 cp.off_stage = take(stage_f, 128);
