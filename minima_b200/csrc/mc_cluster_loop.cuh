@@ -101,8 +101,10 @@ struct ClusterParams {
     int* hgen;                  // [Bcap] sampler step of each sequence in this head phase, -1 = none
     unsigned* go;               // head phases issued (or kExit)
     unsigned* hdone;            // head CTA arrivals
-    unsigned long long* hkey;   // [Bcap][2] best (bans, no bans) over the head CTAs as
-                                // hc_key(value, id), 0 = none; CTA 0 zeroes them once read
+    unsigned long long* hkey;   // [2][Bcap][2] best (bans, no bans) over the head CTAs as
+                                // hc_key(value, id), 0 = none; head phase h uses buffer h & 1,
+                                // which CTA 0 zeroes when it releases phase h (every layer CTA
+                                // read it, at phase h - 2, before the last step barrier)
 };
 
 // ---------------------------------------------------------------- mbarrier
@@ -395,6 +397,24 @@ __device__ bool lc_sync(cg::cluster_group& cl, LcState& S, int cs) {
         for (int r = 0; r < cs; r++) cl.map_shared_rank(S.ints, r)[slot] = 1;
     cl.sync();
     const bool ok = S.ints[slot] == 0;
+    S.epoch++;
+    return ok;
+}
+
+// lc_sync in two halves, so that work can run between the arrival and the
+// wait: lc_arrive publishes this CTA's failure flag of the epoch and
+// arrives (release); lc_wait waits (acquire) and takes the cluster-wide
+// decision.  A CTA arrives exactly once between two waits.
+__device__ __forceinline__ void lc_arrive(cg::cluster_group& cl, LcState& S, int cs) {
+    const int slot = 36 + (S.epoch & 1);
+    __syncthreads();
+    if (threadIdx.x == 0 && S.ints[38])
+        for (int r = 0; r < cs; r++) cl.map_shared_rank(S.ints, r)[slot] = 1;
+    asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+}
+__device__ __forceinline__ bool lc_wait(LcState& S) {
+    asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+    const bool ok = S.ints[36 + (S.epoch & 1)] == 0;
     S.epoch++;
     return ok;
 }
@@ -786,9 +806,12 @@ __device__ bool lc_layer(const ClusterParams& cp, const CSlice& sl, LcState& S,
 // done / generated in ints[40 + slot] / ints[48 + slot].
 // Layer CTA 0: the residual rows of the sequences in hl (nh of them) and
 // each sequence's sampler step (-1 = no logits this phase) for the head
-// CTAs; ends with a CTA barrier (the caller's release of `go` follows).
-__device__ __forceinline__ void lc_publish_rows(const ClusterParams& cp, const LcState& S, const int* hl, int nh) {
+// CTAs, and key buffer kb zeroed for their maxima; ends with a CTA barrier
+// (the caller's release of `go` follows).
+__device__ __forceinline__ void lc_publish_rows(const ClusterParams& cp, const LcState& S, const int* hl, int nh,
+                                                int kb) {
     const LoopParams<float>& p = cp.lp;
+    for (int i = threadIdx.x; i < 2 * p.Bcap; i += blockDim.x) cp.hkey[(size_t)kb * 2 * p.Bcap + i] = 0ull;
     for (int e = threadIdx.x; e < nh * p.D; e += blockDim.x) {
         const int b = hl[e / p.D], k = e % p.D;
         cp.xfin[(size_t)b * p.D + k] = S.x[b * p.D + k];
@@ -820,17 +843,23 @@ __device__ __forceinline__ void hc_unkey(unsigned long long k, float& v, int& id
     id = (int)~(unsigned)k;
 }
 
-__device__ void lc_choose(const ClusterParams& cp, SeqMirror& m, int b, int slot, int* ints) {
+// The next id of sequence b from the head CTAs' keys (buffer kb) and its
+// bookkeeping in the mirror m (generate.c:447-468 and the loop around it).
+// The leader also writes the id and the penalty count; the others only
+// update their own mirror, which therefore stays identical to the leader's
+// (the stop check reads earlier ids from out_ids and takes this one from
+// here).
+__device__ void lc_choose(const ClusterParams& cp, SeqMirror& m, int b, int slot, int* ints, int kb,
+                          bool leader) {
     const LoopParams<float>& p = cp.lp;
     const int lane = threadIdx.x & 31;
     const bool twok = p.s.ngram > 0;
     if (lane != 0) return;
     float bv0, bv1 = -INFINITY;
     int bi0, bi1 = 0x7fffffff;
-    hc_unkey(__ldcg(cp.hkey + 2 * b), bv0, bi0);
-    if (twok) hc_unkey(__ldcg(cp.hkey + 2 * b + 1), bv1, bi1);
-    cp.hkey[2 * b] = 0ull;      // ready for the next head phase (released with `go`)
-    cp.hkey[2 * b + 1] = 0ull;
+    const unsigned long long* key = cp.hkey + ((size_t)kb * p.Bcap + b) * 2;
+    hc_unkey(__ldcg(key), bv0, bi0);
+    if (twok) hc_unkey(__ldcg(key + 1), bv1, bi1);
     if (bi0 == 0x7fffffff) bi0 = 0;
     if (bi1 == 0x7fffffff) bi1 = 0;
     int id;
@@ -841,16 +870,20 @@ __device__ void lc_choose(const ClusterParams& cp, SeqMirror& m, int b, int slot
     if (draws) (void)rng_f32(m.rng);
     const int P = m.P, g = m.gen, nnew = m.nnew;
     uint16_t* out = p.out_ids + (size_t)b * p.out_cap;
-    out[P + g] = (uint16_t)id;
-    if (p.s.pen_active) p.counts[(size_t)b * p.V + id] += 1u;
+    if (leader) {
+        out[P + g] = (uint16_t)id;
+        if (p.s.pen_active) p.counts[(size_t)b * p.V + id] += 1u;
+    }
     const int generated = g + 1;
     m.gen = generated;
     bool stop = false;
     if (p.s.stop_len > 0 && generated >= p.s.min_new && generated >= p.s.stop_len) {
         stop = true;
         const int s0 = P + generated - p.s.stop_len;
-        for (int k = 0; k < p.s.stop_len; k++)
-            if (ld_u16_cg(out + s0 + k) != (int)p.s.stop_ids[k]) { stop = false; break; }
+        for (int k = 0; k < p.s.stop_len; k++) {
+            const int have = s0 + k == P + g ? id : ld_u16_cg(out + s0 + k);
+            if (have != (int)p.s.stop_ids[k]) { stop = false; break; }
+        }
     }
     if (stop) {
         m.result = P + generated - p.s.stop_len;
@@ -1001,7 +1034,7 @@ __device__ void lc_main(const ClusterParams& cp, unsigned char* smem, cg::cluste
             // ---- hand the sampling sequences' residual rows to the head CTAs
             // (which apply the final rmsnorm, generate.c:187-191), release
             // them, wait for all of them, choose the next ids
-            lc_publish_rows(cp, S, hl, nh);
+            lc_publish_rows(cp, S, hl, nh, (int)(heads & 1u));
             if (threadIdx.x == 0) {
                 __threadfence();
                 st_release_u32(cp.go, heads);
@@ -1016,7 +1049,7 @@ __device__ void lc_main(const ClusterParams& cp, unsigned char* smem, cg::cluste
             }
             __syncthreads();
             // one warp per head sequence; bans need the whole CTA afterwards
-            if (warp < nh) lc_choose(cp, S.seq[hl[warp]], hl[warp], warp, S.ints);
+            if (warp < nh) lc_choose(cp, S.seq[hl[warp]], hl[warp], warp, S.ints, (int)(heads & 1u), true);
             __syncthreads();
             if (p.s.ngram > 0)
                 for (int i = 0; i < nh; i++)
@@ -1248,7 +1281,7 @@ __device__ void hc_main(const ClusterParams& cp, unsigned char* smem, int hc) {
                 if (better(red[base + w], ints[64 + base + w], v, id)) { v = red[base + w]; id = ints[64 + base + w]; }
             // this CTA's best into the sequence's maximum over all head CTAs
             // (no candidate: every value was NaN, nothing to publish)
-            if (id != 0x7fffffff) atomicMax(cp.hkey + 2 * (size_t)hl[i] + k, hc_key(v, id));
+            if (id != 0x7fffffff) atomicMax(cp.hkey + ((size_t)(g & 1) * p.Bcap + hl[i]) * 2 + k, hc_key(v, id));
         }
         __threadfence();
         __syncthreads();

@@ -55,10 +55,11 @@
 //    finished that layer's attention.
 // Arrivals may precede the receiver's expect_tx (tx-count goes negative in
 // between, as the mbarrier allows); the chains above keep every phase
-// complete before bytes of the next one of the same barrier are sent.  The
-// step's own cluster barrier (after CTA 0 broadcasts the sampled ids, or
-// one added when no sequence samples) keeps ordering the K/V rows written in
-// the step before later steps' bulk reads and makes failures cluster-wide.
+// complete before bytes of the next one of the same barrier are sent.  One
+// cluster barrier per step remains, split into an arrival after the layers
+// and a wait once every layer CTA has chosen the next ids into its own copy
+// of the sequence table: it orders the K/V rows written in the step before
+// later steps' bulk reads and makes failures cluster-wide.
 // After a failed wait a CTA stops arming, waiting and sending for the rest
 // of the launch (its peers' waits then expire too) and every CTA leaves at
 // that step's barrier; a launch that failed this way lets in-flight copies
@@ -728,21 +729,54 @@ __device__ void cl2_main(const ClusterParams& cp, unsigned char* smem, cg::clust
         for (int l = 0; ok && l < p.L; l++)
             ok = cl2_layer_any<DF>(cp, sl, S, cl, crank, l, t, fl, nf, pa, pbp);
         if (!ok) break;
-        if (nh == 0) {
-            // the dataflow layers have no cluster barrier of their own: one
-            // per step orders this step's K/V rows before later bulk reads
-            // and makes a failure cluster-wide
-            if (df) ok = lc_sync(cl, S, cp.cs);
+        if constexpr (DF) {
+            // The dataflow layers have no cluster barrier of their own; the
+            // step's one (ordering its K/V rows before later bulk reads,
+            // making a failure cluster-wide) is split: the arrival here, the
+            // wait once the next ids are chosen, so the hand-off hides it.
+            // Every layer CTA waits for the head CTAs and chooses the ids
+            // into its own mirror (the same update everywhere); CTA 0 alone
+            // also releases the heads and writes ids, counts and bans.
+            lc_arrive(cl, S, cp.cs);
+            if (nh > 0) {
+                heads++;
+                if (crank == 0) {
+                    lc_publish_rows(cp, S, hl, nh, (int)(heads & 1u));
+                    if (threadIdx.x == 0) {
+                        __threadfence();
+                        st_release_u32(cp.go, heads);
+                    }
+                }
+                if (threadIdx.x == 0) {
+                    const unsigned target = heads * ((unsigned)nhc + p.extra_arrivals);
+                    const unsigned long long t0 = globaltimer_ns();
+                    while ((int)(ld_acquire_u32(cp.hdone) - target) < 0) {
+                        if (globaltimer_ns() - t0 > p.timeout_ns) {
+                            lc_fail(S, p.status, ST_TIMEOUT);   // cluster-wide at the next arrival
+                            break;
+                        }
+                    }
+                }
+                __syncthreads();
+                if (warp < nh)
+                    lc_choose(cp, S.seq[hl[warp]], hl[warp], warp, S.ints, (int)(heads & 1u), crank == 0);
+                __syncthreads();
+                if (crank == 0 && p.s.ngram > 0)
+                    for (int i = 0; i < nh; i++)
+                        if (!S.ints[40 + i]) compute_bans(p, hl[i], S.seq[hl[i]].P + S.ints[48 + i]);
+            }
+            ok = lc_wait(S);
             continue;
         }
-        if (!df) cl2_add_down(cp, S, S.dp, fl, nf);
+        if (nh == 0) continue;
+        cl2_add_down(cp, S, S.dp, fl, nf);
 
         heads++;
         if (crank == 0) {
             // ---- hand the sampling sequences' residual rows to the head CTAs
             // (which apply the final rmsnorm, generate.c:187-191), release
             // them, wait for all of them, choose the next ids
-            lc_publish_rows(cp, S, hl, nh);
+            lc_publish_rows(cp, S, hl, nh, (int)(heads & 1u));
             if (threadIdx.x == 0) {
                 __threadfence();
                 st_release_u32(cp.go, heads);
@@ -756,7 +790,7 @@ __device__ void cl2_main(const ClusterParams& cp, unsigned char* smem, cg::clust
                 }
             }
             __syncthreads();
-            if (warp < nh) lc_choose(cp, S.seq[hl[warp]], hl[warp], warp, S.ints);
+            if (warp < nh) lc_choose(cp, S.seq[hl[warp]], hl[warp], warp, S.ints, (int)(heads & 1u), true);
             __syncthreads();
             if (p.s.ngram > 0)
                 for (int i = 0; i < nh; i++)

@@ -121,7 +121,7 @@ struct mc_session {
     float* xfin;
     int* hgen;
     unsigned* hsync;              // [0] go, [32] hdone (separate lines)
-    unsigned long long* hkey;     // [Bcap][2] head CTAs' greedy maxima
+    unsigned long long* hkey;     // [2][Bcap][2] head CTAs' greedy maxima (by head-phase parity)
     int last_path;                // 0 grid loop, 1 cluster loop
     // batched prefill work buffers (allocated on first use)
     float *pf_x, *pf_xn, *pf_q, *pf_att, *pf_f;
@@ -726,7 +726,7 @@ mc_status session_create(mc_model* m, int max_batch, int max_seq, int page_len, 
             {(void**)&s->xfin, B * D * 4},
             {(void**)&s->hgen, B * 4},
             {(void**)&s->hsync, 64 * 4},
-            {(void**)&s->hkey, B * 2 * 8},
+            {(void**)&s->hkey, 2 * B * 2 * 8},
         };
         s->cl2_version = ~0u;
         for (auto& a : cl_allocs) {
@@ -861,7 +861,7 @@ mc_status run_cluster(mc_session* s, mc::LoopParams<float>& p) {
     MC_CUDA(cudaMemsetAsync(s->stamps, 0, ((size_t)p.T + 1) * 8, s->stream));
     MC_CUDA(cudaMemsetAsync(s->status, 0, 256, s->stream));
     MC_CUDA(cudaMemsetAsync(s->hsync, 0, 64 * 4, s->stream));
-    MC_CUDA(cudaMemsetAsync(s->hkey, 0, (size_t)s->Bcap * 2 * 8, s->stream));
+    MC_CUDA(cudaMemsetAsync(s->hkey, 0, 2 * (size_t)s->Bcap * 2 * 8, s->stream));
     // MINIMA_CUDA_CLUSTER_NONCOOP=1 skips the cooperative attribute (kernel
     // profilers that cannot instrument cooperative cluster launches)
     const char* noncoop = getenv("MINIMA_CUDA_CLUSTER_NONCOOP");
