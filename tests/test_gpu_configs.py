@@ -151,3 +151,42 @@ def test_long_context_oracle_at_moderate_length(c4l2):
     ok, err = close(trace[0, 0], rtrace[0])
     assert ok, err
     assert np.array_equal(out[0, :counts[0]], ref)
+
+
+@pytest.mark.parametrize("loop", ["cluster", "cluster1", "grid"])
+def test_long_context_against_oracle_at_full_length(gpu, monkeypatch, loop):
+    """The config-5 context length (prompt 1900, 4 greedy steps) on a 2-layer
+    model of the default widths, against the oracle at full length: the
+    batched prefill attends over up to 1899 keys, and each token loop over
+    1900-1903 (the cluster loop's two-phase layers in eight K/V tiles, the
+    keys past the first tile on the unit's second CTA; its five-phase layers
+    with keys split over CTAs; the grid loop's split-K attention).  Logits of
+    every step within the bound while the ids agree; a divergence only where
+    the oracle's top-1/top-2 margin is within twice the bound."""
+    for var in ("MINIMA_CUDA_LOOP", "MINIMA_CUDA_DECODE", "MINIMA_CUDA_PREFILL"):
+        monkeypatch.delenv(var, raising=False)
+    if loop != "cluster":
+        monkeypatch.setenv("MINIMA_CUDA_LOOP", loop)
+    d = O.Dims(4096, 128, 2, 4, 512, 2048)
+    hm = host_model(d, 21)
+    orc = O.OrcModel(d, 21)
+    sess = M.Session(M.DeviceModel(hm), 1, 2048)
+    prompt = O.random_prompt(1900, d.vocab, 95)
+    steps = 4
+    out, counts, st, fpos, trace = sess.generate(prompt[None, :], [1900], 2048,
+                                                 M.options(top_k=1, max_new_tokens=steps), [5],
+                                                 trace_steps=steps)
+    assert sess.last_kernel_name() == ("mc::token_loop_kernel" if loop == "grid" else "mc::cluster_loop_kernel")
+    assert sess.cluster_variant() == {"cluster": 2, "cluster1": 0, "grid": -1}[loop]
+    ref, _, _, rtr = orc.generate(prompt, 2048, 2048, O.make_options(top_k=1, max_new_tokens=steps), 5,
+                                  trace_steps=steps)
+    got = out[0, 1900:counts[0]]
+    want = ref[1900:]
+    for s_ in range(steps):
+        ok, err = close(trace[0, s_], rtr[s_])
+        assert ok, (s_, err)
+        if got[s_] != want[s_]:
+            w = np.sort(rtr[s_][np.isfinite(rtr[s_])])
+            margin = float(w[-1] - w[-2])
+            assert margin <= 2 * (ATOL + RTOL * abs(float(w[-1]))), (s_, margin)
+            break
