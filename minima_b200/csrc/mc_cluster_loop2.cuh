@@ -627,7 +627,6 @@ __device__ void cl2_main(const ClusterParams& cp, unsigned char* smem, cg::clust
     const int nhc = (cp.n_clusters - 1) * cp.cs;
     int* fl = S.ints;        // [16]
     int* hl = S.ints + 16;   // [16]
-    int* toks = S.ints + 40; // [8] ids fed at this step
     const int warp = threadIdx.x >> 5;
 
     if (threadIdx.x == 0) {
@@ -706,24 +705,20 @@ __device__ void cl2_main(const ClusterParams& cp, unsigned char* smem, cg::clust
         __syncthreads();
         const int nf = S.ints[32], nh = S.ints[33];
         if (nf == 0) break;
-        // ids fed at position t and this position's RoPE row, in one round trip
-        if (threadIdx.x < nf) {
-            const int b = fl[threadIdx.x];
+        // this position's RoPE row and the embedding of the id fed at t
+        // (generate.c:86-88), in one round trip once decoding (a generated id
+        // is in the sequence table; a prompt id is read first)
+        for (int j = threadIdx.x; j < p.hd / 2; j += blockDim.x)
+            S.rope[j] = p.rope[(size_t)t * (p.hd / 2) + j];
+        for (int e = threadIdx.x; e < nf * p.D; e += blockDim.x) {
+            const int i = e / p.D, k = e % p.D, b = fl[i];
             const SeqMirror& m = S.seq[b];
             int tok = t < m.P ? (int)p.prompts[(size_t)b * p.prompt_stride + t] : m.tok;
             if (tok < 0 || tok >= p.V) {
-                lc_fail(S, p.status, ST_DEVICE);
+                if (k == 0) lc_fail(S, p.status, ST_DEVICE);
                 tok = 0;
             }
-            toks[threadIdx.x] = tok;
-        }
-        for (int j = threadIdx.x; j < p.hd / 2; j += blockDim.x)
-            S.rope[j] = p.rope[(size_t)t * (p.hd / 2) + j];
-        __syncthreads();
-        // embedding of the token at position t (generate.c:86-88)
-        for (int e = threadIdx.x; e < nf * p.D; e += blockDim.x) {
-            const int i = e / p.D, k = e % p.D;
-            S.x[fl[i] * p.D + k] = __ldg(p.tok_emb + (size_t)toks[i] * p.D + k);
+            S.x[b * p.D + k] = __ldg(p.tok_emb + (size_t)tok * p.D + k);
         }
         __syncthreads();
         for (int l = 0; ok && l < p.L; l++)
