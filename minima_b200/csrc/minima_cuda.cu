@@ -142,7 +142,7 @@ struct mc_session {
     CUtensorMap bd_xmap[3];       // xn, att, f as 64-row boxes (the MMA's N side in decode)
     float* bd_part;               // K-slice partials of the decode GEMMs
     size_t bd_part_floats;
-    float* pf_logits;             // [pf_rows][V] lm_head scratch of mc_model_forward
+    float* pf_logits;             // [Bcap x kPrefillChunk][V] lm_head scratch of mc_model_forward
     float* pf_part;               // K-slice partial tiles of the CUDA-core prefill GEMMs
     size_t pf_part_floats;
     unsigned* pf_cnt;             // per-tile arrival counters of those GEMMs (kept at zero)
@@ -893,7 +893,8 @@ bool prefill_ok(const mc_model* m) {
     return m->D % 4 == 0 && m->F % 4 == 0 && m->hd % 2 == 0 && m->hd <= 64 && m->H / m->K <= 128;
 }
 
-constexpr int kPrefillChunk = 256;   // positions per prefill pass
+constexpr int kPrefillChunk = 256;   // positions per prefill pass (CUDA-core GEMMs, logits)
+constexpr int kPfTcRows = 8192;      // tensor-core prefill: rows per pass it aims for
 
 // cuTensorMapEncodeTiled from the driver, looked up once through the runtime.
 PFN_cuTensorMapEncodeTiled_v12000 tc_encoder() {
@@ -1053,7 +1054,19 @@ mc_status run_prefill(mc_session* s, int batch, const uint16_t* prompts, int str
                       int& launches, float* logits = nullptr, bool logits_dev = false, int S = 0,
                       const mc_forward_caches* caps = nullptr) {
     const mc_model* m = s->m;
-    const size_t rows = (size_t)s->Bcap * std::min(kPrefillChunk, s->cap);
+    constexpr bool kB16 = std::is_same<WT, __nv_bfloat16>::value;
+    constexpr int KD = kB16 ? mc::TC_BF16 : mc::TC_TF32;
+    // bf16 operands need rows of a multiple of 8 elements (16-byte strides)
+    // (the cache capture of model_forward runs the fp32 CUDA-core GEMMs)
+    const bool tc = s->pf_tc && !caps && (!kB16 || (m->D % 8 == 0 && m->F % 8 == 0));
+    // positions per pass: kPrefillChunk, or on the tensor-core path (without
+    // logits) up to four times that, so that a small batch of long prompts
+    // still gives each GEMM about kPfTcRows rows: 128-row tiles for every SM
+    int chunk = kPrefillChunk;
+    if (tc && !logits)
+        chunk = std::max(chunk, std::min(4 * kPrefillChunk, (kPfTcRows / std::max(1, s->Bcap) + 63) / 64 * 64));
+    chunk = std::min(chunk, s->cap);
+    const size_t rows = (size_t)s->Bcap * chunk;
     if (s->pf_rows < rows) {
         float** bufs[] = {&s->pf_x, &s->pf_xn, &s->pf_q, &s->pf_att, &s->pf_f};
         for (float** b : bufs) { cudaFree(*b); *b = nullptr; }
@@ -1073,11 +1086,6 @@ mc_status run_prefill(mc_session* s, int batch, const uint16_t* prompts, int str
             *b = nullptr;
         }
     }
-    constexpr bool kB16 = std::is_same<WT, __nv_bfloat16>::value;
-    constexpr int KD = kB16 ? mc::TC_BF16 : mc::TC_TF32;
-    // bf16 operands need rows of a multiple of 8 elements (16-byte strides)
-    // (the cache capture of model_forward runs the fp32 CUDA-core GEMMs)
-    const bool tc = s->pf_tc && !caps && (!kB16 || (m->D % 8 == 0 && m->F % 8 == 0));
     if (caps && (!s->pf_cap_qkv || s->pf_cap_rows < s->pf_rows)) {
         for (float** b : {&s->pf_cap_qkv, &s->pf_cap_up, &s->pf_cap_gate}) {
             cudaFree(*b);
@@ -1103,7 +1111,8 @@ mc_status run_prefill(mc_session* s, int batch, const uint16_t* prompts, int str
         s->pf_maps_ok = false;
     }
     if (logits && !s->pf_logits) {
-        const size_t bytes = s->pf_rows * (size_t)m->V * 4;
+        // logits passes are kPrefillChunk positions (chunk above)
+        const size_t bytes = (size_t)s->Bcap * std::min(kPrefillChunk, s->cap) * (size_t)m->V * 4;
         if (cudaMalloc(&s->pf_logits, bytes) != cudaSuccess) {
             cudaGetLastError();
             return fail(MC_ERR_NOMEM, "model_forward: lm_head scratch (%zu bytes)", bytes);
@@ -1205,9 +1214,9 @@ mc_status run_prefill(mc_session* s, int batch, const uint16_t* prompts, int str
             MC_CUDA(cudaMemsetAsync(s->pf_cnt, 0, 1024 * sizeof(unsigned), st));
         }
     }
-    for (int c0 = 0; c0 < Pf; c0 += kPrefillChunk) {
+    for (int c0 = 0; c0 < Pf; c0 += chunk) {
         a.c0 = c0;
-        a.c1 = std::min(Pf, c0 + kPrefillChunk);
+        a.c1 = std::min(Pf, c0 + chunk);
         a.chunk = a.c1 - a.c0;
         const int M = batch * a.chunk;
         for (int l = 0; l < m->L; l++) {

@@ -104,6 +104,33 @@ def test_tcgen05_prefill_logits(gpu, monkeypatch):
         assert np.array_equal(out_f[b, :counts_f[b]], ref_ids)
 
 
+def test_tcgen05_prefill_longer_than_a_pass(gpu, monkeypatch):
+    """Few sequences with long prompts: the tensor-core prefill takes up to
+    1024 positions per pass (2 sequences: 1024, then the rest), and the
+    decode logits after it stay within the tensor-core bound of the fp32
+    oracle."""
+    dims = O.Dims(4096, 128, 2, 4, 512, 1536)
+    hm = M.HostModel(dims.vocab, dims.dim, dims.n_layers, dims.n_heads, dims.ffn_dim, dims.max_seq,
+                     seed=13)
+    orc = O.OrcModel(dims, 13)
+    P, steps = 1300, 4
+    prompts = np.stack([O.random_prompt(P, dims.vocab, 40 + b) for b in range(2)])
+    monkeypatch.setenv("MINIMA_CUDA_PREFILL", "tcgen05")
+    sess = M.Session(M.DeviceModel(hm), 2, 1536)
+    _, _, _, _, tr = sess.generate(prompts, [P, P], 1536, M.options(top_k=1, max_new_tokens=steps), [1, 2],
+                                   trace_steps=steps)
+    assert sess.last_prefill()[0] == P - 1
+    for b in range(2):
+        _, _, _, ref_tr = orc.generate(prompts[b], 1536, 1536, O.make_options(top_k=1, max_new_tokens=steps),
+                                       b + 1, trace_steps=steps)
+        got, want = tr[b, 0].astype(np.float64), ref_tr[0].astype(np.float64)
+        finite = np.isfinite(want)
+        assert np.array_equal(np.isfinite(got), finite)
+        err = np.abs(got[finite] - want[finite])
+        bound = TC_ATOL + TC_RTOL * np.abs(want[finite])
+        assert np.all(err <= bound), f"max err {err.max():.3e}"
+
+
 def test_tcgen05_bf16_prefill_logits(gpu, monkeypatch):
     """bf16 weights: the prefill GEMMs run as kind::f16 on bf16 copies of the
     activations; decode logits against the oracle with the same bf16-rounded
